@@ -1,0 +1,295 @@
+"""Batch-1 decode throughput of the Llama-3-8B-shape decoder (bf16) on B200.
+
+Workload: Llama-3-8B shape (vocab 128256, d 4096, 32 layers, 32 q / 8 kv heads of 128,
+SwiGLU 14336, RoPE theta 5e5), weights N(0, 0.02) from seed 0, a 2048-token prompt of
+uniform ids from seed 1, then greedy decode.  A step is one decoded token at batch 1; the
+timed steps are decode positions 2048 .. 2048+K-1 (warm-up steps run at the same positions
+first and are overwritten).  Every step streams ~15.3 GB of weights and KV, far above the
+126 MB L2, so no L2 flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` is device-timed (CUDA events on the library's
+stream, max over ranks); `e2e` times the per-token public call inf_forward() with the id
+copied in from pinned host memory and the argmax read back every step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "inference-project_b200"))
+
+METRIC = "batch-1 decode tokens/s and % of HBM roofline (Llama-3-8B shape, bf16), TP 1/2/4/8"
+PROMPT = 2048
+DECODE_STEPS = 1024
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def oracle_decode_rate(cfg_dict: dict, ctx: int, budget_s: float, warmup: int = 1, max_tokens=None):
+    """Tokens/s of the CPU oracle's decode at context `ctx` on all host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle as O
+    threads = os.cpu_count() or 1
+    t0 = time.time()
+    m = O.OracleModel(cfg_dict, seed=0, n_threads=threads)
+    m.fill_kv_synthetic(ctx)
+    setup_s = time.time() - t0
+    tid = int(O.gen_ids(1, 1, cfg_dict["vocab"])[0])
+    pos = ctx
+    for _ in range(warmup):
+        _, tid = m.forward(np.array([tid], np.uint32), pos)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        _, tid = m.forward(np.array([tid], np.uint32), pos + n)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_tokens and n >= max_tokens) or pos + n + 1 >= cfg_dict["max_seq"]:
+            break
+    m.close()
+    return n / el, n, el, threads, setup_s
+
+
+def run_reference(args, rank: int, world: int):
+    """The reference arm: the oracle's CPU restatement of the decoder (the reference itself has
+    no forward pass), timed on the host cores on this workload's config."""
+    if rank != 0:
+        return
+    import infb200 as I
+    cfg = I.preset(3)
+    d = I.oracle_dict(cfg)
+    # each step is one decoded token at ctx 2048+; bounded so the run ends in a few minutes
+    budget = float(os.environ.get("INF_REF_BUDGET_S", "60"))
+    rate, n, el, threads, setup_s = oracle_decode_rate(d, PROMPT, budget, warmup=min(args.warmup, 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s", "n_gpus": world,
+        "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": 1000.0 * el / n, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "llama3-8b-shape batch-1 decode at ctx 2048+", "model": "llama-3-8b-shape",
+                   "global_batch": 1, "seq_len": PROMPT, "parallelism": "cpu"},
+        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{n} decode tokens at ctx {PROMPT}+ with a synthetic KV cache; "
+                                   f"CPU restatement (oracle/llama_ref.c, OpenMP), the reference has no forward pass; "
+                                   f"setup {setup_s:.0f}s untimed"},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, dist):
+    import numpy as np
+    import torch
+
+    import infb200 as I
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    cfg = I.preset(3)
+    steps, warmup = args.steps, args.warmup
+    if PROMPT + max(steps, warmup) > cfg.max_seq:
+        raise SystemExit(f"--steps/--warmup above {cfg.max_seq - PROMPT}")
+    # prompt ids: Philox stream of seed 1 (same generator as the oracle's)
+    import oracle as O
+    prompt = O.gen_ids(1, PROMPT, cfg.vocab_size)
+
+    eng = I.Engine(cfg, seed=0)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    t0 = time.time()
+    _, first = eng.forward(prompt, 0)
+    prefill_s = time.time() - t0
+    eng.decode(first, PROMPT, warmup)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- timed region: K decode steps chained on the device
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = eng.launches
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        ids, st = eng.decode(first, PROMPT, steps, want_ids=False)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launches = eng.launches - l0
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / steps
+
+    # ---- per-kernel durations of one eager step (events around each launch, same stream)
+    prof = {}
+    for _ in range(3):
+        for k, v in eng.profile_step().items():
+            prof[k] = prof.get(k, 0.0) + v / 3
+
+    # ---- e2e: the per-token public call with host buffers
+    tid = first
+    torch.cuda.synchronize()
+    barrier()
+    e0 = time.perf_counter()
+    for s in range(steps):
+        _, tid = eng.forward([tid], PROMPT + s, want_logits=False)
+    e2e_s = time.perf_counter() - e0
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    # ---- roofline of the dominant kernel (gate/up projection + SwiGLU)
+    peak, peak_kind = load_peaks()
+    L, d, F = cfg.n_layers, cfg.dim, cfg.ffn_dim
+    gu_bytes = 2 * F * d * 2 + d * 4 + F * 2
+    gu_ms = prof.get("gate_up", 0.0) / L
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else None
+    avg_ctx = PROMPT + (steps - 1) / 2
+    step_bytes = I.decode_bytes(cfg, int(avg_ctx))
+    step_gbs = step_bytes / (ms_per_step * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        rate, n, el, threads, setup_s = oracle_decode_rate(I.oracle_dict(cfg), PROMPT, args.cpu_budget)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{n} decode tokens ({el:.1f}s) at ctx {PROMPT}+ with a synthetic KV cache, CPU restatement "
+                         f"(oracle/llama_ref.c, OpenMP); weight generation {setup_s:.0f}s untimed"}
+
+    value = world * steps / (ms * 1e-3) if world > 1 else steps / (ms * 1e-3)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (Philox seed-0 N(0,0.02) weights, seed-1 uniform prompt ids)",
+            "config": {"workload": "llama3-8b-shape batch-1 greedy decode, prompt 2048, timed positions 2048..2048+K-1",
+                       "model": "llama-3-8b-shape", "global_batch": world, "seq_len": PROMPT,
+                       "parallelism": "tp1" if world == 1 else f"replicas{world}",
+                       "l2": "no flush: each step streams 15.3 GB (> 126 MB L2)",
+                       "step_bytes": step_bytes, "step_gbs": step_gbs,
+                       "step_roofline_frac": step_gbs / peak, "prefill_s": prefill_s,
+                       "kernel_ms_per_step": prof},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": (achieved / peak) if achieved else None, "traffic": None,
+                         "kernel": "k_gemv gate/up+SwiGLU (per launch: 2*14336*4096 bf16 weights)",
+                         "peak_kind": peak_kind},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 12,
+                    "d2h_bytes_per_step": 20},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=DECODE_STEPS)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        backend = "gloo" if args.impl == "reference" else "nccl"
+        if backend == "nccl":
+            import torch
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

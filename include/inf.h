@@ -1,0 +1,219 @@
+/*
+ * inf.h -- C ABI of the B200 decoder token loop (libinf.so).
+ *
+ * Drop-in for the entry points of gosutek/inference-project's src/main.cu: the model-load
+ * (model_build, src/main.cu:200), the forward (the embed -> RMSNorm prefix in main(),
+ * src/main.cu:396-412, completed into a full decoder) and a generate loop (absent in the
+ * reference).  Types, arenas and the error enum keep the reference's names and meaning
+ * (src/helpers.h:17-41, src/allocator.h:13-38, src/cuda/api/cuda_allocator.cuh:11-26,
+ * src/cuda/api/cuda_mem_wrapper.cuh:10-16).  Unlike the reference, no function aborts:
+ * every failure is returned as an Error_t and described by inf_last_error_detail().
+ *
+ * Plain pointers and sizes only; no torch or CUDA types appear in the signatures
+ * (streams are passed as void*).  One context per GPU; calls on one model are not
+ * re-entrant.
+ */
+#ifndef INF_H
+#define INF_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__cplusplus)
+extern "C" {
+#endif
+
+/* src/helpers.h:17-28 */
+typedef uint8_t  u8;
+typedef uint16_t u16;
+typedef uint32_t u32;
+typedef uint64_t u64;
+typedef int8_t   i8;
+typedef int16_t  i16;
+typedef int32_t  i32;
+typedef int64_t  i64;
+typedef float    f32;
+typedef double   f64;
+typedef i32      b32;
+
+/* src/helpers.h:30-41; values 0-7 keep the reference's numbering. */
+typedef enum Error_t {
+	Success                 = 0,
+	ErrorMemoryAllocation   = 1,
+	ErrorArenaOutOfMemory   = 2,
+	ErrorAlreadyInitialized = 3,
+	ErrorInvalidValue       = 4,
+	ErrorInvalidHostPtr     = 5,
+	ErrorInvalidDevPtr      = 6,
+	ErrorGeneric            = 7,
+	ErrorCuda               = 8,  /* a CUDA runtime call failed; see inf_last_error_detail() */
+	ErrorBadConfig          = 9,  /* InfConfig violates a shape rule */
+	ErrorTokenOutOfRange    = 10, /* an id >= vocab_size reached a kernel */
+	ErrorKvOutOfRange       = 11, /* a position or KV page outside the cache */
+	ErrorNccl               = 12,
+	ErrorTimeout            = 13, /* a bounded device wait expired */
+	ErrorIo                 = 14,
+	ErrorUnsupported        = 15,
+} Error_t;
+
+typedef enum InfDtype {
+	InfF32  = 0,
+	InfBF16 = 1,
+} InfDtype;
+
+/* src/model.cuh:7-15 (Config), extended with the fields a Llama decoder needs. */
+typedef struct InfConfig {
+	u32 vocab_size;
+	u32 dim;
+	u32 n_layers;
+	u32 n_heads;
+	u32 n_kv_heads;
+	u32 head_dim;
+	u32 ffn_dim;
+	u32 max_seq;        /* positions per sequence */
+	u32 max_batch;      /* sequences decoded together (KV slots) */
+	u32 kv_block;       /* tokens per KV page; 16 */
+	u32 kv_pages;       /* 0: max_batch * ceil(max_seq / kv_block) */
+	u32 prefill_chunk;  /* tokens per prefill pass; 0: min(max_seq, 4096) */
+	u32 dtype;          /* InfDtype of weights, KV cache and activations between kernels */
+	f32 norm_eps;
+	f32 rope_theta;
+	f32 init_std;       /* std of the synthetic weights */
+	u32 tp_rank;
+	u32 tp_size;
+} InfConfig;
+
+/* src/allocator.h:13-25 */
+typedef struct HostArena {
+	u64 reserve_size;
+	u64 commit_size;
+	u64 commit_pos;
+	u64 pos;
+} HostArena;
+
+/* src/cuda/api/cuda_allocator.cuh:11-17.  Pushes are 256-byte aligned (the reference
+ * aligns to 8, which is too little for 16-byte vector loads and TMA). */
+typedef struct DevArena {
+	u8* _d_ptr;
+	u64 size;
+	u64 pos;
+} DevArena;
+
+typedef struct ExecCtx {
+	HostArena host_arena;
+	DevArena  dev_arena;
+} ExecCtx;
+
+typedef struct InfEngine InfEngine;
+
+/* src/model.cuh:62-74 (Model): config, the device weight slab and the engine state. */
+typedef struct Model {
+	InfConfig  config;
+	void*      data;        /* device weight slab */
+	u64        model_bsize; /* bytes of weights */
+	InfEngine* engine;
+} Model;
+
+typedef struct InfStats {
+	f64 prefill_ms;
+	f64 decode_ms;
+	u32 n_prompt;
+	u32 n_new;
+	u64 kernel_launches;
+} InfStats;
+
+/* ---- execution context and arenas ------------------------------------------------ */
+/* src/allocator.h:34-35 */
+Error_t exec_ctx_create(ExecCtx** ctx);
+Error_t exec_ctx_destroy(ExecCtx** ctx);
+/* src/allocator.h:36-41 */
+Error_t arena_host_create(HostArena** const arena, const u64 reserve_size, const u64 commit_size);
+Error_t arena_host_destroy(HostArena* arena);
+Error_t arena_host_push(HostArena* const arena, const u64 req_size, void** ptr_out);
+void    arena_host_pop(HostArena* const arena, u64 size);
+void    arena_host_pop_at(HostArena* const arena, u64 pos);
+u64     mem_arena_host_pos_get(const HostArena* const arena);
+/* src/cuda/api/cuda_allocator.cuh:19-26 */
+Error_t arena_dev_create(DevArena* const arena, const u64 bsize);
+Error_t arena_dev_destroy(DevArena* arena);
+Error_t arena_dev_push(DevArena* const arena, const u64 bsize, void** ptr_out);
+void    arena_dev_pop(DevArena* const arena, u64 bsize);
+void    arena_dev_pop_at(DevArena* const arena, u64 pos);
+u64     arena_dev_pos_get(const DevArena* const arena);
+
+/* ---- checked copies: src/cuda/api/cuda_mem_wrapper.cuh:12-16 ------------------------ */
+Error_t cu_memcpy_htd(void* dst, const void* src, const u64 bsize);
+Error_t cu_memcpy_htd_async(void* dst, const void* src, const u64 bsize, void* stream);
+Error_t cu_memcpy_dth(void* dst, const void* src, const u64 bsize);
+Error_t cu_memset(void* s, i32 c, u64 n);
+
+/* ---- stand-alone kernels ----------------------------------------------------------- */
+/* Replaces k_fetch_input_embeddings (src/cuda/kernels/input_embeddings.cuh:20-24) and its
+ * launch (src/main.cu:396-404): out[t,:] = table[ids[t],:] for any dim, bit-exact.  Ids
+ * >= vocab_size produce ErrorTokenOutOfRange (and zero rows) instead of reading out of
+ * bounds.  dtype: InfDtype of table and out.  Device pointers; synchronous. */
+Error_t inf_fetch_input_embeddings(const u32* d_ids, u64 n_tokens, u32 dim, u32 vocab_size, const void* d_table,
+                                   void* d_out, u32 dtype, void* stream);
+/* Replaces k_rmsnorm (src/cuda/kernels/rmsnorm.cuh:15-18, launch src/main.cu:409):
+ * y[t,i] = x[t,i] * g[i] / sqrt(mean_i(x[t,i]^2) + eps), fp32 accumulation, one gain
+ * vector for every row, any dim, y may equal x.  Device pointers; synchronous. */
+Error_t inf_rmsnorm(const void* d_x, void* d_y, u32 rows, u32 dim, const void* d_gain, f32 eps, u32 dtype,
+                    void* stream);
+
+/* ---- model ------------------------------------------------------------------------- */
+/* Built-in shapes: 1 tiny fp32 (d288), 2 TinyLlama-1.1B, 3 Llama-3-8B, 4 Llama-3-8B batch 64,
+ * 5 Llama-3-8B 32k prefill. */
+Error_t inf_config_preset(u32 preset, InfConfig* out);
+/* model_build (src/main.cu:200-352).  weights_path NULL: synthetic weights N(0, init_std)
+ * from `seed` (Philox4x32-10), gains 1.0.  Creates *ctx if it is NULL. */
+Error_t inf_model_build(ExecCtx** ctx, Model* model, const InfConfig* config, const char* weights_path, u64 seed);
+/* model_destroy (src/main.cu:354-358) */
+Error_t inf_model_destroy(ExecCtx** ctx, Model* model);
+
+/* Forward n_tokens of one sequence starting at start_pos (KV written for each).  ids,
+ * logits_out (vocab_size f32 of the last token, may be NULL) and argmax_out (may be NULL)
+ * may be host or device pointers. */
+Error_t inf_forward(Model* model, const u32* ids, u32 n_tokens, u32 start_pos, u32 seq_slot, f32* logits_out,
+                    u32* argmax_out);
+/* One decode token for each of n_seqs sequences: token ids[i] at position positions[i]
+ * of slot seq_slots[i].  logits_out [n_seqs x vocab_size] may be NULL. */
+Error_t inf_forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const u32* ids, const u32* positions,
+                          f32* logits_out, u32* argmax_out);
+/* Prefill the prompt into slot 0, then n_new greedy steps; out_ids[i] is the i-th
+ * generated id.  Host pointers. */
+Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u32* out_ids, InfStats* stats);
+/* Continue a sequence: feed first_id at start_pos, then n_steps - 1 more greedy steps, all
+ * chained on the device (one CUDA graph replay per token, no host round trip).  out_ids
+ * (host or device, may be NULL) receives the n_steps generated ids. */
+Error_t inf_decode(Model* model, u32 seq_slot, u32 start_pos, u32 first_id, u32 n_steps, u32* out_ids,
+                   InfStats* stats);
+/* Release the KV pages of a sequence slot. */
+Error_t inf_seq_reset(Model* model, u32 seq_slot);
+
+/* ---- introspection ------------------------------------------------------------------ */
+const char* inf_error_string(Error_t err);
+const char* inf_last_error_detail(void);
+void*       inf_model_stream(Model* model);
+u64         inf_kernel_launches(Model* model);
+/* Bytes the decode step of one token streams from HBM: weights + KV read for ctx. */
+u64         inf_decode_bytes(const InfConfig* config, u32 ctx);
+/* Time each kernel kind of one eager (non-graph) decode step at the slot's current
+ * position: ms_out[k] for k in InfKernelKind; returns the number of kinds. */
+u32         inf_profile_decode_step(Model* model, f32* ms_out, u32 max_kinds);
+
+typedef enum InfKernelKind {
+	InfKEmbed = 0,
+	InfKQkv   = 1,
+	InfKAttn  = 2,
+	InfKO     = 3,
+	InfKGateUp = 4,
+	InfKDown  = 5,
+	InfKLmHead = 6,
+	InfKNumKinds = 7,
+} InfKernelKind;
+
+#if defined(__cplusplus)
+}
+#endif
+
+#endif /* INF_H */

@@ -1,0 +1,988 @@
+// Engine: model build (model_build, src/main.cu:200-352), forward and generate for the
+// decoder token loop, and the stand-alone kernels of the C ABI (include/inf.h).
+//
+// Device memory is one arena slab (src/cuda/api/cuda_allocator.cu:4-19) holding, in
+// order: weights in the device layout, RoPE tables, the paged KV cache, block tables,
+// activations and decode scratch.  The batch-1 decode step is one CUDA graph whose
+// kernels read the token id and position from device memory and advance them, so
+// replays chain without the host.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <utility>
+#include <vector>
+
+#include "common.cuh"
+#include "k_attn_decode.cuh"
+#include "k_gemv.cuh"
+#include "k_small.cuh"
+#include "runtime.h"
+#include "synth.cuh"
+
+using namespace inf;
+
+struct LayerW {
+	void* wqkv;      // [(Hl + 2 KVl) hd x d], rows of each head in (i, i+hd/2) pairs
+	void* wo;        // [d x Hl hd]
+	void* wgu;       // [2 Fl x d], rows alternate gate_j / up_j
+	void* wd;        // [d x Fl]
+	void* attn_norm; // [d]
+	void* ffn_norm;  // [d]
+	void* kpool;     // [pages][KVl][blk][hd]
+	void* vpool;
+};
+
+struct InfEngine {
+	InfConfig cfg;
+	ExecCtx* ctx = nullptr;
+	int device = 0;
+	int sm_count = 148;
+	cudaStream_t stream = nullptr;
+	size_t esz = 2; // bytes of the storage dtype
+	// local (per tensor-parallel rank) shapes
+	int Hl = 0, KVl = 0, Fl = 0, Vl = 0;
+	// weights
+	void* embed = nullptr;
+	void* lm_head = nullptr;
+	void* final_norm = nullptr;
+	std::vector<LayerW> layers;
+	u64 weight_bytes = 0;
+	float* rope_cos = nullptr;
+	float* rope_sin = nullptr;
+	// paged KV
+	int pages_per_seq = 0, n_pages = 0;
+	int* block_table = nullptr;             // device [max_batch][pages_per_seq]
+	std::vector<int> h_block_table;         // host mirror
+	std::vector<std::vector<int>> seq_pages;
+	std::vector<int> free_pages;
+	// activations / scratch (batch-1 decode)
+	float* resid = nullptr;
+	void* q = nullptr;
+	void* attn = nullptr;
+	void* h = nullptr;
+	float* logits = nullptr;
+	int* ctl = nullptr; // [kCtlWords]: id, pos, slot, step, err (one H2D / one D2H per token)
+	uint32_t* cur_id = nullptr;
+	int* pos = nullptr;
+	int* slot = nullptr;
+	uint32_t* out_ids = nullptr;
+	uint32_t* step = nullptr;
+	unsigned long long* best = nullptr;
+	unsigned* lm_counter = nullptr;
+	float* attn_part = nullptr;
+	unsigned* attn_counters = nullptr;
+	int* err = nullptr;
+	uint32_t* d_ids = nullptr; // staged ids [max_seq]
+	int max_out = 0;
+	int attn_splits = 1;
+	// pinned host staging
+	uint32_t* h_pin = nullptr; // [max_seq + 16]
+	int* h_ctl = nullptr;      // [2 * kCtlWords]: staging in, staging out
+	// decode graph
+	cudaGraphExec_t decode_exec = nullptr;
+	int graph_kernels = 0;
+	u64 launches = 0;
+	bool profiling = false;
+	bool dry = false; // walk the launch sequence without launching (sets kernel attributes)
+	cudaEvent_t prof_ev[2] = {nullptr, nullptr};
+	float prof_ms[InfKNumKinds] = {};
+};
+
+namespace {
+
+enum CtlWord { kCtlId = 0, kCtlPos = 1, kCtlSlot = 2, kCtlStep = 3, kCtlErr = 4, kCtlWords = 8 };
+
+std::mutex g_attr_mutex;
+
+Error_t map_dev_err(int v)
+{
+	switch (v) {
+	case kDevOk: return Success;
+	case kDevTimeout: return fail(ErrorTimeout, "a bounded device wait expired");
+	case kDevTokenRange: return fail(ErrorTokenOutOfRange, "token id >= vocab_size");
+	case kDevKvRange: return fail(ErrorKvOutOfRange, "KV position or page outside the cache");
+	default: return fail(ErrorGeneric, "device error word %d", v);
+	}
+}
+
+Error_t check_dev_err(InfEngine* e)
+{
+	int v = 0;
+	INF_CUDA_TRY(cudaMemcpyAsync(&v, e->err, sizeof v, cudaMemcpyDeviceToHost, e->stream));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	if (v == kDevOk) return Success;
+	INF_CUDA_TRY(cudaMemsetAsync(e->err, 0, sizeof(int), e->stream));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	return map_dev_err(v);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(InfEngine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args)
+{
+	cudaLaunchConfig_t lc = {};
+	lc.gridDim = grid;
+	lc.blockDim = block;
+	lc.dynamicSmemBytes = smem;
+	lc.stream = e->stream;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	lc.attrs = attr;
+	lc.numAttrs = e->profiling ? 0 : 1;
+	if (e->dry) return cudaSuccess;
+	e->launches++;
+	return cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...);
+}
+
+template <typename K>
+cudaError_t set_smem(K kern, size_t bytes)
+{
+	std::lock_guard<std::mutex> lk(g_attr_mutex);
+	return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// --------------------------------------------------------------------------- GEMV
+template <typename T, int UPL, int EPI>
+Error_t launch_gemv_u(InfEngine* e, GemvArgs a)
+{
+	constexpr int RPC = GemvShape<UPL, EPI>::kRpc;
+	const size_t row_bytes = (size_t)a.K * sizeof(T);
+	a.stage_bytes = (uint32_t)(RPC * row_bytes);
+	a.stages = std::min<int>(kGemvMaxStages, (int)(kGemvRingBytes / a.stage_bytes));
+	if (a.stages < 2) return fail(ErrorUnsupported, "gemv: row of %zu bytes too long", row_bytes);
+	const int unit_rows = EpiTraits<EPI>::kPaired ? 2 : 1;
+	const int grid = std::max(1, std::min(e->sm_count, a.N / unit_rows));
+	const size_t smem = gemv_smem_bytes();
+	static bool attr_done = false;
+	if (!attr_done) {
+		INF_CUDA_TRY(set_smem(k_gemv<T, UPL, EPI>, smem));
+		attr_done = true;
+	}
+	INF_CUDA_TRY(launch(e, k_gemv<T, UPL, EPI>, dim3(grid), dim3(kGemvThreads), smem, a));
+	return Success;
+}
+
+template <typename T, int EPI>
+Error_t launch_gemv(InfEngine* e, const GemvArgs& a)
+{
+	const size_t row_bytes = (size_t)a.K * sizeof(T);
+	if (row_bytes % 16 != 0) return fail(ErrorUnsupported, "gemv: K*%zu not a multiple of 16 bytes", sizeof(T));
+	const int units = (int)(row_bytes / 16);
+	const int upl = (units + kGemvConsumers - 1) / kGemvConsumers;
+	if (upl <= 1) return launch_gemv_u<T, 1, EPI>(e, a);
+	if (upl <= 2) return launch_gemv_u<T, 2, EPI>(e, a);
+	if (upl <= 4) return launch_gemv_u<T, 4, EPI>(e, a);
+	if (upl <= 8) return launch_gemv_u<T, 8, EPI>(e, a);
+	return fail(ErrorUnsupported, "gemv: K=%d too long", a.K);
+}
+
+GemvArgs gemv_base(InfEngine* e, const void* W, int N, int K)
+{
+	GemvArgs a;
+	memset(&a, 0, sizeof a);
+	a.W = W;
+	a.N = N;
+	a.K = K;
+	a.eps = e->cfg.norm_eps;
+	a.err = e->err;
+	return a;
+}
+
+// --------------------------------------------------------------------------- decode step
+Error_t prof_begin(InfEngine* e)
+{
+	if (e->profiling) INF_CUDA_TRY(cudaEventRecord(e->prof_ev[0], e->stream));
+	return Success;
+}
+Error_t prof_end(InfEngine* e, int kind)
+{
+	if (!e->profiling) return Success;
+	INF_CUDA_TRY(cudaEventRecord(e->prof_ev[1], e->stream));
+	INF_CUDA_TRY(cudaEventSynchronize(e->prof_ev[1]));
+	float ms = 0.f;
+	INF_CUDA_TRY(cudaEventElapsedTime(&ms, e->prof_ev[0], e->prof_ev[1]));
+	e->prof_ms[kind] += ms;
+	return Success;
+}
+
+template <typename T>
+Error_t enqueue_decode_step(InfEngine* e)
+{
+	const InfConfig& c = e->cfg;
+	const int d = (int)c.dim, hd = (int)c.head_dim;
+	const int kernels_before = (int)e->launches;
+
+	INF_TRY(prof_begin(e));
+	INF_CUDA_TRY(launch(e, k_embed<T, float>, dim3((d + 255) / 256, 1), dim3(256), 0, (const uint32_t*)e->cur_id, 1, d,
+	                    c.vocab_size, (const T*)e->embed, e->resid, e->err));
+	INF_TRY(prof_end(e, InfKEmbed));
+
+	for (u32 l = 0; l < c.n_layers; ++l) {
+		const LayerW& L = e->layers[l];
+		// QKV + RoPE + KV write, RMSNorm fused in front
+		{
+			GemvArgs a = gemv_base(e, L.wqkv, (e->Hl + 2 * e->KVl) * hd, d);
+			a.resid_in = e->resid;
+			a.gain = L.attn_norm;
+			a.out = e->q;
+			a.kpool = L.kpool;
+			a.vpool = L.vpool;
+			a.block_table = e->block_table;
+			a.pages_per_seq = e->pages_per_seq;
+			a.max_pages = e->n_pages;
+			a.pos = e->pos;
+			a.slot = e->slot;
+			a.rope_cos = e->rope_cos;
+			a.rope_sin = e->rope_sin;
+			a.head_dim = hd;
+			a.n_q_heads = e->Hl;
+			a.n_kv_heads = e->KVl;
+			a.kv_block = (int)c.kv_block;
+			a.max_seq = (int)c.max_seq;
+			INF_TRY(prof_begin(e));
+			INF_TRY((launch_gemv<T, kEpiQkv>(e, a)));
+			INF_TRY(prof_end(e, InfKQkv));
+		}
+		// attention
+		{
+			AttnDecodeArgs a;
+			memset(&a, 0, sizeof a);
+			a.q = e->q;
+			a.kpool = L.kpool;
+			a.vpool = L.vpool;
+			a.block_table = e->block_table;
+			a.pages_per_seq = e->pages_per_seq;
+			a.max_pages = e->n_pages;
+			a.tok_slot = e->slot;
+			a.tok_pos = e->pos;
+			a.H = e->Hl;
+			a.KV = e->KVl;
+			a.hd = hd;
+			a.blk = (int)c.kv_block;
+			a.n_splits = e->attn_splits;
+			a.scale = (float)(1.0 / std::sqrt((double)hd));
+			a.part = e->attn_part;
+			a.counters = e->attn_counters;
+			a.out = e->attn;
+			a.err = e->err;
+			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block);
+			INF_TRY(prof_begin(e));
+			INF_CUDA_TRY(launch(e, k_attn_decode<T>, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
+			INF_TRY(prof_end(e, InfKAttn));
+		}
+		// O-proj + residual
+		{
+			GemvArgs a = gemv_base(e, L.wo, d, e->Hl * hd);
+			a.xin = e->attn;
+			a.resid = e->resid;
+			INF_TRY(prof_begin(e));
+			INF_TRY((launch_gemv<T, kEpiResid>(e, a)));
+			INF_TRY(prof_end(e, InfKO));
+		}
+		// gate/up + SwiGLU, RMSNorm fused in front
+		{
+			GemvArgs a = gemv_base(e, L.wgu, 2 * e->Fl, d);
+			a.resid_in = e->resid;
+			a.gain = L.ffn_norm;
+			a.out = e->h;
+			INF_TRY(prof_begin(e));
+			INF_TRY((launch_gemv<T, kEpiSwiglu>(e, a)));
+			INF_TRY(prof_end(e, InfKGateUp));
+		}
+		// down + residual
+		{
+			GemvArgs a = gemv_base(e, L.wd, d, e->Fl);
+			a.xin = e->h;
+			a.resid = e->resid;
+			INF_TRY(prof_begin(e));
+			INF_TRY((launch_gemv<T, kEpiResid>(e, a)));
+			INF_TRY(prof_end(e, InfKDown));
+		}
+	}
+	// final norm + LM head + greedy argmax; advances id, position and step
+	{
+		GemvArgs a = gemv_base(e, e->lm_head, e->Vl, d);
+		a.resid_in = e->resid;
+		a.gain = e->final_norm;
+		a.logits = e->logits;
+		a.best = e->best;
+		a.counter = e->lm_counter;
+		a.cur_id = e->cur_id;
+		a.out_ids = e->out_ids;
+		a.step = e->step;
+		a.pos_rw = e->pos;
+		a.max_out = e->max_out;
+		INF_TRY(prof_begin(e));
+		INF_TRY((launch_gemv<T, kEpiLogits>(e, a)));
+		INF_TRY(prof_end(e, InfKLmHead));
+	}
+	e->graph_kernels = (int)e->launches - kernels_before;
+	return Success;
+}
+
+Error_t enqueue_step(InfEngine* e)
+{
+	return e->cfg.dtype == InfBF16 ? enqueue_decode_step<bf16>(e) : enqueue_decode_step<float>(e);
+}
+
+Error_t build_decode_graph(InfEngine* e)
+{
+	cudaGraph_t g = nullptr;
+	e->dry = true; // shared-memory attributes are set outside the capture
+	const Error_t dr = enqueue_step(e);
+	e->dry = false;
+	INF_TRY(dr);
+	INF_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+	const u64 before = e->launches;
+	Error_t r = enqueue_step(e);
+	cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+	e->launches = before;
+	if (r != Success) {
+		if (g) cudaGraphDestroy(g);
+		return r;
+	}
+	if (ce != cudaSuccess) return fail(ErrorCuda, "graph capture: %s", cudaGetErrorString(ce));
+	ce = cudaGraphInstantiate(&e->decode_exec, g, 0);
+	cudaGraphDestroy(g);
+	if (ce != cudaSuccess) return fail(ErrorCuda, "graph instantiate: %s", cudaGetErrorString(ce));
+	return Success;
+}
+
+Error_t launch_decode_graph(InfEngine* e)
+{
+	INF_CUDA_TRY(cudaGraphLaunch(e->decode_exec, e->stream));
+	e->launches += (u64)e->graph_kernels;
+	return Success;
+}
+
+// --------------------------------------------------------------------------- pages
+Error_t ensure_pages(InfEngine* e, u32 slot, u32 n_positions)
+{
+	const u32 blk = e->cfg.kv_block;
+	const u32 need = (n_positions + blk - 1) / blk;
+	if (need > (u32)e->pages_per_seq) return fail(ErrorKvOutOfRange, "sequence needs %u pages > %d", need, e->pages_per_seq);
+	std::vector<int>& pg = e->seq_pages[slot];
+	bool changed = false;
+	while (pg.size() < need) {
+		if (e->free_pages.empty()) return fail(ErrorArenaOutOfMemory, "KV cache out of pages");
+		const int p = e->free_pages.back();
+		e->free_pages.pop_back();
+		e->h_block_table[(size_t)slot * e->pages_per_seq + pg.size()] = p;
+		pg.push_back(p);
+		changed = true;
+	}
+	if (changed) {
+		// pageable source: the copy is staged before the call returns, ordered on the stream
+		INF_CUDA_TRY(cudaMemcpyAsync(e->block_table + (size_t)slot * e->pages_per_seq,
+		                             e->h_block_table.data() + (size_t)slot * e->pages_per_seq,
+		                             sizeof(int) * e->pages_per_seq, cudaMemcpyHostToDevice, e->stream));
+	}
+	return Success;
+}
+
+Error_t release_pages(InfEngine* e, u32 slot)
+{
+	std::vector<int>& pg = e->seq_pages[slot];
+	for (int p : pg) e->free_pages.push_back(p);
+	pg.clear();
+	std::fill(e->h_block_table.begin() + (size_t)slot * e->pages_per_seq,
+	          e->h_block_table.begin() + (size_t)(slot + 1) * e->pages_per_seq, -1);
+	INF_CUDA_TRY(cudaMemcpyAsync(e->block_table + (size_t)slot * e->pages_per_seq,
+	                             e->h_block_table.data() + (size_t)slot * e->pages_per_seq, sizeof(int) * e->pages_per_seq,
+	                             cudaMemcpyHostToDevice, e->stream));
+	return Success;
+}
+
+// --------------------------------------------------------------------------- build
+Error_t validate(const InfConfig& c)
+{
+	if (c.vocab_size == 0 || c.dim == 0 || c.n_layers == 0 || c.n_heads == 0 || c.n_kv_heads == 0 || c.head_dim == 0 ||
+	    c.ffn_dim == 0 || c.max_seq == 0 || c.max_batch == 0 || c.kv_block == 0)
+		return fail(ErrorBadConfig, "zero-sized config field");
+	if (c.dtype != InfF32 && c.dtype != InfBF16) return fail(ErrorBadConfig, "dtype %u", c.dtype);
+	if (c.n_heads % c.n_kv_heads) return fail(ErrorBadConfig, "n_heads %% n_kv_heads != 0");
+	if (c.head_dim % 2) return fail(ErrorBadConfig, "head_dim must be even");
+	const u32 tp = c.tp_size ? c.tp_size : 1;
+	if (c.tp_rank >= tp) return fail(ErrorBadConfig, "tp_rank >= tp_size");
+	if (c.n_kv_heads % tp || c.ffn_dim % tp || c.vocab_size % tp) return fail(ErrorBadConfig, "shapes not divisible by tp_size");
+	const u32 vec = c.dtype == InfBF16 ? 8 : 4;
+	if (c.dim % vec || c.ffn_dim / tp % vec || (c.n_heads / tp * c.head_dim) % vec)
+		return fail(ErrorBadConfig, "dim, ffn_dim and heads*head_dim must be multiples of %u", vec);
+	if ((c.n_heads / c.n_kv_heads) * c.head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
+		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kAttnThreads * kAttnMaxAcc);
+	if (c.dim > 16384 || c.ffn_dim / tp > 16384) return fail(ErrorUnsupported, "dim/ffn above 16384");
+	if (!(c.norm_eps >= 0.0f) || !(c.rope_theta > 0.0f)) return fail(ErrorBadConfig, "eps/theta");
+	return Success;
+}
+
+struct Pusher {
+	DevArena* a;
+	Error_t err = Success;
+	template <typename P>
+	void push(P** out, u64 bytes)
+	{
+		if (err != Success) return;
+		void* p = nullptr;
+		err = arena_dev_push(a, bytes, &p);
+		*out = (P*)p;
+	}
+};
+
+template <typename T>
+Error_t synth(InfEngine* e, void* dst, u64 rows, u64 cols, SynthArgs a)
+{
+	a.dst = dst;
+	a.rows = rows;
+	a.cols = cols;
+	const u64 n = rows * cols;
+	const int grid = (int)std::min<u64>((n + 255) / 256, (u64)e->sm_count * 16);
+	k_synth<T><<<grid, 256, 0, e->stream>>>(a);
+	INF_CUDA_TRY(cudaGetLastError());
+	return Success;
+}
+
+template <typename T>
+Error_t generate_weights(InfEngine* e, u64 seed)
+{
+	const InfConfig& c = e->cfg;
+	const u64 d = c.dim, hd = c.head_dim;
+	const u32 rk = c.tp_rank;
+	const float scale = synth_scale(c.init_std);
+	auto base = [&](int layer, uint32_t kind) {
+		SynthArgs a;
+		memset(&a, 0, sizeof a);
+		a.key[0] = stream_key(seed, tensor_stream(layer, kind));
+		a.scale = scale;
+		a.map = kMapPlain;
+		return a;
+	};
+	// embedding: full table on every rank; LM head: vocab rows split across ranks
+	{
+		SynthArgs a = base(-1, kEmbed);
+		a.canon_cols = d;
+		INF_TRY(synth<T>(e, e->embed, c.vocab_size, d, a));
+	}
+	{
+		SynthArgs a = base(-1, kLmHead);
+		a.canon_cols = d;
+		a.row_offset = (u64)rk * e->Vl;
+		INF_TRY(synth<T>(e, e->lm_head, e->Vl, d, a));
+	}
+	{
+		SynthArgs a = base(-1, kFinalNorm);
+		a.ones = 1;
+		a.canon_cols = d;
+		INF_TRY(synth<T>(e, e->final_norm, 1, d, a));
+	}
+	for (u32 l = 0; l < c.n_layers; ++l) {
+		const LayerW& L = e->layers[l];
+		{
+			SynthArgs a = base((int)l, kWq);
+			a.map = kMapQkv;
+			a.key[1] = stream_key(seed, tensor_stream((int)l, kWk));
+			a.key[2] = stream_key(seed, tensor_stream((int)l, kWv));
+			a.canon_cols = d;
+			a.head_dim = (int)hd;
+			a.n_q_heads = e->Hl;
+			a.n_kv_heads = e->KVl;
+			a.q_head0 = (int)rk * e->Hl;
+			a.kv_head0 = (int)rk * e->KVl;
+			INF_TRY(synth<T>(e, L.wqkv, (u64)(e->Hl + 2 * e->KVl) * hd, d, a));
+		}
+		{
+			SynthArgs a = base((int)l, kWo); // columns split across ranks (row-parallel)
+			a.canon_cols = (u64)c.n_heads * hd;
+			a.col_offset = (u64)rk * e->Hl * hd;
+			INF_TRY(synth<T>(e, L.wo, d, (u64)e->Hl * hd, a));
+		}
+		{
+			SynthArgs a = base((int)l, kWgate);
+			a.map = kMapGateUp;
+			a.key[1] = stream_key(seed, tensor_stream((int)l, kWup));
+			a.canon_cols = d;
+			a.row_offset = (u64)rk * e->Fl;
+			INF_TRY(synth<T>(e, L.wgu, 2 * (u64)e->Fl, d, a));
+		}
+		{
+			SynthArgs a = base((int)l, kWdown);
+			a.canon_cols = c.ffn_dim;
+			a.col_offset = (u64)rk * e->Fl;
+			INF_TRY(synth<T>(e, L.wd, d, e->Fl, a));
+		}
+		{
+			SynthArgs a = base((int)l, kAttnNorm);
+			a.ones = 1;
+			a.canon_cols = d;
+			INF_TRY(synth<T>(e, L.attn_norm, 1, d, a));
+			INF_TRY(synth<T>(e, L.ffn_norm, 1, d, a));
+		}
+	}
+	return Success;
+}
+
+void rope_tables(const InfConfig& c, std::vector<float>& cs, std::vector<float>& sn)
+{
+	const u32 half = c.head_dim / 2;
+	cs.resize((size_t)c.max_seq * half);
+	sn.resize(cs.size());
+	for (u32 p = 0; p < c.max_seq; ++p)
+		for (u32 i = 0; i < half; ++i) {
+			const double inv_freq = std::pow((double)c.rope_theta, -2.0 * (double)i / (double)c.head_dim);
+			const double ang = (double)p * inv_freq;
+			cs[(size_t)p * half + i] = (float)std::cos(ang);
+			sn[(size_t)p * half + i] = (float)std::sin(ang);
+		}
+}
+
+Error_t engine_build(InfEngine* e, u64 seed)
+{
+	InfConfig& c = e->cfg;
+	if (c.kv_block == 0) c.kv_block = 16;
+	if (c.tp_size == 0) c.tp_size = 1;
+	INF_TRY(validate(c));
+	INF_CUDA_TRY(cudaGetDevice(&e->device));
+	INF_CUDA_TRY(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, e->device));
+	INF_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+	INF_CUDA_TRY(cudaEventCreate(&e->prof_ev[0]));
+	INF_CUDA_TRY(cudaEventCreate(&e->prof_ev[1]));
+	e->esz = c.dtype == InfBF16 ? 2 : 4;
+	const u32 tp = c.tp_size;
+	e->Hl = (int)(c.n_heads / tp);
+	e->KVl = (int)(c.n_kv_heads / tp);
+	e->Fl = (int)(c.ffn_dim / tp);
+	e->Vl = (int)(c.vocab_size / tp);
+	const u64 d = c.dim, hd = c.head_dim, es = e->esz, L = c.n_layers;
+	e->pages_per_seq = (int)((c.max_seq + c.kv_block - 1) / c.kv_block);
+	e->n_pages = c.kv_pages ? (int)c.kv_pages : (int)(c.max_batch * (u32)e->pages_per_seq);
+	e->max_out = (int)c.max_seq;
+	const int G = e->Hl / e->KVl;
+	(void)G;
+	// splits: ~2 CTAs per SM over the KV heads of one token, at most one page per split
+	e->attn_splits = std::max(1, std::min(e->pages_per_seq, (2 * e->sm_count + e->KVl - 1) / e->KVl));
+
+	// ---- sizes
+	const u64 w_layer = ((u64)(e->Hl + 2 * e->KVl) * hd * d + d * e->Hl * hd + 2ull * e->Fl * d + d * e->Fl + 2 * d) * es;
+	const u64 w_total = (2ull * c.vocab_size * d) * es + d * es + L * w_layer; // embed is full, LM head is a shard
+	const u64 page_elems = (u64)e->KVl * c.kv_block * hd;
+	const u64 kv_total = 2ull * L * e->n_pages * page_elems * es;
+	const u64 act = d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + (u64)e->Hl * e->attn_splits * (hd + 2) * 4;
+	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024;
+	const u64 total = w_total + kv_total + act + (u64)c.max_seq * hd * 4 + (u64)c.max_batch * e->pages_per_seq * 4 +
+	                  (u64)c.max_seq * 8 + slack;
+
+	if (!e->ctx) INF_TRY(exec_ctx_create(&e->ctx));
+	INF_TRY(arena_dev_create(&e->ctx->dev_arena, total));
+	Pusher P{&e->ctx->dev_arena};
+	const u64 w_begin = arena_dev_pos_get(&e->ctx->dev_arena);
+	P.push(&e->embed, (u64)c.vocab_size * d * es);
+	e->layers.resize(L);
+	for (u32 l = 0; l < L; ++l) {
+		LayerW& Ly = e->layers[l];
+		P.push(&Ly.wqkv, (u64)(e->Hl + 2 * e->KVl) * hd * d * es);
+		P.push(&Ly.wo, d * e->Hl * hd * es);
+		P.push(&Ly.wgu, 2ull * e->Fl * d * es);
+		P.push(&Ly.wd, d * e->Fl * es);
+		P.push(&Ly.attn_norm, d * es);
+		P.push(&Ly.ffn_norm, d * es);
+	}
+	P.push(&e->final_norm, d * es);
+	P.push(&e->lm_head, (u64)e->Vl * d * es);
+	e->weight_bytes = arena_dev_pos_get(&e->ctx->dev_arena) - w_begin;
+	P.push(&e->rope_cos, (u64)c.max_seq * (hd / 2) * 4);
+	P.push(&e->rope_sin, (u64)c.max_seq * (hd / 2) * 4);
+	for (u32 l = 0; l < L; ++l) {
+		P.push(&e->layers[l].kpool, e->n_pages * page_elems * es);
+		P.push(&e->layers[l].vpool, e->n_pages * page_elems * es);
+	}
+	P.push(&e->block_table, (u64)c.max_batch * e->pages_per_seq * 4);
+	P.push(&e->resid, d * 4);
+	P.push(&e->q, (u64)e->Hl * hd * es);
+	P.push(&e->attn, (u64)e->Hl * hd * es);
+	P.push(&e->h, (u64)e->Fl * es);
+	P.push(&e->logits, (u64)e->Vl * 4);
+	P.push(&e->ctl, kCtlWords * sizeof(int));
+	P.push(&e->best, 16);
+	P.push(&e->lm_counter, 16);
+	P.push(&e->out_ids, (u64)e->max_out * 4);
+	P.push(&e->d_ids, (u64)c.max_seq * 4);
+	P.push(&e->attn_part, (u64)e->Hl * e->attn_splits * (hd + 2) * 4);
+	P.push(&e->attn_counters, (u64)e->KVl * 4);
+	if (P.err != Success) return P.err;
+	e->cur_id = reinterpret_cast<uint32_t*>(e->ctl + kCtlId);
+	e->pos = e->ctl + kCtlPos;
+	e->slot = e->ctl + kCtlSlot;
+	e->step = reinterpret_cast<uint32_t*>(e->ctl + kCtlStep);
+	e->err = e->ctl + kCtlErr;
+
+	INF_CUDA_TRY(cudaMemsetAsync(e->ctx->dev_arena._d_ptr + w_begin + e->weight_bytes, 0,
+	                             arena_dev_pos_get(&e->ctx->dev_arena) - w_begin - e->weight_bytes, e->stream));
+	if (c.dtype == InfBF16) INF_TRY(generate_weights<bf16>(e, seed));
+	else INF_TRY(generate_weights<float>(e, seed));
+
+	std::vector<float> cs, sn;
+	rope_tables(c, cs, sn);
+	INF_CUDA_TRY(cudaMemcpyAsync(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, e->stream));
+	INF_CUDA_TRY(cudaMemcpyAsync(e->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, e->stream));
+	e->h_block_table.assign((size_t)c.max_batch * e->pages_per_seq, -1);
+	INF_CUDA_TRY(cudaMemcpyAsync(e->block_table, e->h_block_table.data(), e->h_block_table.size() * 4,
+	                             cudaMemcpyHostToDevice, e->stream));
+	e->seq_pages.assign(c.max_batch, {});
+	e->free_pages.clear();
+	for (int p = e->n_pages - 1; p >= 0; --p) e->free_pages.push_back(p);
+	INF_CUDA_TRY(cudaMallocHost(&e->h_pin, sizeof(uint32_t) * (c.max_seq + 16)));
+	INF_CUDA_TRY(cudaMallocHost(&e->h_ctl, sizeof(int) * 2 * kCtlWords));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	INF_TRY(build_decode_graph(e));
+	return Success;
+}
+
+void engine_free(InfEngine* e)
+{
+	if (!e) return;
+	if (e->stream) cudaStreamSynchronize(e->stream);
+	if (e->decode_exec) cudaGraphExecDestroy(e->decode_exec);
+	if (e->h_pin) cudaFreeHost(e->h_pin);
+	if (e->h_ctl) cudaFreeHost(e->h_ctl);
+	for (auto& ev : e->prof_ev)
+		if (ev) cudaEventDestroy(ev);
+	if (e->stream) cudaStreamDestroy(e->stream);
+	delete e;
+}
+
+Error_t copy_in_ids(InfEngine* e, const u32* ids, u32 n)
+{
+	if (is_device_ptr(ids)) {
+		INF_CUDA_TRY(cudaMemcpyAsync(e->d_ids, ids, (size_t)n * 4, cudaMemcpyDeviceToDevice, e->stream));
+	} else {
+		for (u32 i = 0; i < n; ++i)
+			if (ids[i] >= e->cfg.vocab_size) return fail(ErrorTokenOutOfRange, "id %u at %u >= vocab %u", ids[i], i, e->cfg.vocab_size);
+		INF_CUDA_TRY(cudaStreamSynchronize(e->stream)); // h_pin may still feed an earlier copy
+		memcpy(e->h_pin, ids, (size_t)n * 4);
+		INF_CUDA_TRY(cudaMemcpyAsync(e->d_ids, e->h_pin, (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+	}
+	return Success;
+}
+
+Error_t set_scalars(InfEngine* e, int slot, int pos)
+{
+	int v[2] = {slot, pos};
+	INF_CUDA_TRY(cudaMemcpyAsync(e->slot, &v[0], 4, cudaMemcpyHostToDevice, e->stream));
+	INF_CUDA_TRY(cudaMemcpyAsync(e->pos, &v[1], 4, cudaMemcpyHostToDevice, e->stream));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	return Success;
+}
+
+// Feeds ids[0..n) (already in d_ids) through the decode graph at consecutive positions.
+Error_t run_tokens(InfEngine* e, u32 n)
+{
+	for (u32 t = 0; t < n; ++t) {
+		INF_CUDA_TRY(cudaMemcpyAsync(e->cur_id, e->d_ids + t, 4, cudaMemcpyDeviceToDevice, e->stream));
+		INF_TRY(launch_decode_graph(e));
+	}
+	return Success;
+}
+
+Error_t copy_out(InfEngine* e, void* dst, const void* src, size_t bytes)
+{
+	const cudaMemcpyKind k = is_device_ptr(dst) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+	INF_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, k, e->stream));
+	return Success;
+}
+
+// One host token: one 12-byte H2D of (id, pos, slot) from pinned memory, one graph launch,
+// one 20-byte D2H of (argmax, ..., err) -- the per-token cost of the public API.
+Error_t forward_one(InfEngine* e, u32 id, u32 pos, u32 slot, f32* logits_out, u32* argmax_out)
+{
+	if (id >= e->cfg.vocab_size) return fail(ErrorTokenOutOfRange, "id %u >= vocab %u", id, e->cfg.vocab_size);
+	int* in = e->h_ctl;
+	int* out = e->h_ctl + kCtlWords;
+	in[kCtlId] = (int)id;
+	in[kCtlPos] = (int)pos;
+	in[kCtlSlot] = (int)slot;
+	INF_CUDA_TRY(cudaMemcpyAsync(e->ctl, in, 3 * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+	INF_TRY(launch_decode_graph(e));
+	INF_CUDA_TRY(cudaMemcpyAsync(out, e->ctl, (kCtlErr + 1) * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+	if (logits_out) INF_TRY(copy_out(e, logits_out, e->logits, sizeof(float) * e->Vl));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	if (out[kCtlErr] != kDevOk) {
+		INF_CUDA_TRY(cudaMemsetAsync(e->err, 0, sizeof(int), e->stream));
+		INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+		return map_dev_err(out[kCtlErr]);
+	}
+	if (argmax_out) {
+		if (is_device_ptr(argmax_out)) INF_CUDA_TRY(cudaMemcpy(argmax_out, &out[kCtlId], 4, cudaMemcpyHostToDevice));
+		else *argmax_out = (u32)out[kCtlId];
+	}
+	return Success;
+}
+
+} // namespace
+
+// =============================================================================== C ABI
+extern "C" {
+
+Error_t inf_config_preset(u32 preset, InfConfig* out)
+{
+	if (!out) return fail(ErrorInvalidValue, "inf_config_preset: NULL");
+	InfConfig c;
+	memset(&c, 0, sizeof c);
+	c.kv_block = 16;
+	c.max_batch = 1;
+	c.norm_eps = 1e-5f;
+	c.init_std = 0.02f;
+	c.tp_size = 1;
+	switch (preset) {
+	case 1:
+		c.vocab_size = 32000; c.dim = 288; c.n_layers = 6; c.n_heads = 6; c.n_kv_heads = 6; c.head_dim = 48;
+		c.ffn_dim = 768; c.max_seq = 256; c.dtype = InfF32; c.rope_theta = 10000.0f;
+		break;
+	case 2:
+		c.vocab_size = 32000; c.dim = 2048; c.n_layers = 22; c.n_heads = 32; c.n_kv_heads = 4; c.head_dim = 64;
+		c.ffn_dim = 5632; c.max_seq = 1024; c.dtype = InfBF16; c.rope_theta = 10000.0f;
+		break;
+	case 3: case 4: case 5:
+		c.vocab_size = 128256; c.dim = 4096; c.n_layers = 32; c.n_heads = 32; c.n_kv_heads = 8; c.head_dim = 128;
+		c.ffn_dim = 14336; c.dtype = InfBF16; c.rope_theta = 500000.0f;
+		c.max_seq = preset == 3 ? 3072 : preset == 4 ? 4352 : 32896;
+		c.max_batch = preset == 4 ? 64 : 1;
+		break;
+	default:
+		return fail(ErrorInvalidValue, "unknown preset %u", preset);
+	}
+	*out = c;
+	return Success;
+}
+
+Error_t inf_model_build(ExecCtx** ctx, Model* model, const InfConfig* config, const char* weights_path, u64 seed)
+{
+	if (!ctx || !model || !config) return fail(ErrorInvalidValue, "inf_model_build: NULL argument");
+	if (weights_path) return fail(ErrorUnsupported, "checkpoint loading is not built; pass NULL for synthetic weights");
+	InfEngine* e = new (std::nothrow) InfEngine();
+	if (!e) return fail(ErrorMemoryAllocation, "engine");
+	e->cfg = *config;
+	e->ctx = *ctx;
+	Error_t r = engine_build(e, seed);
+	if (r != Success) {
+		ExecCtx* c = e->ctx;
+		engine_free(e);
+		if (c && !*ctx) exec_ctx_destroy(&c); // created here: undo
+		else if (c && c->dev_arena._d_ptr) arena_dev_destroy(&c->dev_arena);
+		return r;
+	}
+	*ctx = e->ctx;
+	model->config = e->cfg;
+	model->data = e->embed;
+	model->model_bsize = e->weight_bytes;
+	model->engine = e;
+	return Success;
+}
+
+Error_t inf_model_destroy(ExecCtx** ctx, Model* model)
+{
+	if (!model || !model->engine) return fail(ErrorInvalidValue, "inf_model_destroy: no model");
+	engine_free(model->engine);
+	model->engine = nullptr;
+	model->data = nullptr;
+	if (ctx && *ctx) return exec_ctx_destroy(ctx);
+	return Success;
+}
+
+Error_t inf_forward(Model* model, const u32* ids, u32 n_tokens, u32 start_pos, u32 seq_slot, f32* logits_out,
+                    u32* argmax_out)
+{
+	if (!model || !model->engine || !ids || n_tokens == 0) return fail(ErrorInvalidValue, "inf_forward: bad arguments");
+	InfEngine* e = model->engine;
+	if (seq_slot >= e->cfg.max_batch) return fail(ErrorInvalidValue, "slot %u >= max_batch", seq_slot);
+	if ((u64)start_pos + n_tokens > e->cfg.max_seq) return fail(ErrorKvOutOfRange, "positions beyond max_seq");
+	INF_TRY(ensure_pages(e, seq_slot, start_pos + n_tokens));
+	if (n_tokens == 1 && !is_device_ptr(ids)) return forward_one(e, ids[0], start_pos, seq_slot, logits_out, argmax_out);
+	INF_TRY(copy_in_ids(e, ids, n_tokens));
+	INF_TRY(set_scalars(e, (int)seq_slot, (int)start_pos));
+	INF_TRY(run_tokens(e, n_tokens));
+	if (logits_out) INF_TRY(copy_out(e, logits_out, e->logits, sizeof(float) * e->Vl));
+	if (argmax_out) INF_TRY(copy_out(e, argmax_out, e->cur_id, 4));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	return check_dev_err(e);
+}
+
+Error_t inf_forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const u32* ids, const u32* positions,
+                          f32* logits_out, u32* argmax_out)
+{
+	if (!model || !model->engine || !seq_slots || !ids || !positions || n_seqs == 0)
+		return fail(ErrorInvalidValue, "inf_forward_batch: bad arguments");
+	InfEngine* e = model->engine;
+	for (u32 i = 0; i < n_seqs; ++i) {
+		f32* lo = logits_out ? logits_out + (size_t)i * e->Vl : nullptr;
+		u32* am = argmax_out ? argmax_out + i : nullptr;
+		INF_TRY(inf_forward(model, ids + i, 1, positions[i], seq_slots[i], lo, am));
+	}
+	return Success;
+}
+
+Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u32* out_ids, InfStats* stats)
+{
+	if (!model || !model->engine || !prompt || !out_ids || n_prompt == 0 || n_new == 0)
+		return fail(ErrorInvalidValue, "inf_generate: bad arguments");
+	InfEngine* e = model->engine;
+	if ((u64)n_prompt + n_new - 1 > e->cfg.max_seq) return fail(ErrorKvOutOfRange, "prompt + n_new beyond max_seq");
+	if (n_new > (u32)e->max_out) return fail(ErrorInvalidValue, "n_new above %d", e->max_out);
+	const u64 l0 = e->launches;
+	INF_TRY(release_pages(e, 0));
+	INF_TRY(ensure_pages(e, 0, n_prompt + n_new - 1));
+	INF_TRY(copy_in_ids(e, prompt, n_prompt));
+	INF_TRY(set_scalars(e, 0, 0));
+	cudaEvent_t ev[3];
+	for (auto& x : ev) INF_CUDA_TRY(cudaEventCreate(&x));
+	INF_CUDA_TRY(cudaEventRecord(ev[0], e->stream));
+	INF_TRY(run_tokens(e, n_prompt - 1));
+	INF_CUDA_TRY(cudaMemsetAsync(e->step, 0, 4, e->stream));
+	INF_CUDA_TRY(cudaMemcpyAsync(e->cur_id, e->d_ids + (n_prompt - 1), 4, cudaMemcpyDeviceToDevice, e->stream));
+	INF_TRY(launch_decode_graph(e));
+	INF_CUDA_TRY(cudaEventRecord(ev[1], e->stream));
+	for (u32 s = 1; s < n_new; ++s) INF_TRY(launch_decode_graph(e));
+	INF_CUDA_TRY(cudaEventRecord(ev[2], e->stream));
+	INF_CUDA_TRY(cudaMemcpyAsync(out_ids, e->out_ids, (size_t)n_new * 4,
+	                             is_device_ptr(out_ids) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, e->stream));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	float ms_pre = 0.f, ms_dec = 0.f;
+	cudaEventElapsedTime(&ms_pre, ev[0], ev[1]);
+	cudaEventElapsedTime(&ms_dec, ev[1], ev[2]);
+	for (auto& x : ev) cudaEventDestroy(x);
+	if (stats) {
+		stats->prefill_ms = ms_pre;
+		stats->decode_ms = ms_dec;
+		stats->n_prompt = n_prompt;
+		stats->n_new = n_new;
+		stats->kernel_launches = e->launches - l0;
+	}
+	return check_dev_err(e);
+}
+
+Error_t inf_decode(Model* model, u32 seq_slot, u32 start_pos, u32 first_id, u32 n_steps, u32* out_ids, InfStats* stats)
+{
+	if (!model || !model->engine || n_steps == 0) return fail(ErrorInvalidValue, "inf_decode: bad arguments");
+	InfEngine* e = model->engine;
+	if (seq_slot >= e->cfg.max_batch) return fail(ErrorInvalidValue, "slot %u >= max_batch", seq_slot);
+	if (first_id >= e->cfg.vocab_size) return fail(ErrorTokenOutOfRange, "id %u", first_id);
+	if ((u64)start_pos + n_steps > e->cfg.max_seq) return fail(ErrorKvOutOfRange, "positions beyond max_seq");
+	if (n_steps > (u32)e->max_out) return fail(ErrorInvalidValue, "n_steps above %d", e->max_out);
+	const u64 l0 = e->launches;
+	INF_TRY(ensure_pages(e, seq_slot, start_pos + n_steps));
+	int* in = e->h_ctl;
+	in[kCtlId] = (int)first_id;
+	in[kCtlPos] = (int)start_pos;
+	in[kCtlSlot] = (int)seq_slot;
+	in[kCtlStep] = 0;
+	INF_CUDA_TRY(cudaMemcpyAsync(e->ctl, in, 4 * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+	cudaEvent_t ev[2];
+	for (auto& x : ev) INF_CUDA_TRY(cudaEventCreate(&x));
+	INF_CUDA_TRY(cudaEventRecord(ev[0], e->stream));
+	for (u32 s = 0; s < n_steps; ++s) INF_TRY(launch_decode_graph(e));
+	INF_CUDA_TRY(cudaEventRecord(ev[1], e->stream));
+	if (out_ids)
+		INF_CUDA_TRY(cudaMemcpyAsync(out_ids, e->out_ids, (size_t)n_steps * 4,
+		                             is_device_ptr(out_ids) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, e->stream));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	float ms = 0.f;
+	cudaEventElapsedTime(&ms, ev[0], ev[1]);
+	for (auto& x : ev) cudaEventDestroy(x);
+	if (stats) {
+		stats->prefill_ms = 0.0;
+		stats->decode_ms = ms;
+		stats->n_prompt = 0;
+		stats->n_new = n_steps;
+		stats->kernel_launches = e->launches - l0;
+	}
+	return check_dev_err(e);
+}
+
+Error_t inf_seq_reset(Model* model, u32 seq_slot)
+{
+	if (!model || !model->engine) return fail(ErrorInvalidValue, "inf_seq_reset: no model");
+	if (seq_slot >= model->engine->cfg.max_batch) return fail(ErrorInvalidValue, "slot");
+	return release_pages(model->engine, seq_slot);
+}
+
+void* inf_model_stream(Model* model) { return model && model->engine ? (void*)model->engine->stream : nullptr; }
+
+u64 inf_kernel_launches(Model* model) { return model && model->engine ? model->engine->launches : 0; }
+
+u64 inf_decode_bytes(const InfConfig* c, u32 ctx)
+{
+	if (!c) return 0;
+	const u64 es = c->dtype == InfBF16 ? 2 : 4, d = c->dim, hd = c->head_dim, L = c->n_layers;
+	const u64 layer = ((u64)(c->n_heads + 2 * c->n_kv_heads) * hd * d + d * c->n_heads * hd + 3ull * c->ffn_dim * d + 2 * d) * es;
+	const u64 weights = L * layer + (u64)c->vocab_size * d * es + d * es + d * es; // + LM head, final norm, one embedding row
+	const u64 kv = 2ull * L * c->n_kv_heads * hd * es * ((u64)ctx + 1);       // read ctx, write 1
+	return weights + kv;
+}
+
+u32 inf_profile_decode_step(Model* model, f32* ms_out, u32 max_kinds)
+{
+	if (!model || !model->engine || !ms_out) return 0;
+	InfEngine* e = model->engine;
+	for (float& v : e->prof_ms) v = 0.f;
+	e->profiling = true;
+	const Error_t r = enqueue_step(e);
+	e->profiling = false;
+	if (r != Success) return 0;
+	const u32 n = std::min<u32>(max_kinds, InfKNumKinds);
+	for (u32 k = 0; k < n; ++k) ms_out[k] = e->prof_ms[k];
+	return n;
+}
+
+// ---- stand-alone kernels --------------------------------------------------------------
+
+Error_t inf_fetch_input_embeddings(const u32* d_ids, u64 n_tokens, u32 dim, u32 vocab_size, const void* d_table,
+                                   void* d_out, u32 dtype, void* stream)
+{
+	if (!d_ids || !d_table || !d_out || n_tokens == 0 || dim == 0 || n_tokens > 65535u * 1024u)
+		return fail(ErrorInvalidValue, "inf_fetch_input_embeddings: bad arguments");
+	if (!is_device_ptr(d_ids) || !is_device_ptr(d_table) || !is_device_ptr(d_out))
+		return fail(ErrorInvalidDevPtr, "inf_fetch_input_embeddings: device pointers required");
+	int* d_err = nullptr;
+	INF_CUDA_TRY(cudaMallocAsync((void**)&d_err, sizeof(int), (cudaStream_t)stream));
+	INF_CUDA_TRY(cudaMemsetAsync(d_err, 0, sizeof(int), (cudaStream_t)stream));
+	const size_t es = dtype == InfBF16 ? 2 : 4;
+	const u32 units = (u32)((dim * es + 15) / 16);
+	const dim3 grid((units + 255) / 256, (unsigned)n_tokens);
+	if (dtype == InfBF16)
+		k_embed_copy<bf16><<<grid, 256, 0, (cudaStream_t)stream>>>(d_ids, (int)n_tokens, (int)dim, vocab_size,
+		                                                            (const bf16*)d_table, (bf16*)d_out, d_err);
+	else if (dtype == InfF32)
+		k_embed_copy<float><<<grid, 256, 0, (cudaStream_t)stream>>>(d_ids, (int)n_tokens, (int)dim, vocab_size,
+		                                                             (const float*)d_table, (float*)d_out, d_err);
+	else {
+		cudaFreeAsync(d_err, (cudaStream_t)stream);
+		return fail(ErrorInvalidValue, "dtype %u", dtype);
+	}
+	INF_CUDA_TRY(cudaGetLastError());
+	int h_err = 0;
+	INF_CUDA_TRY(cudaMemcpyAsync(&h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+	INF_CUDA_TRY(cudaFreeAsync(d_err, (cudaStream_t)stream));
+	INF_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+	if (h_err == kDevTokenRange) return fail(ErrorTokenOutOfRange, "token id >= vocab_size");
+	return Success;
+}
+
+Error_t inf_rmsnorm(const void* d_x, void* d_y, u32 rows, u32 dim, const void* d_gain, f32 eps, u32 dtype, void* stream)
+{
+	if (!d_x || !d_y || !d_gain || rows == 0 || dim == 0 || rows > 2147483647u)
+		return fail(ErrorInvalidValue, "inf_rmsnorm: bad arguments");
+	if (!is_device_ptr(d_x) || !is_device_ptr(d_y) || !is_device_ptr(d_gain))
+		return fail(ErrorInvalidDevPtr, "inf_rmsnorm: device pointers required");
+	if (dtype == InfBF16)
+		k_rmsnorm_rows<bf16, bf16, bf16><<<rows, 256, 0, (cudaStream_t)stream>>>((const bf16*)d_x, (bf16*)d_y, (int)rows,
+		                                                                        (int)dim, (const bf16*)d_gain, eps);
+	else if (dtype == InfF32)
+		k_rmsnorm_rows<float, float, float><<<rows, 256, 0, (cudaStream_t)stream>>>(
+		    (const float*)d_x, (float*)d_y, (int)rows, (int)dim, (const float*)d_gain, eps);
+	else
+		return fail(ErrorInvalidValue, "dtype %u", dtype);
+	INF_CUDA_TRY(cudaGetLastError());
+	INF_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+	return Success;
+}
+
+} // extern "C"

@@ -1,0 +1,343 @@
+// Batch-1 decode projections: y = W.x over a row-major [N x K] weight, HBM-bound.
+//
+// One CTA per SM.  A producer warp streams the CTA's contiguous row range through a ring
+// of shared-memory stages with 1-D bulk copies (cp.async.bulk, evict_first), issuing the
+// first stages before griddepcontrol.wait so the weight stream of kernel n+1 overlaps the
+// tail of kernel n (programmatic dependent launch).  Eight consumer warps hold the
+// activation vector in registers (each lane owns 16-byte units u*256 + lane_id), dot every
+// staged row against it, reduce across warps and run a fused epilogue:
+//   kEpiStore   y[row] = round(dot)
+//   kEpiResid   r[row] += dot                           (O-proj and down-proj + residual)
+//   kEpiQkv     RoPE on (i, i+hd/2) row pairs, q -> buffer, k/v -> paged KV cache
+//   kEpiSwiglu  h[j] = round(silu(gate_j) * up_j) on (gate_j, up_j) row pairs
+//   kEpiLogits  logits[row] = dot, then a grid-wide greedy argmax (ties -> lowest index)
+// The prologue either normalises the fp32 residual with the layer's RMSNorm gain
+// (src/cuda/kernels/rmsnorm.cu:11-59 semantics, with eps) or loads a stored vector.
+#pragma once
+
+#include "common.cuh"
+
+namespace inf {
+
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
+constexpr int kGemvThreads = kGemvConsumers + 32;
+constexpr int kGemvRingBytes = 96 * 1024;
+constexpr int kGemvMaxStages = 8;
+
+enum EpiKind : int { kEpiStore = 0, kEpiResid = 1, kEpiQkv = 2, kEpiSwiglu = 3, kEpiLogits = 4 };
+
+template <int EPI> struct EpiTraits {
+	static constexpr bool kPaired = (EPI == kEpiQkv || EPI == kEpiSwiglu);
+	static constexpr bool kNorm = (EPI == kEpiQkv || EPI == kEpiSwiglu || EPI == kEpiLogits);
+};
+
+template <int UPL, int EPI> struct GemvShape {
+	static constexpr int kRpcBase = (8 / UPL) < 1 ? 1 : (8 / UPL);
+	static constexpr int kRpc = (EpiTraits<EPI>::kPaired && kRpcBase < 2) ? 2 : kRpcBase; // rows per chunk
+};
+
+struct GemvArgs {
+	const void* W;
+	int N, K;
+	int stages;
+	uint32_t stage_bytes;
+	// prologue
+	const float* resid_in;  // norm prologue: fp32 [K]
+	const void* gain;       // norm gain [K]
+	float eps;
+	const void* xin;        // plain prologue: [K]
+	// epilogue
+	void* out;              // store: [N]; swiglu: [N/2]; qkv: q [n_q_heads*hd]
+	float* resid;           // resid: fp32 [N]
+	void* kpool;            // qkv: this layer's K pages [pages][kv][blk][hd]
+	void* vpool;
+	const int* block_table; // [slots][pages_per_seq]
+	int pages_per_seq, max_pages;
+	const int* pos;         // device position of the token
+	const int* slot;        // device slot of the token
+	const float* rope_cos;  // [max_seq][hd/2]
+	const float* rope_sin;
+	int head_dim, n_q_heads, n_kv_heads, kv_block, max_seq;
+	float* logits;                // logits: fp32 [N]
+	unsigned long long* best;     // logits: grid argmax key
+	unsigned* counter;            // logits: finished CTAs
+	uint32_t* cur_id;             // logits: next input id
+	uint32_t* out_ids;            // logits: generated ids [max_out]
+	uint32_t* step;               // logits: index into out_ids
+	int* pos_rw;                  // logits: position advanced after the step
+	int max_out;
+	int* err;
+};
+
+template <typename T, int UPL>
+__device__ __forceinline__ float gemv_row_dot(const uint8_t* row, int units_per_row, int ct, const float (&xh)[UPL][Store<T>::kVec])
+{
+	constexpr int VEC = Store<T>::kVec;
+	float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+	for (int u = 0; u < UPL; ++u) {
+		const int unit = u * kGemvConsumers + ct;
+		if (unit < units_per_row) {
+			const uint4 w = *reinterpret_cast<const uint4*>(row + (size_t)unit * 16);
+			float wf[VEC];
+			unpack_unit(w, wf, (const T*)nullptr);
+#pragma unroll
+			for (int v = 0; v < VEC; v += 2) {
+				a0 = fmaf(wf[v], xh[u][v], a0);
+				a1 = fmaf(wf[v + 1], xh[u][v + 1], a1);
+			}
+		}
+	}
+	return a0 + a1;
+}
+
+template <typename T, int UPL, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
+{
+	constexpr int VEC = Store<T>::kVec;
+	constexpr int RPC = GemvShape<UPL, EPI>::kRpc;
+	constexpr bool PAIRED = EpiTraits<EPI>::kPaired;
+	constexpr int UNIT_ROWS = PAIRED ? 2 : 1;
+
+	extern __shared__ __align__(1024) uint8_t smem[];
+	uint8_t* ring = smem;
+	uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGemvRingBytes);
+	uint64_t* empty = full + kGemvMaxStages;
+	float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);      // [2][warps][RPC]
+	float* red_ss = red + 2 * kGemvConsumerWarps * RPC;                  // [warps]
+	unsigned long long* red_best = reinterpret_cast<unsigned long long*>(red_ss + kGemvConsumerWarps + 8);
+	volatile int* abort_flag = reinterpret_cast<volatile int*>(red_best + kGemvConsumerWarps);
+
+	const int tid = threadIdx.x;
+	const int warp = tid >> 5, lane = tid & 31;
+	const int S = a.stages;
+
+	// balanced contiguous row range of this CTA (whole pairs for paired epilogues)
+	const int total_units = a.N / UNIT_ROWS;
+	const int r0 = (int)(((long long)blockIdx.x * total_units) / gridDim.x) * UNIT_ROWS;
+	const int r1 = (int)(((long long)(blockIdx.x + 1) * total_units) / gridDim.x) * UNIT_ROWS;
+	const int n_rows = r1 - r0;
+	const int n_chunks = (n_rows + RPC - 1) / RPC;
+	const size_t row_bytes = (size_t)a.K * sizeof(T);
+
+	if (tid == 0) {
+		for (int s = 0; s < S; ++s) {
+			mbar_init(&full[s], 1);
+			mbar_init(&empty[s], kGemvConsumerWarps);
+		}
+		*abort_flag = 0;
+		mbar_fence_init();
+	}
+	__syncthreads();
+	pdl_trigger();
+
+	if (warp == kGemvConsumerWarps) {
+		// ---------------- producer ----------------
+		if (lane == 0) {
+			const uint64_t pol = policy_evict_first();
+			const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.W) + (size_t)r0 * row_bytes;
+			int issued = 0;
+			for (int i = 0; i < n_chunks; ++i) {
+				const int s = i % S;
+				if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, abort_flag, a.err)) break;
+				const int rows = min(RPC, n_rows - i * RPC);
+				const uint32_t bytes = (uint32_t)(rows * row_bytes);
+				mbar_arrive_expect_tx(&full[s], bytes);
+				bulk_g2s(ring + (size_t)s * a.stage_bytes, wbase + (size_t)i * RPC * row_bytes, bytes, &full[s], pol);
+				++issued;
+			}
+			// never leave the CTA with bulk copies in flight: wait for the last stages to land
+			for (int i = max(0, issued - S); i < issued; ++i) {
+				const int s = i % S;
+				const uint64_t t0 = global_timer_ns();
+				while (!mbar_try_wait(&full[s], (i / S) & 1)) {
+					if (global_timer_ns() - t0 > kWaitLimitNs) {
+						report_err(a.err, kDevTimeout);
+						break;
+					}
+				}
+			}
+		}
+		return;
+	}
+
+	// ---------------- consumers ----------------
+	const int ct = tid; // 0..255
+	const int units_per_row = (int)(row_bytes >> 4);
+	pdl_wait();
+
+	float xh[UPL][VEC];
+	if constexpr (EpiTraits<EPI>::kNorm) {
+		float ss = 0.0f;
+#pragma unroll
+		for (int u = 0; u < UPL; ++u) {
+			const int unit = u * kGemvConsumers + ct;
+#pragma unroll
+			for (int v = 0; v < VEC; ++v) xh[u][v] = 0.0f;
+			if (unit < units_per_row) {
+				const float* src = a.resid_in + (size_t)unit * VEC;
+#pragma unroll
+				for (int v = 0; v < VEC; v += 4) {
+					const float4 f = *reinterpret_cast<const float4*>(src + v);
+					xh[u][v] = f.x; xh[u][v + 1] = f.y; xh[u][v + 2] = f.z; xh[u][v + 3] = f.w;
+				}
+#pragma unroll
+				for (int v = 0; v < VEC; ++v) ss = fmaf(xh[u][v], xh[u][v], ss);
+			}
+		}
+		ss = warp_sum(ss);
+		if (lane == 0) red_ss[warp] = ss;
+		named_bar_sync(1, kGemvConsumers);
+		float tot = 0.0f;
+#pragma unroll
+		for (int w = 0; w < kGemvConsumerWarps; ++w) tot += red_ss[w];
+		const float inv = 1.0f / sqrtf(__fdiv_rn(tot, (float)a.K) + a.eps);
+		const T* g = reinterpret_cast<const T*>(a.gain);
+#pragma unroll
+		for (int u = 0; u < UPL; ++u) {
+			const int unit = u * kGemvConsumers + ct;
+			if (unit < units_per_row) {
+				const uint4 gw = *reinterpret_cast<const uint4*>(g + (size_t)unit * VEC);
+				float gf[VEC];
+				unpack_unit(gw, gf, (const T*)nullptr);
+#pragma unroll
+				for (int v = 0; v < VEC; ++v) xh[u][v] = Store<T>::round(__fmul_rn(__fmul_rn(xh[u][v], inv), gf[v]));
+			}
+		}
+	} else {
+		const T* x = reinterpret_cast<const T*>(a.xin);
+#pragma unroll
+		for (int u = 0; u < UPL; ++u) {
+			const int unit = u * kGemvConsumers + ct;
+			if (unit < units_per_row) {
+				const uint4 xw = *reinterpret_cast<const uint4*>(x + (size_t)unit * VEC);
+				unpack_unit(xw, xh[u], (const T*)nullptr);
+			} else {
+#pragma unroll
+				for (int v = 0; v < VEC; ++v) xh[u][v] = 0.0f;
+			}
+		}
+	}
+
+	unsigned long long best = 0ull;
+	int pos = 0, slot = 0;
+	if constexpr (EPI == kEpiQkv) {
+		pos = *a.pos;
+		slot = *a.slot;
+	}
+
+	for (int i = 0; i < n_chunks; ++i) {
+		const int s = i % S;
+		const bool ok = mbar_wait(&full[s], (i / S) & 1, abort_flag, a.err);
+		const int rows = min(RPC, n_rows - i * RPC);
+		const uint8_t* stage = ring + (size_t)s * a.stage_bytes;
+		float part[RPC];
+#pragma unroll
+		for (int r = 0; r < RPC; ++r) {
+			part[r] = 0.0f;
+			if (ok && r < rows) part[r] = gemv_row_dot<T, UPL>(stage + (size_t)r * row_bytes, units_per_row, ct, xh);
+		}
+		__syncwarp();
+		if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+		for (int r = 0; r < RPC; ++r) part[r] = warp_sum(part[r]);
+		float* rb = red + (i & 1) * kGemvConsumerWarps * RPC;
+		if (lane == 0) {
+#pragma unroll
+			for (int r = 0; r < RPC; ++r) rb[warp * RPC + r] = part[r];
+		}
+		named_bar_sync(1, kGemvConsumers);
+		if (!ok) continue;
+
+		const int n_epi = rows / UNIT_ROWS;
+		if (ct < n_epi) {
+			const int lr = ct * UNIT_ROWS;
+			const int row = r0 + i * RPC + lr;
+			float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+			for (int w = 0; w < kGemvConsumerWarps; ++w) {
+				d0 += rb[w * RPC + lr];
+				if (PAIRED) d1 += rb[w * RPC + lr + 1];
+			}
+			if constexpr (EPI == kEpiStore) {
+				Store<T>::put(reinterpret_cast<T*>(a.out) + row, d0);
+			} else if constexpr (EPI == kEpiResid) {
+				a.resid[row] += d0;
+			} else if constexpr (EPI == kEpiSwiglu) {
+				Store<T>::put(reinterpret_cast<T*>(a.out) + (row >> 1), __fmul_rn(silu(d0), d1));
+			} else if constexpr (EPI == kEpiLogits) {
+				a.logits[row] = d0;
+				const unsigned long long key = argmax_key(d0, (uint32_t)row);
+				best = key > best ? key : best;
+			} else if constexpr (EPI == kEpiQkv) {
+				const int hd = a.head_dim, half = hd >> 1;
+				const int head = row / hd;
+				const int dim = (row % hd) >> 1; // pair (dim, dim + half)
+				float o0 = d0, o1 = d1;
+				if (head < a.n_q_heads + a.n_kv_heads) {
+					const float c = a.rope_cos[(size_t)pos * half + dim];
+					const float sn = a.rope_sin[(size_t)pos * half + dim];
+					o0 = __fsub_rn(__fmul_rn(d0, c), __fmul_rn(d1, sn));
+					o1 = __fadd_rn(__fmul_rn(d1, c), __fmul_rn(d0, sn));
+				}
+				if (head < a.n_q_heads) {
+					T* q = reinterpret_cast<T*>(a.out) + (size_t)head * hd;
+					Store<T>::put(q + dim, o0);
+					Store<T>::put(q + dim + half, o1);
+				} else {
+					const bool is_k = head < a.n_q_heads + a.n_kv_heads;
+					const int kvh = head - a.n_q_heads - (is_k ? 0 : a.n_kv_heads);
+					const int page = a.block_table[(size_t)slot * a.pages_per_seq + pos / a.kv_block];
+					if (page < 0 || page >= a.max_pages || pos >= a.max_seq) {
+						report_err(a.err, kDevKvRange);
+					} else {
+						T* base = reinterpret_cast<T*>(is_k ? a.kpool : a.vpool) +
+						          (((size_t)page * a.n_kv_heads + kvh) * a.kv_block + (pos % a.kv_block)) * hd;
+						Store<T>::put(base + dim, o0);
+						Store<T>::put(base + dim + half, o1);
+					}
+				}
+			}
+		}
+	}
+
+	if constexpr (EPI == kEpiLogits) {
+		// CTA max, then grid max through one atomic; the last CTA publishes the token.
+#pragma unroll
+		for (int o = 16; o > 0; o >>= 1) {
+			const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+			best = other > best ? other : best;
+		}
+		if (lane == 0) red_best[warp] = best;
+		named_bar_sync(1, kGemvConsumers);
+		if (ct == 0) {
+			unsigned long long b = 0ull;
+			for (int w = 0; w < kGemvConsumerWarps; ++w) b = red_best[w] > b ? red_best[w] : b;
+			atomicMax(a.best, b);
+			__threadfence();
+			const unsigned done = atomicAdd(a.counter, 1u);
+			if (done == gridDim.x - 1) {
+				__threadfence();
+				const unsigned long long fin = atomicAdd(a.best, 0ull);
+				const uint32_t id = argmax_key_index(fin);
+				*a.cur_id = id;
+				const uint32_t st = *a.step;
+				if ((int)st < a.max_out) a.out_ids[st] = id;
+				*a.step = st + 1;
+				*a.pos_rw = *a.pos_rw + 1;
+				*a.best = 0ull;
+				*a.counter = 0u;
+			}
+		}
+	}
+}
+
+inline size_t gemv_smem_bytes()
+{
+	return (size_t)kGemvRingBytes + 2 * kGemvMaxStages * sizeof(uint64_t) +
+	       (2 * kGemvConsumerWarps * 8 + kGemvConsumerWarps + 8) * sizeof(float) +
+	       kGemvConsumerWarps * sizeof(unsigned long long) + 16;
+}
+
+} // namespace inf

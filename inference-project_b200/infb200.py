@@ -1,0 +1,279 @@
+"""ctypes binding of libinf.so (include/inf.h) -- the host-side mirror of the reference's
+entry points for Python callers (tests, bench.py).
+
+It mirrors gosutek/inference-project's model-load / forward / generate surface
+(src/main.cu:200 model_build, src/main.cu:354 model_destroy, the embed -> RMSNorm forward of
+src/main.cu:396-412) on top of the C ABI.  There is no fallback: if libinf.so is missing or
+fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libinf.so")
+
+u8, u16, u32, u64, i32, f32, f64 = C.c_uint8, C.c_uint16, C.c_uint32, C.c_uint64, C.c_int32, C.c_float, C.c_double
+vp = C.c_void_p
+
+ERRORS = {
+    0: "Success", 1: "ErrorMemoryAllocation", 2: "ErrorArenaOutOfMemory", 3: "ErrorAlreadyInitialized",
+    4: "ErrorInvalidValue", 5: "ErrorInvalidHostPtr", 6: "ErrorInvalidDevPtr", 7: "ErrorGeneric", 8: "ErrorCuda",
+    9: "ErrorBadConfig", 10: "ErrorTokenOutOfRange", 11: "ErrorKvOutOfRange", 12: "ErrorNccl", 13: "ErrorTimeout",
+    14: "ErrorIo", 15: "ErrorUnsupported",
+}
+F32, BF16 = 0, 1
+KERNEL_KINDS = ["embed", "qkv", "attn", "o_proj", "gate_up", "down", "lm_head"]
+
+
+class InfError(RuntimeError):
+    def __init__(self, code: int, where: str, detail: str):
+        self.code = code
+        self.name = ERRORS.get(code, str(code))
+        super().__init__(f"{where}: {self.name} ({detail})")
+
+
+class InfConfig(C.Structure):
+    _fields_ = [
+        ("vocab_size", u32), ("dim", u32), ("n_layers", u32), ("n_heads", u32), ("n_kv_heads", u32),
+        ("head_dim", u32), ("ffn_dim", u32), ("max_seq", u32), ("max_batch", u32), ("kv_block", u32),
+        ("kv_pages", u32), ("prefill_chunk", u32), ("dtype", u32), ("norm_eps", f32), ("rope_theta", f32),
+        ("init_std", f32), ("tp_rank", u32), ("tp_size", u32),
+    ]
+
+    def as_dict(self) -> dict:
+        d = {k: getattr(self, k) for k, _ in self._fields_}
+        return d
+
+
+class HostArena(C.Structure):
+    _fields_ = [("reserve_size", u64), ("commit_size", u64), ("commit_pos", u64), ("pos", u64)]
+
+
+class DevArena(C.Structure):
+    _fields_ = [("_d_ptr", vp), ("size", u64), ("pos", u64)]
+
+
+class ExecCtx(C.Structure):
+    _fields_ = [("host_arena", HostArena), ("dev_arena", DevArena)]
+
+
+class Model(C.Structure):
+    _fields_ = [("config", InfConfig), ("data", vp), ("model_bsize", u64), ("engine", vp)]
+
+
+class InfStats(C.Structure):
+    _fields_ = [("prefill_ms", f64), ("decode_ms", f64), ("n_prompt", u32), ("n_new", u32),
+                ("kernel_launches", u64)]
+
+
+EXPORTS = [
+    "exec_ctx_create", "exec_ctx_destroy", "arena_host_create", "arena_host_destroy", "arena_host_push",
+    "arena_host_pop", "arena_host_pop_at", "mem_arena_host_pos_get", "arena_dev_create", "arena_dev_destroy",
+    "arena_dev_push", "arena_dev_pop", "arena_dev_pop_at", "arena_dev_pos_get", "cu_memcpy_htd",
+    "cu_memcpy_htd_async", "cu_memcpy_dth", "cu_memset", "inf_fetch_input_embeddings", "inf_rmsnorm",
+    "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
+    "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
+    "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step",
+]
+
+_lib = None
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError(f"{LIB_PATH} is not built (run `make -C {HERE}`); there is no fallback path")
+    L = C.CDLL(LIB_PATH)
+    E = C.c_int
+    sig = {
+        "exec_ctx_create": (E, [C.POINTER(C.POINTER(ExecCtx))]),
+        "exec_ctx_destroy": (E, [C.POINTER(C.POINTER(ExecCtx))]),
+        "arena_host_create": (E, [C.POINTER(C.POINTER(HostArena)), u64, u64]),
+        "arena_host_destroy": (E, [C.POINTER(HostArena)]),
+        "arena_host_push": (E, [C.POINTER(HostArena), u64, C.POINTER(vp)]),
+        "arena_host_pop": (None, [C.POINTER(HostArena), u64]),
+        "arena_host_pop_at": (None, [C.POINTER(HostArena), u64]),
+        "mem_arena_host_pos_get": (u64, [C.POINTER(HostArena)]),
+        "arena_dev_create": (E, [C.POINTER(DevArena), u64]),
+        "arena_dev_destroy": (E, [C.POINTER(DevArena)]),
+        "arena_dev_push": (E, [C.POINTER(DevArena), u64, C.POINTER(vp)]),
+        "arena_dev_pop": (None, [C.POINTER(DevArena), u64]),
+        "arena_dev_pop_at": (None, [C.POINTER(DevArena), u64]),
+        "arena_dev_pos_get": (u64, [C.POINTER(DevArena)]),
+        "cu_memcpy_htd": (E, [vp, vp, u64]),
+        "cu_memcpy_htd_async": (E, [vp, vp, u64, vp]),
+        "cu_memcpy_dth": (E, [vp, vp, u64]),
+        "cu_memset": (E, [vp, i32, u64]),
+        "inf_fetch_input_embeddings": (E, [vp, u64, u32, u32, vp, vp, u32, vp]),
+        "inf_rmsnorm": (E, [vp, vp, u32, u32, vp, f32, u32, vp]),
+        "inf_config_preset": (E, [u32, C.POINTER(InfConfig)]),
+        "inf_model_build": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model), C.POINTER(InfConfig), C.c_char_p, u64]),
+        "inf_model_destroy": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model)]),
+        "inf_forward": (E, [C.POINTER(Model), vp, u32, u32, u32, vp, vp]),
+        "inf_forward_batch": (E, [C.POINTER(Model), u32, vp, vp, vp, vp, vp]),
+        "inf_generate": (E, [C.POINTER(Model), vp, u32, u32, vp, C.POINTER(InfStats)]),
+        "inf_decode": (E, [C.POINTER(Model), u32, u32, u32, u32, vp, C.POINTER(InfStats)]),
+        "inf_seq_reset": (E, [C.POINTER(Model), u32]),
+        "inf_error_string": (C.c_char_p, [E]),
+        "inf_last_error_detail": (C.c_char_p, []),
+        "inf_model_stream": (vp, [C.POINTER(Model)]),
+        "inf_kernel_launches": (u64, [C.POINTER(Model)]),
+        "inf_decode_bytes": (u64, [C.POINTER(InfConfig), u32]),
+        "inf_profile_decode_step": (u32, [C.POINTER(Model), C.POINTER(f32), u32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc: int, where: str) -> None:
+    if rc != 0:
+        raise InfError(rc, where, lib().inf_last_error_detail().decode())
+
+
+def preset(n: int, **overrides) -> InfConfig:
+    c = InfConfig()
+    check(lib().inf_config_preset(n, C.byref(c)), "inf_config_preset")
+    for k, v in overrides.items():
+        setattr(c, k, v)
+    return c
+
+
+def config_from_dict(d: dict) -> InfConfig:
+    c = InfConfig()
+    c.kv_block, c.max_batch, c.norm_eps, c.init_std, c.tp_size = 16, 1, 1e-5, 0.02, 1
+    names = {"vocab": "vocab_size", "ffn": "ffn_dim", "eps": "norm_eps"}
+    for k, v in d.items():
+        if k == "dtype":
+            c.dtype = BF16 if v == "bf16" else F32
+        elif hasattr(c, names.get(k, k)):
+            setattr(c, names.get(k, k), v)
+    return c
+
+
+def oracle_dict(c: InfConfig) -> dict:
+    """The same model as a dict for oracle/oracle.py (tests only)."""
+    return dict(vocab=c.vocab_size, dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads, n_kv_heads=c.n_kv_heads,
+                head_dim=c.head_dim, ffn=c.ffn_dim, max_seq=c.max_seq, eps=c.norm_eps, rope_theta=c.rope_theta,
+                dtype="bf16" if c.dtype == BF16 else "fp32", init_std=c.init_std)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(vp)
+
+
+class Engine:
+    """One model on the current CUDA device (one context per GPU)."""
+
+    def __init__(self, cfg: InfConfig, seed: int = 0):
+        self.cfg = cfg
+        self.ctx = C.POINTER(ExecCtx)()
+        self.model = Model()
+        check(lib().inf_model_build(C.byref(self.ctx), C.byref(self.model), C.byref(cfg), None, seed),
+              "inf_model_build")
+        self.V = cfg.vocab_size // max(1, cfg.tp_size)
+
+    def close(self):
+        if self.model.engine:
+            check(lib().inf_model_destroy(C.byref(self.ctx), C.byref(self.model)), "inf_model_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return lib().inf_model_stream(C.byref(self.model)) or 0
+
+    @property
+    def launches(self) -> int:
+        return int(lib().inf_kernel_launches(C.byref(self.model)))
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(self.model.model_bsize)
+
+    def forward(self, ids, start_pos: int, slot: int = 0, want_logits: bool = True):
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        lg = np.empty(self.V, dtype=np.float32) if want_logits else None
+        am = np.zeros(1, dtype=np.uint32)
+        check(lib().inf_forward(C.byref(self.model), _ptr(ids), ids.size, start_pos, slot,
+                                _ptr(lg) if lg is not None else None, _ptr(am)), "inf_forward")
+        return lg, int(am[0])
+
+    def forward_ptr(self, ids_ptr: int, n: int, start_pos: int, slot: int, logits_ptr, argmax_ptr):
+        """Device- or host-pointer variant (torch tensors' data_ptr())."""
+        check(lib().inf_forward(C.byref(self.model), vp(ids_ptr), n, start_pos, slot,
+                                vp(logits_ptr) if logits_ptr else None, vp(argmax_ptr) if argmax_ptr else None),
+              "inf_forward")
+
+    def forward_batch(self, slots, ids, positions, want_logits: bool = False):
+        slots = np.ascontiguousarray(slots, dtype=np.uint32)
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        positions = np.ascontiguousarray(positions, dtype=np.uint32)
+        n = ids.size
+        lg = np.empty((n, self.V), dtype=np.float32) if want_logits else None
+        am = np.zeros(n, dtype=np.uint32)
+        check(lib().inf_forward_batch(C.byref(self.model), n, _ptr(slots), _ptr(ids), _ptr(positions),
+                                      _ptr(lg) if lg is not None else None, _ptr(am)), "inf_forward_batch")
+        return lg, am
+
+    def generate(self, prompt, n_new: int):
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(n_new, dtype=np.uint32)
+        st = InfStats()
+        check(lib().inf_generate(C.byref(self.model), _ptr(prompt), prompt.size, n_new, _ptr(out), C.byref(st)),
+              "inf_generate")
+        return out, st
+
+    def decode(self, first_id: int, start_pos: int, n_steps: int, slot: int = 0, want_ids: bool = True):
+        out = np.zeros(n_steps, dtype=np.uint32) if want_ids else None
+        st = InfStats()
+        check(lib().inf_decode(C.byref(self.model), slot, start_pos, first_id, n_steps,
+                               _ptr(out) if out is not None else None, C.byref(st)), "inf_decode")
+        return out, st
+
+    def reset(self, slot: int = 0):
+        check(lib().inf_seq_reset(C.byref(self.model), slot), "inf_seq_reset")
+
+    def profile_step(self) -> dict:
+        ms = (f32 * 8)()
+        n = lib().inf_profile_decode_step(C.byref(self.model), ms, 8)
+        return {KERNEL_KINDS[k]: float(ms[k]) for k in range(n)}
+
+
+def decode_bytes(cfg: InfConfig, ctx: int) -> int:
+    return int(lib().inf_decode_bytes(C.byref(cfg), ctx))
+
+
+def fetch_input_embeddings(d_ids: int, n: int, dim: int, vocab: int, d_table: int, d_out: int, dtype: int,
+                           stream: int = 0) -> None:
+    check(lib().inf_fetch_input_embeddings(vp(d_ids), n, dim, vocab, vp(d_table), vp(d_out), dtype,
+                                           vp(stream) if stream else None), "inf_fetch_input_embeddings")
+
+
+def rmsnorm(d_x: int, d_y: int, rows: int, dim: int, d_gain: int, eps: float, dtype: int, stream: int = 0) -> None:
+    check(lib().inf_rmsnorm(vp(d_x), vp(d_y), rows, dim, vp(d_gain), eps, dtype, vp(stream) if stream else None),
+          "inf_rmsnorm")

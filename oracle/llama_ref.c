@@ -1,0 +1,564 @@
+/*
+ * CPU oracle for the decoder token loop -- TEST INFRASTRUCTURE ONLY (see llama_ref.h).
+ * Loaded by tests/, __graft_entry__.smoke() and bench.py's CPU legs; never by the product.
+ *
+ * Numerics (the rounding points the device path also uses):
+ *   residual stream r            fp32
+ *   normalised activation x^     bf16(r * (1/sqrt(mean(r^2)+eps)) * g)    [rmsnorm.cu:11-59 + eps]
+ *   q, k, v after RoPE           bf16 (k, v are what the KV cache stores)
+ *   attention output             bf16
+ *   SwiGLU product h             bf16(silu(gate) * up)
+ *   logits                       fp32, greedy argmax with ties to the lowest index
+ * In fp32 mode (bf16 == 0) every rounding point is the identity.
+ */
+#include "llama_ref.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------- */
+/* synthetic data                                                             */
+/* ------------------------------------------------------------------------- */
+
+/* SplitMix64 (Steele, Lea, Flood, OOPSLA 2014). */
+uint64_t orc_splitmix64(uint64_t x)
+{
+	uint64_t z = x + 0x9E3779B97F4A7C15ull;
+	z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+	z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+	return z ^ (z >> 31);
+}
+
+/* Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11): ten rounds, key bumped by the
+ * Weyl constants between rounds. */
+void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4])
+{
+	uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3];
+	uint32_t k0 = key[0], k1 = key[1];
+	for (int r = 0; r < 10; ++r) {
+		const uint64_t p0 = (uint64_t)0xD2511F53u * c0;
+		const uint64_t p1 = (uint64_t)0xCD9E8D57u * c2;
+		const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+		const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+		c0 = hi1 ^ c1 ^ k0;
+		c1 = lo1;
+		c2 = hi0 ^ c3 ^ k1;
+		c3 = lo0;
+		k0 += 0x9E3779B9u;
+		k1 += 0xBB67AE85u;
+	}
+	out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+void orc_stream_key(uint64_t seed, uint64_t stream, uint32_t key[2])
+{
+	const uint64_t k = orc_splitmix64(orc_splitmix64(seed) ^ stream);
+	key[0] = (uint32_t)k;
+	key[1] = (uint32_t)(k >> 32);
+}
+
+/* Irwin-Hall(4) approximation of N(0, std): four 22-bit uniforms summed, centred, and
+ * scaled by std*sqrt(3)/2^22.  The centred sum is an exact fp32 integer and the scale is
+ * one IEEE multiply, so host and device produce identical bits. */
+float orc_init_scale(float std)
+{
+	return (float)((double)std * 1.7320508075688772 / 4194304.0);
+}
+
+static inline float normal_from_words(const uint32_t w[4], float scale)
+{
+	const int32_t s = (int32_t)((w[0] >> 10) + (w[1] >> 10) + (w[2] >> 10) + (w[3] >> 10)) - (1 << 23);
+	return (float)s * scale;
+}
+
+float orc_normal_value(uint64_t seed, uint64_t stream, uint64_t idx, float scale)
+{
+	uint32_t key[2], ctr[4] = { (uint32_t)idx, (uint32_t)(idx >> 32), 0u, 0u }, w[4];
+	orc_stream_key(seed, stream, key);
+	orc_philox4x32_10(ctr, key, w);
+	return normal_from_words(w, scale);
+}
+
+/* round-to-nearest-even on the fp32 bit pattern */
+uint16_t orc_f32_to_bf16(float x)
+{
+	uint32_t u;
+	memcpy(&u, &x, 4);
+	if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return (uint16_t)0x7FC0u;
+	u += 0x7FFFu + ((u >> 16) & 1u);
+	return (uint16_t)(u >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t h)
+{
+	const uint32_t u = (uint32_t)h << 16;
+	float f;
+	memcpy(&f, &u, 4);
+	return f;
+}
+
+static inline float round_store(float x, int bf16)
+{
+	return bf16 ? orc_bf16_to_f32(orc_f32_to_bf16(x)) : x;
+}
+
+void orc_fill_tensor(uint64_t seed, uint64_t stream, uint64_t n, float std, int bf16, void* out)
+{
+	uint32_t key[2];
+	orc_stream_key(seed, stream, key);
+	const float scale = orc_init_scale(std);
+#pragma omp parallel for schedule(static)
+	for (int64_t i = 0; i < (int64_t)n; ++i) {
+		uint32_t ctr[4] = { (uint32_t)i, (uint32_t)((uint64_t)i >> 32), 0u, 0u }, w[4];
+		orc_philox4x32_10(ctr, key, w);
+		const float v = normal_from_words(w, scale);
+		if (bf16) ((uint16_t*)out)[i] = orc_f32_to_bf16(v);
+		else ((float*)out)[i] = v;
+	}
+}
+
+/* Lemire's multiply-shift reduction of the first Philox word into [lo, hi]. */
+uint32_t orc_uniform_u32(uint64_t seed, uint64_t stream, uint64_t idx, uint32_t lo, uint32_t hi_inclusive)
+{
+	uint32_t key[2], ctr[4] = { (uint32_t)idx, (uint32_t)(idx >> 32), 0u, 0u }, w[4];
+	orc_stream_key(seed, stream, key);
+	orc_philox4x32_10(ctr, key, w);
+	const uint64_t range = (uint64_t)hi_inclusive - lo + 1u;
+	return lo + (uint32_t)(((uint64_t)w[0] * range) >> 32);
+}
+
+void orc_gen_ids(uint64_t seed, uint64_t stream, uint64_t n, uint32_t vocab, uint32_t* out)
+{
+	for (uint64_t i = 0; i < n; ++i) out[i] = orc_uniform_u32(seed, stream, i, 0u, vocab - 1u);
+}
+
+uint64_t orc_tensor_stream(int32_t layer, uint32_t kind)
+{
+	return ((uint64_t)(int64_t)(layer + 1) << 8) | kind;
+}
+
+void orc_rope_table(uint32_t max_seq, uint32_t head_dim, float theta, float* cos_out, float* sin_out)
+{
+	const uint32_t half = head_dim / 2;
+	for (uint32_t p = 0; p < max_seq; ++p) {
+		for (uint32_t i = 0; i < half; ++i) {
+			const double inv_freq = pow((double)theta, -2.0 * (double)i / (double)head_dim);
+			const double a = (double)p * inv_freq;
+			cos_out[(uint64_t)p * half + i] = (float)cos(a);
+			sin_out[(uint64_t)p * half + i] = (float)sin(a);
+		}
+	}
+}
+
+/* ------------------------------------------------------------------------- */
+/* stage oracles                                                              */
+/* ------------------------------------------------------------------------- */
+
+static inline float wval(const void* W, int bf16, uint64_t i)
+{
+	return bf16 ? orc_bf16_to_f32(((const uint16_t*)W)[i]) : ((const float*)W)[i];
+}
+
+void orc_embed_gather(const uint32_t* ids, uint64_t n, uint32_t dim, const void* table, int bf16, float* out)
+{
+	for (uint64_t t = 0; t < n; ++t)
+		for (uint32_t i = 0; i < dim; ++i) out[t * dim + i] = wval(table, bf16, (uint64_t)ids[t] * dim + i);
+}
+
+static float rms_inv(const float* x, uint32_t dim, float eps)
+{
+	float acc[16] = { 0 };
+	uint32_t i = 0;
+	for (; i + 16 <= dim; i += 16)
+		for (int j = 0; j < 16; ++j) acc[j] += x[i + j] * x[i + j];
+	float ss = 0.f;
+	for (int j = 0; j < 16; ++j) ss += acc[j];
+	for (; i < dim; ++i) ss += x[i] * x[i];
+	return 1.0f / sqrtf(ss / (float)dim + eps);
+}
+
+void orc_rmsnorm(const float* x, uint64_t rows, uint32_t dim, const void* g, int bf16, float eps, float* y)
+{
+	for (uint64_t r = 0; r < rows; ++r) {
+		const float inv = rms_inv(x + r * dim, dim, eps);
+		for (uint32_t i = 0; i < dim; ++i)
+			y[r * dim + i] = round_store((x[r * dim + i] * inv) * wval(g, bf16, i), bf16);
+	}
+}
+
+static inline float dot_bf16(const uint16_t* w, const float* x, uint64_t n)
+{
+	float acc[16] = { 0 };
+	uint64_t i = 0;
+	for (; i + 16 <= n; i += 16)
+		for (int j = 0; j < 16; ++j) acc[j] += orc_bf16_to_f32(w[i + j]) * x[i + j];
+	float s = 0.f;
+	for (int j = 0; j < 16; ++j) s += acc[j];
+	for (; i < n; ++i) s += orc_bf16_to_f32(w[i]) * x[i];
+	return s;
+}
+
+static inline float dot_f32(const float* w, const float* x, uint64_t n)
+{
+	float acc[16] = { 0 };
+	uint64_t i = 0;
+	for (; i + 16 <= n; i += 16)
+		for (int j = 0; j < 16; ++j) acc[j] += w[i + j] * x[i + j];
+	float s = 0.f;
+	for (int j = 0; j < 16; ++j) s += acc[j];
+	for (; i < n; ++i) s += w[i] * x[i];
+	return s;
+}
+
+void orc_matvec(const void* W, int bf16, uint64_t rows, uint64_t cols, const float* x, float* y)
+{
+#pragma omp parallel for schedule(static)
+	for (int64_t r = 0; r < (int64_t)rows; ++r) {
+		y[r] = bf16 ? dot_bf16((const uint16_t*)W + (uint64_t)r * cols, x, cols)
+		            : dot_f32((const float*)W + (uint64_t)r * cols, x, cols);
+	}
+}
+
+uint32_t orc_argmax(const float* x, uint64_t n)
+{
+	uint64_t best = 0;
+	for (uint64_t i = 1; i < n; ++i)
+		if (x[i] > x[best]) best = i;
+	return (uint32_t)best;
+}
+
+/* ------------------------------------------------------------------------- */
+/* model                                                                      */
+/* ------------------------------------------------------------------------- */
+
+enum {
+	K_EMBED = 0, K_LM_HEAD = 1, K_FINAL_NORM = 2,
+	K_WQ = 8, K_WK = 9, K_WV = 10, K_WO = 11, K_WGATE = 12, K_WUP = 13, K_WDOWN = 14,
+	K_ATTN_NORM = 15, K_FFN_NORM = 16,
+};
+
+typedef struct OrcLayer {
+	void *wq, *wk, *wv, *wo, *wg, *wu, *wd, *attn_norm, *ffn_norm;
+} OrcLayer;
+
+struct OrcModel {
+	OrcConfig cfg;
+	int       n_threads;
+	void*     embed;
+	void*     lm_head;
+	void*     final_norm;
+	OrcLayer* layers;
+	float*    rope_cos;
+	float*    rope_sin;
+	float*    kcache; /* [slot][layer][pos][kv][hd] */
+	float*    vcache;
+	/* scratch */
+	float *r, *xh, *q, *k, *v, *att, *o, *tmp, *gate, *up, *h, *scores, *logits;
+	/* layer-0 stage outputs of the last token, for stage tests */
+	float *dbg_q, *dbg_k, *dbg_v, *dbg_att;
+};
+
+static void* alloc_tensor(const OrcModel* m, uint64_t n)
+{
+	return calloc(n, m->cfg.bf16 ? 2 : 4);
+}
+
+static void* gen_tensor(const OrcModel* m, uint64_t seed, int32_t layer, uint32_t kind, uint64_t n)
+{
+	void* t = alloc_tensor(m, n);
+	if (t) orc_fill_tensor(seed, orc_tensor_stream(layer, kind), n, m->cfg.init_std, (int)m->cfg.bf16, t);
+	return t;
+}
+
+static void* ones_tensor(const OrcModel* m, uint64_t n)
+{
+	void* t = alloc_tensor(m, n);
+	if (!t) return NULL;
+	for (uint64_t i = 0; i < n; ++i) {
+		if (m->cfg.bf16) ((uint16_t*)t)[i] = 0x3F80u;
+		else ((float*)t)[i] = 1.0f;
+	}
+	return t;
+}
+
+const void* orc_model_weight(const OrcModel* m, int32_t layer, uint32_t kind)
+{
+	if (layer < 0) {
+		switch (kind) {
+		case K_EMBED: return m->embed;
+		case K_LM_HEAD: return m->lm_head;
+		case K_FINAL_NORM: return m->final_norm;
+		default: return NULL;
+		}
+	}
+	if ((uint32_t)layer >= m->cfg.n_layers) return NULL;
+	const OrcLayer* L = &m->layers[layer];
+	switch (kind) {
+	case K_WQ: return L->wq;
+	case K_WK: return L->wk;
+	case K_WV: return L->wv;
+	case K_WO: return L->wo;
+	case K_WGATE: return L->wg;
+	case K_WUP: return L->wu;
+	case K_WDOWN: return L->wd;
+	case K_ATTN_NORM: return L->attn_norm;
+	case K_FFN_NORM: return L->ffn_norm;
+	default: return NULL;
+	}
+}
+
+OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
+{
+	if (!cfg || cfg->n_heads == 0 || cfg->n_kv_heads == 0 || cfg->n_heads % cfg->n_kv_heads || cfg->head_dim % 2 ||
+	    cfg->n_slots == 0 || cfg->max_seq == 0)
+		return NULL;
+#ifdef _OPENMP
+	if (n_threads > 0) omp_set_num_threads(n_threads);
+#endif
+	OrcModel* m = (OrcModel*)calloc(1, sizeof *m);
+	if (!m) return NULL;
+	m->cfg = *cfg;
+	m->n_threads = n_threads;
+	const uint64_t V = cfg->vocab, d = cfg->dim, H = cfg->n_heads, KV = cfg->n_kv_heads, hd = cfg->head_dim,
+	               F = cfg->ffn, L = cfg->n_layers;
+	m->embed = gen_tensor(m, seed, -1, K_EMBED, V * d);
+	m->lm_head = gen_tensor(m, seed, -1, K_LM_HEAD, V * d);
+	m->final_norm = ones_tensor(m, d);
+	m->layers = (OrcLayer*)calloc(L, sizeof(OrcLayer));
+	for (uint32_t l = 0; l < L; ++l) {
+		OrcLayer* Ly = &m->layers[l];
+		Ly->wq = gen_tensor(m, seed, (int32_t)l, K_WQ, H * hd * d);
+		Ly->wk = gen_tensor(m, seed, (int32_t)l, K_WK, KV * hd * d);
+		Ly->wv = gen_tensor(m, seed, (int32_t)l, K_WV, KV * hd * d);
+		Ly->wo = gen_tensor(m, seed, (int32_t)l, K_WO, d * H * hd);
+		Ly->wg = gen_tensor(m, seed, (int32_t)l, K_WGATE, F * d);
+		Ly->wu = gen_tensor(m, seed, (int32_t)l, K_WUP, F * d);
+		Ly->wd = gen_tensor(m, seed, (int32_t)l, K_WDOWN, d * F);
+		Ly->attn_norm = ones_tensor(m, d);
+		Ly->ffn_norm = ones_tensor(m, d);
+	}
+	m->rope_cos = (float*)malloc(sizeof(float) * cfg->max_seq * (hd / 2));
+	m->rope_sin = (float*)malloc(sizeof(float) * cfg->max_seq * (hd / 2));
+	orc_rope_table(cfg->max_seq, (uint32_t)hd, cfg->rope_theta, m->rope_cos, m->rope_sin);
+	const uint64_t kv_elems = (uint64_t)cfg->n_slots * L * cfg->max_seq * KV * hd;
+	m->kcache = (float*)calloc(kv_elems, sizeof(float));
+	m->vcache = (float*)calloc(kv_elems, sizeof(float));
+	const uint64_t big = (F > d ? F : d);
+	m->r = (float*)calloc(d, 4);
+	m->xh = (float*)calloc(d, 4);
+	m->q = (float*)calloc(H * hd, 4);
+	m->k = (float*)calloc(KV * hd, 4);
+	m->v = (float*)calloc(KV * hd, 4);
+	m->att = (float*)calloc(H * hd, 4);
+	m->o = (float*)calloc(d, 4);
+	m->tmp = (float*)calloc(big, 4);
+	m->gate = (float*)calloc(F, 4);
+	m->up = (float*)calloc(F, 4);
+	m->h = (float*)calloc(F, 4);
+	m->scores = (float*)calloc(H * (uint64_t)cfg->max_seq, 4);
+	m->logits = (float*)calloc(V, 4);
+	m->dbg_q = (float*)calloc(H * hd, 4);
+	m->dbg_k = (float*)calloc(KV * hd, 4);
+	m->dbg_v = (float*)calloc(KV * hd, 4);
+	m->dbg_att = (float*)calloc(H * hd, 4);
+	if (!m->embed || !m->lm_head || !m->kcache || !m->vcache || !m->scores || !m->logits) {
+		orc_model_destroy(m);
+		return NULL;
+	}
+	for (uint32_t l = 0; l < L; ++l)
+		if (!m->layers[l].wq || !m->layers[l].wd || !m->layers[l].wg || !m->layers[l].wu) {
+			orc_model_destroy(m);
+			return NULL;
+		}
+	return m;
+}
+
+void orc_model_destroy(OrcModel* m)
+{
+	if (!m) return;
+	free(m->embed); free(m->lm_head); free(m->final_norm);
+	if (m->layers) {
+		for (uint32_t l = 0; l < m->cfg.n_layers; ++l) {
+			OrcLayer* Ly = &m->layers[l];
+			free(Ly->wq); free(Ly->wk); free(Ly->wv); free(Ly->wo);
+			free(Ly->wg); free(Ly->wu); free(Ly->wd); free(Ly->attn_norm); free(Ly->ffn_norm);
+		}
+		free(m->layers);
+	}
+	free(m->rope_cos); free(m->rope_sin); free(m->kcache); free(m->vcache);
+	free(m->r); free(m->xh); free(m->q); free(m->k); free(m->v); free(m->att); free(m->o); free(m->tmp);
+	free(m->gate); free(m->up); free(m->h); free(m->scores); free(m->logits);
+	free(m->dbg_q); free(m->dbg_k); free(m->dbg_v); free(m->dbg_att);
+	free(m);
+}
+
+static inline float* kv_at(const OrcModel* m, float* cache, uint32_t slot, uint32_t layer, uint32_t pos)
+{
+	const OrcConfig* c = &m->cfg;
+	const uint64_t per_pos = (uint64_t)c->n_kv_heads * c->head_dim;
+	return cache + (((uint64_t)slot * c->n_layers + layer) * c->max_seq + pos) * per_pos;
+}
+
+static void rope_inplace(float* x, uint32_t n_heads, uint32_t hd, const float* cs, const float* sn)
+{
+	const uint32_t half = hd / 2;
+	for (uint32_t h = 0; h < n_heads; ++h) {
+		float* v = x + (uint64_t)h * hd;
+		for (uint32_t i = 0; i < half; ++i) {
+			const float a = v[i], b = v[i + half];
+			v[i] = a * cs[i] - b * sn[i];
+			v[i + half] = b * cs[i] + a * sn[i];
+		}
+	}
+}
+
+/* one token through the model at position pos (KV for pos written) */
+static void forward_token(OrcModel* m, uint32_t slot, uint32_t id, uint32_t pos, float* logits_out)
+{
+	const OrcConfig* c = &m->cfg;
+	const int bf = (int)c->bf16;
+	const uint32_t d = c->dim, H = c->n_heads, KV = c->n_kv_heads, hd = c->head_dim, F = c->ffn;
+	const uint32_t group = H / KV, half = hd / 2;
+	const float attn_scale = (float)(1.0 / sqrt((double)hd));
+	const float* cs = m->rope_cos + (uint64_t)pos * half;
+	const float* sn = m->rope_sin + (uint64_t)pos * half;
+
+	orc_embed_gather(&id, 1, d, m->embed, bf, m->r);
+	for (uint32_t l = 0; l < c->n_layers; ++l) {
+		const OrcLayer* Ly = &m->layers[l];
+		orc_rmsnorm(m->r, 1, d, Ly->attn_norm, bf, c->eps, m->xh);
+		orc_matvec(Ly->wq, bf, (uint64_t)H * hd, d, m->xh, m->q);
+		orc_matvec(Ly->wk, bf, (uint64_t)KV * hd, d, m->xh, m->k);
+		orc_matvec(Ly->wv, bf, (uint64_t)KV * hd, d, m->xh, m->v);
+		rope_inplace(m->q, H, hd, cs, sn);
+		rope_inplace(m->k, KV, hd, cs, sn);
+		for (uint32_t i = 0; i < H * hd; ++i) m->q[i] = round_store(m->q[i], bf);
+		for (uint32_t i = 0; i < KV * hd; ++i) {
+			m->k[i] = round_store(m->k[i], bf);
+			m->v[i] = round_store(m->v[i], bf);
+		}
+		memcpy(kv_at(m, m->kcache, slot, l, pos), m->k, sizeof(float) * KV * hd);
+		memcpy(kv_at(m, m->vcache, slot, l, pos), m->v, sizeof(float) * KV * hd);
+		const uint32_t ctx = pos + 1;
+#pragma omp parallel for schedule(static)
+		for (int32_t h = 0; h < (int32_t)H; ++h) {
+			const uint32_t g = (uint32_t)h / group;
+			const float* qh = m->q + (uint64_t)h * hd;
+			float* sc = m->scores + (uint64_t)h * c->max_seq;
+			float mx = -INFINITY;
+			for (uint32_t t = 0; t < ctx; ++t) {
+				const float* kt = kv_at(m, m->kcache, slot, l, t) + (uint64_t)g * hd;
+				const float s = dot_f32(kt, qh, hd) * attn_scale;
+				sc[t] = s;
+				if (s > mx) mx = s;
+			}
+			float den = 0.f;
+			for (uint32_t t = 0; t < ctx; ++t) {
+				sc[t] = expf(sc[t] - mx);
+				den += sc[t];
+			}
+			float* oh = m->att + (uint64_t)h * hd;
+			for (uint32_t i = 0; i < hd; ++i) oh[i] = 0.f;
+			for (uint32_t t = 0; t < ctx; ++t) {
+				const float* vt = kv_at(m, m->vcache, slot, l, t) + (uint64_t)g * hd;
+				for (uint32_t i = 0; i < hd; ++i) oh[i] += sc[t] * vt[i];
+			}
+			for (uint32_t i = 0; i < hd; ++i) oh[i] = round_store(oh[i] / den, bf);
+		}
+		if (l == 0) {
+			memcpy(m->dbg_q, m->q, sizeof(float) * H * hd);
+			memcpy(m->dbg_k, m->k, sizeof(float) * KV * hd);
+			memcpy(m->dbg_v, m->v, sizeof(float) * KV * hd);
+			memcpy(m->dbg_att, m->att, sizeof(float) * H * hd);
+		}
+		orc_matvec(Ly->wo, bf, d, (uint64_t)H * hd, m->att, m->o);
+		for (uint32_t i = 0; i < d; ++i) m->r[i] += m->o[i];
+
+		orc_rmsnorm(m->r, 1, d, Ly->ffn_norm, bf, c->eps, m->xh);
+		orc_matvec(Ly->wg, bf, F, d, m->xh, m->gate);
+		orc_matvec(Ly->wu, bf, F, d, m->xh, m->up);
+		for (uint32_t j = 0; j < F; ++j) {
+			const float gt = m->gate[j];
+			const float s = gt / (1.0f + expf(-gt));
+			m->h[j] = round_store(s * m->up[j], bf);
+		}
+		orc_matvec(Ly->wd, bf, d, F, m->h, m->o);
+		for (uint32_t i = 0; i < d; ++i) m->r[i] += m->o[i];
+	}
+	if (logits_out) {
+		orc_rmsnorm(m->r, 1, d, m->final_norm, bf, c->eps, m->xh);
+		orc_matvec(m->lm_head, bf, c->vocab, d, m->xh, logits_out);
+	}
+}
+
+int orc_forward(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t n, uint32_t start_pos,
+                float* logits_all, float* logits_last, uint32_t* argmax_last)
+{
+	const OrcConfig* c = &m->cfg;
+	if (slot >= c->n_slots) return -1;
+	if ((uint64_t)start_pos + n > c->max_seq) return -2;
+	for (uint32_t t = 0; t < n; ++t)
+		if (ids[t] >= c->vocab) return -3;
+	for (uint32_t t = 0; t < n; ++t) {
+		const int last = (t + 1 == n);
+		float* lo = logits_all ? logits_all + (uint64_t)t * c->vocab : (last ? m->logits : NULL);
+		forward_token(m, slot, ids[t], start_pos + t, lo);
+		if (last && lo) {
+			if (logits_last && logits_last != lo) memcpy(logits_last, lo, sizeof(float) * c->vocab);
+			if (argmax_last) *argmax_last = orc_argmax(lo, c->vocab);
+		}
+	}
+	return 0;
+}
+
+int orc_generate(OrcModel* m, uint32_t slot, const uint32_t* prompt, uint32_t n_prompt, uint32_t n_new,
+                 uint32_t* out_ids, float* logits_steps)
+{
+	const OrcConfig* c = &m->cfg;
+	if (n_prompt == 0 || n_new == 0) return -4;
+	if ((uint64_t)n_prompt + n_new - 1 > c->max_seq) return -2;
+	uint32_t next = 0;
+	int rc = orc_forward(m, slot, prompt, n_prompt, 0, NULL, logits_steps, &next);
+	if (rc) return rc;
+	out_ids[0] = next;
+	for (uint32_t s = 1; s < n_new; ++s) {
+		float* lo = logits_steps ? logits_steps + (uint64_t)s * c->vocab : NULL;
+		rc = orc_forward(m, slot, &out_ids[s - 1], 1, n_prompt + s - 1, NULL, lo, &next);
+		if (rc) return rc;
+		out_ids[s] = next;
+	}
+	return 0;
+}
+
+int orc_fill_kv_synthetic(OrcModel* m, uint32_t slot, uint32_t ctx, uint64_t seed)
+{
+	const OrcConfig* c = &m->cfg;
+	if (slot >= c->n_slots || ctx > c->max_seq) return -1;
+	const uint64_t per_pos = (uint64_t)c->n_kv_heads * c->head_dim;
+	for (uint32_t l = 0; l < c->n_layers; ++l) {
+		float* kb = kv_at(m, m->kcache, slot, l, 0);
+		float* vb = kv_at(m, m->vcache, slot, l, 0);
+		orc_fill_tensor(seed, 0x3000000ull | ((uint64_t)l << 1), (uint64_t)ctx * per_pos, 1.0f, 0, kb);
+		orc_fill_tensor(seed, 0x3000000ull | ((uint64_t)l << 1) | 1u, (uint64_t)ctx * per_pos, 1.0f, 0, vb);
+		if (c->bf16)
+			for (uint64_t i = 0; i < (uint64_t)ctx * per_pos; ++i) {
+				kb[i] = round_store(kb[i], 1);
+				vb[i] = round_store(vb[i], 1);
+			}
+	}
+	return 0;
+}
+
+int orc_last_layer0(const OrcModel* m, float* q, float* k, float* v, float* attn)
+{
+	const OrcConfig* c = &m->cfg;
+	if (q) memcpy(q, m->dbg_q, sizeof(float) * c->n_heads * c->head_dim);
+	if (k) memcpy(k, m->dbg_k, sizeof(float) * c->n_kv_heads * c->head_dim);
+	if (v) memcpy(v, m->dbg_v, sizeof(float) * c->n_kv_heads * c->head_dim);
+	if (attn) memcpy(attn, m->dbg_att, sizeof(float) * c->n_heads * c->head_dim);
+	return 0;
+}

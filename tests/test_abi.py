@@ -1,0 +1,97 @@
+"""CPU tests of the C ABI: libinf.so loads, exports every function include/inf.h declares,
+and the host-only parts (presets, arenas, byte model, error strings) behave without a GPU."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+import infb200 as I
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "inf.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\**\s+\**([a-z_][a-z0-9_]*)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_binding_surface():
+    decl = declared_functions()
+    assert "inf_model_build" in decl and "inf_generate" in decl and "exec_ctx_create" in decl
+    assert set(decl) == set(I.EXPORTS), set(decl) ^ set(I.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    L = I.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+
+
+def test_presets():
+    c3 = I.preset(3)
+    assert (c3.vocab_size, c3.dim, c3.n_layers, c3.n_heads, c3.n_kv_heads, c3.head_dim, c3.ffn_dim) == \
+        (128256, 4096, 32, 32, 8, 128, 14336)
+    assert c3.dtype == I.BF16 and abs(c3.rope_theta - 5e5) < 1 and c3.max_seq >= 2048 + 1024
+    c1 = I.preset(1)
+    assert (c1.dim, c1.n_layers, c1.head_dim, c1.ffn_dim, c1.dtype) == (288, 6, 48, 768, I.F32)
+    assert I.preset(4).max_batch == 64 and I.preset(5).max_seq >= 32768 + 128
+    with pytest.raises(I.InfError) as e:
+        I.preset(9)
+    assert e.value.code == 4
+
+
+def test_decode_bytes_model():
+    c = I.preset(3)
+    w = 32 * ((32 + 16) * 128 * 4096 + 4096 * 4096 + 3 * 14336 * 4096 + 2 * 4096) * 2 + 128256 * 4096 * 2 + 2 * 4096 * 2
+    kv = 2 * 32 * 8 * 128 * 2 * (2560 + 1)
+    assert I.decode_bytes(c, 2560) == w + kv
+    assert abs(w / 1e9 - 15.01) < 0.01  # 15.01 GB of weights per token
+
+
+def test_error_strings():
+    L = I.lib()
+    assert L.inf_error_string(0) == b"Success"
+    assert L.inf_error_string(10) == b"ErrorTokenOutOfRange"
+    assert L.inf_error_string(7) == b"ErrorGeneric"
+
+
+def test_host_arena_semantics():
+    L = I.lib()
+    a = C.POINTER(I.HostArena)()
+    assert L.arena_host_create(C.byref(a), 1 << 24, 1 << 16) == 0
+    p0 = L.mem_arena_host_pos_get(a)
+    ptr = C.c_void_p()
+    assert L.arena_host_push(a, 100, C.byref(ptr)) == 0
+    assert ptr.value % 8 == 0
+    C.memset(ptr, 7, 100)
+    big = C.c_void_p()
+    assert L.arena_host_push(a, 1 << 20, C.byref(big)) == 0  # grows past the first commit
+    C.memset(big, 1, 1 << 20)
+    assert L.arena_host_push(a, 1 << 30, C.byref(big)) == 2  # ErrorArenaOutOfMemory
+    L.arena_host_pop_at(a, p0)
+    assert L.mem_arena_host_pos_get(a) == p0
+    L.arena_host_pop(a, 1 << 40)  # never pops the header
+    assert L.mem_arena_host_pos_get(a) >= 32
+    assert L.arena_host_destroy(a) == 0
+
+
+def test_exec_ctx_lifecycle_without_device():
+    L = I.lib()
+    ctx = C.POINTER(I.ExecCtx)()
+    assert L.exec_ctx_create(C.byref(ctx)) == 0
+    assert ctx.contents.dev_arena._d_ptr is None
+    assert L.exec_ctx_create(C.byref(ctx)) == 3  # ErrorAlreadyInitialized
+    assert L.exec_ctx_destroy(C.byref(ctx)) == 0
+    assert not ctx
+    assert L.exec_ctx_destroy(C.byref(ctx)) == 4  # ErrorInvalidValue
+
+
+def test_model_build_rejects_bad_config_without_touching_the_device():
+    c = I.preset(3)
+    c.n_kv_heads = 5  # 32 % 5 != 0
+    with pytest.raises(I.InfError) as e:
+        I.Engine(c)
+    assert e.value.code == 9  # ErrorBadConfig
