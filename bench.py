@@ -149,7 +149,6 @@ def run_ours(args, rank: int, world: int, dist):
     import torch
 
     import infb200 as I
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -157,9 +156,7 @@ def run_ours(args, rank: int, world: int, dist):
     steps, warmup = args.steps, args.warmup
     if PROMPT + max(steps, warmup) > cfg.max_seq:
         raise SystemExit(f"--steps/--warmup above {cfg.max_seq - PROMPT}")
-    # prompt ids: Philox stream of seed 1 (same generator as the oracle's)
-    import oracle as O
-    prompt = O.gen_ids(1, PROMPT, cfg.vocab_size)
+    prompt = I.synth_ids(1, PROMPT, cfg.vocab_size)  # seed-1 uniform prompt ids
 
     eng = I.Engine(cfg, seed=0)
     stream = torch.cuda.ExternalStream(eng.stream)
@@ -194,7 +191,7 @@ def run_ours(args, rank: int, world: int, dist):
     # ---- per-kernel durations of one eager step (events around each launch, same stream)
     prof = {}
     for _ in range(3):
-        for k, v in eng.profile_step().items():
+        for k, v in eng.profile_step(PROMPT + steps - 1, first).items():
             prof[k] = prof.get(k, 0.0) + v / 3
 
     # ---- e2e: the per-token public call with host buffers
@@ -263,7 +260,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs use a short one)")
     args = ap.parse_args()
+    globals()["PROMPT"] = args.prompt
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 

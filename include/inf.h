@@ -190,6 +190,11 @@ Error_t inf_decode(Model* model, u32 seq_slot, u32 start_pos, u32 first_id, u32 
 /* Release the KV pages of a sequence slot. */
 Error_t inf_seq_reset(Model* model, u32 seq_slot);
 
+/* Synthetic inputs: n integers uniform in [lo, hi_inclusive] from Philox4x32-10 keyed by
+ * SplitMix64(SplitMix64(seed) ^ stream), counter i, Lemire multiply-shift.  Prompt ids use
+ * stream 0x1000000 + sequence, context lengths 0x2000000.  Host memory, no device work. */
+Error_t inf_synth_ids(u64 seed, u64 stream, u64 n, u32 lo, u32 hi_inclusive, u32* out);
+
 /* ---- introspection ------------------------------------------------------------------ */
 const char* inf_error_string(Error_t err);
 const char* inf_last_error_detail(void);
@@ -197,9 +202,10 @@ void*       inf_model_stream(Model* model);
 u64         inf_kernel_launches(Model* model);
 /* Bytes the decode step of one token streams from HBM: weights + KV read for ctx. */
 u64         inf_decode_bytes(const InfConfig* config, u32 ctx);
-/* Time each kernel kind of one eager (non-graph) decode step at the slot's current
- * position: ms_out[k] for k in InfKernelKind; returns the number of kinds. */
-u32         inf_profile_decode_step(Model* model, f32* ms_out, u32 max_kinds);
+/* Time each kernel kind of one eager (non-graph) decode step of token `id` at `pos` of
+ * the slot, with CUDA events around every launch on the model's stream: ms_out[k] for k in
+ * InfKernelKind.  Returns the number of kinds (0 on error). */
+u32         inf_profile_decode_step(Model* model, u32 seq_slot, u32 pos, u32 id, f32* ms_out, u32 max_kinds);
 
 typedef enum InfKernelKind {
 	InfKEmbed = 0,

@@ -897,6 +897,27 @@ Error_t inf_decode(Model* model, u32 seq_slot, u32 start_pos, u32 first_id, u32 
 	return check_dev_err(e);
 }
 
+Error_t inf_synth_ids(u64 seed, u64 stream, u64 n, u32 lo, u32 hi_inclusive, u32* out)
+{
+	if (!out || hi_inclusive < lo) return fail(ErrorInvalidValue, "inf_synth_ids: bad arguments");
+	const PhiloxKey key = stream_key(seed, stream);
+	const u64 range = (u64)hi_inclusive - lo + 1u;
+	for (u64 i = 0; i < n; ++i) {
+		uint32_t c0 = (uint32_t)i, c1 = (uint32_t)(i >> 32), c2 = 0, c3 = 0, k0 = key.k0, k1 = key.k1;
+		for (int r = 0; r < 10; ++r) {
+			const u64 p0 = (u64)0xD2511F53u * c0, p1 = (u64)0xCD9E8D57u * c2;
+			c0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0;
+			c1 = (uint32_t)p1;
+			c2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1;
+			c3 = (uint32_t)p0;
+			k0 += 0x9E3779B9u;
+			k1 += 0xBB67AE85u;
+		}
+		out[i] = lo + (u32)(((u64)c0 * range) >> 32);
+	}
+	return Success;
+}
+
 Error_t inf_seq_reset(Model* model, u32 seq_slot)
 {
 	if (!model || !model->engine) return fail(ErrorInvalidValue, "inf_seq_reset: no model");
@@ -918,10 +939,17 @@ u64 inf_decode_bytes(const InfConfig* c, u32 ctx)
 	return weights + kv;
 }
 
-u32 inf_profile_decode_step(Model* model, f32* ms_out, u32 max_kinds)
+u32 inf_profile_decode_step(Model* model, u32 seq_slot, u32 pos, u32 id, f32* ms_out, u32 max_kinds)
 {
 	if (!model || !model->engine || !ms_out) return 0;
 	InfEngine* e = model->engine;
+	if (seq_slot >= e->cfg.max_batch || pos >= e->cfg.max_seq || id >= e->cfg.vocab_size) return 0;
+	if (ensure_pages(e, seq_slot, pos + 1) != Success) return 0;
+	int* in = e->h_ctl;
+	in[kCtlId] = (int)id;
+	in[kCtlPos] = (int)pos;
+	in[kCtlSlot] = (int)seq_slot;
+	if (cudaMemcpyAsync(e->ctl, in, 3 * sizeof(int), cudaMemcpyHostToDevice, e->stream) != cudaSuccess) return 0;
 	for (float& v : e->prof_ms) v = 0.f;
 	e->profiling = true;
 	const Error_t r = enqueue_step(e);

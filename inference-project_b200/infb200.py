@@ -78,7 +78,7 @@ EXPORTS = [
     "cu_memcpy_htd_async", "cu_memcpy_dth", "cu_memset", "inf_fetch_input_embeddings", "inf_rmsnorm",
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
-    "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step",
+    "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids",
 ]
 
 _lib = None
@@ -130,7 +130,8 @@ def lib():
         "inf_model_stream": (vp, [C.POINTER(Model)]),
         "inf_kernel_launches": (u64, [C.POINTER(Model)]),
         "inf_decode_bytes": (u64, [C.POINTER(InfConfig), u32]),
-        "inf_profile_decode_step": (u32, [C.POINTER(Model), C.POINTER(f32), u32]),
+        "inf_profile_decode_step": (u32, [C.POINTER(Model), u32, u32, u32, C.POINTER(f32), u32]),
+        "inf_synth_ids": (E, [u64, u64, u64, u32, u32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -258,10 +259,29 @@ class Engine:
     def reset(self, slot: int = 0):
         check(lib().inf_seq_reset(C.byref(self.model), slot), "inf_seq_reset")
 
-    def profile_step(self) -> dict:
+    def profile_step(self, pos: int, token: int, slot: int = 0) -> dict:
         ms = (f32 * 8)()
-        n = lib().inf_profile_decode_step(C.byref(self.model), ms, 8)
+        n = lib().inf_profile_decode_step(C.byref(self.model), slot, pos, token, ms, 8)
+        if n == 0:
+            raise InfError(7, "inf_profile_decode_step", lib().inf_last_error_detail().decode())
         return {KERNEL_KINDS[k]: float(ms[k]) for k in range(n)}
+
+
+STREAM_PROMPT = 0x1000000
+STREAM_CTX_LEN = 0x2000000
+
+
+def synth_ids(seed: int, n: int, vocab: int, stream: int = STREAM_PROMPT) -> np.ndarray:
+    """Seeded uniform ids in [0, vocab) (the workloads' prompts)."""
+    out = np.empty(n, dtype=np.uint32)
+    check(lib().inf_synth_ids(seed, stream, n, 0, vocab - 1, _ptr(out)), "inf_synth_ids")
+    return out
+
+
+def synth_uniform(seed: int, stream: int, n: int, lo: int, hi: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.uint32)
+    check(lib().inf_synth_ids(seed, stream, n, lo, hi, _ptr(out)), "inf_synth_ids")
+    return out
 
 
 def decode_bytes(cfg: InfConfig, ctx: int) -> int:

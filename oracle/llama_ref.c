@@ -10,6 +10,10 @@
  *   SwiGLU product h             bf16(silu(gate) * up)
  *   logits                       fp32, greedy argmax with ties to the lowest index
  * In fp32 mode (bf16 == 0) every rounding point is the identity.
+ *
+ * Between rounding points the oracle accumulates in double (dot products, sums of squares,
+ * softmax sums), so each stored value is the correctly computed one and a comparison with
+ * the device measures only the device's own fp32 accumulation error.
  */
 #include "llama_ref.h"
 
@@ -171,14 +175,14 @@ void orc_embed_gather(const uint32_t* ids, uint64_t n, uint32_t dim, const void*
 
 static float rms_inv(const float* x, uint32_t dim, float eps)
 {
-	float acc[16] = { 0 };
+	double acc[8] = { 0 };
 	uint32_t i = 0;
-	for (; i + 16 <= dim; i += 16)
-		for (int j = 0; j < 16; ++j) acc[j] += x[i + j] * x[i + j];
-	float ss = 0.f;
-	for (int j = 0; j < 16; ++j) ss += acc[j];
-	for (; i < dim; ++i) ss += x[i] * x[i];
-	return 1.0f / sqrtf(ss / (float)dim + eps);
+	for (; i + 8 <= dim; i += 8)
+		for (int j = 0; j < 8; ++j) acc[j] += (double)x[i + j] * (double)x[i + j];
+	double ss = 0.0;
+	for (int j = 0; j < 8; ++j) ss += acc[j];
+	for (; i < dim; ++i) ss += (double)x[i] * (double)x[i];
+	return 1.0f / sqrtf((float)ss / (float)dim + eps);
 }
 
 void orc_rmsnorm(const float* x, uint64_t rows, uint32_t dim, const void* g, int bf16, float eps, float* y)
@@ -190,27 +194,28 @@ void orc_rmsnorm(const float* x, uint64_t rows, uint32_t dim, const void* g, int
 	}
 }
 
-static inline float dot_bf16(const uint16_t* w, const float* x, uint64_t n)
+/* products of two floats are exact in double; only the sum rounds */
+static inline double dot_bf16_d(const uint16_t* w, const float* x, uint64_t n)
 {
-	float acc[16] = { 0 };
+	double acc[8] = { 0 };
 	uint64_t i = 0;
-	for (; i + 16 <= n; i += 16)
-		for (int j = 0; j < 16; ++j) acc[j] += orc_bf16_to_f32(w[i + j]) * x[i + j];
-	float s = 0.f;
-	for (int j = 0; j < 16; ++j) s += acc[j];
-	for (; i < n; ++i) s += orc_bf16_to_f32(w[i]) * x[i];
+	for (; i + 8 <= n; i += 8)
+		for (int j = 0; j < 8; ++j) acc[j] += (double)orc_bf16_to_f32(w[i + j]) * (double)x[i + j];
+	double s = 0.0;
+	for (int j = 0; j < 8; ++j) s += acc[j];
+	for (; i < n; ++i) s += (double)orc_bf16_to_f32(w[i]) * (double)x[i];
 	return s;
 }
 
-static inline float dot_f32(const float* w, const float* x, uint64_t n)
+static inline double dot_f32_d(const float* w, const float* x, uint64_t n)
 {
-	float acc[16] = { 0 };
+	double acc[8] = { 0 };
 	uint64_t i = 0;
-	for (; i + 16 <= n; i += 16)
-		for (int j = 0; j < 16; ++j) acc[j] += w[i + j] * x[i + j];
-	float s = 0.f;
-	for (int j = 0; j < 16; ++j) s += acc[j];
-	for (; i < n; ++i) s += w[i] * x[i];
+	for (; i + 8 <= n; i += 8)
+		for (int j = 0; j < 8; ++j) acc[j] += (double)w[i + j] * (double)x[i + j];
+	double s = 0.0;
+	for (int j = 0; j < 8; ++j) s += acc[j];
+	for (; i < n; ++i) s += (double)w[i] * (double)x[i];
 	return s;
 }
 
@@ -218,8 +223,8 @@ void orc_matvec(const void* W, int bf16, uint64_t rows, uint64_t cols, const flo
 {
 #pragma omp parallel for schedule(static)
 	for (int64_t r = 0; r < (int64_t)rows; ++r) {
-		y[r] = bf16 ? dot_bf16((const uint16_t*)W + (uint64_t)r * cols, x, cols)
-		            : dot_f32((const float*)W + (uint64_t)r * cols, x, cols);
+		y[r] = (float)(bf16 ? dot_bf16_d((const uint16_t*)W + (uint64_t)r * cols, x, cols)
+		                    : dot_f32_d((const float*)W + (uint64_t)r * cols, x, cols));
 	}
 }
 
@@ -314,6 +319,7 @@ const void* orc_model_weight(const OrcModel* m, int32_t layer, uint32_t kind)
 OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 {
 	if (!cfg || cfg->n_heads == 0 || cfg->n_kv_heads == 0 || cfg->n_heads % cfg->n_kv_heads || cfg->head_dim % 2 ||
+	    cfg->head_dim > 512 ||
 	    cfg->n_slots == 0 || cfg->max_seq == 0)
 		return NULL;
 #ifdef _OPENMP
@@ -449,25 +455,26 @@ static void forward_token(OrcModel* m, uint32_t slot, uint32_t id, uint32_t pos,
 			const uint32_t g = (uint32_t)h / group;
 			const float* qh = m->q + (uint64_t)h * hd;
 			float* sc = m->scores + (uint64_t)h * c->max_seq;
-			float mx = -INFINITY;
+			double mx = -INFINITY;
 			for (uint32_t t = 0; t < ctx; ++t) {
 				const float* kt = kv_at(m, m->kcache, slot, l, t) + (uint64_t)g * hd;
-				const float s = dot_f32(kt, qh, hd) * attn_scale;
+				const float s = (float)dot_f32_d(kt, qh, hd) * attn_scale;
 				sc[t] = s;
 				if (s > mx) mx = s;
 			}
-			float den = 0.f;
+			double den = 0.0;
 			for (uint32_t t = 0; t < ctx; ++t) {
-				sc[t] = expf(sc[t] - mx);
+				sc[t] = (float)exp((double)sc[t] - mx);
 				den += sc[t];
 			}
-			float* oh = m->att + (uint64_t)h * hd;
-			for (uint32_t i = 0; i < hd; ++i) oh[i] = 0.f;
+			double acc[512];
+			for (uint32_t i = 0; i < hd; ++i) acc[i] = 0.0;
 			for (uint32_t t = 0; t < ctx; ++t) {
 				const float* vt = kv_at(m, m->vcache, slot, l, t) + (uint64_t)g * hd;
-				for (uint32_t i = 0; i < hd; ++i) oh[i] += sc[t] * vt[i];
+				for (uint32_t i = 0; i < hd; ++i) acc[i] += (double)sc[t] * (double)vt[i];
 			}
-			for (uint32_t i = 0; i < hd; ++i) oh[i] = round_store(oh[i] / den, bf);
+			float* oh = m->att + (uint64_t)h * hd;
+			for (uint32_t i = 0; i < hd; ++i) oh[i] = round_store((float)(acc[i] / den), bf);
 		}
 		if (l == 0) {
 			memcpy(m->dbg_q, m->q, sizeof(float) * H * hd);
@@ -482,9 +489,9 @@ static void forward_token(OrcModel* m, uint32_t slot, uint32_t id, uint32_t pos,
 		orc_matvec(Ly->wg, bf, F, d, m->xh, m->gate);
 		orc_matvec(Ly->wu, bf, F, d, m->xh, m->up);
 		for (uint32_t j = 0; j < F; ++j) {
-			const float gt = m->gate[j];
-			const float s = gt / (1.0f + expf(-gt));
-			m->h[j] = round_store(s * m->up[j], bf);
+			const double gt = m->gate[j];
+			const double s = gt / (1.0 + exp(-gt));
+			m->h[j] = round_store((float)(s * (double)m->up[j]), bf);
 		}
 		orc_matvec(Ly->wd, bf, d, F, m->h, m->o);
 		for (uint32_t i = 0; i < d; ++i) m->r[i] += m->o[i];

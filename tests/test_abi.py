@@ -95,3 +95,12 @@ def test_model_build_rejects_bad_config_without_touching_the_device():
     with pytest.raises(I.InfError) as e:
         I.Engine(c)
     assert e.value.code == 9  # ErrorBadConfig
+
+
+def test_library_id_generator_matches_oracle():
+    import oracle as O
+    import numpy as np
+    np.testing.assert_array_equal(I.synth_ids(1, 300, 128256), O.gen_ids(1, 300, 128256))
+    lens = I.synth_uniform(2, I.STREAM_CTX_LEN, 64, 512, 4096)
+    want = [O.uniform_u32(2, O.STREAM_CTX_LEN, i, 512, 4096) for i in range(64)]
+    np.testing.assert_array_equal(lens, np.array(want, np.uint32))
