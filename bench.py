@@ -152,7 +152,7 @@ def run_ours(args, rank: int, world: int, dist):
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    cfg = I.preset(3)
+    cfg = I.preset(3, n_layers=args.layers)
     steps, warmup = args.steps, args.warmup
     if PROMPT + max(steps, warmup) > cfg.max_seq:
         raise SystemExit(f"--steps/--warmup above {cfg.max_seq - PROMPT}")
@@ -232,7 +232,8 @@ def run_ours(args, rank: int, world: int, dist):
             "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (Philox seed-0 N(0,0.02) weights, seed-1 uniform prompt ids)",
             "config": {"workload": "llama3-8b-shape batch-1 greedy decode, prompt 2048, timed positions 2048..2048+K-1",
-                       "model": "llama-3-8b-shape", "global_batch": world, "seq_len": PROMPT,
+                       "model": "llama-3-8b-shape" if args.layers == 32 else f"llama-3-8b-shape-{args.layers}-layers",
+                       "global_batch": world, "seq_len": PROMPT,
                        "parallelism": "tp1" if world == 1 else f"replicas{world}",
                        "l2": "no flush: each step streams 15.3 GB (> 126 MB L2)",
                        "step_bytes": step_bytes, "step_gbs": step_gbs,
@@ -261,6 +262,7 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs use a short one)")
+    ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
     args = ap.parse_args()
     globals()["PROMPT"] = args.prompt
     if args.warmup < 3:

@@ -160,6 +160,12 @@ Error_t inf_fetch_input_embeddings(const u32* d_ids, u64 n_tokens, u32 dim, u32 
 Error_t inf_rmsnorm(const void* d_x, void* d_y, u32 rows, u32 dim, const void* d_gain, f32 eps, u32 dtype,
                     void* stream);
 
+/* The prefill projection on the tensor cores (tcgen05, TMA): Y[T x N] = X[T x K] . W[N x K]^T,
+ * bf16 inputs (row-major, 16-byte aligned, K % 8 == 0), fp32 accumulation, Y bf16 (RNE) or
+ * f32 (out_f32 != 0).  Device pointers; synchronous.  The reference has no projection
+ * (src/model.cuh:44-50 declares wq/wk/wv/wo only). */
+Error_t inf_gemm_bf16(const void* d_x, const void* d_w, void* d_y, u32 T, u32 N, u32 K, u32 out_f32, void* stream);
+
 /* ---- model ------------------------------------------------------------------------- */
 /* Built-in shapes: 1 tiny fp32 (d288), 2 TinyLlama-1.1B, 3 Llama-3-8B, 4 Llama-3-8B batch 64,
  * 5 Llama-3-8B 32k prefill. */
@@ -196,6 +202,18 @@ Error_t inf_seq_reset(Model* model, u32 seq_slot);
 Error_t inf_synth_ids(u64 seed, u64 stream, u64 n, u32 lo, u32 hi_inclusive, u32* out);
 
 /* ---- introspection ------------------------------------------------------------------ */
+typedef enum InfBuffer {
+	InfBufResid  = 0, /* residual stream of the last decode token, f32 [dim] */
+	InfBufQ      = 1, /* query of the last decode token, last layer [n_heads * head_dim] */
+	InfBufAttn   = 2, /* attention output, last layer [n_heads * head_dim] */
+	InfBufH      = 3, /* SwiGLU product, last layer [ffn_dim] */
+	InfBufLogits = 4, /* logits of the last token [vocab_size] */
+	InfBufK      = 5, /* K the cache holds for (layer, slot, pos) [n_kv_heads * head_dim] */
+	InfBufV      = 6, /* V the cache holds for (layer, slot, pos) */
+} InfBuffer;
+/* Copy one engine buffer to host floats (bf16 widened).  For test and debugging; the
+ * reference's equivalent is print_dev_buf_bf16 (src/main.cu:44-61). */
+Error_t     inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 pos, f32* out, u64 n_out);
 const char* inf_error_string(Error_t err);
 const char* inf_last_error_detail(void);
 void*       inf_model_stream(Model* model);

@@ -6,6 +6,8 @@
 // activations and decode scratch.  The batch-1 decode step is one CUDA graph whose
 // kernels read the token id and position from device memory and advance them, so
 // replays chain without the host.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -16,6 +18,8 @@
 #include "common.cuh"
 #include "k_attn_decode.cuh"
 #include "k_gemv.cuh"
+#include "k_attn_prefill.cuh"
+#include "k_gemm_tc.cuh"
 #include "k_small.cuh"
 #include "runtime.h"
 #include "synth.cuh"
@@ -76,6 +80,17 @@ struct InfEngine {
 	uint32_t* d_ids = nullptr; // staged ids [max_seq]
 	int max_out = 0;
 	int attn_splits = 1;
+	int attn_max_pages_split = 1;
+	// multi-token (prefill) buffers, prefill_chunk rows each
+	int chunk = 0;
+	float* resid_p = nullptr;  // [chunk][d] f32
+	void* xhat_p = nullptr;    // [chunk][d]
+	void* q_p = nullptr;       // [chunk][Hl*hd]
+	void* attn_p = nullptr;    // [chunk][Hl*hd]
+	void* h_p = nullptr;       // [chunk][Fl]
+	int* tok_pos = nullptr;    // [chunk]
+	int* tok_slot = nullptr;   // [chunk]
+	int* h_tok = nullptr;      // pinned [2 * chunk]
 	// pinned host staging
 	uint32_t* h_pin = nullptr; // [max_seq + 16]
 	int* h_ctl = nullptr;      // [2 * kCtlWords]: staging in, staging out
@@ -261,12 +276,19 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.hd = hd;
 			a.blk = (int)c.kv_block;
 			a.n_splits = e->attn_splits;
+			a.max_pages_split = e->attn_max_pages_split;
 			a.scale = (float)(1.0 / std::sqrt((double)hd));
 			a.part = e->attn_part;
 			a.counters = e->attn_counters;
 			a.out = e->attn;
 			a.err = e->err;
-			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block);
+			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
+			                                           e->attn_max_pages_split, e->attn_splits);
+			static bool attn_attr = false;
+			if (!attn_attr) {
+				INF_CUDA_TRY(set_smem(k_attn_decode<T>, smem));
+				attn_attr = true;
+			}
 			INF_TRY(prof_begin(e));
 			INF_CUDA_TRY(launch(e, k_attn_decode<T>, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
 			INF_TRY(prof_end(e, InfKAttn));
@@ -325,6 +347,186 @@ Error_t enqueue_step(InfEngine* e)
 {
 	return e->cfg.dtype == InfBF16 ? enqueue_decode_step<bf16>(e) : enqueue_decode_step<float>(e);
 }
+
+// --------------------------------------------------------------------------- prefill
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+Error_t tensor_map_2d(CUtensorMap* m, const void* base, u64 rows, u64 cols, u32 box_rows)
+{
+	if (!g_encode) {
+		cudaDriverEntryPointQueryResult q;
+		void* fn = nullptr;
+		INF_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+		if (q != cudaDriverEntryPointSuccess || !fn) return fail(ErrorCuda, "cuTensorMapEncodeTiled unavailable");
+		g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+	}
+	const cuuint64_t dims[2] = {cols, rows};
+	const cuuint64_t strides[1] = {cols * 2};
+	const cuuint32_t box[2] = {(cuuint32_t)kTcBK, box_rows};
+	const cuuint32_t estr[2] = {1, 1};
+	const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+	                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+	                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	if (r != CUDA_SUCCESS) return fail(ErrorCuda, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+	return Success;
+}
+
+// D[T x N] = X[T x K] . W[N x K]^T on the tensor cores, fused epilogue a.epi
+Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
+{
+	if (a.K % 8 != 0) return fail(ErrorUnsupported, "gemm: K %% 8 != 0");
+	CUtensorMap tx, tw;
+	INF_TRY(tensor_map_2d(&tx, X, (u64)a.T, (u64)a.K, kTcBM));
+	INF_TRY(tensor_map_2d(&tw, W, (u64)a.N, (u64)a.K, kTcBN));
+	const size_t smem = gemm_tc_smem_bytes();
+	static bool attr_done = false;
+	if (!attr_done) {
+		INF_CUDA_TRY(set_smem(k_gemm_tc, smem));
+		attr_done = true;
+	}
+	a.err = e->err;
+	const dim3 grid((a.N + kTcBN - 1) / kTcBN, (a.T + kTcBM - 1) / kTcBM);
+	INF_CUDA_TRY(launch(e, k_gemm_tc, grid, dim3(kTcThreads), smem, tx, tw, a));
+	return Success;
+}
+
+TcArgs tc_base(InfEngine* e, int T, int N, int K, int epi)
+{
+	TcArgs a;
+	memset(&a, 0, sizeof a);
+	a.T = T;
+	a.N = N;
+	a.K = K;
+	a.epi = epi;
+	a.err = e->err;
+	return a;
+}
+
+// One chunk of T tokens of one sequence (positions and slots already in tok_pos/tok_slot),
+// all layers on the tensor cores; leaves the residual of every token in resid_p.
+Error_t enqueue_prefill_layers(InfEngine* e, int T)
+{
+	const InfConfig& c = e->cfg;
+	const int d = (int)c.dim, hd = (int)c.head_dim, G = e->Hl / e->KVl;
+	INF_CUDA_TRY(launch(e, k_embed<bf16, float>, dim3((d + 255) / 256, T), dim3(256), 0, (const uint32_t*)e->d_ids, T, d,
+	                    c.vocab_size, (const bf16*)e->embed, e->resid_p, e->err));
+	const size_t pf_smem = attn_prefill_smem_bytes(G, hd, (int)c.kv_block);
+	static bool pf_attr = false;
+	if (!pf_attr) {
+		INF_CUDA_TRY(set_smem(k_attn_prefill<bf16>, pf_smem));
+		pf_attr = true;
+	}
+	for (u32 l = 0; l < c.n_layers; ++l) {
+		const LayerW& L = e->layers[l];
+		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
+		                    (bf16*)e->xhat_p, T, d, (const bf16*)L.attn_norm, c.norm_eps));
+		{
+			TcArgs a = tc_base(e, T, (e->Hl + 2 * e->KVl) * hd, d, kTcQkv);
+			a.out = e->q_p;
+			a.kpool = L.kpool;
+			a.vpool = L.vpool;
+			a.block_table = e->block_table;
+			a.pages_per_seq = e->pages_per_seq;
+			a.max_pages = e->n_pages;
+			a.max_seq = (int)c.max_seq;
+			a.tok_pos = e->tok_pos;
+			a.tok_slot = e->tok_slot;
+			a.rope_cos = e->rope_cos;
+			a.rope_sin = e->rope_sin;
+			a.head_dim = hd;
+			a.n_q_heads = e->Hl;
+			a.n_kv_heads = e->KVl;
+			a.kv_block = (int)c.kv_block;
+			INF_TRY(launch_gemm_tc(e, e->xhat_p, L.wqkv, a));
+		}
+		{
+			AttnPrefillArgs a;
+			memset(&a, 0, sizeof a);
+			a.q = e->q_p;
+			a.kpool = L.kpool;
+			a.vpool = L.vpool;
+			a.block_table = e->block_table;
+			a.pages_per_seq = e->pages_per_seq;
+			a.max_pages = e->n_pages;
+			a.tok_pos = e->tok_pos;
+			a.tok_slot = e->tok_slot;
+			a.T = T;
+			a.H = e->Hl;
+			a.KV = e->KVl;
+			a.hd = hd;
+			a.blk = (int)c.kv_block;
+			a.scale = (float)(1.0 / std::sqrt((double)hd));
+			a.out = e->attn_p;
+			a.err = e->err;
+			INF_CUDA_TRY(launch(e, k_attn_prefill<bf16>, dim3(e->KVl, (T + kPfTq - 1) / kPfTq), dim3(kPfThreads), pf_smem, a));
+		}
+		{
+			TcArgs a = tc_base(e, T, d, e->Hl * hd, kTcResid);
+			a.resid = e->resid_p;
+			INF_TRY(launch_gemm_tc(e, e->attn_p, L.wo, a));
+		}
+		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
+		                    (bf16*)e->xhat_p, T, d, (const bf16*)L.ffn_norm, c.norm_eps));
+		{
+			TcArgs a = tc_base(e, T, 2 * e->Fl, d, kTcSwiglu);
+			a.out = e->h_p;
+			INF_TRY(launch_gemm_tc(e, e->xhat_p, L.wgu, a));
+		}
+		{
+			TcArgs a = tc_base(e, T, d, e->Fl, kTcResid);
+			a.resid = e->resid_p;
+			INF_TRY(launch_gemm_tc(e, e->h_p, L.wd, a));
+		}
+	}
+	return Success;
+}
+
+// Final norm + LM head + argmax of one residual row (the decode GEMV); advances the ctl
+// block exactly like a decode step (pos += 1, id = argmax).
+Error_t enqueue_lm_head_row(InfEngine* e, const float* resid_row)
+{
+	GemvArgs a = gemv_base(e, e->lm_head, e->Vl, (int)e->cfg.dim);
+	a.resid_in = resid_row;
+	a.gain = e->final_norm;
+	a.logits = e->logits;
+	a.best = e->best;
+	a.counter = e->lm_counter;
+	a.cur_id = e->cur_id;
+	a.out_ids = e->out_ids;
+	a.step = e->step;
+	a.pos_rw = e->pos;
+	a.max_out = e->max_out;
+	return e->cfg.dtype == InfBF16 ? launch_gemv<bf16, kEpiLogits>(e, a) : launch_gemv<float, kEpiLogits>(e, a);
+}
+
+// Prefill of n tokens (already in d_ids) of one slot from start: chunks of e->chunk tokens
+// on the tensor cores, then the LM head of the last token.  Leaves ctl = (argmax, start+n, slot).
+Error_t run_prefill(InfEngine* e, u32 n, u32 start, u32 slot)
+{
+	for (u32 c0 = 0; c0 < n; c0 += (u32)e->chunk) {
+		const int T = (int)std::min<u32>((u32)e->chunk, n - c0);
+		INF_CUDA_TRY(cudaStreamSynchronize(e->stream)); // h_tok reuse
+		for (int t = 0; t < T; ++t) {
+			e->h_tok[t] = (int)(start + c0 + t);
+			e->h_tok[e->chunk + t] = (int)slot;
+		}
+		INF_CUDA_TRY(cudaMemcpyAsync(e->tok_pos, e->h_tok, sizeof(int) * T, cudaMemcpyHostToDevice, e->stream));
+		INF_CUDA_TRY(cudaMemcpyAsync(e->tok_slot, e->h_tok + e->chunk, sizeof(int) * T, cudaMemcpyHostToDevice, e->stream));
+		if (c0 > 0)
+			INF_CUDA_TRY(cudaMemcpyAsync(e->d_ids, e->d_ids + c0, sizeof(u32) * T, cudaMemcpyDeviceToDevice, e->stream));
+		INF_TRY(enqueue_prefill_layers(e, T));
+		if (c0 + (u32)T == n) {
+			int* in = e->h_ctl;
+			in[kCtlPos] = (int)(start + n - 1);
+			in[kCtlSlot] = (int)slot;
+			INF_CUDA_TRY(cudaMemcpyAsync(e->pos, &in[kCtlPos], 2 * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+			INF_TRY(enqueue_lm_head_row(e, e->resid_p + (size_t)(T - 1) * e->cfg.dim));
+		}
+	}
+	return Success;
+}
+
+bool use_tc_prefill(const InfEngine* e, u32 n) { return e->cfg.dtype == InfBF16 && e->chunk > 0 && n > 1; }
 
 Error_t build_decode_graph(InfEngine* e)
 {
@@ -409,6 +611,10 @@ Error_t validate(const InfConfig& c)
 	const u32 vec = c.dtype == InfBF16 ? 8 : 4;
 	if (c.dim % vec || c.ffn_dim / tp % vec || (c.n_heads / tp * c.head_dim) % vec)
 		return fail(ErrorBadConfig, "dim, ffn_dim and heads*head_dim must be multiples of %u", vec);
+	if ((c.n_heads / c.n_kv_heads) * c.head_dim * kPfTq > (u32)(kPfThreads * kPfMaxAcc))
+		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kPfThreads * kPfMaxAcc / kPfTq);
+	if (kAttnThreads % (c.n_heads / c.n_kv_heads) != 0)
+		return fail(ErrorUnsupported, "GQA group must divide %d", kAttnThreads);
 	if ((c.n_heads / c.n_kv_heads) * c.head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kAttnThreads * kAttnMaxAcc);
 	if (c.dim > 16384 || c.ffn_dim / tp > 16384) return fail(ErrorUnsupported, "dim/ffn above 16384");
@@ -559,14 +765,21 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	const int G = e->Hl / e->KVl;
 	(void)G;
 	// splits: ~2 CTAs per SM over the KV heads of one token, at most one page per split
-	e->attn_splits = std::max(1, std::min(e->pages_per_seq, (2 * e->sm_count + e->KVl - 1) / e->KVl));
+	// about one CTA per SM over the KV heads of one token, each split within the smem budget
+	e->attn_max_pages_split = attn_decode_max_pages_split((int)c.kv_block, (int)hd, e->esz);
+	e->attn_splits = std::max((e->sm_count + e->KVl - 1) / e->KVl,
+	                          (e->pages_per_seq + e->attn_max_pages_split - 1) / e->attn_max_pages_split);
+	e->attn_splits = std::max(1, std::min(e->attn_splits, e->pages_per_seq));
+	// multi-token passes run on the tensor cores (bf16 models); fp32 models feed tokens one by one
+	e->chunk = c.dtype == InfBF16 ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u)) : 0;
 
 	// ---- sizes
 	const u64 w_layer = ((u64)(e->Hl + 2 * e->KVl) * hd * d + d * e->Hl * hd + 2ull * e->Fl * d + d * e->Fl + 2 * d) * es;
 	const u64 w_total = (2ull * c.vocab_size * d) * es + d * es + L * w_layer; // embed is full, LM head is a shard
 	const u64 page_elems = (u64)e->KVl * c.kv_block * hd;
 	const u64 kv_total = 2ull * L * e->n_pages * page_elems * es;
-	const u64 act = d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + (u64)e->Hl * e->attn_splits * (hd + 2) * 4;
+	const u64 act = d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + (u64)e->Hl * e->attn_splits * (hd + 2) * 4 +
+	                (u64)e->chunk * (d * 4 + d * es + 2ull * e->Hl * hd * es + (u64)e->Fl * es + 8) + 16 * 256;
 	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024;
 	const u64 total = w_total + kv_total + act + (u64)c.max_seq * hd * 4 + (u64)c.max_batch * e->pages_per_seq * 4 +
 	                  (u64)c.max_seq * 8 + slack;
@@ -608,6 +821,15 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	P.push(&e->d_ids, (u64)c.max_seq * 4);
 	P.push(&e->attn_part, (u64)e->Hl * e->attn_splits * (hd + 2) * 4);
 	P.push(&e->attn_counters, (u64)e->KVl * 4);
+	if (e->chunk > 0) {
+		P.push(&e->resid_p, (u64)e->chunk * d * 4);
+		P.push(&e->xhat_p, (u64)e->chunk * d * es);
+		P.push(&e->q_p, (u64)e->chunk * e->Hl * hd * es);
+		P.push(&e->attn_p, (u64)e->chunk * e->Hl * hd * es);
+		P.push(&e->h_p, (u64)e->chunk * e->Fl * es);
+		P.push(&e->tok_pos, (u64)e->chunk * 4);
+		P.push(&e->tok_slot, (u64)e->chunk * 4);
+	}
 	if (P.err != Success) return P.err;
 	e->cur_id = reinterpret_cast<uint32_t*>(e->ctl + kCtlId);
 	e->pos = e->ctl + kCtlPos;
@@ -632,6 +854,7 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	for (int p = e->n_pages - 1; p >= 0; --p) e->free_pages.push_back(p);
 	INF_CUDA_TRY(cudaMallocHost(&e->h_pin, sizeof(uint32_t) * (c.max_seq + 16)));
 	INF_CUDA_TRY(cudaMallocHost(&e->h_ctl, sizeof(int) * 2 * kCtlWords));
+	if (e->chunk > 0) INF_CUDA_TRY(cudaMallocHost(&e->h_tok, sizeof(int) * 2 * e->chunk));
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
 	INF_TRY(build_decode_graph(e));
 	return Success;
@@ -644,6 +867,7 @@ void engine_free(InfEngine* e)
 	if (e->decode_exec) cudaGraphExecDestroy(e->decode_exec);
 	if (e->h_pin) cudaFreeHost(e->h_pin);
 	if (e->h_ctl) cudaFreeHost(e->h_ctl);
+	if (e->h_tok) cudaFreeHost(e->h_tok);
 	for (auto& ev : e->prof_ev)
 		if (ev) cudaEventDestroy(ev);
 	if (e->stream) cudaStreamDestroy(e->stream);
@@ -798,8 +1022,11 @@ Error_t inf_forward(Model* model, const u32* ids, u32 n_tokens, u32 start_pos, u
 	INF_TRY(ensure_pages(e, seq_slot, start_pos + n_tokens));
 	if (n_tokens == 1 && !is_device_ptr(ids)) return forward_one(e, ids[0], start_pos, seq_slot, logits_out, argmax_out);
 	INF_TRY(copy_in_ids(e, ids, n_tokens));
-	INF_TRY(set_scalars(e, (int)seq_slot, (int)start_pos));
-	INF_TRY(run_tokens(e, n_tokens));
+	if (use_tc_prefill(e, n_tokens)) INF_TRY(run_prefill(e, n_tokens, start_pos, seq_slot));
+	else {
+		INF_TRY(set_scalars(e, (int)seq_slot, (int)start_pos));
+		INF_TRY(run_tokens(e, n_tokens));
+	}
 	if (logits_out) INF_TRY(copy_out(e, logits_out, e->logits, sizeof(float) * e->Vl));
 	if (argmax_out) INF_TRY(copy_out(e, argmax_out, e->cur_id, 4));
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -835,10 +1062,15 @@ Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u
 	cudaEvent_t ev[3];
 	for (auto& x : ev) INF_CUDA_TRY(cudaEventCreate(&x));
 	INF_CUDA_TRY(cudaEventRecord(ev[0], e->stream));
-	INF_TRY(run_tokens(e, n_prompt - 1));
-	INF_CUDA_TRY(cudaMemsetAsync(e->step, 0, 4, e->stream));
-	INF_CUDA_TRY(cudaMemcpyAsync(e->cur_id, e->d_ids + (n_prompt - 1), 4, cudaMemcpyDeviceToDevice, e->stream));
-	INF_TRY(launch_decode_graph(e));
+	if (use_tc_prefill(e, n_prompt)) {
+		INF_CUDA_TRY(cudaMemsetAsync(e->step, 0, 4, e->stream));
+		INF_TRY(run_prefill(e, n_prompt, 0, 0)); // writes out_ids[0]
+	} else {
+		INF_TRY(run_tokens(e, n_prompt - 1));
+		INF_CUDA_TRY(cudaMemsetAsync(e->step, 0, 4, e->stream));
+		INF_CUDA_TRY(cudaMemcpyAsync(e->cur_id, e->d_ids + (n_prompt - 1), 4, cudaMemcpyDeviceToDevice, e->stream));
+		INF_TRY(launch_decode_graph(e));
+	}
 	INF_CUDA_TRY(cudaEventRecord(ev[1], e->stream));
 	for (u32 s = 1; s < n_new; ++s) INF_TRY(launch_decode_graph(e));
 	INF_CUDA_TRY(cudaEventRecord(ev[2], e->stream));
@@ -918,6 +1150,58 @@ Error_t inf_synth_ids(u64 seed, u64 stream, u64 n, u32 lo, u32 hi_inclusive, u32
 	return Success;
 }
 
+Error_t inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 pos, f32* out, u64 n_out)
+{
+	if (!model || !model->engine || !out) return fail(ErrorInvalidValue, "inf_debug_read: bad arguments");
+	InfEngine* e = model->engine;
+	const InfConfig& c = e->cfg;
+	const u64 hd = c.head_dim;
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	const void* src = nullptr;
+	u64 n = 0;
+	bool is_f32 = false;
+	std::vector<uint8_t> tmp;
+	switch (buffer) {
+	case InfBufResid: src = e->resid; n = c.dim; is_f32 = true; break;
+	case InfBufQ: src = e->q; n = (u64)e->Hl * hd; break;
+	case InfBufAttn: src = e->attn; n = (u64)e->Hl * hd; break;
+	case InfBufH: src = e->h; n = (u64)e->Fl; break;
+	case InfBufLogits: src = e->logits; n = (u64)e->Vl; is_f32 = true; break;
+	case InfBufK:
+	case InfBufV: {
+		if (layer >= c.n_layers || seq_slot >= c.max_batch || pos >= c.max_seq)
+			return fail(ErrorInvalidValue, "inf_debug_read: layer/slot/pos");
+		const int page = e->h_block_table[(size_t)seq_slot * e->pages_per_seq + pos / c.kv_block];
+		if (page < 0) return fail(ErrorKvOutOfRange, "inf_debug_read: position has no page");
+		n = (u64)e->KVl * hd;
+		if (n_out < n) return fail(ErrorInvalidValue, "inf_debug_read: need %llu floats", (unsigned long long)n);
+		tmp.resize(n * e->esz);
+		const uint8_t* pool = (const uint8_t*)(buffer == InfBufK ? e->layers[layer].kpool : e->layers[layer].vpool);
+		for (int kvh = 0; kvh < e->KVl; ++kvh) {
+			const size_t off = ((((size_t)page * e->KVl + kvh) * c.kv_block) + pos % c.kv_block) * hd * e->esz;
+			INF_CUDA_TRY(cudaMemcpy(tmp.data() + (size_t)kvh * hd * e->esz, pool + off, hd * e->esz, cudaMemcpyDeviceToHost));
+		}
+		break;
+	}
+	default: return fail(ErrorInvalidValue, "inf_debug_read: buffer %u", buffer);
+	}
+	if (n_out < n) return fail(ErrorInvalidValue, "inf_debug_read: need %llu floats", (unsigned long long)n);
+	if (src) {
+		tmp.resize(n * (is_f32 ? 4 : e->esz));
+		INF_CUDA_TRY(cudaMemcpy(tmp.data(), src, tmp.size(), cudaMemcpyDeviceToHost));
+	}
+	if (is_f32 || e->esz == 4) {
+		memcpy(out, tmp.data(), n * 4);
+	} else {
+		const uint16_t* h = (const uint16_t*)tmp.data();
+		for (u64 i = 0; i < n; ++i) {
+			const uint32_t u = (uint32_t)h[i] << 16;
+			memcpy(&out[i], &u, 4);
+		}
+	}
+	return Success;
+}
+
 Error_t inf_seq_reset(Model* model, u32 seq_slot)
 {
 	if (!model || !model->engine) return fail(ErrorInvalidValue, "inf_seq_reset: no model");
@@ -992,6 +1276,33 @@ Error_t inf_fetch_input_embeddings(const u32* d_ids, u64 n_tokens, u32 dim, u32 
 	INF_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
 	if (h_err == kDevTokenRange) return fail(ErrorTokenOutOfRange, "token id >= vocab_size");
 	return Success;
+}
+
+Error_t inf_gemm_bf16(const void* d_x, const void* d_w, void* d_y, u32 T, u32 N, u32 K, u32 out_f32, void* stream)
+{
+	if (!d_x || !d_w || !d_y || T == 0 || N == 0 || K == 0 || K % 8 != 0 || T > 65535u * kTcBM)
+		return fail(ErrorInvalidValue, "inf_gemm_bf16: bad arguments");
+	if (!is_device_ptr(d_x) || !is_device_ptr(d_w) || !is_device_ptr(d_y))
+		return fail(ErrorInvalidDevPtr, "inf_gemm_bf16: device pointers required");
+	if (((uintptr_t)d_x | (uintptr_t)d_w) & 15) return fail(ErrorInvalidValue, "inf_gemm_bf16: 16-byte alignment");
+	InfEngine tmp;
+	tmp.stream = (cudaStream_t)stream;
+	int* d_err = nullptr;
+	INF_CUDA_TRY(cudaMallocAsync((void**)&d_err, sizeof(int), tmp.stream));
+	INF_CUDA_TRY(cudaMemsetAsync(d_err, 0, sizeof(int), tmp.stream));
+	tmp.err = d_err;
+	TcArgs a = tc_base(&tmp, (int)T, (int)N, (int)K, out_f32 ? kTcStoreF32 : kTcStore);
+	a.out = d_y;
+	Error_t r = launch_gemm_tc(&tmp, d_x, d_w, a);
+	int h_err = 0;
+	if (r == Success) {
+		INF_CUDA_TRY(cudaMemcpyAsync(&h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, tmp.stream));
+	}
+	cudaFreeAsync(d_err, tmp.stream);
+	INF_CUDA_TRY(cudaStreamSynchronize(tmp.stream));
+	tmp.stream = nullptr;
+	if (r != Success) return r;
+	return map_dev_err(h_err);
 }
 
 Error_t inf_rmsnorm(const void* d_x, void* d_y, u32 rows, u32 dim, const void* d_gain, f32 eps, u32 dtype, void* stream)

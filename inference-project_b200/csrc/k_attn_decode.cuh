@@ -1,13 +1,20 @@
 // Decode attention over the paged KV cache (flash-decoding with a split-K combine).
 //
-// One query token per sequence (batch of B tokens, each with its own slot and position).
-// Grid (kv_heads, splits, B); a CTA owns one KV head of one token -- i.e. the G = H/KV
-// query heads that share it (GQA), so every K/V page is read once for the whole group --
-// and a contiguous range of the token's pages.  Per page: K tile -> shared memory (fp32),
-// scores for G x kv_block, online softmax, V tile -> shared memory, accumulate.  Partial
-// (max, sum, acc) go to scratch; the last CTA of each (token, KV head) -- found with an
-// atomic ticket, no spinning -- combines the splits and writes the rounded output.
-// Pages past the context hold stale data and are masked by position.
+// One query token per sequence (a batch of B tokens, each with its own slot and position).
+// Grid (kv_heads, splits, B): a CTA owns one KV head of one token -- the G = H/KV query heads
+// that share it (GQA), so every K/V page is read once for the whole group -- and a
+// contiguous range of at most max_pages_split pages of the token's context.
+//
+// Latency is what matters at batch 1 (a layer's KV is a few MB), so:
+//   * every page of the split is fetched at once with a 1-D bulk copy per K and V block,
+//     each page on its own mbarrier; pages older than the current token's page are issued
+//     before griddepcontrol.wait (they were written by earlier steps), overlapping the QKV
+//     kernel that is still writing this token's K/V;
+//   * the CTA works on slabs of 128/G tokens so each thread owns one (head, token) score;
+//   * partial (max, sum, acc) go to scratch and the last CTA of each (token, KV head) --
+//     found with an atomic ticket, no spinning -- combines the splits, computing the split
+//     weights once.
+// Positions past the context (stale slots in the last page) are masked.
 #pragma once
 
 #include "common.cuh"
@@ -15,7 +22,9 @@
 namespace inf {
 
 constexpr int kAttnThreads = 128;
-constexpr int kAttnMaxAcc = 8; // (G * head_dim) / kAttnThreads outputs per thread
+constexpr int kAttnMaxAcc = 8;        // (G * head_dim) / 128 outputs per thread
+constexpr int kAttnMaxPagesSplit = 16; // mbarriers per CTA
+constexpr int kAttnSmemBudget = 96 * 1024;
 
 struct AttnDecodeArgs {
 	const void* q;           // [B][H*hd]
@@ -25,7 +34,7 @@ struct AttnDecodeArgs {
 	int pages_per_seq, max_pages;
 	const int* tok_slot;     // [B]
 	const int* tok_pos;      // [B]
-	int H, KV, hd, blk, n_splits;
+	int H, KV, hd, blk, n_splits, max_pages_split;
 	float scale;
 	float* part;             // [B][H][n_splits][hd + 2]
 	unsigned* counters;      // [B][KV]
@@ -36,21 +45,26 @@ struct AttnDecodeArgs {
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeArgs a)
 {
-	extern __shared__ __align__(16) float sm[];
+	extern __shared__ __align__(128) uint8_t sm_raw[];
 	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
 	const int G = a.H / a.KV, hd = a.hd, blk = a.blk;
-	float* q_s = sm;                 // [G][hd]
-	float* kv_s = q_s + G * hd;      // [blk][hd]
-	float* p_s = kv_s + blk * hd;    // [G][blk]
-	float* m_s = p_s + G * blk;      // [G]
-	float* l_s = m_s + G;            // [G]
-	float* al_s = l_s + G;           // [G]
+	const int TS = kAttnThreads / G;               // tokens per slab
+	const size_t blk_bytes = (size_t)blk * hd * sizeof(T);
+	uint8_t* kbuf = sm_raw;                                        // [max_pages_split][blk][hd]
+	uint8_t* vbuf = kbuf + (size_t)a.max_pages_split * blk_bytes;
+	float* q_s = reinterpret_cast<float*>(vbuf + (size_t)a.max_pages_split * blk_bytes); // [G][hd]
+	float* s_s = q_s + G * hd;                                     // [G][TS]
+	float* m_s = s_s + G * TS;                                     // [G]
+	float* l_s = m_s + G;
+	float* al_s = l_s + G;
+	float* w_s = al_s + G;                                         // combine weights [G][n_splits]
+	uint64_t* bars = reinterpret_cast<uint64_t*>(w_s + G * a.n_splits + 2);
+	bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(bars) + 7) & ~(uintptr_t)7);
 	__shared__ int last_flag;
+	__shared__ int abort_flag;
 
-	const int tid = threadIdx.x;
-	pdl_wait();
-	pdl_trigger();
-
+	const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+	// slot, position and block table are not written by the kernels of this step
 	const int slot = a.tok_slot[b];
 	const int pos = a.tok_pos[b];
 	const int ctx = pos + 1;
@@ -58,6 +72,37 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	const int pps = (n_pages + a.n_splits - 1) / a.n_splits;
 	const int p_begin = split * pps;
 	const int p_end = min(n_pages, p_begin + pps);
+	const int np = max(0, p_end - p_begin);
+	const int cur_page = pos / blk; // holds this step's K/V: fetched after the wait
+
+	if (tid == 0) {
+		abort_flag = 0;
+		for (int j = 0; j < np; ++j) mbar_init(&bars[j], 1);
+		mbar_fence_init();
+	}
+	__syncthreads();
+	auto issue = [&](int j) {
+		const int p = p_begin + j;
+		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p];
+		if (page < 0 || page >= a.max_pages) {
+			report_err(a.err, kDevKvRange);
+			mbar_arrive(&bars[j]); // completes the phase with nothing in flight; data masked below
+			return;
+		}
+		const size_t off = (((size_t)page * a.KV + kvh) * blk) * hd;
+		mbar_arrive_expect_tx(&bars[j], (uint32_t)(2 * blk_bytes));
+		const uint64_t pol = policy_evict_first();
+		bulk_g2s(kbuf + j * blk_bytes, reinterpret_cast<const T*>(a.kpool) + off, (uint32_t)blk_bytes, &bars[j], pol);
+		bulk_g2s(vbuf + j * blk_bytes, reinterpret_cast<const T*>(a.vpool) + off, (uint32_t)blk_bytes, &bars[j], pol);
+	};
+	if (tid == 0)
+		for (int j = 0; j < np; ++j)
+			if (p_begin + j < cur_page) issue(j);
+	pdl_wait();
+	pdl_trigger();
+	if (tid == 0)
+		for (int j = 0; j < np; ++j)
+			if (p_begin + j >= cur_page) issue(j);
 
 	const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.H * hd + (size_t)kvh * G * hd;
 	for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = Store<T>::get(qb + i);
@@ -70,77 +115,93 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	for (int j = 0; j < kAttnMaxAcc; ++j) acc[j] = 0.0f;
 	__syncthreads();
 
-	const size_t page_elems = (size_t)a.KV * blk * hd;
-	for (int p = p_begin; p < p_end; ++p) {
-		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p];
-		const bool bad = page < 0 || page >= a.max_pages;
-		if (bad && tid == 0) report_err(a.err, kDevKvRange);
-		const T* kt = reinterpret_cast<const T*>(a.kpool) + (bad ? 0 : (size_t)page * page_elems) + (size_t)kvh * blk * hd;
-		const T* vt = reinterpret_cast<const T*>(a.vpool) + (bad ? 0 : (size_t)page * page_elems) + (size_t)kvh * blk * hd;
-		for (int i = tid; i < blk * hd; i += kAttnThreads) kv_s[i] = bad ? 0.0f : Store<T>::get(kt + i);
-		__syncthreads();
-		for (int e = tid; e < G * blk; e += kAttnThreads) {
-			const int g = e / blk, t = e % blk;
-			const int tok = p * blk + t;
+	const int n_tok = np * blk;
+	const int my_g = tid / TS, my_t = tid % TS;
+	int waited = 0; // pages known to have landed
+	for (int t0 = 0; t0 < n_tok; t0 += TS) {
+		// make sure every page this slab touches has landed
+		const int need = min(np, (t0 + TS + blk - 1) / blk);
+		for (; waited < need; ++waited)
+			if (!abort_flag && !mbar_wait(&bars[waited], 0, (volatile int*)&abort_flag, a.err)) abort_flag = 1;
+		// scores: one (head, token) per thread; rotated reads avoid bank conflicts
+		{
+			const int tl = t0 + my_t;
+			const int tok = p_begin * blk + tl;
 			float s = -INFINITY;
-			if (tok < ctx && !bad) {
-				const float* qr = q_s + g * hd;
-				const float* kr = kv_s + t * hd;
-				float d = 0.0f;
-				for (int i = 0; i < hd; ++i) d = fmaf(qr[i], kr[i], d);
-				s = d * a.scale;
-			}
-			p_s[e] = s;
-		}
-		__syncthreads();
-		if (tid < G) {
-			float mx = m_s[tid];
-			for (int t = 0; t < blk; ++t) mx = fmaxf(mx, p_s[tid * blk + t]);
-			float alpha = 1.0f, sum = 0.0f;
-			if (mx != -INFINITY) {
-				alpha = expf(m_s[tid] - mx);
-				for (int t = 0; t < blk; ++t) {
-					const float e = expf(p_s[tid * blk + t] - mx);
-					p_s[tid * blk + t] = e;
-					sum += e;
+			if (tl < n_tok && tok < ctx && !abort_flag) {
+				const T* kr = reinterpret_cast<const T*>(kbuf) + (size_t)tl * hd;
+				const float* qr = q_s + my_g * hd;
+				const int rot = (2 * my_t) % hd;
+				float d0 = 0.0f, d1 = 0.0f;
+				for (int i = 0; i < hd; i += 2) {
+					int k0 = i + rot;
+					if (k0 >= hd) k0 -= hd;
+					d0 = fmaf(qr[k0], Store<T>::get(kr + k0), d0);
+					d1 = fmaf(qr[k0 + 1], Store<T>::get(kr + k0 + 1), d1);
 				}
-			} else {
-				for (int t = 0; t < blk; ++t) p_s[tid * blk + t] = 0.0f;
+				s = (d0 + d1) * a.scale;
 			}
-			l_s[tid] = l_s[tid] * alpha + sum;
-			m_s[tid] = mx;
-			al_s[tid] = alpha;
+			s_s[my_g * TS + my_t] = s;
 		}
 		__syncthreads();
-		for (int i = tid; i < blk * hd; i += kAttnThreads) kv_s[i] = bad ? 0.0f : Store<T>::get(vt + i);
+		// online softmax, one warp per head
+		for (int g = warp; g < G; g += kAttnThreads / 32) {
+			float mx = -INFINITY;
+			for (int j = lane; j < TS; j += 32) mx = fmaxf(mx, s_s[g * TS + j]);
+			mx = warp_max(mx);
+			const float m_old = m_s[g];
+			const float m_new = fmaxf(m_old, mx);
+			float sum = 0.0f;
+			for (int j = lane; j < TS; j += 32) {
+				const float sv = s_s[g * TS + j];
+				const float e = (m_new == -INFINITY) ? 0.0f : expf(sv - m_new);
+				s_s[g * TS + j] = e;
+				sum += e;
+			}
+			sum = warp_sum(sum);
+			if (lane == 0) {
+				const float alpha = (m_new == -INFINITY) ? 1.0f : expf(m_old - m_new);
+				l_s[g] = l_s[g] * alpha + sum;
+				m_s[g] = m_new;
+				al_s[g] = alpha;
+			}
+		}
 		__syncthreads();
+		const int t_hi = min(TS, n_tok - t0);
 #pragma unroll
-		for (int j = 0; j < kAttnMaxAcc; ++j) {
-			const int o = tid + j * kAttnThreads;
+		for (int jj = 0; jj < kAttnMaxAcc; ++jj) {
+			const int o = tid + jj * kAttnThreads;
 			if (o < G * hd) {
 				const int g = o / hd, i = o % hd;
-				float v = acc[j] * al_s[g];
-				for (int t = 0; t < blk; ++t) v = fmaf(p_s[g * blk + t], kv_s[t * hd + i], v);
-				acc[j] = v;
+				float v = acc[jj] * al_s[g];
+				const float* pr = s_s + g * TS;
+				const T* vc = reinterpret_cast<const T*>(vbuf) + (size_t)t0 * hd + i;
+				for (int j = 0; j < t_hi; ++j) v = fmaf(pr[j], Store<T>::get(vc + (size_t)j * hd), v);
+				acc[jj] = v;
 			}
 		}
 		__syncthreads();
 	}
+	// pages issued but never waited for (abort) must land before the CTA exits
+	if (tid == 0)
+		for (int j = waited; j < np; ++j) {
+			const uint64_t t0 = global_timer_ns();
+			while (!mbar_try_wait(&bars[j], 0))
+				if (global_timer_ns() - t0 > kWaitLimitNs) break;
+		}
 
 	// partials: [b][h][split][hd + 2] = (acc..., m, l)
 	const int hd2 = hd + 2;
 #pragma unroll
-	for (int j = 0; j < kAttnMaxAcc; ++j) {
-		const int o = tid + j * kAttnThreads;
+	for (int jj = 0; jj < kAttnMaxAcc; ++jj) {
+		const int o = tid + jj * kAttnThreads;
 		if (o < G * hd) {
 			const int g = o / hd, i = o % hd;
-			const int h = kvh * G + g;
-			a.part[(((size_t)b * a.H + h) * a.n_splits + split) * hd2 + i] = acc[j];
+			a.part[(((size_t)b * a.H + kvh * G + g) * a.n_splits + split) * hd2 + i] = acc[jj];
 		}
 	}
 	if (tid < G) {
-		const int h = kvh * G + tid;
-		float* pr = a.part + (((size_t)b * a.H + h) * a.n_splits + split) * hd2;
+		float* pr = a.part + (((size_t)b * a.H + kvh * G + tid) * a.n_splits + split) * hd2;
 		pr[hd] = m_s[tid];
 		pr[hd + 1] = l_s[tid];
 	}
@@ -154,31 +215,55 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	if (!last_flag) return;
 	__threadfence();
 
+	// combine: weights exp(m_s - M) / L once per (head, split)
+	for (int g = warp; g < G; g += kAttnThreads / 32) {
+		const float* pr = a.part + (((size_t)b * a.H + kvh * G + g) * a.n_splits) * hd2;
+		float M = -INFINITY;
+		for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, __ldcg(pr + (size_t)s * hd2 + hd));
+		M = warp_max(M);
+		float L = 0.0f;
+		for (int s = lane; s < a.n_splits; s += 32) {
+			const float ms = __ldcg(pr + (size_t)s * hd2 + hd);
+			const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+			w_s[g * a.n_splits + s] = w;
+			L += w * __ldcg(pr + (size_t)s * hd2 + hd + 1);
+		}
+		L = warp_sum(L);
+		__syncwarp();
+		const float invL = L > 0.0f ? 1.0f / L : 0.0f;
+		for (int s = lane; s < a.n_splits; s += 32) w_s[g * a.n_splits + s] *= invL;
+	}
+	__syncthreads();
 	T* ob = reinterpret_cast<T*>(a.out) + (size_t)b * a.H * hd;
 	for (int o = tid; o < G * hd; o += kAttnThreads) {
 		const int g = o / hd, i = o % hd;
-		const int h = kvh * G + g;
-		const float* pr = a.part + (((size_t)b * a.H + h) * a.n_splits) * hd2;
-		float M = -INFINITY;
-		for (int s = 0; s < a.n_splits; ++s) M = fmaxf(M, __ldcg(pr + (size_t)s * hd2 + hd));
-		float L = 0.0f, v = 0.0f;
-		if (M != -INFINITY) {
-			for (int s = 0; s < a.n_splits; ++s) {
-				const float ms = __ldcg(pr + (size_t)s * hd2 + hd);
-				if (ms == -INFINITY) continue;
-				const float w = expf(ms - M);
-				L += w * __ldcg(pr + (size_t)s * hd2 + hd + 1);
-				v += w * __ldcg(pr + (size_t)s * hd2 + i);
-			}
+		const float* pr = a.part + (((size_t)b * a.H + kvh * G + g) * a.n_splits) * hd2 + i;
+		const float* w = w_s + g * a.n_splits;
+		float v0 = 0.0f, v1 = 0.0f;
+		int s = 0;
+		for (; s + 1 < a.n_splits; s += 2) {
+			v0 = fmaf(w[s], __ldcg(pr + (size_t)s * hd2), v0);
+			v1 = fmaf(w[s + 1], __ldcg(pr + (size_t)(s + 1) * hd2), v1);
 		}
-		Store<T>::put(ob + h * hd + i, L > 0.0f ? v / L : 0.0f);
+		if (s < a.n_splits) v0 = fmaf(w[s], __ldcg(pr + (size_t)s * hd2), v0);
+		Store<T>::put(ob + (size_t)(kvh * G + g) * hd + i, v0 + v1);
 	}
 	if (tid == 0) a.counters[b * a.KV + kvh] = 0u;
 }
 
-inline size_t attn_decode_smem_bytes(int G, int hd, int blk)
+// pages per split that fit the shared-memory budget
+inline int attn_decode_max_pages_split(int blk, int hd, size_t esz)
 {
-	return sizeof(float) * ((size_t)G * hd + (size_t)blk * hd + (size_t)G * blk + 3 * G);
+	const size_t page = 2 * (size_t)blk * hd * esz;
+	return (int)std::min<size_t>(kAttnMaxPagesSplit, std::max<size_t>(1, kAttnSmemBudget / page));
+}
+
+inline size_t attn_decode_smem_bytes(int G, int hd, int blk, size_t esz, int max_pages_split, int n_splits)
+{
+	const int TS = kAttnThreads / G;
+	return 2 * (size_t)max_pages_split * blk * hd * esz +
+	       sizeof(float) * ((size_t)G * hd + (size_t)G * TS + 3 * G + (size_t)G * n_splits + 2) + 8 +
+	       kAttnMaxPagesSplit * sizeof(uint64_t);
 }
 
 } // namespace inf

@@ -141,10 +141,10 @@ __device__ __forceinline__ void tc_epilogue_row(const TcArgs& a, int t, int n0, 
 		const int pos = a.tok_pos[t], slot = a.tok_slot[t];
 		int page = -1;
 		if (pos >= 0 && pos < a.max_seq) page = a.block_table[(size_t)slot * a.pages_per_seq + pos / a.kv_block];
-#pragma unroll 4
+#pragma unroll
 		for (int i = 0; i < 32; i += 2) {
 			const int row = n0 + i;
-			if (row + 1 >= a.N + 1) break;
+			if (row >= a.N) continue;
 			const int head = row / hd, dim = (row % hd) >> 1;
 			const float d0 = v[i], d1 = v[i + 1];
 			float o0 = d0, o1 = d1;

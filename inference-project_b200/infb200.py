@@ -76,9 +76,10 @@ EXPORTS = [
     "arena_host_pop", "arena_host_pop_at", "mem_arena_host_pos_get", "arena_dev_create", "arena_dev_destroy",
     "arena_dev_push", "arena_dev_pop", "arena_dev_pop_at", "arena_dev_pos_get", "cu_memcpy_htd",
     "cu_memcpy_htd_async", "cu_memcpy_dth", "cu_memset", "inf_fetch_input_embeddings", "inf_rmsnorm",
+    "inf_gemm_bf16",
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
-    "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids",
+    "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
 ]
 
 _lib = None
@@ -117,6 +118,7 @@ def lib():
         "cu_memset": (E, [vp, i32, u64]),
         "inf_fetch_input_embeddings": (E, [vp, u64, u32, u32, vp, vp, u32, vp]),
         "inf_rmsnorm": (E, [vp, vp, u32, u32, vp, f32, u32, vp]),
+        "inf_gemm_bf16": (E, [vp, vp, vp, u32, u32, u32, u32, vp]),
         "inf_config_preset": (E, [u32, C.POINTER(InfConfig)]),
         "inf_model_build": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model), C.POINTER(InfConfig), C.c_char_p, u64]),
         "inf_model_destroy": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model)]),
@@ -132,6 +134,7 @@ def lib():
         "inf_decode_bytes": (u64, [C.POINTER(InfConfig), u32]),
         "inf_profile_decode_step": (u32, [C.POINTER(Model), u32, u32, u32, C.POINTER(f32), u32]),
         "inf_synth_ids": (E, [u64, u64, u64, u32, u32, vp]),
+        "inf_debug_read": (E, [C.POINTER(Model), u32, u32, u32, u32, vp, u64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -256,6 +259,19 @@ class Engine:
                                _ptr(out) if out is not None else None, C.byref(st)), "inf_decode")
         return out, st
 
+    BUFFERS = {"resid": 0, "q": 1, "attn": 2, "h": 3, "logits": 4, "k": 5, "v": 6}
+
+    def debug_read(self, name: str, layer: int = 0, slot: int = 0, pos: int = 0) -> np.ndarray:
+        n = max(self.cfg.dim, self.cfg.ffn_dim, self.V, self.cfg.n_heads * self.cfg.head_dim)
+        out = np.empty(n, dtype=np.float32)
+        check(lib().inf_debug_read(C.byref(self.model), self.BUFFERS[name], layer, slot, pos, _ptr(out), n),
+              "inf_debug_read")
+        tp = max(1, self.cfg.tp_size)
+        sizes = {"resid": self.cfg.dim, "q": self.cfg.n_heads // tp * self.cfg.head_dim,
+                 "attn": self.cfg.n_heads // tp * self.cfg.head_dim, "h": self.cfg.ffn_dim // tp, "logits": self.V,
+                 "k": self.cfg.n_kv_heads // tp * self.cfg.head_dim, "v": self.cfg.n_kv_heads // tp * self.cfg.head_dim}
+        return out[:sizes[name]].copy()
+
     def reset(self, slot: int = 0):
         check(lib().inf_seq_reset(C.byref(self.model), slot), "inf_seq_reset")
 
@@ -292,6 +308,11 @@ def fetch_input_embeddings(d_ids: int, n: int, dim: int, vocab: int, d_table: in
                            stream: int = 0) -> None:
     check(lib().inf_fetch_input_embeddings(vp(d_ids), n, dim, vocab, vp(d_table), vp(d_out), dtype,
                                            vp(stream) if stream else None), "inf_fetch_input_embeddings")
+
+
+def gemm_bf16(d_x: int, d_w: int, d_y: int, T: int, N: int, K: int, out_f32: bool, stream: int = 0) -> None:
+    check(lib().inf_gemm_bf16(vp(d_x), vp(d_w), vp(d_y), T, N, K, int(out_f32), vp(stream) if stream else None),
+          "inf_gemm_bf16")
 
 
 def rmsnorm(d_x: int, d_y: int, rows: int, dim: int, d_gain: int, eps: float, dtype: int, stream: int = 0) -> None:

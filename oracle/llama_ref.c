@@ -173,6 +173,23 @@ void orc_embed_gather(const uint32_t* ids, uint64_t n, uint32_t dim, const void*
 		for (uint32_t i = 0; i < dim; ++i) out[t * dim + i] = wval(table, bf16, (uint64_t)ids[t] * dim + i);
 }
 
+/* Accumulation width between rounding points: double (default) or, for measuring how far two
+ * correct fp32 implementations drift apart, float (orc_set_accum_f32(1)). */
+static int g_accum_f32 = 0;
+void orc_set_accum_f32(int on) { g_accum_f32 = on; }
+
+static inline double dot_bf16_f(const uint16_t* w, const float* x, uint64_t n)
+{
+	float acc[16] = { 0 };
+	uint64_t i = 0;
+	for (; i + 16 <= n; i += 16)
+		for (int j = 0; j < 16; ++j) acc[j] += orc_bf16_to_f32(w[i + j]) * x[i + j];
+	float s = 0.f;
+	for (int j = 0; j < 16; ++j) s += acc[j];
+	for (; i < n; ++i) s += orc_bf16_to_f32(w[i]) * x[i];
+	return s;
+}
+
 static float rms_inv(const float* x, uint32_t dim, float eps)
 {
 	double acc[8] = { 0 };
@@ -223,7 +240,8 @@ void orc_matvec(const void* W, int bf16, uint64_t rows, uint64_t cols, const flo
 {
 #pragma omp parallel for schedule(static)
 	for (int64_t r = 0; r < (int64_t)rows; ++r) {
-		y[r] = (float)(bf16 ? dot_bf16_d((const uint16_t*)W + (uint64_t)r * cols, x, cols)
+		y[r] = (float)(bf16 ? (g_accum_f32 ? dot_bf16_f((const uint16_t*)W + (uint64_t)r * cols, x, cols)
+		                                   : dot_bf16_d((const uint16_t*)W + (uint64_t)r * cols, x, cols))
 		                    : dot_f32_d((const float*)W + (uint64_t)r * cols, x, cols));
 	}
 }
@@ -264,7 +282,7 @@ struct OrcModel {
 	/* scratch */
 	float *r, *xh, *q, *k, *v, *att, *o, *tmp, *gate, *up, *h, *scores, *logits;
 	/* layer-0 stage outputs of the last token, for stage tests */
-	float *dbg_q, *dbg_k, *dbg_v, *dbg_att;
+	float *dbg_q, *dbg_k, *dbg_v, *dbg_att, *dbg_h, *dbg_r;
 };
 
 static void* alloc_tensor(const OrcModel* m, uint64_t n)
@@ -371,6 +389,8 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 	m->dbg_k = (float*)calloc(KV * hd, 4);
 	m->dbg_v = (float*)calloc(KV * hd, 4);
 	m->dbg_att = (float*)calloc(H * hd, 4);
+	m->dbg_h = (float*)calloc(F, 4);
+	m->dbg_r = (float*)calloc(d, 4);
 	if (!m->embed || !m->lm_head || !m->kcache || !m->vcache || !m->scores || !m->logits) {
 		orc_model_destroy(m);
 		return NULL;
@@ -398,7 +418,7 @@ void orc_model_destroy(OrcModel* m)
 	free(m->rope_cos); free(m->rope_sin); free(m->kcache); free(m->vcache);
 	free(m->r); free(m->xh); free(m->q); free(m->k); free(m->v); free(m->att); free(m->o); free(m->tmp);
 	free(m->gate); free(m->up); free(m->h); free(m->scores); free(m->logits);
-	free(m->dbg_q); free(m->dbg_k); free(m->dbg_v); free(m->dbg_att);
+	free(m->dbg_q); free(m->dbg_k); free(m->dbg_v); free(m->dbg_att); free(m->dbg_h); free(m->dbg_r);
 	free(m);
 }
 
@@ -495,6 +515,10 @@ static void forward_token(OrcModel* m, uint32_t slot, uint32_t id, uint32_t pos,
 		}
 		orc_matvec(Ly->wd, bf, d, F, m->h, m->o);
 		for (uint32_t i = 0; i < d; ++i) m->r[i] += m->o[i];
+		if (l == 0) {
+			memcpy(m->dbg_h, m->h, sizeof(float) * F);
+			memcpy(m->dbg_r, m->r, sizeof(float) * d);
+		}
 	}
 	if (logits_out) {
 		orc_rmsnorm(m->r, 1, d, m->final_norm, bf, c->eps, m->xh);
@@ -557,6 +581,23 @@ int orc_fill_kv_synthetic(OrcModel* m, uint32_t slot, uint32_t ctx, uint64_t see
 				vb[i] = round_store(vb[i], 1);
 			}
 	}
+	return 0;
+}
+
+int orc_last_layer0_mlp(const OrcModel* m, float* h, float* resid)
+{
+	if (h) memcpy(h, m->dbg_h, sizeof(float) * m->cfg.ffn);
+	if (resid) memcpy(resid, m->dbg_r, sizeof(float) * m->cfg.dim);
+	return 0;
+}
+
+int orc_kv_read(const OrcModel* m, uint32_t slot, uint32_t layer, uint32_t pos, float* k, float* v)
+{
+	const OrcConfig* c = &m->cfg;
+	if (slot >= c->n_slots || layer >= c->n_layers || pos >= c->max_seq) return -1;
+	const uint64_t n = (uint64_t)c->n_kv_heads * c->head_dim;
+	if (k) memcpy(k, kv_at(m, m->kcache, slot, layer, pos), sizeof(float) * n);
+	if (v) memcpy(v, kv_at(m, m->vcache, slot, layer, pos), sizeof(float) * n);
 	return 0;
 }
 

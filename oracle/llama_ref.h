@@ -82,8 +82,14 @@ int orc_generate(OrcModel* m, uint32_t slot, const uint32_t* prompt, uint32_t n_
 int orc_fill_kv_synthetic(OrcModel* m, uint32_t slot, uint32_t ctx, uint64_t seed);
 /* per-stage debug output of the last forward (layer 0 only): q,k,v after RoPE, attention out */
 int orc_last_layer0(const OrcModel* m, float* q, float* k, float* v, float* attn);
+/* layer 0 SwiGLU product h and the residual after layer 0, of the last token */
+int orc_last_layer0_mlp(const OrcModel* m, float* h, float* resid);
+/* K and V the cache holds for (slot, layer, pos): [n_kv_heads * head_dim] each */
+int orc_kv_read(const OrcModel* m, uint32_t slot, uint32_t layer, uint32_t pos, float* k, float* v);
 
 uint32_t orc_argmax(const float* x, uint64_t n);
+/* 1: accumulate projections in float (to measure the drift between two fp32 orders) */
+void     orc_set_accum_f32(int on);
 
 #ifdef __cplusplus
 }

@@ -80,6 +80,11 @@ def lib():
         L.orc_fill_kv_synthetic.argtypes = [vp, u32, u32, u64]
         L.orc_last_layer0.restype = C.c_int
         L.orc_last_layer0.argtypes = [vp, vp, vp, vp, vp]
+        L.orc_last_layer0_mlp.restype = C.c_int
+        L.orc_last_layer0_mlp.argtypes = [vp, vp, vp]
+        L.orc_kv_read.restype = C.c_int
+        L.orc_kv_read.argtypes = [vp, u32, u32, u32, vp, vp]
+        L.orc_set_accum_f32.argtypes = [C.c_int]
         L.orc_argmax.restype = u32
         L.orc_argmax.argtypes = [vp, u64]
         _lib = L
@@ -212,6 +217,20 @@ class OracleModel:
         rc = lib().orc_fill_kv_synthetic(self.h, slot, ctx, seed)
         if rc:
             raise ValueError("orc_fill_kv_synthetic failed")
+
+    def layer0_mlp(self):
+        h = np.empty(self.c.ffn, np.float32)
+        r = np.empty(self.c.dim, np.float32)
+        lib().orc_last_layer0_mlp(self.h, _p(h), _p(r))
+        return h, r
+
+    def kv(self, layer: int, pos: int, slot: int = 0):
+        n = self.c.n_kv_heads * self.c.head_dim
+        k = np.empty(n, np.float32)
+        v = np.empty(n, np.float32)
+        if lib().orc_kv_read(self.h, slot, layer, pos, _p(k), _p(v)):
+            raise ValueError("orc_kv_read")
+        return k, v
 
     def layer0(self):
         c = self.c

@@ -1,0 +1,101 @@
+"""Per-stage GPU parity: one-layer models of every workload shape, compared stage by stage
+with the oracle (q, K/V cache, attention output, SwiGLU product, logits) on identical
+weights and ids.  One layer keeps fp32 accumulation-order noise from cascading, so each
+stored bf16 value must equal the oracle's or sit one bf16 ulp away (a rounding-boundary
+flip), and the fraction of exact matches is high."""
+import numpy as np
+import pytest
+
+import infb200 as I
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_bf16(x):
+    x = np.maximum(np.abs(x), 1e-30)
+    return np.exp2(np.floor(np.log2(x)) - 7)
+
+
+def assert_bf16_close(got, want, name, min_exact=0.97, max_ulps=1.0):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    d = np.abs(got - want) / ulp_bf16(np.maximum(np.abs(got), np.abs(want)))
+    d[(got == want)] = 0.0
+    exact = float(np.mean(got == want))
+    assert float(d.max()) <= max_ulps + 1e-9, f"{name}: {d.max():.2f} ulps (exact {exact:.4f})"
+    assert exact >= min_exact, f"{name}: only {exact:.4f} exactly equal"
+
+
+def assert_f32_close(got, want, name, rtol=1e-4):
+    scale = float(np.abs(want).max()) + 1e-12
+    err = float(np.abs(np.asarray(got) - np.asarray(want)).max())
+    assert err <= rtol * scale, f"{name}: max-abs {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("preset", [1, 2, 3])
+def test_decode_path_stages(cuda, preset):
+    cfg = I.preset(preset, n_layers=1, max_seq=64)
+    n = 12
+    prompt = I.synth_ids(7, n, cfg.vocab_size)
+    with I.Engine(cfg) as eng:
+        for t in range(n):                          # every token through the decode kernels
+            lg, am = eng.forward(prompt[t:t + 1], t)
+        got = {k: eng.debug_read(k) for k in ("q", "attn", "h", "resid", "logits")}
+        kv = [(eng.debug_read("k", 0, 0, t), eng.debug_read("v", 0, 0, t)) for t in range(n)]
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0)
+    o_lg, o_am = orc.forward(prompt, 0)
+    q, _, _, att = orc.layer0()
+    h, resid = orc.layer0_mlp()
+    if cfg.dtype == I.BF16:
+        assert_bf16_close(got["q"], q, "q")
+        for t in range(n):
+            k, v = orc.kv(0, t)
+            assert_bf16_close(kv[t][0], k, f"k[{t}]")
+            assert_bf16_close(kv[t][1], v, f"v[{t}]")
+        assert_bf16_close(got["attn"], att, "attention", min_exact=0.95)
+        assert_bf16_close(got["h"], h, "swiglu", min_exact=0.95)
+        assert_f32_close(got["resid"], resid, "residual", rtol=2e-2)
+        assert float(np.abs(got["logits"] - o_lg).max()) <= 2e-2
+    else:
+        assert_f32_close(got["q"], q, "q")
+        assert_f32_close(got["attn"], att, "attention")
+        assert_f32_close(got["h"], h, "swiglu")
+        assert_f32_close(got["resid"], resid, "residual")
+        assert_f32_close(got["logits"], o_lg, "logits")
+    np.testing.assert_array_equal(lg, got["logits"])
+    assert am == o_am or np.sort(o_lg)[-1] - np.sort(o_lg)[-2] < 2e-2
+
+
+@pytest.mark.parametrize("preset,n", [(2, 200), (3, 300)])
+def test_tensor_core_prefill_stages(cuda, preset, n):
+    """One multi-token pass (tcgen05 GEMMs, prefill attention): every position's K and V in
+    the paged cache, and the last token's logits."""
+    cfg = I.preset(preset, n_layers=1, max_seq=512)
+    prompt = I.synth_ids(8, n, cfg.vocab_size)
+    with I.Engine(cfg) as eng:
+        lg, _ = eng.forward(prompt, 0)
+        kv = [(eng.debug_read("k", 0, 0, t), eng.debug_read("v", 0, 0, t)) for t in range(n)]
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0)
+    o_lg, _ = orc.forward(prompt, 0)
+    for t in range(n):
+        k, v = orc.kv(0, t)
+        assert_bf16_close(kv[t][0], k, f"k[{t}]")
+        assert_bf16_close(kv[t][1], v, f"v[{t}]")
+    assert float(np.abs(lg - o_lg).max()) <= 2e-2
+
+
+def test_rope_positions_far_into_the_cache(cuda):
+    """Positions near max_seq use the far end of the RoPE table and the last KV pages."""
+    cfg = I.preset(2, n_layers=1, max_seq=1024)
+    start = 1000
+    ids = I.synth_ids(9, 24, cfg.vocab_size)
+    with I.Engine(cfg) as eng:
+        eng.forward(I.synth_ids(10, start, cfg.vocab_size), 0)  # fill the cache with one multi-token pass
+        eng.forward(ids, start)
+        got = [eng.debug_read("k", 0, 0, start + t) for t in range(24)]
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0)
+    orc.forward(I.synth_ids(10, start, cfg.vocab_size), 0)
+    orc.forward(ids, start)
+    for t in range(24):
+        assert_bf16_close(got[t], orc.kv(0, start + t)[0], f"k[{start + t}]")
