@@ -162,6 +162,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 	    "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
 	    : "memory");
 }
+// Bulk prefetch of a global range into L2 (no shared memory, no completion tracking).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes)
+{
+	asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first()
 {
 	uint64_t p;

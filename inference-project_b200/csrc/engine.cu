@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <utility>
 #include <vector>
 
@@ -150,11 +151,18 @@ cudaError_t launch(InfEngine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, 
 	return cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...);
 }
 
+// Raises a kernel's dynamic shared-memory ceiling to `bytes` if it is below it (models of
+// different shapes in one process need different sizes for the same kernel).
 template <typename K>
 cudaError_t set_smem(K kern, size_t bytes)
 {
+	static std::unordered_map<const void*, size_t> set_to;
 	std::lock_guard<std::mutex> lk(g_attr_mutex);
-	return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+	size_t& cur = set_to[reinterpret_cast<const void*>(kern)];
+	if (bytes <= cur) return cudaSuccess;
+	const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+	if (e == cudaSuccess) cur = bytes;
+	return e;
 }
 
 // --------------------------------------------------------------------------- GEMV
@@ -169,11 +177,7 @@ Error_t launch_gemv_u(InfEngine* e, GemvArgs a)
 	const int unit_rows = EpiTraits<EPI>::kPaired ? 2 : 1;
 	const int grid = std::max(1, std::min(e->sm_count, a.N / unit_rows));
 	const size_t smem = gemv_smem_bytes();
-	static bool attr_done = false;
-	if (!attr_done) {
-		INF_CUDA_TRY(set_smem(k_gemv<T, UPL, EPI>, smem));
-		attr_done = true;
-	}
+	INF_CUDA_TRY(set_smem(k_gemv<T, UPL, EPI>, smem));
 	INF_CUDA_TRY(launch(e, k_gemv<T, UPL, EPI>, dim3(grid), dim3(kGemvThreads), smem, a));
 	return Success;
 }
@@ -284,11 +288,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.err = e->err;
 			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
 			                                           e->attn_max_pages_split, e->attn_splits);
-			static bool attn_attr = false;
-			if (!attn_attr) {
-				INF_CUDA_TRY(set_smem(k_attn_decode<T>, smem));
-				attn_attr = true;
-			}
+			INF_CUDA_TRY(set_smem(k_attn_decode<T>, smem));
 			INF_TRY(prof_begin(e));
 			INF_CUDA_TRY(launch(e, k_attn_decode<T>, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
 			INF_TRY(prof_end(e, InfKAttn));
@@ -379,11 +379,7 @@ Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
 	INF_TRY(tensor_map_2d(&tx, X, (u64)a.T, (u64)a.K, kTcBM));
 	INF_TRY(tensor_map_2d(&tw, W, (u64)a.N, (u64)a.K, kTcBN));
 	const size_t smem = gemm_tc_smem_bytes();
-	static bool attr_done = false;
-	if (!attr_done) {
-		INF_CUDA_TRY(set_smem(k_gemm_tc, smem));
-		attr_done = true;
-	}
+	INF_CUDA_TRY(set_smem(k_gemm_tc, smem));
 	a.err = e->err;
 	const dim3 grid((a.N + kTcBN - 1) / kTcBN, (a.T + kTcBM - 1) / kTcBM);
 	INF_CUDA_TRY(launch(e, k_gemm_tc, grid, dim3(kTcThreads), smem, tx, tw, a));
@@ -411,11 +407,7 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 	INF_CUDA_TRY(launch(e, k_embed<bf16, float>, dim3((d + 255) / 256, T), dim3(256), 0, (const uint32_t*)e->d_ids, T, d,
 	                    c.vocab_size, (const bf16*)e->embed, e->resid_p, e->err));
 	const size_t pf_smem = attn_prefill_smem_bytes(G, hd, (int)c.kv_block);
-	static bool pf_attr = false;
-	if (!pf_attr) {
-		INF_CUDA_TRY(set_smem(k_attn_prefill<bf16>, pf_smem));
-		pf_attr = true;
-	}
+	INF_CUDA_TRY(set_smem(k_attn_prefill<bf16>, pf_smem));
 	for (u32 l = 0; l < c.n_layers; ++l) {
 		const LayerW& L = e->layers[l];
 		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,

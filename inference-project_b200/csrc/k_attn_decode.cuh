@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 		mbar_fence_init();
 	}
 	__syncthreads();
+	// thread j issues page j's two copies (page ids are read in parallel, not one by one)
 	auto issue = [&](int j) {
 		const int p = p_begin + j;
 		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p];
@@ -95,14 +96,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 		bulk_g2s(kbuf + j * blk_bytes, reinterpret_cast<const T*>(a.kpool) + off, (uint32_t)blk_bytes, &bars[j], pol);
 		bulk_g2s(vbuf + j * blk_bytes, reinterpret_cast<const T*>(a.vpool) + off, (uint32_t)blk_bytes, &bars[j], pol);
 	};
-	if (tid == 0)
-		for (int j = 0; j < np; ++j)
-			if (p_begin + j < cur_page) issue(j);
+	if (tid < np && p_begin + tid < cur_page) issue(tid);
 	pdl_wait();
 	pdl_trigger();
-	if (tid == 0)
-		for (int j = 0; j < np; ++j)
-			if (p_begin + j >= cur_page) issue(j);
+	if (tid < np && p_begin + tid >= cur_page) issue(tid);
 
 	const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.H * hd + (size_t)kvh * G * hd;
 	for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = Store<T>::get(qb + i);
@@ -182,7 +179,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 		}
 		__syncthreads();
 	}
-	// pages issued but never waited for (abort) must land before the CTA exits
+	// pages issued but never waited for (abort) must land before the CTA exits or the page
+	// buffers are reused for the combine
 	if (tid == 0)
 		for (int j = waited; j < np; ++j) {
 			const uint64_t t0 = global_timer_ns();
@@ -215,18 +213,45 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	if (!last_flag) return;
 	__threadfence();
 
-	// combine: weights exp(m_s - M) / L once per (head, split)
+	// combine.  The G heads' partials of this (token, KV head) are one contiguous block of
+	// G * n_splits * (hd + 2) floats; copy it into the (now idle) page buffers with
+	// independent 16-byte loads, eight in flight per thread, then reduce from shared memory.
+	float* pc = reinterpret_cast<float*>(sm_raw);
+	const size_t n_part = (size_t)G * a.n_splits * hd2;
+	if (n_part * sizeof(float) <= 2 * (size_t)a.max_pages_split * blk_bytes && (n_part & 3) == 0) {
+		const float4* src = reinterpret_cast<const float4*>(a.part + (((size_t)b * a.H + kvh * G) * a.n_splits) * hd2);
+		float4* dst = reinterpret_cast<float4*>(pc);
+		const int n4 = (int)(n_part >> 2);
+		for (int base = 0; base < n4; base += 8 * kAttnThreads) {
+			float4 r[8];
+#pragma unroll
+			for (int u = 0; u < 8; ++u) {
+				const int idx = base + u * kAttnThreads + tid;
+				if (idx < n4) r[u] = __ldcg(src + idx);
+			}
+#pragma unroll
+			for (int u = 0; u < 8; ++u) {
+				const int idx = base + u * kAttnThreads + tid;
+				if (idx < n4) dst[idx] = r[u];
+			}
+		}
+	} else {
+		const float* src = a.part + (((size_t)b * a.H + kvh * G) * a.n_splits) * hd2;
+		for (size_t idx = tid; idx < n_part; idx += kAttnThreads) pc[idx] = __ldcg(src + idx);
+	}
+	__syncthreads();
+	// weights exp(m_s - M) / L once per (head, split)
 	for (int g = warp; g < G; g += kAttnThreads / 32) {
-		const float* pr = a.part + (((size_t)b * a.H + kvh * G + g) * a.n_splits) * hd2;
+		const float* pr = pc + (size_t)g * a.n_splits * hd2;
 		float M = -INFINITY;
-		for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, __ldcg(pr + (size_t)s * hd2 + hd));
+		for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, pr[(size_t)s * hd2 + hd]);
 		M = warp_max(M);
 		float L = 0.0f;
 		for (int s = lane; s < a.n_splits; s += 32) {
-			const float ms = __ldcg(pr + (size_t)s * hd2 + hd);
+			const float ms = pr[(size_t)s * hd2 + hd];
 			const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
 			w_s[g * a.n_splits + s] = w;
-			L += w * __ldcg(pr + (size_t)s * hd2 + hd + 1);
+			L += w * pr[(size_t)s * hd2 + hd + 1];
 		}
 		L = warp_sum(L);
 		__syncwarp();
@@ -237,15 +262,15 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	T* ob = reinterpret_cast<T*>(a.out) + (size_t)b * a.H * hd;
 	for (int o = tid; o < G * hd; o += kAttnThreads) {
 		const int g = o / hd, i = o % hd;
-		const float* pr = a.part + (((size_t)b * a.H + kvh * G + g) * a.n_splits) * hd2 + i;
+		const float* pr = pc + (size_t)g * a.n_splits * hd2 + i;
 		const float* w = w_s + g * a.n_splits;
 		float v0 = 0.0f, v1 = 0.0f;
 		int s = 0;
 		for (; s + 1 < a.n_splits; s += 2) {
-			v0 = fmaf(w[s], __ldcg(pr + (size_t)s * hd2), v0);
-			v1 = fmaf(w[s + 1], __ldcg(pr + (size_t)(s + 1) * hd2), v1);
+			v0 = fmaf(w[s], pr[(size_t)s * hd2], v0);
+			v1 = fmaf(w[s + 1], pr[(size_t)(s + 1) * hd2], v1);
 		}
-		if (s < a.n_splits) v0 = fmaf(w[s], __ldcg(pr + (size_t)s * hd2), v0);
+		if (s < a.n_splits) v0 = fmaf(w[s], pr[(size_t)s * hd2], v0);
 		Store<T>::put(ob + (size_t)(kvh * G + g) * hd + i, v0 + v1);
 	}
 	if (tid == 0) a.counters[b * a.KV + kvh] = 0u;

@@ -24,6 +24,7 @@ constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
 constexpr int kGemvThreads = kGemvConsumers + 32;
 constexpr int kGemvRingBytes = 96 * 1024;
 constexpr int kGemvMaxStages = 8;
+constexpr int kGemvPrefetch = 4; // chunks prefetched into L2 beyond the ring
 
 enum EpiKind : int { kEpiStore = 0, kEpiResid = 1, kEpiQkv = 2, kEpiSwiglu = 3, kEpiLogits = 4 };
 
@@ -137,14 +138,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 		if (lane == 0) {
 			const uint64_t pol = policy_evict_first();
 			const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.W) + (size_t)r0 * row_bytes;
+			auto chunk_bytes = [&](int i) { return (uint32_t)(min(RPC, n_rows - i * RPC) * row_bytes); };
+			// L2 prefetch runs kGemvPrefetch chunks ahead of the shared-memory ring, so each SM
+			// has more bytes in flight than its ring holds
+			const int pf_end0 = min(n_chunks, S + kGemvPrefetch);
+			for (int i = S; i < pf_end0; ++i) bulk_prefetch_l2(wbase + (size_t)i * RPC * row_bytes, chunk_bytes(i));
 			int issued = 0;
 			for (int i = 0; i < n_chunks; ++i) {
 				const int s = i % S;
 				if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, abort_flag, a.err)) break;
-				const int rows = min(RPC, n_rows - i * RPC);
-				const uint32_t bytes = (uint32_t)(rows * row_bytes);
+				const uint32_t bytes = chunk_bytes(i);
 				mbar_arrive_expect_tx(&full[s], bytes);
 				bulk_g2s(ring + (size_t)s * a.stage_bytes, wbase + (size_t)i * RPC * row_bytes, bytes, &full[s], pol);
+				const int pf = i + S + kGemvPrefetch;
+				if (pf < n_chunks) bulk_prefetch_l2(wbase + (size_t)pf * RPC * row_bytes, chunk_bytes(pf));
 				++issued;
 			}
 			// never leave the CTA with bulk copies in flight: wait for the last stages to land
