@@ -166,6 +166,21 @@ Error_t inf_rmsnorm(const void* d_x, void* d_y, u32 rows, u32 dim, const void* d
  * (src/model.cuh:44-50 declares wq/wk/wv/wo only). */
 Error_t inf_gemm_bf16(const void* d_x, const void* d_w, void* d_y, u32 T, u32 N, u32 K, u32 out_f32, void* stream);
 
+/* Decode attention over a paged KV cache for n_tokens query tokens (one per sequence), the
+ * kernel the decode step runs (no reference counterpart: src/model.cuh:44-50 stops at the
+ * projection weights).  q, out: [n_tokens][n_heads*head_dim]; kpool, vpool:
+ * [n_pages][n_kv_heads][kv_block][head_dim]; block_table: [slots][pages_per_seq] i32;
+ * tok_slot, tok_pos: [n_tokens] i32 -- token i attends positions 0..tok_pos[i] of its slot.
+ * dtype: InfDtype of q, K/V and out.  d_scratch: device memory of at least
+ * inf_attn_decode_scratch_bytes(...) bytes (split partials, tickets, error word), 16-byte
+ * aligned; its contents on entry do not matter.  Synchronous. */
+u64     inf_attn_decode_scratch_bytes(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
+                                      u32 pages_per_seq, u32 dtype);
+Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
+                        u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos, u32 n_tokens,
+                        u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype, void* d_out,
+                        void* d_scratch, u64 scratch_bytes, void* stream);
+
 /* ---- model ------------------------------------------------------------------------- */
 /* Built-in shapes: 1 tiny fp32 (d288), 2 TinyLlama-1.1B, 3 Llama-3-8B, 4 Llama-3-8B batch 64,
  * 5 Llama-3-8B 32k prefill. */
@@ -193,6 +208,16 @@ Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u
  * (host or device, may be NULL) receives the n_steps generated ids. */
 Error_t inf_decode(Model* model, u32 seq_slot, u32 start_pos, u32 first_id, u32 n_steps, u32* out_ids,
                    InfStats* stats);
+/* ---- tensor parallelism (one process and one model per GPU, tp_rank/tp_size in the config)
+ * Column-parallel QKV (KV heads per rank) and gate/up, row-parallel O and down, vocabulary-
+ * parallel LM head.  The two all-reduces of each layer and the cross-shard argmax run inside
+ * the projection kernels over NVLink peer memory.  Setup: every rank calls inf_tp_export,
+ * the caller gathers the tp_size handles (any host transport, e.g. torch.distributed), and
+ * every rank calls inf_tp_connect with all handles in rank order.  All ranks must then run
+ * the same sequence of calls.  With tp_size > 1, logits_out receives this rank's vocabulary
+ * shard (vocab_size / tp_size floats) and argmax_out the global greedy id. */
+Error_t inf_tp_export(Model* model, void* handle_out, u64 handle_bytes); /* 64-byte CUDA IPC handle */
+Error_t inf_tp_connect(Model* model, const void* handles, u32 n_ranks);
 /* Release the KV pages of a sequence slot. */
 Error_t inf_seq_reset(Model* model, u32 seq_slot);
 

@@ -101,13 +101,18 @@ struct InfEngine {
 	u64 launches = 0;
 	bool profiling = false;
 	bool dry = false; // walk the launch sequence without launching (sets kernel attributes)
+	// tensor parallelism over peer memory (tp_size > 1)
+	TpComm tpc;                        // size 1 until inf_tp_connect
+	u64 comm_off = 0;                  // offset of this rank's comm region in its arena
+	std::vector<void*> peer_bases;     // opened IPC mappings (nullptr for self)
+	unsigned pf_round = 0;             // multi-token all-reduce rounds issued so far
 	cudaEvent_t prof_ev[2] = {nullptr, nullptr};
 	float prof_ms[InfKNumKinds] = {};
 };
 
 namespace {
 
-enum CtlWord { kCtlId = 0, kCtlPos = 1, kCtlSlot = 2, kCtlStep = 3, kCtlErr = 4, kCtlWords = 8 };
+enum CtlWord { kCtlId = 0, kCtlPos = 1, kCtlSlot = 2, kCtlStep = 3, kCtlErr = 4, kCtlEpoch = 5, kCtlWords = 8 };
 
 std::mutex g_attr_mutex;
 
@@ -205,6 +210,7 @@ GemvArgs gemv_base(InfEngine* e, const void* W, int N, int K)
 	a.K = K;
 	a.eps = e->cfg.norm_eps;
 	a.err = e->err;
+	a.tp = e->tpc;
 	return a;
 }
 
@@ -296,6 +302,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 		// O-proj + residual
 		{
 			GemvArgs a = gemv_base(e, L.wo, d, e->Hl * hd);
+			a.tp_round_index = 2 * (int)l;
 			a.xin = e->attn;
 			a.resid = e->resid;
 			INF_TRY(prof_begin(e));
@@ -315,6 +322,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 		// down + residual
 		{
 			GemvArgs a = gemv_base(e, L.wd, d, e->Fl);
+			a.tp_round_index = 2 * (int)l + 1;
 			a.xin = e->h;
 			a.resid = e->resid;
 			INF_TRY(prof_begin(e));
@@ -325,6 +333,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 	// final norm + LM head + greedy argmax; advances id, position and step
 	{
 		GemvArgs a = gemv_base(e, e->lm_head, e->Vl, d);
+		a.row_base = (int)e->cfg.tp_rank * e->Vl;
 		a.resid_in = e->resid;
 		a.gain = e->final_norm;
 		a.logits = e->logits;
@@ -386,6 +395,10 @@ Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
 	return Success;
 }
 
+// Row-parallel projection + residual: local GEMM into the fp32 partial buffer, then the
+// two-shot peer-memory all-reduce adds the sum over ranks into the residual.
+Error_t launch_gemm_resid_tp(InfEngine* e, const void* X, const void* W, TcArgs a);
+
 TcArgs tc_base(InfEngine* e, int T, int N, int K, int epi)
 {
 	TcArgs a;
@@ -396,6 +409,20 @@ TcArgs tc_base(InfEngine* e, int T, int N, int K, int epi)
 	a.epi = epi;
 	a.err = e->err;
 	return a;
+}
+
+Error_t launch_gemm_resid_tp(InfEngine* e, const void* X, const void* W, TcArgs a)
+{
+	if (e->tpc.size <= 1) return launch_gemm_tc(e, X, W, a);
+	float* resid = a.resid;
+	a.epi = kTcStoreF32;
+	a.out = e->tpc.part[e->tpc.rank];
+	INF_TRY(launch_gemm_tc(e, X, W, a));
+	const int n = a.T * a.N;
+	const int grid = std::min(kTpMaxCtas, std::max(1, std::min(e->sm_count, (n + 4095) / 4096)));
+	const unsigned round = ++e->pf_round;
+	INF_CUDA_TRY(launch(e, k_tp_allreduce_add, dim3(grid), dim3(256), 0, e->tpc, n, round, resid, e->err));
+	return Success;
 }
 
 // One chunk of T tokens of one sequence (positions and slots already in tok_pos/tok_slot),
@@ -455,7 +482,7 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 		{
 			TcArgs a = tc_base(e, T, d, e->Hl * hd, kTcResid);
 			a.resid = e->resid_p;
-			INF_TRY(launch_gemm_tc(e, e->attn_p, L.wo, a));
+			INF_TRY(launch_gemm_resid_tp(e, e->attn_p, L.wo, a));
 		}
 		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
 		                    (bf16*)e->xhat_p, T, d, (const bf16*)L.ffn_norm, c.norm_eps));
@@ -467,7 +494,7 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 		{
 			TcArgs a = tc_base(e, T, d, e->Fl, kTcResid);
 			a.resid = e->resid_p;
-			INF_TRY(launch_gemm_tc(e, e->h_p, L.wd, a));
+			INF_TRY(launch_gemm_resid_tp(e, e->h_p, L.wd, a));
 		}
 	}
 	return Success;
@@ -478,6 +505,7 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 Error_t enqueue_lm_head_row(InfEngine* e, const float* resid_row)
 {
 	GemvArgs a = gemv_base(e, e->lm_head, e->Vl, (int)e->cfg.dim);
+	a.row_base = (int)e->cfg.tp_rank * e->Vl;
 	a.resid_in = resid_row;
 	a.gain = e->final_norm;
 	a.logits = e->logits;
@@ -610,6 +638,7 @@ Error_t validate(const InfConfig& c)
 	if ((c.n_heads / c.n_kv_heads) * c.head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kAttnThreads * kAttnMaxAcc);
 	if (c.dim > 16384 || c.ffn_dim / tp > 16384) return fail(ErrorUnsupported, "dim/ffn above 16384");
+	if (tp > (u32)kTpMax) return fail(ErrorUnsupported, "tp_size above %d", kTpMax);
 	if (!(c.norm_eps >= 0.0f) || !(c.rope_theta > 0.0f)) return fail(ErrorBadConfig, "eps/theta");
 	return Success;
 }
@@ -770,7 +799,10 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	const u64 w_total = (2ull * c.vocab_size * d) * es + d * es + L * w_layer; // embed is full, LM head is a shard
 	const u64 page_elems = (u64)e->KVl * c.kv_block * hd;
 	const u64 kv_total = 2ull * L * e->n_pages * page_elems * es;
-	const u64 act = d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + (u64)e->Hl * e->attn_splits * (hd + 2) * 4 +
+	const u64 comm = c.tp_size > 1 ? (2ull * c.tp_size * d * 4 + 2ull * c.tp_size * kTpMaxCtas * 4 + 64ull * c.tp_size +
+	                                   (e->chunk > 0 ? 2ull * (u64)(c.prefill_chunk ? c.prefill_chunk : 4096) * d * 4 : 0) + 8 * 256)
+	                                : 0;
+	const u64 act = comm + d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + (u64)e->Hl * e->attn_splits * (hd + 2) * 4 +
 	                (u64)e->chunk * (d * 4 + d * es + 2ull * e->Hl * hd * es + (u64)e->Fl * es + 8) + 16 * 256;
 	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024;
 	const u64 total = w_total + kv_total + act + (u64)c.max_seq * hd * 4 + (u64)c.max_batch * e->pages_per_seq * 4 +
@@ -822,12 +854,37 @@ Error_t engine_build(InfEngine* e, u64 seed)
 		P.push(&e->tok_pos, (u64)e->chunk * 4);
 		P.push(&e->tok_slot, (u64)e->chunk * 4);
 	}
+	if (c.tp_size > 1) {
+		// peer-visible region, same offsets on every rank (identical shapes, deterministic layout)
+		e->comm_off = arena_dev_pos_get(&e->ctx->dev_arena);
+		TpComm& t = e->tpc;
+		memset(&t, 0, sizeof t);
+		t.rank = (int)c.tp_rank;
+		t.size = 1; // becomes tp_size in inf_tp_connect
+		t.dim = (int)d;
+		const int r = (int)c.tp_rank, N = (int)c.tp_size;
+		P.push(&t.inbox[r], 2ull * N * d * 4);
+		P.push(&t.flags[r], (u64)N * kTpMaxCtas * 4);
+		P.push(&t.am_inbox[r], 2ull * N * 8);
+		P.push(&t.am_flags[r], (u64)N * 4);
+		P.push(&t.ready[r], (u64)N * 4);
+		P.push(&t.done[r], (u64)N * kTpMaxCtas * 4);
+		if (e->chunk > 0) {
+			P.push(&t.part[r], (u64)e->chunk * d * 4);
+			P.push(&t.red[r], (u64)e->chunk * d * 4);
+		}
+	}
 	if (P.err != Success) return P.err;
 	e->cur_id = reinterpret_cast<uint32_t*>(e->ctl + kCtlId);
 	e->pos = e->ctl + kCtlPos;
 	e->slot = e->ctl + kCtlSlot;
 	e->step = reinterpret_cast<uint32_t*>(e->ctl + kCtlStep);
 	e->err = e->ctl + kCtlErr;
+	e->tpc.epoch = reinterpret_cast<const uint32_t*>(e->ctl + kCtlEpoch);
+	if (c.tp_size <= 1) {
+		e->tpc.size = 1;
+		e->tpc.rank = 0;
+	}
 
 	INF_CUDA_TRY(cudaMemsetAsync(e->ctx->dev_arena._d_ptr + w_begin + e->weight_bytes, 0,
 	                             arena_dev_pos_get(&e->ctx->dev_arena) - w_begin - e->weight_bytes, e->stream));
@@ -857,6 +914,8 @@ void engine_free(InfEngine* e)
 	if (!e) return;
 	if (e->stream) cudaStreamSynchronize(e->stream);
 	if (e->decode_exec) cudaGraphExecDestroy(e->decode_exec);
+	for (void* p : e->peer_bases)
+		if (p) cudaIpcCloseMemHandle(p);
 	if (e->h_pin) cudaFreeHost(e->h_pin);
 	if (e->h_ctl) cudaFreeHost(e->h_ctl);
 	if (e->h_tok) cudaFreeHost(e->h_tok);
@@ -1142,6 +1201,64 @@ Error_t inf_synth_ids(u64 seed, u64 stream, u64 n, u32 lo, u32 hi_inclusive, u32
 	return Success;
 }
 
+Error_t inf_tp_export(Model* model, void* handle_out, u64 handle_bytes)
+{
+	if (!model || !model->engine || !handle_out) return fail(ErrorInvalidValue, "inf_tp_export: bad arguments");
+	if (handle_bytes < sizeof(cudaIpcMemHandle_t)) return fail(ErrorInvalidValue, "inf_tp_export: need %zu bytes", sizeof(cudaIpcMemHandle_t));
+	InfEngine* e = model->engine;
+	if (e->cfg.tp_size <= 1) return fail(ErrorInvalidValue, "inf_tp_export: tp_size is 1");
+	cudaIpcMemHandle_t h;
+	INF_CUDA_TRY(cudaIpcGetMemHandle(&h, e->ctx->dev_arena._d_ptr));
+	memcpy(handle_out, &h, sizeof h);
+	return Success;
+}
+
+Error_t inf_tp_connect(Model* model, const void* handles, u32 n_ranks)
+{
+	if (!model || !model->engine || !handles) return fail(ErrorInvalidValue, "inf_tp_connect: bad arguments");
+	InfEngine* e = model->engine;
+	const InfConfig& c = e->cfg;
+	if (c.tp_size <= 1 || n_ranks != c.tp_size) return fail(ErrorInvalidValue, "inf_tp_connect: %u handles for tp_size %u", n_ranks, c.tp_size);
+	if (e->tpc.size > 1) return fail(ErrorAlreadyInitialized, "inf_tp_connect: already connected");
+	TpComm t = e->tpc;
+	const int me = (int)c.tp_rank;
+	auto rebase = [&](auto* local, uint8_t* base) {
+		using P = decltype(local);
+		return (P)(base + ((uint8_t*)local - e->ctx->dev_arena._d_ptr));
+	};
+	e->peer_bases.assign(c.tp_size, nullptr);
+	for (u32 k = 0; k < c.tp_size; ++k) {
+		uint8_t* base = e->ctx->dev_arena._d_ptr;
+		if ((int)k != me) {
+			cudaIpcMemHandle_t h;
+			memcpy(&h, (const uint8_t*)handles + (size_t)k * sizeof h, sizeof h);
+			void* p = nullptr;
+			INF_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+			e->peer_bases[k] = p;
+			base = (uint8_t*)p;
+		}
+		t.inbox[k] = rebase(e->tpc.inbox[me], base);
+		t.flags[k] = rebase(e->tpc.flags[me], base);
+		t.am_inbox[k] = rebase(e->tpc.am_inbox[me], base);
+		t.am_flags[k] = rebase(e->tpc.am_flags[me], base);
+		t.ready[k] = rebase(e->tpc.ready[me], base);
+		t.done[k] = rebase(e->tpc.done[me], base);
+		if (e->chunk > 0) {
+			t.part[k] = rebase(e->tpc.part[me], base);
+			t.red[k] = rebase(e->tpc.red[me], base);
+		}
+	}
+	t.size = (int)c.tp_size;
+	e->tpc = t;
+	// the decode graph bakes the comm descriptor into its kernel arguments: rebuild it
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	if (e->decode_exec) {
+		cudaGraphExecDestroy(e->decode_exec);
+		e->decode_exec = nullptr;
+	}
+	return build_decode_graph(e);
+}
+
 Error_t inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 pos, f32* out, u64 n_out)
 {
 	if (!model || !model->engine || !out) return fail(ErrorInvalidValue, "inf_debug_read: bad arguments");
@@ -1294,6 +1411,106 @@ Error_t inf_gemm_bf16(const void* d_x, const void* d_w, void* d_y, u32 T, u32 N,
 	INF_CUDA_TRY(cudaStreamSynchronize(tmp.stream));
 	tmp.stream = nullptr;
 	if (r != Success) return r;
+	return map_dev_err(h_err);
+}
+
+// ---- stand-alone decode attention -------------------------------------------------------
+
+namespace {
+struct AttnPlan {
+	int splits, max_pages_split;
+	size_t part_bytes, counter_bytes, smem;
+};
+
+Error_t attn_plan(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 pages_per_seq, u32 dtype,
+                  AttnPlan* p)
+{
+	if (n_tokens == 0 || n_heads == 0 || n_kv_heads == 0 || head_dim == 0 || head_dim % 2 || kv_block == 0 ||
+	    pages_per_seq == 0 || n_heads % n_kv_heads || (dtype != InfBF16 && dtype != InfF32) || n_tokens > 65535)
+		return fail(ErrorInvalidValue, "attention: bad shape");
+	const u32 G = n_heads / n_kv_heads;
+	if (kAttnThreads % G || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
+		return fail(ErrorUnsupported, "attention: GQA group %u x head_dim %u", G, head_dim);
+	const size_t esz = dtype == InfBF16 ? 2 : 4;
+	if ((kv_block * head_dim * esz) % 16) return fail(ErrorUnsupported, "attention: page block not a multiple of 16 bytes");
+	int sms = 148, dev = 0;
+	if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+	p->max_pages_split = attn_decode_max_pages_split((int)kv_block, (int)head_dim, esz);
+	const int per_tok = std::max(1, (sms + (int)(n_kv_heads * n_tokens) - 1) / (int)(n_kv_heads * n_tokens));
+	p->splits = std::max(per_tok, ((int)pages_per_seq + p->max_pages_split - 1) / p->max_pages_split);
+	p->splits = std::max(1, std::min(p->splits, (int)pages_per_seq));
+	p->part_bytes = (size_t)n_tokens * n_heads * p->splits * (head_dim + 2) * sizeof(float);
+	p->counter_bytes = (size_t)n_tokens * n_kv_heads * sizeof(unsigned) + 16; // + error word
+	p->smem = attn_decode_smem_bytes((int)G, (int)head_dim, (int)kv_block, esz, p->max_pages_split, p->splits);
+	return Success;
+}
+
+Error_t attn_launch(const AttnPlan& P, AttnDecodeArgs a, u32 n_tokens, u32 dtype, cudaStream_t st)
+{
+	a.n_splits = P.splits;
+	a.max_pages_split = P.max_pages_split;
+	const dim3 g((unsigned)a.KV, (unsigned)P.splits, n_tokens);
+	if (dtype == InfBF16) {
+		INF_CUDA_TRY(set_smem(k_attn_decode<bf16>, P.smem));
+		k_attn_decode<bf16><<<g, kAttnThreads, P.smem, st>>>(a);
+	} else {
+		INF_CUDA_TRY(set_smem(k_attn_decode<float>, P.smem));
+		k_attn_decode<float><<<g, kAttnThreads, P.smem, st>>>(a);
+	}
+	INF_CUDA_TRY(cudaGetLastError());
+	return Success;
+}
+} // namespace
+
+u64 inf_attn_decode_scratch_bytes(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
+                                  u32 pages_per_seq, u32 dtype)
+{
+	AttnPlan P;
+	if (attn_plan(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P) != Success) return 0;
+	return (u64)(P.part_bytes + P.counter_bytes);
+}
+
+Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
+                        u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos, u32 n_tokens,
+                        u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype, void* d_out,
+                        void* d_scratch, u64 scratch_bytes, void* stream)
+{
+	if (!d_q || !d_kpool || !d_vpool || !d_block_table || !d_tok_slot || !d_tok_pos || !d_out || !d_scratch)
+		return fail(ErrorInvalidValue, "inf_attn_decode: NULL pointer");
+	AttnPlan P;
+	INF_TRY(attn_plan(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P));
+	if (scratch_bytes < P.part_bytes + P.counter_bytes)
+		return fail(ErrorInvalidValue, "inf_attn_decode: scratch needs %zu bytes", P.part_bytes + P.counter_bytes);
+	if (((uintptr_t)d_scratch & 15) || ((uintptr_t)d_kpool & 15) || ((uintptr_t)d_vpool & 15))
+		return fail(ErrorInvalidValue, "inf_attn_decode: 16-byte alignment");
+	const cudaStream_t st = (cudaStream_t)stream;
+	uint8_t* scr = (uint8_t*)d_scratch;
+	unsigned* counters = (unsigned*)(scr + P.part_bytes);
+	int* err = (int*)(scr + P.part_bytes + P.counter_bytes - 16);
+	INF_CUDA_TRY(cudaMemsetAsync(counters, 0, P.counter_bytes, st)); // tickets and error word start at zero
+	AttnDecodeArgs a;
+	memset(&a, 0, sizeof a);
+	a.q = d_q;
+	a.kpool = d_kpool;
+	a.vpool = d_vpool;
+	a.block_table = d_block_table;
+	a.pages_per_seq = (int)pages_per_seq;
+	a.max_pages = (int)n_pages;
+	a.tok_slot = d_tok_slot;
+	a.tok_pos = d_tok_pos;
+	a.H = (int)n_heads;
+	a.KV = (int)n_kv_heads;
+	a.hd = (int)head_dim;
+	a.blk = (int)kv_block;
+	a.scale = (float)(1.0 / std::sqrt((double)head_dim));
+	a.part = (float*)scr;
+	a.counters = counters;
+	a.out = d_out;
+	a.err = err;
+	INF_TRY(attn_launch(P, a, n_tokens, dtype, st));
+	int h_err = 0;
+	INF_CUDA_TRY(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+	INF_CUDA_TRY(cudaStreamSynchronize(st));
 	return map_dev_err(h_err);
 }
 

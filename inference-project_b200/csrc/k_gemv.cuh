@@ -16,6 +16,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "k_tp.cuh"
 
 namespace inf {
 
@@ -69,6 +70,11 @@ struct GemvArgs {
 	int* pos_rw;                  // logits: position advanced after the step
 	int max_out;
 	int* err;
+	// tensor parallelism: tp.size > 1 turns kEpiResid into a fused all-reduce of the rows'
+	// partial sums and kEpiLogits into a cross-shard argmax (logit row + row_base = token id)
+	TpComm tp;
+	int tp_round_index;
+	int row_base;
 };
 
 template <typename T, int UPL>
@@ -109,6 +115,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 	float* red_ss = red + 2 * kGemvConsumerWarps * RPC;                  // [warps]
 	unsigned long long* red_best = reinterpret_cast<unsigned long long*>(red_ss + kGemvConsumerWarps + 8);
 	volatile int* abort_flag = reinterpret_cast<volatile int*>(red_best + kGemvConsumerWarps);
+	float* tp_stage = reinterpret_cast<float*>(red_best + kGemvConsumerWarps + 2); // [kTpMaxRowsCta]
+	const bool tp_on = a.tp.size > 1;
 
 	const int tid = threadIdx.x;
 	const int warp = tid >> 5, lane = tid & 31;
@@ -270,12 +278,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 			if constexpr (EPI == kEpiStore) {
 				Store<T>::put(reinterpret_cast<T*>(a.out) + row, d0);
 			} else if constexpr (EPI == kEpiResid) {
-				a.resid[row] += d0;
+				if (tp_on) tp_stage[row - r0] = d0;
+				else a.resid[row] += d0;
 			} else if constexpr (EPI == kEpiSwiglu) {
 				Store<T>::put(reinterpret_cast<T*>(a.out) + (row >> 1), __fmul_rn(silu(d0), d1));
 			} else if constexpr (EPI == kEpiLogits) {
 				a.logits[row] = d0;
-				const unsigned long long key = argmax_key(d0, (uint32_t)row);
+				const unsigned long long key = argmax_key(d0, (uint32_t)(row + a.row_base));
 				best = key > best ? key : best;
 			} else if constexpr (EPI == kEpiQkv) {
 				const int hd = a.head_dim, half = hd >> 1;
@@ -309,6 +318,37 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 		}
 	}
 
+	if constexpr (EPI == kEpiResid) {
+		if (tp_on) {
+			// fused all-reduce: push this CTA's rows to every rank, flag, wait for the same CTA
+			// of every rank, then sum the ranks' partials in rank order (identical on all ranks)
+			const TpComm& c = a.tp;
+			const unsigned round = tp_round(c, a.tp_round_index);
+			const int par = (int)(round & 1u);
+			named_bar_sync(1, kGemvConsumers);
+			for (int i = ct; i < n_rows * c.size; i += kGemvConsumers) {
+				const int k = i / n_rows, r = i % n_rows;
+				c.inbox[k][((size_t)par * c.size + c.rank) * c.dim + r0 + r] = tp_stage[r];
+			}
+			__threadfence_system();
+			named_bar_sync(1, kGemvConsumers);
+			if (ct == 0) {
+				for (int k = 0; k < c.size; ++k) st_release_sys(c.flags[k] + c.rank * kTpMaxCtas + blockIdx.x, round);
+				for (int k = 0; k < c.size; ++k)
+					if (!tp_wait_flag(c.flags[c.rank] + k * kTpMaxCtas + blockIdx.x, round, a.err)) *abort_flag = 1;
+			}
+			named_bar_sync(1, kGemvConsumers);
+			if (!*abort_flag) {
+				const float* in = c.inbox[c.rank] + (size_t)par * c.size * c.dim;
+				for (int r = ct; r < n_rows; r += kGemvConsumers) {
+					float v = 0.0f;
+					for (int k = 0; k < c.size; ++k) v += __ldcv(in + (size_t)k * c.dim + r0 + r);
+					a.resid[r0 + r] += v;
+				}
+			}
+		}
+	}
+
 	if constexpr (EPI == kEpiLogits) {
 		// CTA max, then grid max through one atomic; the last CTA publishes the token.
 #pragma unroll
@@ -326,7 +366,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 			const unsigned done = atomicAdd(a.counter, 1u);
 			if (done == gridDim.x - 1) {
 				__threadfence();
-				const unsigned long long fin = atomicAdd(a.best, 0ull);
+				unsigned long long fin = atomicAdd(a.best, 0ull);
+				if (tp_on) {
+					// cross-shard argmax: every rank publishes its best key, takes the max of all
+					const TpComm& c = a.tp;
+					const unsigned round = tp_round(c, kTpRoundLm);
+					const int par = (int)(*c.epoch & 1u);
+					for (int k = 0; k < c.size; ++k) c.am_inbox[k][par * c.size + c.rank] = fin;
+					__threadfence_system();
+					for (int k = 0; k < c.size; ++k) st_release_sys(c.am_flags[k] + c.rank, round);
+					bool ok = true;
+					for (int k = 0; k < c.size; ++k) ok = tp_wait_flag(c.am_flags[c.rank] + k, round, a.err) && ok;
+					if (ok)
+						for (int k = 0; k < c.size; ++k) {
+							const unsigned long long o = *(volatile unsigned long long*)&c.am_inbox[c.rank][par * c.size + k];
+							fin = o > fin ? o : fin;
+						}
+				}
 				const uint32_t id = argmax_key_index(fin);
 				*a.cur_id = id;
 				const uint32_t st = *a.step;
@@ -335,6 +391,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 				*a.pos_rw = *a.pos_rw + 1;
 				*a.best = 0ull;
 				*a.counter = 0u;
+				if (tp_on) *(uint32_t*)a.tp.epoch = *a.tp.epoch + 1u;
 			}
 		}
 	}
@@ -344,7 +401,7 @@ inline size_t gemv_smem_bytes()
 {
 	return (size_t)kGemvRingBytes + 2 * kGemvMaxStages * sizeof(uint64_t) +
 	       (2 * kGemvConsumerWarps * 8 + kGemvConsumerWarps + 8) * sizeof(float) +
-	       kGemvConsumerWarps * sizeof(unsigned long long) + 16;
+	       kGemvConsumerWarps * sizeof(unsigned long long) + 16 + kTpMaxRowsCta * sizeof(float);
 }
 
 } // namespace inf

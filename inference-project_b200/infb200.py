@@ -76,10 +76,11 @@ EXPORTS = [
     "arena_host_pop", "arena_host_pop_at", "mem_arena_host_pos_get", "arena_dev_create", "arena_dev_destroy",
     "arena_dev_push", "arena_dev_pop", "arena_dev_pop_at", "arena_dev_pos_get", "cu_memcpy_htd",
     "cu_memcpy_htd_async", "cu_memcpy_dth", "cu_memset", "inf_fetch_input_embeddings", "inf_rmsnorm",
-    "inf_gemm_bf16",
+    "inf_gemm_bf16", "inf_attn_decode_scratch_bytes", "inf_attn_decode",
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
+    "inf_tp_export", "inf_tp_connect",
 ]
 
 _lib = None
@@ -119,6 +120,8 @@ def lib():
         "inf_fetch_input_embeddings": (E, [vp, u64, u32, u32, vp, vp, u32, vp]),
         "inf_rmsnorm": (E, [vp, vp, u32, u32, vp, f32, u32, vp]),
         "inf_gemm_bf16": (E, [vp, vp, vp, u32, u32, u32, u32, vp]),
+        "inf_attn_decode_scratch_bytes": (u64, [u32, u32, u32, u32, u32, u32, u32]),
+        "inf_attn_decode": (E, [vp, vp, vp, vp, u32, u32, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, u64, vp]),
         "inf_config_preset": (E, [u32, C.POINTER(InfConfig)]),
         "inf_model_build": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model), C.POINTER(InfConfig), C.c_char_p, u64]),
         "inf_model_destroy": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model)]),
@@ -135,6 +138,8 @@ def lib():
         "inf_profile_decode_step": (u32, [C.POINTER(Model), u32, u32, u32, C.POINTER(f32), u32]),
         "inf_synth_ids": (E, [u64, u64, u64, u32, u32, vp]),
         "inf_debug_read": (E, [C.POINTER(Model), u32, u32, u32, u32, vp, u64]),
+        "inf_tp_export": (E, [C.POINTER(Model), vp, u64]),
+        "inf_tp_connect": (E, [C.POINTER(Model), vp, u32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -259,6 +264,17 @@ class Engine:
                                _ptr(out) if out is not None else None, C.byref(st)), "inf_decode")
         return out, st
 
+    def tp_export(self) -> bytes:
+        buf = (C.c_uint8 * 64)()
+        check(lib().inf_tp_export(C.byref(self.model), buf, 64), "inf_tp_export")
+        return bytes(buf)
+
+    def tp_connect(self, handles) -> None:
+        """handles: the tp_size exported handles in rank order."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(lib().inf_tp_connect(C.byref(self.model), buf, len(handles)), "inf_tp_connect")
+
     BUFFERS = {"resid": 0, "q": 1, "attn": 2, "h": 3, "logits": 4, "k": 5, "v": 6}
 
     def debug_read(self, name: str, layer: int = 0, slot: int = 0, pos: int = 0) -> np.ndarray:
@@ -313,6 +329,18 @@ def fetch_input_embeddings(d_ids: int, n: int, dim: int, vocab: int, d_table: in
 def gemm_bf16(d_x: int, d_w: int, d_y: int, T: int, N: int, K: int, out_f32: bool, stream: int = 0) -> None:
     check(lib().inf_gemm_bf16(vp(d_x), vp(d_w), vp(d_y), T, N, K, int(out_f32), vp(stream) if stream else None),
           "inf_gemm_bf16")
+
+
+def attn_decode_scratch_bytes(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype) -> int:
+    return int(lib().inf_attn_decode_scratch_bytes(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq,
+                                                   dtype))
+
+
+def attn_decode(d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_tokens, n_heads, n_kv_heads, head_dim,
+                kv_block, dtype, d_out, d_scratch, scratch_bytes, stream=0) -> None:
+    check(lib().inf_attn_decode(vp(d_q), vp(d_k), vp(d_v), vp(d_bt), pages_per_seq, n_pages, vp(d_slot), vp(d_pos),
+                                n_tokens, n_heads, n_kv_heads, head_dim, kv_block, dtype, vp(d_out), vp(d_scratch),
+                                scratch_bytes, vp(stream) if stream else None), "inf_attn_decode")
 
 
 def rmsnorm(d_x: int, d_y: int, rows: int, dim: int, d_gain: int, eps: float, dtype: int, stream: int = 0) -> None:

@@ -124,3 +124,72 @@ def test_rmsnorm_matches_reference_kernel_on_its_valid_domain(cuda, dim):
     orc = O.rmsnorm(O.bf16_to_f32(xb)[None], g, 0.0)[0]
     np.testing.assert_allclose(ref, ours, rtol=2 ** -7, atol=1e-6)
     np.testing.assert_allclose(orc, ours, rtol=2 ** -7, atol=1e-6)
+
+
+def _attn_reference(torch, q, kp, vp_, bt, slots, pos, H, KV, hd, blk):
+    """Plain fp32 attention of each token over positions 0..pos of its slot."""
+    G = H // KV
+    outs = []
+    for i in range(q.shape[0]):
+        n = int(pos[i]) + 1
+        pages = bt[int(slots[i]), : (n + blk - 1) // blk].long()
+        K = kp[pages].float().permute(1, 0, 2, 3).reshape(KV, -1, hd)[:, :n]   # [KV, n, hd]
+        V = vp_[pages].float().permute(1, 0, 2, 3).reshape(KV, -1, hd)[:, :n]
+        qi = q[i].float().view(KV, G, hd)
+        s = torch.einsum("kgd,knd->kgn", qi, K) / hd ** 0.5
+        p = torch.softmax(s, dim=-1)
+        outs.append(torch.einsum("kgn,knd->kgd", p, V).reshape(H * hd))
+    return torch.stack(outs)
+
+
+@pytest.mark.parametrize("H,KV,hd,dtype,positions", [
+    (32, 8, 128, "bf16", [0, 15, 16, 1000, 2047, 2560]),
+    (32, 4, 64, "bf16", [5, 511, 512, 1023]),
+    (6, 6, 48, "fp32", [0, 17, 255]),
+    (4, 2, 16, "bf16", [3, 63]),
+])
+def test_attn_decode_kernel_vs_torch_fp32(cuda, H, KV, hd, dtype, positions):
+    torch = cuda
+    blk = 16
+    max_seq = max(positions) + 1
+    pps = (max_seq + blk - 1) // blk
+    n = len(positions)
+    n_pages = n * pps + 3
+    g = torch.Generator(device="cuda").manual_seed(H * hd + n)
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    kp = torch.randn(n_pages, KV, blk, hd, device="cuda", generator=g).to(tdt)
+    vp_ = torch.randn(n_pages, KV, blk, hd, device="cuda", generator=g).to(tdt)
+    q = (torch.randn(n, H * hd, device="cuda", generator=g) * 0.5).to(tdt)
+    perm = torch.randperm(n_pages, device="cuda", generator=g).int()
+    bt = perm[: n * pps].view(n, pps).contiguous()
+    slots = torch.arange(n, dtype=torch.int32, device="cuda")
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    code = I.BF16 if dtype == "bf16" else I.F32
+    nb = I.attn_decode_scratch_bytes(n, H, KV, hd, blk, pps, code)
+    scratch = torch.full((nb,), 0x7F, dtype=torch.uint8, device="cuda")  # contents on entry do not matter
+    for _ in range(2):
+        I.attn_decode(q.data_ptr(), kp.data_ptr(), vp_.data_ptr(), bt.data_ptr(), pps, n_pages, slots.data_ptr(),
+                      pos.data_ptr(), n, H, KV, hd, blk, code, out.data_ptr(), scratch.data_ptr(), nb)
+    ref = _attn_reference(torch, q, kp, vp_, bt, slots, pos, H, KV, hd, blk)
+    if dtype == "bf16":
+        torch.testing.assert_close(out.float(), ref, rtol=2 ** -7, atol=2e-3)
+    else:
+        torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_attn_decode_rejects_bad_page(cuda):
+    torch = cuda
+    H, KV, hd, blk, pps = 8, 2, 64, 16, 4
+    kp = torch.zeros(4, KV, blk, hd, dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros(1, H * hd, dtype=torch.bfloat16, device="cuda")
+    bt = torch.tensor([[0, 1, 99, 2]], dtype=torch.int32, device="cuda")  # page 99 is outside the pool
+    slot = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = torch.tensor([40], dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    nb = I.attn_decode_scratch_bytes(1, H, KV, hd, blk, pps, I.BF16)
+    scratch = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    with pytest.raises(I.InfError) as e:
+        I.attn_decode(q.data_ptr(), kp.data_ptr(), kp.data_ptr(), bt.data_ptr(), pps, 4, slot.data_ptr(),
+                      pos.data_ptr(), 1, H, KV, hd, blk, I.BF16, out.data_ptr(), scratch.data_ptr(), nb)
+    assert e.value.code == 11
