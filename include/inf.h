@@ -180,6 +180,19 @@ Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpoo
                         u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos, u32 n_tokens,
                         u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype, void* d_out,
                         void* d_scratch, u64 scratch_bytes, void* stream);
+/* inf_attn_decode for callers that cannot allocate device memory -- a serving loop that must
+ * not call cudaMalloc/cudaFree mid-step (they synchronize the device), or a runtime whose
+ * device memory is all committed to a pre-sized arena.  No counterpart in the reference.
+ * The scratch is a 4 MiB array built into the library (held on every GPU that loads it
+ * until the process exits); shapes needing more return ErrorInvalidValue.  The first call
+ * on each device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  All calls share the array: calls whose work
+ * overlaps on the GPU race and must be ordered by the caller (same stream, or events).
+ * Allocates nothing.  Synchronous. */
+Error_t inf_attn_decode_noalloc(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
+                                u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos,
+                                u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype,
+                                void* d_out, void* stream);
 
 /* ---- model ------------------------------------------------------------------------- */
 /* Built-in shapes: 1 tiny fp32 (d288), 2 TinyLlama-1.1B, 3 Llama-3-8B, 4 Llama-3-8B batch 64,

@@ -80,7 +80,7 @@ EXPORTS = [
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
-    "inf_tp_export", "inf_tp_connect",
+    "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc",
 ]
 
 _lib = None
@@ -139,6 +139,7 @@ def lib():
         "inf_synth_ids": (E, [u64, u64, u64, u32, u32, vp]),
         "inf_debug_read": (E, [C.POINTER(Model), u32, u32, u32, u32, vp, u64]),
         "inf_tp_export": (E, [C.POINTER(Model), vp, u64]),
+        "inf_attn_decode_noalloc": (E, [vp, vp, vp, vp, u32, u32, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp]),
         "inf_tp_connect": (E, [C.POINTER(Model), vp, u32]),
     }
     for name, (res, args) in sig.items():
@@ -341,6 +342,14 @@ def attn_decode(d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_to
     check(lib().inf_attn_decode(vp(d_q), vp(d_k), vp(d_v), vp(d_bt), pages_per_seq, n_pages, vp(d_slot), vp(d_pos),
                                 n_tokens, n_heads, n_kv_heads, head_dim, kv_block, dtype, vp(d_out), vp(d_scratch),
                                 scratch_bytes, vp(stream) if stream else None), "inf_attn_decode")
+
+
+def attn_decode_noalloc(d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_tokens, n_heads, n_kv_heads,
+                        head_dim, kv_block, dtype, d_out, stream=0) -> None:
+    """inf_attn_decode without a scratch argument: for callers that cannot allocate."""
+    check(lib().inf_attn_decode_noalloc(vp(d_q), vp(d_k), vp(d_v), vp(d_bt), pages_per_seq, n_pages, vp(d_slot),
+                                        vp(d_pos), n_tokens, n_heads, n_kv_heads, head_dim, kv_block, dtype,
+                                        vp(d_out), vp(stream) if stream else None), "inf_attn_decode_noalloc")
 
 
 def rmsnorm(d_x: int, d_y: int, rows: int, dim: int, d_gain: int, eps: float, dtype: int, stream: int = 0) -> None:
