@@ -71,10 +71,12 @@ def test_decode_path_stages(cuda, preset):
     assert am == o_am or np.sort(o_lg)[-1] - np.sort(o_lg)[-2] < 2e-2
 
 
-@pytest.mark.parametrize("preset,n", [(2, 200), (3, 300)])
-def test_tensor_core_prefill_stages(cuda, preset, n):
+@pytest.mark.parametrize("preset,n,drift", [(2, 200, 0.0144), (3, 300, 0.0161)])
+def test_tensor_core_prefill_stages(cuda, preset, n, drift):
     """One multi-token pass (tcgen05 GEMMs, prefill attention): every position's K and V in
-    the paged cache, and the last token's logits."""
+    the paged cache, and the last token's logits within twice the measured drift between
+    fp32 and double accumulation of the same one-layer model and prompt (`drift`, from
+    oracle/llama_ref.c with orc_set_accum_f32; it grows with the prompt length)."""
     cfg = I.preset(preset, n_layers=1, max_seq=512)
     prompt = I.synth_ids(8, n, cfg.vocab_size)
     with I.Engine(cfg) as eng:
@@ -86,7 +88,7 @@ def test_tensor_core_prefill_stages(cuda, preset, n):
         k, v = orc.kv(0, t)
         assert_bf16_close(kv[t][0], k, f"k[{t}]")
         assert_bf16_close(kv[t][1], v, f"v[{t}]")
-    assert float(np.abs(lg - o_lg).max()) <= 2e-2
+    assert float(np.abs(lg - o_lg).max()) <= 2 * drift
 
 
 def test_rope_positions_far_into_the_cache(cuda):
