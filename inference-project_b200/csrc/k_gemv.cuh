@@ -25,7 +25,8 @@ constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
 constexpr int kGemvThreads = kGemvConsumers + 32;
 constexpr int kGemvRingBytes = 96 * 1024;
 constexpr int kGemvMaxStages = 8;
-constexpr int kGemvPrefetch = 4; // chunks prefetched into L2 beyond the ring
+constexpr int kGemvPrefetch = 4;    // chunks prefetched into L2 beyond the ring
+constexpr int kGemvFlushRows = 128; // rows per deferred-epilogue window
 
 enum EpiKind : int { kEpiStore = 0, kEpiResid = 1, kEpiQkv = 2, kEpiSwiglu = 3, kEpiLogits = 4 };
 
@@ -77,6 +78,55 @@ struct GemvArgs {
 	int row_base;
 };
 
+// Sum of RPC per-lane row partials across the warp, transposed: at the first log2(RPC)
+// butterfly levels each lane keeps half of its rows and hands the other half to its partner,
+// so one value per lane survives; after the remaining levels lane l holds the full sum of
+// row row_of_lane<RPC>(l).  6 shuffles for 4 rows instead of 20.
+template <int RPC>
+__device__ __forceinline__ int row_of_lane(int lane)
+{
+	if constexpr (RPC == 8) return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+	else if constexpr (RPC == 4) return ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+	else if constexpr (RPC == 2) return (lane >> 4) & 1;
+	else return 0;
+}
+
+template <int RPC>
+__device__ __forceinline__ float reduce_rows(const float (&p)[RPC], int lane)
+{
+	constexpr unsigned kFull = 0xFFFFFFFFu;
+	if constexpr (RPC == 1) {
+		return warp_sum(p[0]);
+	} else if constexpr (RPC == 2) {
+		const bool b16 = lane & 16;
+		float s = (b16 ? p[1] : p[0]) + __shfl_xor_sync(kFull, b16 ? p[0] : p[1], 16);
+#pragma unroll
+		for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+		return s;
+	} else if constexpr (RPC == 4) {
+		const bool b16 = lane & 16, b8 = lane & 8;
+		float q[2];
+#pragma unroll
+		for (int j = 0; j < 2; ++j) q[j] = (b16 ? p[2 + j] : p[j]) + __shfl_xor_sync(kFull, b16 ? p[j] : p[2 + j], 16);
+		float s = (b8 ? q[1] : q[0]) + __shfl_xor_sync(kFull, b8 ? q[0] : q[1], 8);
+#pragma unroll
+		for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+		return s;
+	} else {
+		static_assert(RPC == 8, "rows per chunk");
+		const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+		float q[4], r[2];
+#pragma unroll
+		for (int j = 0; j < 4; ++j) q[j] = (b16 ? p[4 + j] : p[j]) + __shfl_xor_sync(kFull, b16 ? p[j] : p[4 + j], 16);
+#pragma unroll
+		for (int j = 0; j < 2; ++j) r[j] = (b8 ? q[2 + j] : q[j]) + __shfl_xor_sync(kFull, b8 ? q[j] : q[2 + j], 8);
+		float s = (b4 ? r[1] : r[0]) + __shfl_xor_sync(kFull, b4 ? r[0] : r[1], 4);
+		s += __shfl_xor_sync(kFull, s, 2);
+		s += __shfl_xor_sync(kFull, s, 1);
+		return s;
+	}
+}
+
 template <typename T, int UPL>
 __device__ __forceinline__ float gemv_row_dot(const uint8_t* row, int units_per_row, int ct, const float (&xh)[UPL][Store<T>::kVec])
 {
@@ -111,8 +161,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 	uint8_t* ring = smem;
 	uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGemvRingBytes);
 	uint64_t* empty = full + kGemvMaxStages;
-	float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);      // [2][warps][RPC]
-	float* red_ss = red + 2 * kGemvConsumerWarps * RPC;                  // [warps]
+	float* wpart = reinterpret_cast<float*>(empty + kGemvMaxStages);    // [warps][kGemvFlushRows]
+	float* red_ss = wpart + kGemvConsumerWarps * kGemvFlushRows;          // [warps]
 	unsigned long long* red_best = reinterpret_cast<unsigned long long*>(red_ss + kGemvConsumerWarps + 8);
 	volatile int* abort_flag = reinterpret_cast<volatile int*>(red_best + kGemvConsumerWarps);
 	float* tp_stage = reinterpret_cast<float*>(red_best + kGemvConsumerWarps + 2); // [kTpMaxRowsCta]
@@ -242,6 +292,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 		slot = *a.slot;
 	}
 
+	// Each warp reduces its RPC row partials across lanes (transposed butterfly: one value
+	// per lane survives) and parks them in wpart; the cross-warp sum and the epilogue run
+	// for a window of kGemvFlushRows rows at a time, so chunks flow without a block barrier.
+	constexpr int kChunksPerFlush = kGemvFlushRows / RPC;
+	const int my_row = row_of_lane<RPC>(lane);
+	const bool row_writer = (lane & (32 / RPC - 1)) == 0;
+	int w0 = 0; // first CTA-local row of the current window
 	for (int i = 0; i < n_chunks; ++i) {
 		const int s = i % S;
 		const bool ok = mbar_wait(&full[s], (i / S) & 1, abort_flag, a.err);
@@ -255,25 +312,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 		}
 		__syncwarp();
 		if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-		for (int r = 0; r < RPC; ++r) part[r] = warp_sum(part[r]);
-		float* rb = red + (i & 1) * kGemvConsumerWarps * RPC;
-		if (lane == 0) {
-#pragma unroll
-			for (int r = 0; r < RPC; ++r) rb[warp * RPC + r] = part[r];
-		}
-		named_bar_sync(1, kGemvConsumers);
-		if (!ok) continue;
+		const float v = reduce_rows<RPC>(part, lane);
+		if (row_writer && my_row < rows) wpart[warp * kGemvFlushRows + (i * RPC - w0) + my_row] = v;
+		if ((i + 1) % kChunksPerFlush != 0 && i + 1 != n_chunks) continue;
 
-		const int n_epi = rows / UNIT_ROWS;
-		if (ct < n_epi) {
-			const int lr = ct * UNIT_ROWS;
-			const int row = r0 + i * RPC + lr;
+		// ---- flush: epilogue of window rows [w0, w0 + nw)
+		const int nw = min(n_rows, (i + 1) * RPC) - w0;
+		named_bar_sync(1, kGemvConsumers);
+		for (int e = ct; e < nw / UNIT_ROWS; e += kGemvConsumers) {
+			const int lr = e * UNIT_ROWS;
+			const int row = r0 + w0 + lr;
 			float d0 = 0.0f, d1 = 0.0f;
 #pragma unroll
 			for (int w = 0; w < kGemvConsumerWarps; ++w) {
-				d0 += rb[w * RPC + lr];
-				if (PAIRED) d1 += rb[w * RPC + lr + 1];
+				d0 += wpart[w * kGemvFlushRows + lr];
+				if (PAIRED) d1 += wpart[w * kGemvFlushRows + lr + 1];
 			}
 			if constexpr (EPI == kEpiStore) {
 				Store<T>::put(reinterpret_cast<T*>(a.out) + row, d0);
@@ -316,6 +369,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 				}
 			}
 		}
+		named_bar_sync(1, kGemvConsumers); // the window buffer is reused by the next chunks
+		w0 += nw;
 	}
 
 	if constexpr (EPI == kEpiResid) {
@@ -400,7 +455,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 inline size_t gemv_smem_bytes()
 {
 	return (size_t)kGemvRingBytes + 2 * kGemvMaxStages * sizeof(uint64_t) +
-	       (2 * kGemvConsumerWarps * 8 + kGemvConsumerWarps + 8) * sizeof(float) +
+	       (kGemvConsumerWarps * kGemvFlushRows + kGemvConsumerWarps + 8) * sizeof(float) +
 	       kGemvConsumerWarps * sizeof(unsigned long long) + 16 + kTpMaxRowsCta * sizeof(float);
 }
 
