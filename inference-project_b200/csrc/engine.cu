@@ -75,7 +75,10 @@ struct InfEngine {
 	uint32_t* step = nullptr;
 	unsigned long long* best = nullptr;
 	unsigned* lm_counter = nullptr;
-	float* attn_part = nullptr;
+	float* attn_part = nullptr;  // split partials, sized for the larger of batch 1 and max_batch
+	int attn_splits_batch = 1;    // splits when max_batch tokens share one launch
+	float* logits_p = nullptr;    // [max_batch][Vl] batched-decode logits
+	uint32_t* argmax_p = nullptr; // [max_batch]
 	unsigned* attn_counters = nullptr;
 	int* err = nullptr;
 	uint32_t* d_ids = nullptr; // staged ids [max_seq]
@@ -294,9 +297,11 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.err = e->err;
 			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
 			                                           e->attn_max_pages_split, e->attn_splits);
-			INF_CUDA_TRY(set_smem(k_attn_decode<T>, smem));
+			const AttnKernel<T> ak = attn_decode_kernel<T>(e->Hl / e->KVl, hd);
+			if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+			INF_CUDA_TRY(set_smem(ak, smem));
 			INF_TRY(prof_begin(e));
-			INF_CUDA_TRY(launch(e, k_attn_decode<T>, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
+			INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
 			INF_TRY(prof_end(e, InfKAttn));
 		}
 		// O-proj + residual
@@ -548,6 +553,97 @@ Error_t run_prefill(InfEngine* e, u32 n, u32 start, u32 slot)
 
 bool use_tc_prefill(const InfEngine* e, u32 n) { return e->cfg.dtype == InfBF16 && e->chunk > 0 && n > 1; }
 
+// One decode token for each of B sequences (ids in d_ids, slots/positions in tok_slot/tok_pos):
+// the projections run once for all B tokens on the tensor cores, attention is the split-K
+// decode kernel with one grid slice per token, the LM head is a GEMM plus a row argmax.
+Error_t enqueue_decode_batch(InfEngine* e, int B)
+{
+	const InfConfig& c = e->cfg;
+	const int d = (int)c.dim, hd = (int)c.head_dim;
+	INF_CUDA_TRY(launch(e, k_embed<bf16, float>, dim3((d + 255) / 256, B), dim3(256), 0, (const uint32_t*)e->d_ids, B, d,
+	                    c.vocab_size, (const bf16*)e->embed, e->resid_p, e->err));
+	for (u32 l = 0; l < c.n_layers; ++l) {
+		const LayerW& L = e->layers[l];
+		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
+		                    (bf16*)e->xhat_p, B, d, (const bf16*)L.attn_norm, c.norm_eps));
+		{
+			TcArgs a = tc_base(e, B, (e->Hl + 2 * e->KVl) * hd, d, kTcQkv);
+			a.out = e->q_p;
+			a.kpool = L.kpool;
+			a.vpool = L.vpool;
+			a.block_table = e->block_table;
+			a.pages_per_seq = e->pages_per_seq;
+			a.max_pages = e->n_pages;
+			a.max_seq = (int)c.max_seq;
+			a.tok_pos = e->tok_pos;
+			a.tok_slot = e->tok_slot;
+			a.rope_cos = e->rope_cos;
+			a.rope_sin = e->rope_sin;
+			a.head_dim = hd;
+			a.n_q_heads = e->Hl;
+			a.n_kv_heads = e->KVl;
+			a.kv_block = (int)c.kv_block;
+			INF_TRY(launch_gemm_tc(e, e->xhat_p, L.wqkv, a));
+		}
+		{
+			AttnDecodeArgs a;
+			memset(&a, 0, sizeof a);
+			a.q = e->q_p;
+			a.kpool = L.kpool;
+			a.vpool = L.vpool;
+			a.block_table = e->block_table;
+			a.pages_per_seq = e->pages_per_seq;
+			a.max_pages = e->n_pages;
+			a.tok_slot = e->tok_slot;
+			a.tok_pos = e->tok_pos;
+			a.H = e->Hl;
+			a.KV = e->KVl;
+			a.hd = hd;
+			a.blk = (int)c.kv_block;
+			a.n_splits = e->attn_splits_batch;
+			a.max_pages_split = e->attn_max_pages_split;
+			a.scale = (float)(1.0 / std::sqrt((double)hd));
+			a.part = e->attn_part;
+			a.counters = e->attn_counters;
+			a.out = e->attn_p;
+			a.err = e->err;
+			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2, e->attn_max_pages_split,
+			                                           e->attn_splits_batch);
+			const AttnKernel<bf16> ak = attn_decode_kernel<bf16>(e->Hl / e->KVl, hd);
+			if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+			INF_CUDA_TRY(set_smem(ak, smem));
+			INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAttnThreads), smem, a));
+		}
+		{
+			TcArgs a = tc_base(e, B, d, e->Hl * hd, kTcResid);
+			a.resid = e->resid_p;
+			INF_TRY(launch_gemm_resid_tp(e, e->attn_p, L.wo, a));
+		}
+		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
+		                    (bf16*)e->xhat_p, B, d, (const bf16*)L.ffn_norm, c.norm_eps));
+		{
+			TcArgs a = tc_base(e, B, 2 * e->Fl, d, kTcSwiglu);
+			a.out = e->h_p;
+			INF_TRY(launch_gemm_tc(e, e->xhat_p, L.wgu, a));
+		}
+		{
+			TcArgs a = tc_base(e, B, d, e->Fl, kTcResid);
+			a.resid = e->resid_p;
+			INF_TRY(launch_gemm_resid_tp(e, e->h_p, L.wd, a));
+		}
+	}
+	INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
+	                    (bf16*)e->xhat_p, B, d, (const bf16*)e->final_norm, c.norm_eps));
+	{
+		TcArgs a = tc_base(e, B, e->Vl, d, kTcStoreF32);
+		a.out = e->logits_p;
+		INF_TRY(launch_gemm_tc(e, e->xhat_p, e->lm_head, a));
+	}
+	INF_CUDA_TRY(launch(e, k_argmax_rows, dim3(B), dim3(256), 0, (const float*)e->logits_p, e->Vl,
+	                    (uint32_t)(c.tp_rank * (u32)e->Vl), e->argmax_p));
+	return Success;
+}
+
 Error_t build_decode_graph(InfEngine* e)
 {
 	cudaGraph_t g = nullptr;
@@ -633,8 +729,11 @@ Error_t validate(const InfConfig& c)
 		return fail(ErrorBadConfig, "dim, ffn_dim and heads*head_dim must be multiples of %u", vec);
 	if ((c.n_heads / c.n_kv_heads) * c.head_dim * kPfTq > (u32)(kPfThreads * kPfMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kPfThreads * kPfMaxAcc / kPfTq);
-	if (kAttnThreads % (c.n_heads / c.n_kv_heads) != 0)
-		return fail(ErrorUnsupported, "GQA group must divide %d", kAttnThreads);
+	{
+		const u32 G = c.n_heads / c.n_kv_heads;
+		if (G != 1 && G != 2 && G != 4 && G != 8) return fail(ErrorUnsupported, "GQA group %u (1, 2, 4 or 8)", G);
+		if (c.head_dim > 256) return fail(ErrorUnsupported, "head_dim above 256");
+	}
 	if ((c.n_heads / c.n_kv_heads) * c.head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kAttnThreads * kAttnMaxAcc);
 	if (c.dim > 16384 || c.ffn_dim / tp > 16384) return fail(ErrorUnsupported, "dim/ffn above 16384");
@@ -791,6 +890,10 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	e->attn_splits = std::max((e->sm_count + e->KVl - 1) / e->KVl,
 	                          (e->pages_per_seq + e->attn_max_pages_split - 1) / e->attn_max_pages_split);
 	e->attn_splits = std::max(1, std::min(e->attn_splits, e->pages_per_seq));
+	e->attn_splits_batch = std::max((e->sm_count + e->KVl * (int)c.max_batch - 1) / (e->KVl * (int)c.max_batch),
+	                                (e->pages_per_seq + e->attn_max_pages_split - 1) / e->attn_max_pages_split);
+	e->attn_splits_batch = std::max(1, std::min(e->attn_splits_batch, e->pages_per_seq));
+	const u64 part_floats = std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * e->attn_splits_batch) * (hd + 2);
 	// multi-token passes run on the tensor cores (bf16 models); fp32 models feed tokens one by one
 	e->chunk = c.dtype == InfBF16 ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u)) : 0;
 
@@ -802,7 +905,8 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	const u64 comm = c.tp_size > 1 ? (2ull * c.tp_size * d * 4 + 2ull * c.tp_size * kTpMaxCtas * 4 + 64ull * c.tp_size +
 	                                   (e->chunk > 0 ? 2ull * (u64)(c.prefill_chunk ? c.prefill_chunk : 4096) * d * 4 : 0) + 8 * 256)
 	                                : 0;
-	const u64 act = comm + d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + (u64)e->Hl * e->attn_splits * (hd + 2) * 4 +
+	const u64 batch_bufs = c.max_batch > 1 ? (u64)c.max_batch * ((u64)e->Vl * 4 + 4) + 512 : 0;
+	const u64 act = comm + batch_bufs + d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + part_floats * 4 +
 	                (u64)e->chunk * (d * 4 + d * es + 2ull * e->Hl * hd * es + (u64)e->Fl * es + 8) + 16 * 256;
 	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024;
 	const u64 total = w_total + kv_total + act + (u64)c.max_seq * hd * 4 + (u64)c.max_batch * e->pages_per_seq * 4 +
@@ -843,8 +947,12 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	P.push(&e->lm_counter, 16);
 	P.push(&e->out_ids, (u64)e->max_out * 4);
 	P.push(&e->d_ids, (u64)c.max_seq * 4);
-	P.push(&e->attn_part, (u64)e->Hl * e->attn_splits * (hd + 2) * 4);
-	P.push(&e->attn_counters, (u64)e->KVl * 4);
+	P.push(&e->attn_part, part_floats * 4);
+	P.push(&e->attn_counters, (u64)c.max_batch * e->KVl * 4);
+	if (c.max_batch > 1) {
+		P.push(&e->logits_p, (u64)c.max_batch * e->Vl * 4);
+		P.push(&e->argmax_p, (u64)c.max_batch * 4);
+	}
 	if (e->chunk > 0) {
 		P.push(&e->resid_p, (u64)e->chunk * d * 4);
 		P.push(&e->xhat_p, (u64)e->chunk * d * es);
@@ -1090,12 +1198,40 @@ Error_t inf_forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const 
 	if (!model || !model->engine || !seq_slots || !ids || !positions || n_seqs == 0)
 		return fail(ErrorInvalidValue, "inf_forward_batch: bad arguments");
 	InfEngine* e = model->engine;
-	for (u32 i = 0; i < n_seqs; ++i) {
-		f32* lo = logits_out ? logits_out + (size_t)i * e->Vl : nullptr;
-		u32* am = argmax_out ? argmax_out + i : nullptr;
-		INF_TRY(inf_forward(model, ids + i, 1, positions[i], seq_slots[i], lo, am));
+	const InfConfig& c = e->cfg;
+	const bool host_args = !is_device_ptr(seq_slots) && !is_device_ptr(ids) && !is_device_ptr(positions);
+	const bool batched = host_args && c.dtype == InfBF16 && c.tp_size <= 1 && n_seqs > 1 && n_seqs <= c.max_batch &&
+	                     (int)n_seqs <= e->chunk && e->logits_p;
+	if (!batched) {
+		for (u32 i = 0; i < n_seqs; ++i) {
+			f32* lo = logits_out ? logits_out + (size_t)i * e->Vl : nullptr;
+			u32* am = argmax_out ? argmax_out + i : nullptr;
+			INF_TRY(inf_forward(model, ids + i, 1, positions[i], seq_slots[i], lo, am));
+		}
+		return Success;
 	}
-	return Success;
+	std::vector<char> seen(c.max_batch, 0);
+	for (u32 i = 0; i < n_seqs; ++i) {
+		if (seq_slots[i] >= c.max_batch) return fail(ErrorInvalidValue, "slot %u >= max_batch", seq_slots[i]);
+		if (seen[seq_slots[i]]++) return fail(ErrorInvalidValue, "slot %u appears twice in one batch", seq_slots[i]);
+		if (positions[i] >= c.max_seq) return fail(ErrorKvOutOfRange, "position %u beyond max_seq", positions[i]);
+		if (ids[i] >= c.vocab_size) return fail(ErrorTokenOutOfRange, "id %u >= vocab %u", ids[i], c.vocab_size);
+	}
+	for (u32 i = 0; i < n_seqs; ++i) INF_TRY(ensure_pages(e, seq_slots[i], positions[i] + 1));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream)); // pinned staging reuse
+	for (u32 i = 0; i < n_seqs; ++i) {
+		e->h_pin[i] = ids[i];
+		e->h_tok[i] = (int)positions[i];
+		e->h_tok[e->chunk + i] = (int)seq_slots[i];
+	}
+	INF_CUDA_TRY(cudaMemcpyAsync(e->d_ids, e->h_pin, sizeof(u32) * n_seqs, cudaMemcpyHostToDevice, e->stream));
+	INF_CUDA_TRY(cudaMemcpyAsync(e->tok_pos, e->h_tok, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, e->stream));
+	INF_CUDA_TRY(cudaMemcpyAsync(e->tok_slot, e->h_tok + e->chunk, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, e->stream));
+	INF_TRY(enqueue_decode_batch(e, (int)n_seqs));
+	if (logits_out) INF_TRY(copy_out(e, logits_out, e->logits_p, sizeof(float) * e->Vl * n_seqs));
+	if (argmax_out) INF_TRY(copy_out(e, argmax_out, e->argmax_p, sizeof(u32) * n_seqs));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	return check_dev_err(e);
 }
 
 Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u32* out_ids, InfStats* stats)
@@ -1429,7 +1565,7 @@ Error_t attn_plan(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 k
 	    pages_per_seq == 0 || n_heads % n_kv_heads || (dtype != InfBF16 && dtype != InfF32) || n_tokens > 65535)
 		return fail(ErrorInvalidValue, "attention: bad shape");
 	const u32 G = n_heads / n_kv_heads;
-	if (kAttnThreads % G || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
+	if ((G != 1 && G != 2 && G != 4 && G != 8) || head_dim > 256 || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "attention: GQA group %u x head_dim %u", G, head_dim);
 	const size_t esz = dtype == InfBF16 ? 2 : 4;
 	if ((kv_block * head_dim * esz) % 16) return fail(ErrorUnsupported, "attention: page block not a multiple of 16 bytes");
@@ -1450,12 +1586,17 @@ Error_t attn_launch(const AttnPlan& P, AttnDecodeArgs a, u32 n_tokens, u32 dtype
 	a.n_splits = P.splits;
 	a.max_pages_split = P.max_pages_split;
 	const dim3 g((unsigned)a.KV, (unsigned)P.splits, n_tokens);
+	const int G = a.H / a.KV;
 	if (dtype == InfBF16) {
-		INF_CUDA_TRY(set_smem(k_attn_decode<bf16>, P.smem));
-		k_attn_decode<bf16><<<g, kAttnThreads, P.smem, st>>>(a);
+		const AttnKernel<bf16> k = attn_decode_kernel<bf16>(G, a.hd);
+		if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
+		INF_CUDA_TRY(set_smem(k, P.smem));
+		k<<<g, kAttnThreads, P.smem, st>>>(a);
 	} else {
-		INF_CUDA_TRY(set_smem(k_attn_decode<float>, P.smem));
-		k_attn_decode<float><<<g, kAttnThreads, P.smem, st>>>(a);
+		const AttnKernel<float> k = attn_decode_kernel<float>(G, a.hd);
+		if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
+		INF_CUDA_TRY(set_smem(k, P.smem));
+		k<<<g, kAttnThreads, P.smem, st>>>(a);
 	}
 	INF_CUDA_TRY(cudaGetLastError());
 	return Success;
@@ -1465,7 +1606,7 @@ Error_t attn_launch(const AttnPlan& P, AttnDecodeArgs a, u32 n_tokens, u32 dtype
 u64 inf_attn_decode_scratch_bytes(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
                                   u32 pages_per_seq, u32 dtype)
 {
-	AttnPlan P;
+	AttnPlan P = {};
 	if (attn_plan(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P) != Success) return 0;
 	return (u64)(P.part_bytes + P.counter_bytes);
 }

@@ -5,26 +5,30 @@
 // that share it (GQA), so every K/V page is read once for the whole group -- and a
 // contiguous range of at most max_pages_split pages of the token's context.
 //
-// Latency is what matters at batch 1 (a layer's KV is a few MB), so:
+// At batch 1 a layer's KV is a few MB, so the kernel is built for latency:
 //   * every page of the split is fetched at once with a 1-D bulk copy per K and V block,
 //     each page on its own mbarrier; pages older than the current token's page are issued
-//     before griddepcontrol.wait (they were written by earlier steps), overlapping the QKV
-//     kernel that is still writing this token's K/V;
-//   * the CTA works on slabs of 128/G tokens so each thread owns one (head, token) score;
+//     before griddepcontrol.wait (earlier steps wrote them), overlapping the QKV kernel that
+//     is still writing this token's K/V;
+//   * scores: 8 warps take tokens round-robin, lanes split head_dim, the G queries sit in
+//     registers and the G partial dots are reduced with one transposed butterfly;
+//   * one softmax pass over all the split's scores (no online rescaling inside a CTA);
+//   * P.V: warps again take tokens round-robin and are summed through shared memory;
 //   * partial (max, sum, acc) go to scratch and the last CTA of each (token, KV head) --
-//     found with an atomic ticket, no spinning -- combines the splits, computing the split
-//     weights once.
+//     found with an atomic ticket, no spinning -- combines the splits.
 // Positions past the context (stale slots in the last page) are masked.
 #pragma once
 
 #include "common.cuh"
+#include "k_gemv.cuh" // reduce_rows / row_of_lane
 
 namespace inf {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnMaxAcc = 8;        // (G * head_dim) / 128 outputs per thread
-constexpr int kAttnMaxPagesSplit = 16; // mbarriers per CTA
-constexpr int kAttnSmemBudget = 96 * 1024;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kAttnMaxAcc = 4;          // (G * head_dim) / 256 outputs per thread
+constexpr int kAttnMaxPagesSplit = 16;  // mbarriers per CTA
+constexpr int kAttnSmemBudget = 64 * 1024;
 
 struct AttnDecodeArgs {
 	const void* q;           // [B][H*hd]
@@ -42,28 +46,48 @@ struct AttnDecodeArgs {
 	int* err;
 };
 
-template <typename T>
+// head_dim values per lane of a warp
+inline int attn_vpl(int hd) { return hd <= 32 ? 1 : hd <= 64 ? 2 : hd <= 128 ? 4 : 8; }
+
+// page buffers, also reused for the P.V reduction and the split combine
+__host__ __device__ inline size_t attn_region_bytes(int G, int hd, int blk, size_t esz, int max_pages_split)
+{
+	const size_t kv = 2 * (size_t)max_pages_split * blk * hd * esz;
+	const size_t pv = (size_t)kAttnWarps * G * hd * sizeof(float);
+	return ((kv > pv ? kv : pv) + 15) & ~(size_t)15;
+}
+
+// VPL consecutive head_dim values of one K/V row as floats (lanes past head_dim read nothing)
+template <typename T, int VPL>
+__device__ __forceinline__ void load_vals(const T* row, int d0, int hd, float (&v)[VPL])
+{
+#pragma unroll
+	for (int j = 0; j < VPL; ++j) v[j] = (d0 + j < hd) ? Store<T>::get(row + d0 + j) : 0.0f;
+}
+
+template <typename T, int G, int VPL>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeArgs a)
 {
 	extern __shared__ __align__(128) uint8_t sm_raw[];
 	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
-	const int G = a.H / a.KV, hd = a.hd, blk = a.blk;
-	const int TS = kAttnThreads / G;               // tokens per slab
+	const int hd = a.hd, blk = a.blk;
 	const size_t blk_bytes = (size_t)blk * hd * sizeof(T);
+	const int max_tok = a.max_pages_split * blk;
 	uint8_t* kbuf = sm_raw;                                        // [max_pages_split][blk][hd]
 	uint8_t* vbuf = kbuf + (size_t)a.max_pages_split * blk_bytes;
-	float* q_s = reinterpret_cast<float*>(vbuf + (size_t)a.max_pages_split * blk_bytes); // [G][hd]
-	float* s_s = q_s + G * hd;                                     // [G][TS]
-	float* m_s = s_s + G * TS;                                     // [G]
-	float* l_s = m_s + G;
-	float* al_s = l_s + G;
-	float* w_s = al_s + G;                                         // combine weights [G][n_splits]
+	const size_t region = attn_region_bytes(G, hd, blk, sizeof(T), a.max_pages_split);
+	float* s_s = reinterpret_cast<float*>(sm_raw + region);       // [G][max_tok]
+	float* m_s = s_s + G * max_tok;                                // [G]
+	float* l_s = m_s + G;                                          // [G]
+	float* w_s = l_s + G;                                          // combine weights [G][n_splits]
 	uint64_t* bars = reinterpret_cast<uint64_t*>(w_s + G * a.n_splits + 2);
 	bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(bars) + 7) & ~(uintptr_t)7);
+	float* pv_red = reinterpret_cast<float*>(kbuf); // [warps][G*hd], reuses the page buffers after P.V
 	__shared__ int last_flag;
 	__shared__ int abort_flag;
 
 	const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+	const int d0 = lane * VPL; // this lane's head_dim slice
 	// slot, position and block table are not written by the kernels of this step
 	const int slot = a.tok_slot[b];
 	const int pos = a.tok_pos[b];
@@ -74,6 +98,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	const int p_end = min(n_pages, p_begin + pps);
 	const int np = max(0, p_end - p_begin);
 	const int cur_page = pos / blk; // holds this step's K/V: fetched after the wait
+	const int n_tok = np * blk;
+	const int tok0 = p_begin * blk;
 
 	if (tid == 0) {
 		abort_flag = 0;
@@ -83,8 +109,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	__syncthreads();
 	// thread j issues page j's two copies (page ids are read in parallel, not one by one)
 	auto issue = [&](int j) {
-		const int p = p_begin + j;
-		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p];
+		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p_begin + j];
 		if (page < 0 || page >= a.max_pages) {
 			report_err(a.err, kDevKvRange);
 			mbar_arrive(&bars[j]); // completes the phase with nothing in flight; data masked below
@@ -101,102 +126,95 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	pdl_trigger();
 	if (tid < np && p_begin + tid >= cur_page) issue(tid);
 
-	const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.H * hd + (size_t)kvh * G * hd;
-	for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = Store<T>::get(qb + i);
-	if (tid < G) {
+	// the G queries of this KV head, this lane's head_dim slice, in registers
+	float qr[G][VPL];
+	{
+		const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.H * hd + (size_t)kvh * G * hd;
+#pragma unroll
+		for (int g = 0; g < G; ++g) load_vals<T, VPL>(qb + (size_t)g * hd, d0, hd, qr[g]);
+	}
+
+	// ---- scores
+	const int my_g = row_of_lane<G>(lane);
+	const bool g_writer = (lane & (32 / G - 1)) == 0;
+	int waited = 0;
+	for (int t = warp; t < n_tok; t += kAttnWarps) {
+		for (const int need = t / blk + 1; waited < need; ++waited)
+			if (!abort_flag && !mbar_wait(&bars[waited], 0, (volatile int*)&abort_flag, a.err)) abort_flag = 1;
+		float kv[VPL];
+		load_vals<T, VPL>(reinterpret_cast<const T*>(kbuf) + (size_t)t * hd, d0, hd, kv);
+		float part[G];
+#pragma unroll
+		for (int g = 0; g < G; ++g) {
+			float s = 0.0f;
+#pragma unroll
+			for (int j = 0; j < VPL; ++j) s = fmaf(qr[g][j], kv[j], s);
+			part[g] = s;
+		}
+		const float s = reduce_rows<G>(part, lane);
+		if (g_writer) s_s[my_g * max_tok + t] = (tok0 + t < ctx && !abort_flag) ? s * a.scale : -INFINITY;
+	}
+	// a warp that saw fewer pages than exist must still observe every page before the V pass
+	for (; waited < np; ++waited)
+		if (!abort_flag && !mbar_wait(&bars[waited], 0, (volatile int*)&abort_flag, a.err)) abort_flag = 1;
+	__syncthreads();
+
+	// ---- softmax over the split, one warp per head
+	for (int g = warp; g < G; g += kAttnWarps) {
+		float mx = -INFINITY;
+		for (int t = lane; t < n_tok; t += 32) mx = fmaxf(mx, s_s[g * max_tok + t]);
+		mx = warp_max(mx);
+		float sum = 0.0f;
+		for (int t = lane; t < n_tok; t += 32) {
+			const float e = (mx == -INFINITY) ? 0.0f : expf(s_s[g * max_tok + t] - mx);
+			s_s[g * max_tok + t] = e;
+			sum += e;
+		}
+		sum = warp_sum(sum);
+		if (lane == 0) {
+			m_s[g] = mx;
+			l_s[g] = sum;
+		}
+	}
+	if (n_tok == 0 && tid < G) {
 		m_s[tid] = -INFINITY;
 		l_s[tid] = 0.0f;
 	}
-	float acc[kAttnMaxAcc];
-#pragma unroll
-	for (int j = 0; j < kAttnMaxAcc; ++j) acc[j] = 0.0f;
 	__syncthreads();
 
-	const int n_tok = np * blk;
-	const int my_g = tid / TS, my_t = tid % TS;
-	int waited = 0; // pages known to have landed
-	for (int t0 = 0; t0 < n_tok; t0 += TS) {
-		// make sure every page this slab touches has landed
-		const int need = min(np, (t0 + TS + blk - 1) / blk);
-		for (; waited < need; ++waited)
-			if (!abort_flag && !mbar_wait(&bars[waited], 0, (volatile int*)&abort_flag, a.err)) abort_flag = 1;
-		// scores: one (head, token) per thread; rotated reads avoid bank conflicts
-		{
-			const int tl = t0 + my_t;
-			const int tok = p_begin * blk + tl;
-			float s = -INFINITY;
-			if (tl < n_tok && tok < ctx && !abort_flag) {
-				const T* kr = reinterpret_cast<const T*>(kbuf) + (size_t)tl * hd;
-				const float* qr = q_s + my_g * hd;
-				const int rot = (2 * my_t) % hd;
-				float d0 = 0.0f, d1 = 0.0f;
-				for (int i = 0; i < hd; i += 2) {
-					int k0 = i + rot;
-					if (k0 >= hd) k0 -= hd;
-					d0 = fmaf(qr[k0], Store<T>::get(kr + k0), d0);
-					d1 = fmaf(qr[k0 + 1], Store<T>::get(kr + k0 + 1), d1);
-				}
-				s = (d0 + d1) * a.scale;
-			}
-			s_s[my_g * TS + my_t] = s;
-		}
-		__syncthreads();
-		// online softmax, one warp per head
-		for (int g = warp; g < G; g += kAttnThreads / 32) {
-			float mx = -INFINITY;
-			for (int j = lane; j < TS; j += 32) mx = fmaxf(mx, s_s[g * TS + j]);
-			mx = warp_max(mx);
-			const float m_old = m_s[g];
-			const float m_new = fmaxf(m_old, mx);
-			float sum = 0.0f;
-			for (int j = lane; j < TS; j += 32) {
-				const float sv = s_s[g * TS + j];
-				const float e = (m_new == -INFINITY) ? 0.0f : expf(sv - m_new);
-				s_s[g * TS + j] = e;
-				sum += e;
-			}
-			sum = warp_sum(sum);
-			if (lane == 0) {
-				const float alpha = (m_new == -INFINITY) ? 1.0f : expf(m_old - m_new);
-				l_s[g] = l_s[g] * alpha + sum;
-				m_s[g] = m_new;
-				al_s[g] = alpha;
-			}
-		}
-		__syncthreads();
-		const int t_hi = min(TS, n_tok - t0);
+	// ---- P.V: warps split the tokens, lanes split head_dim
+	float acc[G][VPL];
 #pragma unroll
-		for (int jj = 0; jj < kAttnMaxAcc; ++jj) {
-			const int o = tid + jj * kAttnThreads;
-			if (o < G * hd) {
-				const int g = o / hd, i = o % hd;
-				float v = acc[jj] * al_s[g];
-				const float* pr = s_s + g * TS;
-				const T* vc = reinterpret_cast<const T*>(vbuf) + (size_t)t0 * hd + i;
-				for (int j = 0; j < t_hi; ++j) v = fmaf(pr[j], Store<T>::get(vc + (size_t)j * hd), v);
-				acc[jj] = v;
-			}
+	for (int g = 0; g < G; ++g)
+#pragma unroll
+		for (int j = 0; j < VPL; ++j) acc[g][j] = 0.0f;
+	for (int t = warp; t < n_tok; t += kAttnWarps) {
+		float vv[VPL];
+		load_vals<T, VPL>(reinterpret_cast<const T*>(vbuf) + (size_t)t * hd, d0, hd, vv);
+#pragma unroll
+		for (int g = 0; g < G; ++g) {
+			const float p = s_s[g * max_tok + t];
+#pragma unroll
+			for (int j = 0; j < VPL; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
 		}
-		__syncthreads();
 	}
-	// pages issued but never waited for (abort) must land before the CTA exits or the page
-	// buffers are reused for the combine
-	if (tid == 0)
-		for (int j = waited; j < np; ++j) {
-			const uint64_t t0 = global_timer_ns();
-			while (!mbar_try_wait(&bars[j], 0))
-				if (global_timer_ns() - t0 > kWaitLimitNs) break;
-		}
+	// cross-warp sum through shared memory (the page buffers are free once every warp is done)
+	__syncthreads();
+#pragma unroll
+	for (int g = 0; g < G; ++g)
+#pragma unroll
+		for (int j = 0; j < VPL; ++j)
+			if (d0 + j < hd) pv_red[(size_t)warp * G * hd + g * hd + d0 + j] = acc[g][j];
+	__syncthreads();
 
 	// partials: [b][h][split][hd + 2] = (acc..., m, l)
 	const int hd2 = hd + 2;
+	for (int o = tid; o < G * hd; o += kAttnThreads) {
+		float v = 0.0f;
 #pragma unroll
-	for (int jj = 0; jj < kAttnMaxAcc; ++jj) {
-		const int o = tid + jj * kAttnThreads;
-		if (o < G * hd) {
-			const int g = o / hd, i = o % hd;
-			a.part[(((size_t)b * a.H + kvh * G + g) * a.n_splits + split) * hd2 + i] = acc[jj];
-		}
+		for (int w = 0; w < kAttnWarps; ++w) v += pv_red[(size_t)w * G * hd + o];
+		const int g = o / hd, i = o % hd;
+		a.part[(((size_t)b * a.H + kvh * G + g) * a.n_splits + split) * hd2 + i] = v;
 	}
 	if (tid < G) {
 		float* pr = a.part + (((size_t)b * a.H + kvh * G + tid) * a.n_splits + split) * hd2;
@@ -241,7 +259,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	}
 	__syncthreads();
 	// weights exp(m_s - M) / L once per (head, split)
-	for (int g = warp; g < G; g += kAttnThreads / 32) {
+	for (int g = warp; g < G; g += kAttnWarps) {
 		const float* pr = pc + (size_t)g * a.n_splits * hd2;
 		float M = -INFINITY;
 		for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, pr[(size_t)s * hd2 + hd]);
@@ -285,10 +303,27 @@ inline int attn_decode_max_pages_split(int blk, int hd, size_t esz)
 
 inline size_t attn_decode_smem_bytes(int G, int hd, int blk, size_t esz, int max_pages_split, int n_splits)
 {
-	const int TS = kAttnThreads / G;
-	return 2 * (size_t)max_pages_split * blk * hd * esz +
-	       sizeof(float) * ((size_t)G * hd + (size_t)G * TS + 3 * G + (size_t)G * n_splits + 2) + 8 +
+	return attn_region_bytes(G, hd, blk, esz, max_pages_split) +
+	       sizeof(float) * ((size_t)G * max_pages_split * blk + 2 * G + (size_t)G * n_splits + 2) + 8 +
 	       kAttnMaxPagesSplit * sizeof(uint64_t);
 }
+
+template <typename T>
+using AttnKernel = void (*)(AttnDecodeArgs);
+
+// the instantiation for a GQA group G in {1,2,4,8} and head_dim <= 256 (nullptr otherwise)
+template <typename T>
+inline AttnKernel<T> attn_decode_kernel(int G, int hd)
+{
+	const int vpl = attn_vpl(hd);
+#define INF_ATTN_CASE(g, v) \
+	if (G == g && vpl == v) return k_attn_decode<T, g, v>;
+#define INF_ATTN_G(g) INF_ATTN_CASE(g, 1) INF_ATTN_CASE(g, 2) INF_ATTN_CASE(g, 4) INF_ATTN_CASE(g, 8)
+	INF_ATTN_G(1) INF_ATTN_G(2) INF_ATTN_G(4) INF_ATTN_G(8)
+#undef INF_ATTN_G
+#undef INF_ATTN_CASE
+	return nullptr;
+}
+
 
 } // namespace inf

@@ -92,4 +92,31 @@ __global__ void k_rmsnorm_rows(const InT* x, OutT* y, int rows, int dim,
 	}
 }
 
+// Greedy argmax of each row of a [rows x n] fp32 matrix (ties -> lowest index), one CTA per
+// row; the token id is the column index plus col_base (vocabulary shard offset).
+__global__ void k_argmax_rows(const float* __restrict__ x, int n, uint32_t col_base, uint32_t* __restrict__ out)
+{
+	pdl_wait();
+	pdl_trigger();
+	const float* row = x + (size_t)blockIdx.x * n;
+	unsigned long long best = 0ull;
+	for (int i = threadIdx.x; i < n; i += blockDim.x) {
+		const unsigned long long k = argmax_key(row[i], (uint32_t)i + col_base);
+		best = k > best ? k : best;
+	}
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) {
+		const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+		best = other > best ? other : best;
+	}
+	__shared__ unsigned long long red[32];
+	if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+	__syncthreads();
+	if (threadIdx.x == 0) {
+		for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+		best = red[0] > best ? red[0] : best;
+		out[blockIdx.x] = argmax_key_index(best);
+	}
+}
+
 } // namespace inf

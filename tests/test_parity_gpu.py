@@ -181,8 +181,40 @@ def test_forward_batch_matches_single(cuda):
         for i, p in enumerate(prompts):
             _ = eng.forward(p, 0, slot=i)
             l1, a1 = eng.forward([nxt[i]], len(p), slot=i)
-            np.testing.assert_array_equal(l1, lg[i])  # identical kernels and inputs
-            assert a1 == am[i]
+            # batched path (tensor-core GEMMs, one attention launch) vs the batch-1 GEMV path
+            assert float(np.abs(l1 - lg[i]).max()) <= 2 * DRIFT_TINYLLAMA_2
+            assert cosine(l1, lg[i]) >= COSINE_MIN
+            top = np.sort(l1)
+            assert a1 == am[i] or top[-1] - top[-2] < 2 * DRIFT_TINYLLAMA_2
+
+
+def test_batched_decode_ragged_contexts_steps(cuda):
+    """16 sequences with context lengths spread over [20, 400], four batched decode steps
+    (tensor-core projections, one attention launch for all tokens, LM-head GEMM + row argmax)
+    against stepping every sequence alone through the batch-1 path on a second engine with
+    the same prompts; both sides are fed the same tokens."""
+    cfg = I.preset(2, n_layers=2, max_seq=512, max_batch=16)
+    B = 16
+    lens = I.synth_uniform(2, I.STREAM_CTX_LEN, B, 20, 400)
+    prompts = [I.synth_ids(100 + i, int(lens[i]), cfg.vocab_size) for i in range(B)]
+    with I.Engine(cfg) as eb, I.Engine(cfg) as es:
+        cur = []
+        for i, p in enumerate(prompts):
+            _, am = eb.forward(p, 0, slot=i)
+            _, am2 = es.forward(p, 0, slot=i)
+            assert am == am2
+            cur.append(am)
+        pos = lens.astype(np.uint32).copy()
+        bound = 2 * DRIFT_TINYLLAMA_2
+        for step in range(4):
+            lg, am = eb.forward_batch(np.arange(B), np.array(cur, np.uint32), pos, want_logits=True)
+            for i in range(B):
+                ls, a_s = es.forward([cur[i]], int(pos[i]), slot=i)
+                assert float(np.abs(ls - lg[i]).max()) <= bound, f"step {step} seq {i}"
+                top = np.sort(ls)
+                assert am[i] == a_s or top[-1] - top[-2] < bound
+            cur = am.tolist()
+            pos += 1
 
 
 def test_errors_are_returned_not_aborted(cuda):

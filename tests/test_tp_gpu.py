@@ -1,0 +1,108 @@
+"""Tensor parallelism on 2 GPUs: one child process per GPU, sharded weights, the per-layer
+all-reduces and the cross-shard argmax inside the projection kernels over NVLink peer
+memory.  Handles are exchanged over gloo (host plumbing only).  Skipped with fewer than two
+GPUs.  NCCL is not used; no kernel uses multicast."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import infb200 as I
+
+pytestmark = pytest.mark.gpu
+
+DRIFT_TINYLLAMA_2 = 0.0197  # fp32 vs double accumulation, 2 layers (see test_parity_gpu.py)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, preset, layers, prompt, n_new, mode, out_q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    res = {"rank": rank}
+    try:
+        cfg = I.preset(preset, n_layers=layers, max_seq=512, tp_rank=rank, tp_size=world)
+        with I.Engine(cfg) as eng:
+            handles = [None] * world
+            dist.all_gather_object(handles, eng.tp_export())
+            eng.tp_connect(handles)
+            if mode == "generate":
+                lg, am = eng.forward(np.asarray(prompt, np.uint32), 0)
+                ids, _ = eng.decode(am, len(prompt), n_new)
+                res.update(first=am, ids=ids.tolist(), logits=lg.tolist())
+            elif mode == "timeout":
+                lg, am = eng.forward(np.asarray(prompt, np.uint32), 0)
+                dist.barrier()
+                if rank == 0:  # rank 1 stops taking part: rank 0's all-reduce waits run out
+                    try:
+                        eng.decode(am, len(prompt), 1)
+                        res["code"] = 0
+                    except I.InfError as e:
+                        res["code"] = e.code
+                    eng.debug_read("resid")  # the context is still usable
+                dist.barrier()
+            torch.cuda.synchronize()
+            dist.barrier()
+    except Exception as e:  # reported to the parent
+        res["error"] = repr(e)
+    out_q.put(res)
+    dist.destroy_process_group()
+
+
+def _run(world, **kw):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, kw["preset"], kw["layers"], kw["prompt"], kw["n_new"],
+                                               kw["mode"], q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    out.sort(key=lambda r: r["rank"])
+    for r in out:
+        assert "error" not in r, r["error"]
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_greedy_matches_single_gpu(cuda, world):
+    prompt = I.synth_ids(1, 40, 32000).tolist()
+    cfg = I.preset(2, n_layers=2, max_seq=512)
+    with I.Engine(cfg) as eng:
+        lg_ref, am_ref = eng.forward(np.asarray(prompt, np.uint32), 0)
+        ids_ref, _ = eng.decode(am_ref, len(prompt), 32)
+    if cfg.n_kv_heads % world:
+        pytest.skip("KV heads do not split over this many ranks")
+    out = _run(world, preset=2, layers=2, prompt=prompt, n_new=32, mode="generate")
+    for r in out[1:]:
+        assert r["ids"] == out[0]["ids"] and r["first"] == out[0]["first"]  # ranks agree exactly
+    logits = np.concatenate([np.asarray(r["logits"], np.float32) for r in out])
+    assert float(np.abs(logits - lg_ref).max()) <= 2 * DRIFT_TINYLLAMA_2
+    assert out[0]["first"] == am_ref
+    agree = int(np.sum(np.asarray(out[0]["ids"]) == ids_ref))
+    assert agree >= 28, f"{agree}/32 greedy ids equal to the single-GPU run"
+
+
+def test_tp_peer_that_stops_gives_timeout(cuda):
+    out = _run(2, preset=2, layers=1, prompt=I.synth_ids(2, 8, 32000).tolist(), n_new=1, mode="timeout")
+    assert out[0]["code"] == 13  # ErrorTimeout
