@@ -1,10 +1,10 @@
 // Batch-1 decode projections: y = W.x over a row-major [N x K] weight, HBM-bound.
 //
-// One CTA per SM.  A producer warp streams the CTA's contiguous row range through a ring
+// One CTA per SM (two fit, so the next kernel's CTA can start early).  A producer warp streams the CTA's contiguous row range through a ring
 // of shared-memory stages with 1-D bulk copies (cp.async.bulk, evict_first), issuing the
 // first stages before griddepcontrol.wait so the weight stream of kernel n+1 overlaps the
-// tail of kernel n (programmatic dependent launch).  Eight consumer warps hold the
-// activation vector in registers (each lane owns 16-byte units u*256 + lane_id), dot every
+// tail of kernel n (programmatic dependent launch).  Sixteen consumer warps hold the
+// activation vector in registers (each lane owns 16-byte units u*512 + lane_id), dot every
 // staged row against it, reduce across warps and run a fused epilogue:
 //   kEpiStore   y[row] = round(dot)
 //   kEpiResid   r[row] += dot                           (O-proj and down-proj + residual)
@@ -20,7 +20,7 @@
 
 namespace inf {
 
-constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvConsumerWarps = 16;
 constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
 constexpr int kGemvThreads = kGemvConsumers + 32;
 constexpr int kGemvRingBytes = 96 * 1024;
@@ -36,7 +36,8 @@ template <int EPI> struct EpiTraits {
 };
 
 template <int UPL, int EPI> struct GemvShape {
-	static constexpr int kRpcBase = (8 / UPL) < 1 ? 1 : (8 / UPL);
+	// rows per chunk so that a chunk is ~32 KB: 2048 units of 16 bytes over the consumer lanes
+	static constexpr int kRpcBase = (2048 / (UPL * kGemvConsumers)) < 1 ? 1 : (2048 / (UPL * kGemvConsumers));
 	static constexpr int kRpc = (EpiTraits<EPI>::kPaired && kRpcBase < 2) ? 2 : kRpcBase; // rows per chunk
 };
 
