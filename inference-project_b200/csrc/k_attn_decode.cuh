@@ -29,6 +29,7 @@ constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxAcc = 4;          // (G * head_dim) / 256 outputs per thread
 constexpr int kAttnMaxPagesSplit = 16;  // mbarriers per CTA
 constexpr int kAttnSmemBudget = 64 * 1024;
+constexpr int kAttnTokIlp = 4;          // tokens a warp works on at once
 
 struct AttnDecodeArgs {
 	const void* q;           // [B][H*hd]
@@ -137,22 +138,35 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	// ---- scores
 	const int my_g = row_of_lane<G>(lane);
 	const bool g_writer = (lane & (32 / G - 1)) == 0;
+	// kAttnTokIlp tokens per warp iteration, so their loads, dots and shuffle trees interleave
 	int waited = 0;
-	for (int t = warp; t < n_tok; t += kAttnWarps) {
-		for (const int need = t / blk + 1; waited < need; ++waited)
+	for (int t0 = warp * kAttnTokIlp; t0 < n_tok; t0 += kAttnWarps * kAttnTokIlp) {
+		for (const int need = min(np, (t0 + kAttnTokIlp - 1) / blk + 1); waited < need; ++waited)
 			if (!abort_flag && !mbar_wait(&bars[waited], 0, (volatile int*)&abort_flag, a.err)) abort_flag = 1;
-		float kv[VPL];
-		load_vals<T, VPL>(reinterpret_cast<const T*>(kbuf) + (size_t)t * hd, d0, hd, kv);
-		float part[G];
+		float kv[kAttnTokIlp][VPL];
 #pragma unroll
-		for (int g = 0; g < G; ++g) {
-			float s = 0.0f;
-#pragma unroll
-			for (int j = 0; j < VPL; ++j) s = fmaf(qr[g][j], kv[j], s);
-			part[g] = s;
+		for (int u = 0; u < kAttnTokIlp; ++u) {
+			const int t = min(t0 + u, n_tok - 1);
+			load_vals<T, VPL>(reinterpret_cast<const T*>(kbuf) + (size_t)t * hd, d0, hd, kv[u]);
 		}
-		const float s = reduce_rows<G>(part, lane);
-		if (g_writer) s_s[my_g * max_tok + t] = (tok0 + t < ctx && !abort_flag) ? s * a.scale : -INFINITY;
+		float sc[kAttnTokIlp];
+#pragma unroll
+		for (int u = 0; u < kAttnTokIlp; ++u) {
+			float part[G];
+#pragma unroll
+			for (int g = 0; g < G; ++g) {
+				float s = 0.0f;
+#pragma unroll
+				for (int j = 0; j < VPL; ++j) s = fmaf(qr[g][j], kv[u][j], s);
+				part[g] = s;
+			}
+			sc[u] = reduce_rows<G>(part, lane);
+		}
+#pragma unroll
+		for (int u = 0; u < kAttnTokIlp; ++u) {
+			const int t = t0 + u;
+			if (g_writer && t < n_tok) s_s[my_g * max_tok + t] = (tok0 + t < ctx && !abort_flag) ? sc[u] * a.scale : -INFINITY;
+		}
 	}
 	// a warp that saw fewer pages than exist must still observe every page before the V pass
 	for (; waited < np; ++waited)
@@ -188,15 +202,22 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	for (int g = 0; g < G; ++g)
 #pragma unroll
 		for (int j = 0; j < VPL; ++j) acc[g][j] = 0.0f;
-	for (int t = warp; t < n_tok; t += kAttnWarps) {
-		float vv[VPL];
-		load_vals<T, VPL>(reinterpret_cast<const T*>(vbuf) + (size_t)t * hd, d0, hd, vv);
+	for (int t0 = warp * kAttnTokIlp; t0 < n_tok; t0 += kAttnWarps * kAttnTokIlp) {
+		float vv[kAttnTokIlp][VPL], pp[kAttnTokIlp][G];
 #pragma unroll
-		for (int g = 0; g < G; ++g) {
-			const float p = s_s[g * max_tok + t];
+		for (int u = 0; u < kAttnTokIlp; ++u) {
+			const bool in = t0 + u < n_tok;
+			const int t = in ? t0 + u : n_tok - 1;
+			load_vals<T, VPL>(reinterpret_cast<const T*>(vbuf) + (size_t)t * hd, d0, hd, vv[u]);
 #pragma unroll
-			for (int j = 0; j < VPL; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
+			for (int g = 0; g < G; ++g) pp[u][g] = in ? s_s[g * max_tok + t] : 0.0f;
 		}
+#pragma unroll
+		for (int u = 0; u < kAttnTokIlp; ++u)
+#pragma unroll
+			for (int g = 0; g < G; ++g)
+#pragma unroll
+				for (int j = 0; j < VPL; ++j) acc[g][j] = fmaf(pp[u][g], vv[u][j], acc[g][j]);
 	}
 	// cross-warp sum through shared memory (the page buffers are free once every warp is done)
 	__syncthreads();
