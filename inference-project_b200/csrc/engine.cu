@@ -77,6 +77,7 @@ struct InfEngine {
 	unsigned* lm_counter = nullptr;
 	float* attn_part = nullptr;  // split partials, sized for the larger of batch 1 and max_batch
 	int attn_splits_batch = 1;    // splits when max_batch tokens share one launch
+	int attn_max_pages_split_batch = 1;
 	float* logits_p = nullptr;    // [max_batch][Vl] batched-decode logits
 	uint32_t* argmax_p = nullptr; // [max_batch]
 	unsigned* attn_counters = nullptr;
@@ -200,7 +201,6 @@ Error_t launch_gemv(InfEngine* e, const GemvArgs& a)
 	if (upl <= 1) return launch_gemv_u<T, 1, EPI>(e, a);
 	if (upl <= 2) return launch_gemv_u<T, 2, EPI>(e, a);
 	if (upl <= 4) return launch_gemv_u<T, 4, EPI>(e, a);
-	if (upl <= 8) return launch_gemv_u<T, 8, EPI>(e, a);
 	return fail(ErrorUnsupported, "gemv: K=%d too long", a.K);
 }
 
@@ -601,14 +601,14 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 			a.hd = hd;
 			a.blk = (int)c.kv_block;
 			a.n_splits = e->attn_splits_batch;
-			a.max_pages_split = e->attn_max_pages_split;
+			a.max_pages_split = e->attn_max_pages_split_batch;
 			a.scale = (float)(1.0 / std::sqrt((double)hd));
 			a.part = e->attn_part;
 			a.counters = e->attn_counters;
 			a.out = e->attn_p;
 			a.err = e->err;
-			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2, e->attn_max_pages_split,
-			                                           e->attn_splits_batch);
+			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2,
+			                                           e->attn_max_pages_split_batch, e->attn_splits_batch);
 			const AttnKernel<bf16> ak = attn_decode_kernel<bf16>(e->Hl / e->KVl, hd);
 			if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
 			INF_CUDA_TRY(set_smem(ak, smem));
@@ -736,7 +736,9 @@ Error_t validate(const InfConfig& c)
 	}
 	if ((c.n_heads / c.n_kv_heads) * c.head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kAttnThreads * kAttnMaxAcc);
-	if (c.dim > 16384 || c.ffn_dim / tp > 16384) return fail(ErrorUnsupported, "dim/ffn above 16384");
+	const u32 max_k = c.dtype == InfBF16 ? 16384 : 8192; // one 16-byte unit per consumer lane and 4 per row
+	if (c.dim > max_k || c.ffn_dim / tp > max_k || (c.n_heads / tp) * c.head_dim > max_k)
+		return fail(ErrorUnsupported, "dim, ffn_dim or heads*head_dim above %u", max_k);
 	if (tp > (u32)kTpMax) return fail(ErrorUnsupported, "tp_size above %d", kTpMax);
 	if (!(c.norm_eps >= 0.0f) || !(c.rope_theta > 0.0f)) return fail(ErrorBadConfig, "eps/theta");
 	return Success;
@@ -886,13 +888,10 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	(void)G;
 	// splits: ~2 CTAs per SM over the KV heads of one token, at most one page per split
 	// about one CTA per SM over the KV heads of one token, each split within the smem budget
-	e->attn_max_pages_split = attn_decode_max_pages_split((int)c.kv_block, (int)hd, e->esz);
-	e->attn_splits = std::max((e->sm_count + e->KVl - 1) / e->KVl,
-	                          (e->pages_per_seq + e->attn_max_pages_split - 1) / e->attn_max_pages_split);
-	e->attn_splits = std::max(1, std::min(e->attn_splits, e->pages_per_seq));
-	e->attn_splits_batch = std::max((e->sm_count + e->KVl * (int)c.max_batch - 1) / (e->KVl * (int)c.max_batch),
-	                                (e->pages_per_seq + e->attn_max_pages_split - 1) / e->attn_max_pages_split);
-	e->attn_splits_batch = std::max(1, std::min(e->attn_splits_batch, e->pages_per_seq));
+	attn_decode_plan(e->sm_count, e->KVl, 1, e->pages_per_seq, (int)c.kv_block, (int)hd, e->esz, &e->attn_splits,
+	                 &e->attn_max_pages_split);
+	attn_decode_plan(e->sm_count, e->KVl, (int)c.max_batch, e->pages_per_seq, (int)c.kv_block, (int)hd, e->esz,
+	                 &e->attn_splits_batch, &e->attn_max_pages_split_batch);
 	const u64 part_floats = std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * e->attn_splits_batch) * (hd + 2);
 	// multi-token passes run on the tensor cores (bf16 models); fp32 models feed tokens one by one
 	e->chunk = c.dtype == InfBF16 ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u)) : 0;
@@ -1571,10 +1570,8 @@ Error_t attn_plan(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 k
 	if ((kv_block * head_dim * esz) % 16) return fail(ErrorUnsupported, "attention: page block not a multiple of 16 bytes");
 	int sms = 148, dev = 0;
 	if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-	p->max_pages_split = attn_decode_max_pages_split((int)kv_block, (int)head_dim, esz);
-	const int per_tok = std::max(1, (sms + (int)(n_kv_heads * n_tokens) - 1) / (int)(n_kv_heads * n_tokens));
-	p->splits = std::max(per_tok, ((int)pages_per_seq + p->max_pages_split - 1) / p->max_pages_split);
-	p->splits = std::max(1, std::min(p->splits, (int)pages_per_seq));
+	attn_decode_plan(sms, (int)n_kv_heads, (int)n_tokens, (int)pages_per_seq, (int)kv_block, (int)head_dim, esz,
+	                 &p->splits, &p->max_pages_split);
 	p->part_bytes = (size_t)n_tokens * n_heads * p->splits * (head_dim + 2) * sizeof(float);
 	p->counter_bytes = (size_t)n_tokens * n_kv_heads * sizeof(unsigned) + 16; // + error word
 	p->smem = attn_decode_smem_bytes((int)G, (int)head_dim, (int)kv_block, esz, p->max_pages_split, p->splits);

@@ -28,7 +28,7 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxAcc = 4;          // (G * head_dim) / 256 outputs per thread
 constexpr int kAttnMaxPagesSplit = 16;  // mbarriers per CTA
-constexpr int kAttnSmemBudget = 64 * 1024;
+constexpr int kAttnSmemBudget = 96 * 1024; // page buffers of one CTA
 constexpr int kAttnTokIlp = 4;          // tokens a warp works on at once
 
 struct AttnDecodeArgs {
@@ -50,12 +50,30 @@ struct AttnDecodeArgs {
 // head_dim values per lane of a warp
 inline int attn_vpl(int hd) { return hd <= 32 ? 1 : hd <= 64 ? 2 : hd <= 128 ? 4 : 8; }
 
-// page buffers, also reused for the P.V reduction and the split combine
-__host__ __device__ inline size_t attn_region_bytes(int G, int hd, int blk, size_t esz, int max_pages_split)
+constexpr size_t kAttnCombineStageMax = 96 * 1024; // larger split partials are combined from global memory
+
+// bytes of one (token, KV head)'s split partials, and whether the combine stages them
+__host__ __device__ inline size_t attn_combine_bytes(int G, int hd, int n_splits)
 {
-	const size_t kv = 2 * (size_t)max_pages_split * blk * hd * esz;
+	return (size_t)G * n_splits * (hd + 2) * sizeof(float);
+}
+__host__ __device__ inline bool attn_combine_staged(int G, int hd, int n_splits)
+{
+	const size_t b = attn_combine_bytes(G, hd, n_splits);
+	return b <= kAttnCombineStageMax && (b & 15) == 0;
+}
+
+// page buffers, also reused for the P.V reduction and, when staged, the split combine
+__host__ __device__ inline size_t attn_region_bytes(int G, int hd, int blk, size_t esz, int max_pages_split, int n_splits)
+{
+	size_t r = 2 * (size_t)max_pages_split * blk * hd * esz;
 	const size_t pv = (size_t)kAttnWarps * G * hd * sizeof(float);
-	return ((kv > pv ? kv : pv) + 15) & ~(size_t)15;
+	r = r > pv ? r : pv;
+	if (attn_combine_staged(G, hd, n_splits)) {
+		const size_t cb = attn_combine_bytes(G, hd, n_splits);
+		r = r > cb ? r : cb;
+	}
+	return (r + 15) & ~(size_t)15;
 }
 
 // VPL consecutive head_dim values of one K/V row as floats (lanes past head_dim read nothing)
@@ -76,7 +94,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	const int max_tok = a.max_pages_split * blk;
 	uint8_t* kbuf = sm_raw;                                        // [max_pages_split][blk][hd]
 	uint8_t* vbuf = kbuf + (size_t)a.max_pages_split * blk_bytes;
-	const size_t region = attn_region_bytes(G, hd, blk, sizeof(T), a.max_pages_split);
+	const size_t region = attn_region_bytes(G, hd, blk, sizeof(T), a.max_pages_split, a.n_splits);
 	float* s_s = reinterpret_cast<float*>(sm_raw + region);       // [G][max_tok]
 	float* m_s = s_s + G * max_tok;                                // [G]
 	float* l_s = m_s + G;                                          // [G]
@@ -253,13 +271,16 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 	__threadfence();
 
 	// combine.  The G heads' partials of this (token, KV head) are one contiguous block of
-	// G * n_splits * (hd + 2) floats; copy it into the (now idle) page buffers with
-	// independent 16-byte loads, eight in flight per thread, then reduce from shared memory.
-	float* pc = reinterpret_cast<float*>(sm_raw);
+	// G * n_splits * (hd + 2) floats.  When it fits the region (sized for it on the host with
+	// the same rule) it is copied into the idle page buffers with independent 16-byte loads,
+	// eight in flight per thread; otherwise the reduction reads it from global memory.
+	const bool staged = attn_combine_staged(G, hd, a.n_splits);
+	const float* pc = staged ? reinterpret_cast<const float*>(sm_raw)
+	                         : a.part + (((size_t)b * a.H + kvh * G) * a.n_splits) * hd2;
 	const size_t n_part = (size_t)G * a.n_splits * hd2;
-	if (n_part * sizeof(float) <= 2 * (size_t)a.max_pages_split * blk_bytes && (n_part & 3) == 0) {
+	if (staged) {
 		const float4* src = reinterpret_cast<const float4*>(a.part + (((size_t)b * a.H + kvh * G) * a.n_splits) * hd2);
-		float4* dst = reinterpret_cast<float4*>(pc);
+		float4* dst = reinterpret_cast<float4*>(sm_raw);
 		const int n4 = (int)(n_part >> 2);
 		for (int base = 0; base < n4; base += 8 * kAttnThreads) {
 			float4 r[8];
@@ -274,23 +295,22 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 				if (idx < n4) dst[idx] = r[u];
 			}
 		}
-	} else {
-		const float* src = a.part + (((size_t)b * a.H + kvh * G) * a.n_splits) * hd2;
-		for (size_t idx = tid; idx < n_part; idx += kAttnThreads) pc[idx] = __ldcg(src + idx);
 	}
 	__syncthreads();
+	// other CTAs wrote the partials: from global memory they are read past L1
+	auto rd = [&](const float* p) { return staged ? *p : __ldcg(p); };
 	// weights exp(m_s - M) / L once per (head, split)
 	for (int g = warp; g < G; g += kAttnWarps) {
 		const float* pr = pc + (size_t)g * a.n_splits * hd2;
 		float M = -INFINITY;
-		for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, pr[(size_t)s * hd2 + hd]);
+		for (int s = lane; s < a.n_splits; s += 32) M = fmaxf(M, rd(pr + (size_t)s * hd2 + hd));
 		M = warp_max(M);
 		float L = 0.0f;
 		for (int s = lane; s < a.n_splits; s += 32) {
-			const float ms = pr[(size_t)s * hd2 + hd];
+			const float ms = rd(pr + (size_t)s * hd2 + hd);
 			const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
 			w_s[g * a.n_splits + s] = w;
-			L += w * pr[(size_t)s * hd2 + hd + 1];
+			L += w * rd(pr + (size_t)s * hd2 + hd + 1);
 		}
 		L = warp_sum(L);
 		__syncwarp();
@@ -306,10 +326,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
 		float v0 = 0.0f, v1 = 0.0f;
 		int s = 0;
 		for (; s + 1 < a.n_splits; s += 2) {
-			v0 = fmaf(w[s], pr[(size_t)s * hd2], v0);
-			v1 = fmaf(w[s + 1], pr[(size_t)(s + 1) * hd2], v1);
+			v0 = fmaf(w[s], rd(pr + (size_t)s * hd2), v0);
+			v1 = fmaf(w[s + 1], rd(pr + (size_t)(s + 1) * hd2), v1);
 		}
-		if (s < a.n_splits) v0 = fmaf(w[s], pr[(size_t)s * hd2], v0);
+		if (s < a.n_splits) v0 = fmaf(w[s], rd(pr + (size_t)s * hd2), v0);
 		Store<T>::put(ob + (size_t)(kvh * G + g) * hd + i, v0 + v1);
 	}
 	if (tid == 0) a.counters[b * a.KV + kvh] = 0u;
@@ -322,9 +342,23 @@ inline int attn_decode_max_pages_split(int blk, int hd, size_t esz)
 	return (int)std::min<size_t>(kAttnMaxPagesSplit, std::max<size_t>(1, kAttnSmemBudget / page));
 }
 
+// Splits per (token, KV head): at most one CTA per SM when the context fits (so the next
+// kernel's CTA can start beside it), more when a split would exceed the page budget.  The
+// page buffers are sized for the pages a split actually needs.
+inline void attn_decode_plan(int sms, int kv_heads, int tokens, int pages_per_seq, int blk, int hd, size_t esz,
+                             int* splits, int* max_pages_split)
+{
+	const int budget = attn_decode_max_pages_split(blk, hd, esz);
+	int s = std::max(1, sms / std::max(1, kv_heads * tokens));
+	s = std::max(s, (pages_per_seq + budget - 1) / budget);
+	s = std::min(s, pages_per_seq);
+	*splits = s;
+	*max_pages_split = (pages_per_seq + s - 1) / s;
+}
+
 inline size_t attn_decode_smem_bytes(int G, int hd, int blk, size_t esz, int max_pages_split, int n_splits)
 {
-	return attn_region_bytes(G, hd, blk, esz, max_pages_split) +
+	return attn_region_bytes(G, hd, blk, esz, max_pages_split, n_splits) +
 	       sizeof(float) * ((size_t)G * max_pages_split * blk + 2 * G + (size_t)G * n_splits + 2) + 8 +
 	       kAttnMaxPagesSplit * sizeof(uint64_t);
 }

@@ -1,6 +1,6 @@
 // Batch-1 decode projections: y = W.x over a row-major [N x K] weight, HBM-bound.
 //
-// One CTA per SM (two fit, so the next kernel's CTA can start early).  A producer warp streams the CTA's contiguous row range through a ring
+// One CTA per SM.  A producer warp streams the CTA's contiguous row range through a ring
 // of shared-memory stages with 1-D bulk copies (cp.async.bulk, evict_first), issuing the
 // first stages before griddepcontrol.wait so the weight stream of kernel n+1 overlaps the
 // tail of kernel n (programmatic dependent launch).  Sixteen consumer warps hold the
