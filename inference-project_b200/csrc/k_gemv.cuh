@@ -386,9 +386,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 				const int k = i / n_rows, r = i % n_rows;
 				c.inbox[k][((size_t)par * c.size + c.rank) * c.dim + r0 + r] = tp_stage[r];
 			}
-			__threadfence_system();
+			// the barrier orders every thread's peer stores before thread 0's fence and
+			// release stores (one system-scope fence per CTA, not one per thread)
 			named_bar_sync(1, kGemvConsumers);
 			if (ct == 0) {
+				__threadfence_system();
 				for (int k = 0; k < c.size; ++k) st_release_sys(c.flags[k] + c.rank * kTpMaxCtas + blockIdx.x, round);
 				for (int k = 0; k < c.size; ++k)
 					if (!tp_wait_flag(c.flags[c.rank] + k * kTpMaxCtas + blockIdx.x, round, a.err)) *abort_flag = 1;

@@ -93,9 +93,9 @@ __global__ void __launch_bounds__(256) k_tp_allreduce_add(TpComm c, int n, unsig
 			for (int k = 0; k < N; ++k) c.red[k][i] = v;
 		}
 	}
-	__threadfence_system();
-	__syncthreads();
+	__syncthreads(); // orders every thread's peer stores before thread 0's fence and release
 	if (threadIdx.x == 0) {
+		__threadfence_system();
 		for (int k = 0; k < N; ++k) st_release_sys(c.done[k] + me * kTpMaxCtas + g, round);
 		for (int k = 0; k < N; ++k)
 			if (!tp_wait_flag(c.done[me] + k * kTpMaxCtas + g, round, err)) ok = 0;
