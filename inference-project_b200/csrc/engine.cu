@@ -901,7 +901,7 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	const u64 w_total = (2ull * c.vocab_size * d) * es + d * es + L * w_layer; // embed is full, LM head is a shard
 	const u64 page_elems = (u64)e->KVl * c.kv_block * hd;
 	const u64 kv_total = 2ull * L * e->n_pages * page_elems * es;
-	const u64 comm = c.tp_size > 1 ? (2ull * c.tp_size * d * 4 + 2ull * c.tp_size * kTpMaxCtas * 4 + 64ull * c.tp_size +
+	const u64 comm = c.tp_size > 1 ? (2ull * c.tp_size * d * 8 + 2ull * c.tp_size * kTpMaxCtas * 4 + 64ull * c.tp_size +
 	                                   (e->chunk > 0 ? 2ull * (u64)(c.prefill_chunk ? c.prefill_chunk : 4096) * d * 4 : 0) + 8 * 256)
 	                                : 0;
 	const u64 batch_bufs = c.max_batch > 1 ? (u64)c.max_batch * ((u64)e->Vl * 4 + 4) + 512 : 0;
@@ -970,8 +970,7 @@ Error_t engine_build(InfEngine* e, u64 seed)
 		t.size = 1; // becomes tp_size in inf_tp_connect
 		t.dim = (int)d;
 		const int r = (int)c.tp_rank, N = (int)c.tp_size;
-		P.push(&t.inbox[r], 2ull * N * d * 4);
-		P.push(&t.flags[r], (u64)N * kTpMaxCtas * 4);
+		P.push(&t.inbox[r], 2ull * N * d * 8);
 		P.push(&t.am_inbox[r], 2ull * N * 8);
 		P.push(&t.am_flags[r], (u64)N * 4);
 		P.push(&t.ready[r], (u64)N * 4);
@@ -1373,7 +1372,6 @@ Error_t inf_tp_connect(Model* model, const void* handles, u32 n_ranks)
 			base = (uint8_t*)p;
 		}
 		t.inbox[k] = rebase(e->tpc.inbox[me], base);
-		t.flags[k] = rebase(e->tpc.flags[me], base);
 		t.am_inbox[k] = rebase(e->tpc.am_inbox[me], base);
 		t.am_flags[k] = rebase(e->tpc.am_flags[me], base);
 		t.ready[k] = rebase(e->tpc.ready[me], base);

@@ -376,31 +376,30 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 
 	if constexpr (EPI == kEpiResid) {
 		if (tp_on) {
-			// fused all-reduce: push this CTA's rows to every rank, flag, wait for the same CTA
-			// of every rank, then sum the ranks' partials in rank order (identical on all ranks)
+			// fused all-reduce: every rank's partials for this CTA's rows go to every rank as
+			// (value, round) slots; each rank sums the ranks' values in rank order (identical on
+			// all ranks).  No flag and no fence: a slot is complete when it carries the round.
 			const TpComm& c = a.tp;
 			const unsigned round = tp_round(c, a.tp_round_index);
 			const int par = (int)(round & 1u);
 			named_bar_sync(1, kGemvConsumers);
 			for (int i = ct; i < n_rows * c.size; i += kGemvConsumers) {
 				const int k = i / n_rows, r = i % n_rows;
-				c.inbox[k][((size_t)par * c.size + c.rank) * c.dim + r0 + r] = tp_stage[r];
+				st_relaxed_sys_u64(c.inbox[k] + ((size_t)par * c.size + c.rank) * c.dim + r0 + r, ll_pack(tp_stage[r], round));
 			}
-			// the barrier orders every thread's peer stores before thread 0's fence and
-			// release stores (one system-scope fence per CTA, not one per thread)
-			named_bar_sync(1, kGemvConsumers);
-			if (ct == 0) {
-				__threadfence_system();
-				for (int k = 0; k < c.size; ++k) st_release_sys(c.flags[k] + c.rank * kTpMaxCtas + blockIdx.x, round);
-				for (int k = 0; k < c.size; ++k)
-					if (!tp_wait_flag(c.flags[c.rank] + k * kTpMaxCtas + blockIdx.x, round, a.err)) *abort_flag = 1;
+			// collect: thread i waits for (rank k, row r); the sums are formed in rank order
+			float* recv = wpart; // the epilogue window is idle now: [size][n_rows]
+			bool ok = true;
+			for (int i = ct; i < n_rows * c.size; i += kGemvConsumers) {
+				const int k = i / n_rows, r = i % n_rows;
+				recv[i] = ll_wait(c.inbox[c.rank] + ((size_t)par * c.size + k) * c.dim + r0 + r, round, a.err, &ok);
 			}
+			if (!ok) *abort_flag = 1;
 			named_bar_sync(1, kGemvConsumers);
 			if (!*abort_flag) {
-				const float* in = c.inbox[c.rank] + (size_t)par * c.size * c.dim;
 				for (int r = ct; r < n_rows; r += kGemvConsumers) {
 					float v = 0.0f;
-					for (int k = 0; k < c.size; ++k) v += __ldcv(in + (size_t)k * c.dim + r0 + r);
+					for (int k = 0; k < c.size; ++k) v += recv[k * n_rows + r];
 					a.resid[r0 + r] += v;
 				}
 			}
@@ -430,8 +429,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 					const TpComm& c = a.tp;
 					const unsigned round = tp_round(c, kTpRoundLm);
 					const int par = (int)(*c.epoch & 1u);
+					// one thread: its key stores are ordered before its own release stores
 					for (int k = 0; k < c.size; ++k) c.am_inbox[k][par * c.size + c.rank] = fin;
-					__threadfence_system();
 					for (int k = 0; k < c.size; ++k) st_release_sys(c.am_flags[k] + c.rank, round);
 					bool ok = true;
 					for (int k = 0; k < c.size; ++k) ok = tp_wait_flag(c.am_flags[c.rank] + k, round, a.err) && ok;

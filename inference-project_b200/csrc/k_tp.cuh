@@ -3,7 +3,7 @@
 // a system-scope release store of a round number as the flag, an acquire load to wait.
 //
 // Round numbers are shared by all ranks without communication: every rank runs the same
-// steps, so round = epoch * kTpRoundsPerStep + index, where epoch advances once per decode
+// steps, so round = (epoch + 1) * kTpRoundsPerStep + index, where epoch advances once per decode
 // step (by the LM-head kernel) and index is fixed per call site (2 * layer + {0, 1} for the
 // two all-reduces of a layer, kTpRoundLm for the argmax).
 #pragma once
@@ -21,9 +21,9 @@ constexpr int kTpMaxRowsCta = 256; // rows a GEMV CTA may own when it exchanges 
 struct TpComm {
 	int rank, size;
 	const uint32_t* epoch;                 // device counter, +1 per decode step
-	// decode-step all-reduce of [dim] fp32 partials, double-buffered by round parity
-	float* inbox[kTpMax];                  // rank k's inbox base: [2][size][dim]
-	unsigned* flags[kTpMax];               // rank k's flags: [size][kTpMaxCtas]
+	// decode-step all-reduce of [dim] fp32 partials, double-buffered by round parity; each
+	// slot is one 8-byte store of (value bits, round) so it carries its own flag
+	unsigned long long* inbox[kTpMax];     // rank k's inbox base: [2][size][dim]
 	// greedy argmax across vocabulary shards
 	unsigned long long* am_inbox[kTpMax];  // rank k's: [2][size]
 	unsigned* am_flags[kTpMax];            // rank k's: [size]
@@ -39,6 +39,39 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
 {
 	asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
+{
+	asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p)
+{
+	unsigned long long v;
+	asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+	return v;
+}
+__device__ __forceinline__ unsigned long long ll_pack(float v, unsigned round)
+{
+	return ((unsigned long long)round << 32) | __float_as_uint(v);
+}
+
+// Bounded wait until an (value, round) slot carries `round`; returns the value (0 and
+// kDevTimeout if the peer never writes it).
+__device__ __forceinline__ float ll_wait(const unsigned long long* slot, unsigned round, int* err, bool* ok)
+{
+	unsigned long long v = ld_relaxed_sys_u64(slot);
+	if ((unsigned)(v >> 32) != round) {
+		const uint64_t t0 = global_timer_ns();
+		while ((unsigned)((v = ld_relaxed_sys_u64(slot)) >> 32) != round) {
+			if (global_timer_ns() - t0 > kWaitLimitNs) {
+				report_err(err, kDevTimeout);
+				*ok = false;
+				return 0.0f;
+			}
+		}
+	}
+	return __uint_as_float((unsigned)v);
+}
+
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
 {
 	unsigned v;
@@ -57,12 +90,12 @@ __device__ __forceinline__ bool tp_wait_flag(const unsigned* flag, unsigned roun
 			report_err(err, kDevTimeout);
 			return false;
 		}
-		__nanosleep(64);
 	}
 	return true;
 }
 
-__device__ __forceinline__ unsigned tp_round(const TpComm& c, int index) { return *c.epoch * kTpRoundsPerStep + index; }
+// never 0: exchange buffers start zeroed, and a zero round would look complete
+__device__ __forceinline__ unsigned tp_round(const TpComm& c, int index) { return (*c.epoch + 1u) * kTpRoundsPerStep + index; }
 
 // Two-shot all-reduce of part[0..n) across ranks, added into dst (every rank ends with the
 // same dst: slices are reduced in rank order and the reduced values are copied, not
