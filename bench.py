@@ -27,6 +27,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "inference-project_b200"))
 
 METRIC = "batch-1 decode tokens/s and % of HBM roofline (Llama-3-8B shape, bf16), TP 1/2/4/8"
+# DRAM bytes (read + write) that ncu counted for one gate/up + SwiGLU launch at TP 1
+# (234.96 MB read + 3.38 MB write; the algorithmic figure is 234.9 MB)
+GATEUP_NCU_TRAFFIC = 238.34e6
 PROMPT = 2048
 DECODE_STEPS = 1024
 
@@ -248,7 +251,10 @@ def run_ours(args, rank: int, world: int, dist):
                        "step_roofline_frac": step_gbs / (peak * world), "prefill_s": prefill_s,
                        "kernel_ms_per_step": prof},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": (achieved / peak) if achieved else None, "traffic": None,
+                         "frac": (achieved / peak) if achieved else None,
+                         # dram__bytes_read.sum + dram__bytes_write.sum of one full-width launch
+                         # (ncu capture of the same kernel and shape), scaled to this rank's shard
+                         "traffic": GATEUP_NCU_TRAFFIC * Fl / F, "traffic_unit": "bytes per launch",
                          "kernel": f"k_gemv gate/up+SwiGLU (per launch: 2*{Fl}*4096 bf16 weights)",
                          "peak_kind": peak_kind},
             "cpu_baseline": cpu,

@@ -204,6 +204,17 @@ Error_t launch_gemv(InfEngine* e, const GemvArgs& a)
 	return fail(ErrorUnsupported, "gemv: K=%d too long", a.K);
 }
 
+// the projection that follows in the decode step, for the producer's L2 warm-up
+void gemv_next(InfEngine* e, GemvArgs& a, const void* W, int N, int K, bool paired)
+{
+	a.nx_W = W;
+	a.nx_N = N;
+	a.nx_K = K;
+	a.nx_unit_rows = paired ? 2 : 1;
+	a.nx_grid = std::max(1, std::min(e->sm_count, N / a.nx_unit_rows));
+	a.nx_bytes = kGemvNextPrefetch;
+}
+
 GemvArgs gemv_base(InfEngine* e, const void* W, int N, int K)
 {
 	GemvArgs a;
@@ -310,6 +321,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.tp_round_index = 2 * (int)l;
 			a.xin = e->attn;
 			a.resid = e->resid;
+			gemv_next(e, a, L.wgu, 2 * e->Fl, d, true);
 			INF_TRY(prof_begin(e));
 			INF_TRY((launch_gemv<T, kEpiResid>(e, a)));
 			INF_TRY(prof_end(e, InfKO));
@@ -320,6 +332,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.resid_in = e->resid;
 			a.gain = L.ffn_norm;
 			a.out = e->h;
+			gemv_next(e, a, L.wd, d, e->Fl, false);
 			INF_TRY(prof_begin(e));
 			INF_TRY((launch_gemv<T, kEpiSwiglu>(e, a)));
 			INF_TRY(prof_end(e, InfKGateUp));
@@ -330,6 +343,8 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.tp_round_index = 2 * (int)l + 1;
 			a.xin = e->h;
 			a.resid = e->resid;
+			if (l + 1 < c.n_layers) gemv_next(e, a, e->layers[l + 1].wqkv, (e->Hl + 2 * e->KVl) * hd, d, true);
+			else gemv_next(e, a, e->lm_head, e->Vl, d, false);
 			INF_TRY(prof_begin(e));
 			INF_TRY((launch_gemv<T, kEpiResid>(e, a)));
 			INF_TRY(prof_end(e, InfKDown));

@@ -27,6 +27,7 @@ constexpr int kGemvRingBytes = 96 * 1024;
 constexpr int kGemvMaxStages = 8;
 constexpr int kGemvPrefetch = 4;    // chunks prefetched into L2 beyond the ring
 constexpr int kGemvFlushRows = 128; // rows per deferred-epilogue window
+constexpr uint32_t kGemvNextPrefetch = 192 * 1024; // bytes of the next projection warmed per CTA
 
 enum EpiKind : int { kEpiStore = 0, kEpiResid = 1, kEpiQkv = 2, kEpiSwiglu = 3, kEpiLogits = 4 };
 
@@ -77,6 +78,13 @@ struct GemvArgs {
 	TpComm tp;
 	int tp_round_index;
 	int row_base;
+	// the next projection of the step: once its last chunk is issued, the producer warms L2
+	// with the head of the slice that the same CTA index owns there.  Two projection CTAs do
+	// not always fit on one SM, so the next kernel's own stream may only start when this
+	// kernel's CTAs leave; the warm-up keeps HBM busy across that boundary.
+	const void* nx_W;
+	int nx_N, nx_K, nx_unit_rows, nx_grid;
+	uint32_t nx_bytes; // multiple of 16
 };
 
 // Sum of RPC per-lane row partials across the warp, transposed: at the first log2(RPC)
@@ -212,6 +220,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 				const int pf = i + S + kGemvPrefetch;
 				if (pf < n_chunks) bulk_prefetch_l2(wbase + (size_t)pf * RPC * row_bytes, chunk_bytes(pf));
 				++issued;
+			}
+			if (a.nx_W && issued == n_chunks && (int)blockIdx.x < a.nx_grid) {
+				const int tu = a.nx_N / a.nx_unit_rows;
+				const int q0 = (int)(((long long)blockIdx.x * tu) / a.nx_grid) * a.nx_unit_rows;
+				const int q1 = (int)(((long long)(blockIdx.x + 1) * tu) / a.nx_grid) * a.nx_unit_rows;
+				const size_t nrb = (size_t)a.nx_K * sizeof(T);
+				const uint8_t* p = reinterpret_cast<const uint8_t*>(a.nx_W) + (size_t)q0 * nrb;
+				size_t left = min((size_t)(q1 - q0) * nrb, (size_t)a.nx_bytes);
+				while (left > 0) {
+					const uint32_t n = (uint32_t)min(left, (size_t)32768);
+					bulk_prefetch_l2(p, n);
+					p += n;
+					left -= n;
+				}
 			}
 			// never leave the CTA with bulk copies in flight: wait for the last stages to land
 			for (int i = max(0, issued - S); i < issued; ++i) {
