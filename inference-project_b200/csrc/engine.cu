@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "k_attn_decode.cuh"
+#include "k_attn_cluster.cuh"
 #include "k_gemv.cuh"
 #include "k_attn_prefill.cuh"
 #include "k_gemm_tc.cuh"
@@ -86,6 +87,8 @@ struct InfEngine {
 	int max_out = 0;
 	int attn_splits = 1;
 	int attn_max_pages_split = 1;
+	int attn_cl_splits = 0;       // batch-1 decode attention as one cluster per KV head (0: split-K)
+	int attn_cl_pages = 0;
 	// multi-token (prefill) buffers, prefill_chunk rows each
 	int chunk = 0;
 	float* resid_p = nullptr;  // [chunk][d] f32
@@ -228,6 +231,78 @@ GemvArgs gemv_base(InfEngine* e, const void* W, int N, int K)
 	return a;
 }
 
+// --------------------------------------------------------------------------- cluster attention
+template <typename T>
+Error_t attn_cl_fit(InfEngine* e, int G, int hd, int cs, int mp, bool* ok)
+{
+	*ok = false;
+	const AttnKernel<T> k = attn_decode_cl_kernel<T>(G, hd);
+	if (!k) return Success;
+	const size_t smem = attn_cl_layout(G, hd, (int)e->cfg.kv_block, sizeof(T), mp, cs).total;
+	INF_CUDA_TRY(set_smem(k, smem));
+	if (cs > 8) INF_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+	cudaLaunchConfig_t lc = {};
+	lc.gridDim = dim3(cs, e->KVl, 1);
+	lc.blockDim = dim3(kAttnThreads);
+	lc.dynamicSmemBytes = smem;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeClusterDimension;
+	attr[0].val.clusterDim.x = cs;
+	attr[0].val.clusterDim.y = 1;
+	attr[0].val.clusterDim.z = 1;
+	lc.attrs = attr;
+	lc.numAttrs = 1;
+	int n = 0;
+	if (cudaOccupancyMaxActiveClusters(&n, k, &lc) != cudaSuccess) {
+		(void)cudaGetLastError(); // not placeable: use the split-K kernel
+		return Success;
+	}
+	*ok = n >= 1;
+	return Success;
+}
+
+Error_t attn_cl_choose(InfEngine* e, int G, int hd)
+{
+	e->attn_cl_splits = 0;
+	e->attn_cl_pages = 0;
+	for (int cs = kAttnClMaxSplits; cs >= 8; cs >>= 1) {
+		const int mp = attn_cl_pages_per_split(cs, e->pages_per_seq, (int)e->cfg.kv_block, hd, e->esz, G);
+		if (mp == 0) continue;
+		bool ok = false;
+		if (e->cfg.dtype == InfBF16) INF_TRY(attn_cl_fit<bf16>(e, G, hd, cs, mp, &ok));
+		else INF_TRY(attn_cl_fit<float>(e, G, hd, cs, mp, &ok));
+		if (!ok) continue;
+		e->attn_cl_splits = cs;
+		e->attn_cl_pages = mp;
+		return Success;
+	}
+	return Success;
+}
+
+// launch with a cluster of cluster_x CTAs along x and the programmatic-dependency edge
+template <typename... KArgs, typename... Args>
+cudaError_t launch_cluster(InfEngine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_x,
+                           Args&&... args)
+{
+	cudaLaunchConfig_t lc = {};
+	lc.gridDim = grid;
+	lc.blockDim = block;
+	lc.dynamicSmemBytes = smem;
+	lc.stream = e->stream;
+	cudaLaunchAttribute attr[2];
+	attr[0].id = cudaLaunchAttributeClusterDimension;
+	attr[0].val.clusterDim.x = cluster_x;
+	attr[0].val.clusterDim.y = 1;
+	attr[0].val.clusterDim.z = 1;
+	attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[1].val.programmaticStreamSerializationAllowed = 1;
+	lc.attrs = attr;
+	lc.numAttrs = e->profiling ? 1 : 2;
+	if (e->dry) return cudaSuccess;
+	e->launches++;
+	return cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...);
+}
+
 // --------------------------------------------------------------------------- decode step
 Error_t prof_begin(InfEngine* e)
 {
@@ -306,14 +381,27 @@ Error_t enqueue_decode_step(InfEngine* e)
 			a.counters = e->attn_counters;
 			a.out = e->attn;
 			a.err = e->err;
-			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
-			                                           e->attn_max_pages_split, e->attn_splits);
-			const AttnKernel<T> ak = attn_decode_kernel<T>(e->Hl / e->KVl, hd);
-			if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
-			INF_CUDA_TRY(set_smem(ak, smem));
-			INF_TRY(prof_begin(e));
-			INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
-			INF_TRY(prof_end(e, InfKAttn));
+			if (e->attn_cl_splits > 0) {
+				a.n_splits = e->attn_cl_splits;
+				a.max_pages_split = e->attn_cl_pages;
+				const int cs = e->attn_cl_splits;
+				const size_t smem = attn_cl_layout(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T), e->attn_cl_pages, cs).total;
+				const AttnKernel<T> ak = attn_decode_cl_kernel<T>(e->Hl / e->KVl, hd);
+				if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+				INF_CUDA_TRY(set_smem(ak, smem));
+				INF_TRY(prof_begin(e));
+				INF_CUDA_TRY(launch_cluster(e, ak, dim3(cs, e->KVl, 1), dim3(kAttnThreads), smem, cs, a));
+				INF_TRY(prof_end(e, InfKAttn));
+			} else {
+				const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
+				                                           e->attn_max_pages_split, e->attn_splits);
+				const AttnKernel<T> ak = attn_decode_kernel<T>(e->Hl / e->KVl, hd);
+				if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+				INF_CUDA_TRY(set_smem(ak, smem));
+				INF_TRY(prof_begin(e));
+				INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
+				INF_TRY(prof_end(e, InfKAttn));
+			}
 		}
 		// O-proj + residual
 		{
@@ -900,13 +988,15 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	e->n_pages = c.kv_pages ? (int)c.kv_pages : (int)(c.max_batch * (u32)e->pages_per_seq);
 	e->max_out = (int)c.max_seq;
 	const int G = e->Hl / e->KVl;
-	(void)G;
-	// splits: ~2 CTAs per SM over the KV heads of one token, at most one page per split
-	// about one CTA per SM over the KV heads of one token, each split within the smem budget
+	// split-K attention: about one CTA per SM over the KV heads of the tokens, each split
+	// within the shared-memory budget
 	attn_decode_plan(e->sm_count, e->KVl, 1, e->pages_per_seq, (int)c.kv_block, (int)hd, e->esz, &e->attn_splits,
 	                 &e->attn_max_pages_split);
 	attn_decode_plan(e->sm_count, e->KVl, (int)c.max_batch, e->pages_per_seq, (int)c.kv_block, (int)hd, e->esz,
 	                 &e->attn_splits_batch, &e->attn_max_pages_split_batch);
+	// batch-1 decode: one cluster per KV head when the longest context fits its shared memory
+	// and the GPU can place a cluster of that size
+	INF_TRY(attn_cl_choose(e, G, (int)hd));
 	const u64 part_floats = std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * e->attn_splits_batch) * (hd + 2);
 	// multi-token passes run on the tensor cores (bf16 models); fp32 models feed tokens one by one
 	e->chunk = c.dtype == InfBF16 ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u)) : 0;
