@@ -25,7 +25,7 @@ constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
 constexpr int kGemvThreads = kGemvConsumers + 32;
 constexpr int kGemvRingBytes = 96 * 1024;
 constexpr int kGemvMaxStages = 8;
-constexpr int kGemvPrefetch = 4;    // chunks prefetched into L2 beyond the ring
+constexpr int kGemvPrefetch = 2;    // chunks prefetched into L2 beyond the ring
 constexpr int kGemvFlushRows = 128; // rows per deferred-epilogue window
 constexpr uint32_t kGemvNextPrefetch = 192 * 1024; // bytes of the next projection warmed per CTA
 
