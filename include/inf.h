@@ -81,7 +81,14 @@ typedef struct InfConfig {
 	f32 init_std;       /* std of the synthetic weights */
 	u32 tp_rank;
 	u32 tp_size;
+	u32 prefill_attention; /* InfPrefillAttention */
 } InfConfig;
+
+/* Which kernel computes causal attention in prefill passes. */
+typedef enum InfPrefillAttention {
+	InfPrefillAttnAuto = 0, /* tensor cores (tcgen05/TMEM) for bf16 with head_dim 64 or 128, else SIMT */
+	InfPrefillAttnSimt = 1, /* the fp32 SIMT kernel (P kept in fp32) */
+} InfPrefillAttention;
 
 /* src/allocator.h:13-25 */
 typedef struct HostArena {

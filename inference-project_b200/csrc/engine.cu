@@ -21,6 +21,7 @@
 #include "k_attn_cluster.cuh"
 #include "k_gemv.cuh"
 #include "k_attn_prefill.cuh"
+#include "k_attn_prefill_tc.cuh"
 #include "k_gemm_tc.cuh"
 #include "k_small.cuh"
 #include "runtime.h"
@@ -87,6 +88,7 @@ struct InfEngine {
 	int max_out = 0;
 	int attn_splits = 1;
 	int attn_max_pages_split = 1;
+	bool pf_tc = false;           // prefill attention on the tensor cores (k_attn_prefill_tc.cuh)
 	int attn_cl_splits = 0;       // batch-1 decode attention as one cluster per KV head (0: split-K)
 	int attn_cl_pages = 0;
 	// multi-token (prefill) buffers, prefill_chunk rows each
@@ -541,8 +543,9 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 	const int d = (int)c.dim, hd = (int)c.head_dim, G = e->Hl / e->KVl;
 	INF_CUDA_TRY(launch(e, k_embed<bf16, float>, dim3((d + 255) / 256, T), dim3(256), 0, (const uint32_t*)e->d_ids, T, d,
 	                    c.vocab_size, (const bf16*)e->embed, e->resid_p, e->err));
-	const size_t pf_smem = attn_prefill_smem_bytes(G, hd, (int)c.kv_block);
-	INF_CUDA_TRY(set_smem(k_attn_prefill<bf16>, pf_smem));
+	const size_t pf_smem = e->pf_tc ? attn_prefill_tc_smem_bytes(hd) : attn_prefill_smem_bytes(G, hd, (int)c.kv_block);
+	if (e->pf_tc) INF_CUDA_TRY(set_smem(k_attn_prefill_tc, pf_smem));
+	else INF_CUDA_TRY(set_smem(k_attn_prefill<bf16>, pf_smem));
 	for (u32 l = 0; l < c.n_layers; ++l) {
 		const LayerW& L = e->layers[l];
 		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
@@ -585,7 +588,17 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 			a.scale = (float)(1.0 / std::sqrt((double)hd));
 			a.out = e->attn_p;
 			a.err = e->err;
-			INF_CUDA_TRY(launch(e, k_attn_prefill<bf16>, dim3(e->KVl, (T + kPfTq - 1) / kPfTq), dim3(kPfThreads), pf_smem, a));
+			if (e->pf_tc) {
+				// the layer's K and V pools as [pages * KV * blk rows][hd], boxes of blk rows x 64
+				const u64 rows = (u64)e->n_pages * e->KVl * c.kv_block;
+				CUtensorMap tk, tv;
+				INF_TRY(tensor_map_2d(&tk, L.kpool, rows, (u64)hd, c.kv_block));
+				INF_TRY(tensor_map_2d(&tv, L.vpool, rows, (u64)hd, c.kv_block));
+				const int tq = kPtRows / G;
+				INF_CUDA_TRY(launch(e, k_attn_prefill_tc, dim3(e->KVl, (T + tq - 1) / tq), dim3(kPtThreads), pf_smem, tk, tv, a));
+			} else {
+				INF_CUDA_TRY(launch(e, k_attn_prefill<bf16>, dim3(e->KVl, (T + kPfTq - 1) / kPfTq), dim3(kPfThreads), pf_smem, a));
+			}
 		}
 		{
 			TcArgs a = tc_base(e, T, d, e->Hl * hd, kTcResid);
@@ -997,6 +1010,8 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	// batch-1 decode: one cluster per KV head when the longest context fits its shared memory
 	// and the GPU can place a cluster of that size
 	INF_TRY(attn_cl_choose(e, G, (int)hd));
+	e->pf_tc = c.dtype == InfBF16 && c.prefill_attention == InfPrefillAttnAuto && (hd == 64 || hd == 128) &&
+	           kPtRows % G == 0 && c.kv_block % 8 == 0 && kPtKeys % c.kv_block == 0;
 	const u64 part_floats = std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * e->attn_splits_batch) * (hd + 2);
 	// multi-token passes run on the tensor cores (bf16 models); fp32 models feed tokens one by one
 	e->chunk = c.dtype == InfBF16 ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u)) : 0;

@@ -27,6 +27,7 @@ ERRORS = {
     14: "ErrorIo", 15: "ErrorUnsupported",
 }
 F32, BF16 = 0, 1
+PREFILL_ATTN_AUTO, PREFILL_ATTN_SIMT = 0, 1  # InfPrefillAttention
 KERNEL_KINDS = ["embed", "qkv", "attn", "o_proj", "gate_up", "down", "lm_head"]
 
 
@@ -42,7 +43,7 @@ class InfConfig(C.Structure):
         ("vocab_size", u32), ("dim", u32), ("n_layers", u32), ("n_heads", u32), ("n_kv_heads", u32),
         ("head_dim", u32), ("ffn_dim", u32), ("max_seq", u32), ("max_batch", u32), ("kv_block", u32),
         ("kv_pages", u32), ("prefill_chunk", u32), ("dtype", u32), ("norm_eps", f32), ("rope_theta", f32),
-        ("init_std", f32), ("tp_rank", u32), ("tp_size", u32),
+        ("init_std", f32), ("tp_rank", u32), ("tp_size", u32), ("prefill_attention", u32),
     ]
 
     def as_dict(self) -> dict:
