@@ -490,6 +490,23 @@ Error_t tensor_map_2d(CUtensorMap* m, const void* base, u64 rows, u64 cols, u32 
 	return Success;
 }
 
+// A layer's paged K or V pool [pages][KV][blk][hd] as a 4-D tensor (hd, row, head, page) with
+// boxes of 64 head dims x blk rows x 1 head x box_pages pages, SWIZZLE_128B.
+Error_t tensor_map_kv(CUtensorMap* m, const void* base, u32 hd, u32 blk, u32 kv, u32 pages, u32 box_pages)
+{
+	CUtensorMap dummy;
+	INF_TRY(tensor_map_2d(&dummy, base, 8, 64, 8)); // resolves the driver entry point
+	const cuuint64_t dims[4] = {hd, blk, kv, pages};
+	const cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)blk * hd * 2, (cuuint64_t)kv * blk * hd * 2};
+	const cuuint32_t box[4] = {64, blk, 1, box_pages};
+	const cuuint32_t estr[4] = {1, 1, 1, 1};
+	const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+	                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+	                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	if (r != CUDA_SUCCESS) return fail(ErrorCuda, "cuTensorMapEncodeTiled (K/V pool) failed (%d)", (int)r);
+	return Success;
+}
+
 // D[T x N] = X[T x K] . W[N x K]^T on the tensor cores, fused epilogue a.epi
 Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
 {
@@ -589,13 +606,16 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 			a.out = e->attn_p;
 			a.err = e->err;
 			if (e->pf_tc) {
-				// the layer's K and V pools as [pages * KV * blk rows][hd], boxes of blk rows x 64
-				const u64 rows = (u64)e->n_pages * e->KVl * c.kv_block;
-				CUtensorMap tk, tv;
-				INF_TRY(tensor_map_2d(&tk, L.kpool, rows, (u64)hd, c.kv_block));
-				INF_TRY(tensor_map_2d(&tv, L.vpool, rows, (u64)hd, c.kv_block));
+				// the layer's K and V pools, boxes of one tile's pages and of one page
+				const u32 bp = kPtKeys / c.kv_block;
+				CUtensorMap tk8, tk1, tv8, tv1;
+				INF_TRY(tensor_map_kv(&tk8, L.kpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, bp));
+				INF_TRY(tensor_map_kv(&tk1, L.kpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
+				INF_TRY(tensor_map_kv(&tv8, L.vpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, bp));
+				INF_TRY(tensor_map_kv(&tv1, L.vpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
 				const int tq = kPtRows / G;
-				INF_CUDA_TRY(launch(e, k_attn_prefill_tc, dim3(e->KVl, (T + tq - 1) / tq), dim3(kPtThreads), pf_smem, tk, tv, a));
+				INF_CUDA_TRY(launch(e, k_attn_prefill_tc, dim3(e->KVl, (T + tq - 1) / tq), dim3(kPtThreads), pf_smem, tk8, tk1,
+				                    tv8, tv1, a));
 			} else {
 				INF_CUDA_TRY(launch(e, k_attn_prefill<bf16>, dim3(e->KVl, (T + kPfTq - 1) / kPfTq), dim3(kPfThreads), pf_smem, a));
 			}

@@ -3,8 +3,9 @@
 // Flash attention over the paged KV cache.  A CTA owns 128 query rows: 128/G consecutive
 // tokens of one sequence times the G query heads that share one KV head, so each K/V tile is
 // read once for the whole GQA group.  Row r = tq * G + g.  Per tile of 128 keys (8 pages of 16):
-//   warp 0      loads the tile's K and V pages with 2-D TMA (SWIZZLE_128B boxes of 16 keys x 64
-//               head dims, no multicast) into a 2-stage ring;
+//   warp 0      loads the tile's K and V pages with 4-D TMA (SWIZZLE_128B boxes of 64 head dims
+//               x 16 keys x 8 consecutive pages, or one page per box when the ids are not
+//               consecutive; no multicast) into 2-stage K and V rings;
 //   warp 1      allocates TMEM (S: 128 columns, O: head_dim columns) and issues, from one
 //               thread, S = Q.K^T (both operands K-major) and O += P.V (P K-major from shared
 //               memory, V MN-major: the page rows are keys, contiguous along head_dim);
@@ -40,6 +41,23 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_lbo(uint32_t smem_addr, uint
 	return d;
 }
 
+// tcgen05.ld of 32 columns without the wait (several loads, then one tcgen05.wait::ld)
+__device__ __forceinline__ void tmem_ld_32cols_nowait(uint32_t taddr, float* v)
+{
+	uint32_t r[32];
+	asm volatile(
+	    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+	    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+	    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+	    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+	      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+	      "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+	      "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+	    : "r"(taddr));
+#pragma unroll
+	for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const float (&v)[32])
 {
 	uint32_t r[32];
@@ -57,6 +75,17 @@ __device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const float (&v)[
 	asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 4-D tiled TMA load (head_dim, row in page, KV head, page) of the paged K/V pool
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar,
+                                            uint64_t policy)
+{
+	asm volatile(
+	    "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+	    " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+	    "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+	    : "memory");
+}
+
 // byte offset of 16-byte chunk c (0..7) of row r inside a SWIZZLE_128B block of 128-byte rows
 __device__ __forceinline__ uint32_t sw128_off(int r, int c)
 {
@@ -64,25 +93,38 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c)
 }
 
 struct PtLayout {
-	size_t q, kv, p, bars, total;
-	uint32_t stage_bytes, halves;
+	size_t q, k, v, p, bars, total;
+	uint32_t tile_bytes, halves; // one K or V tile: halves x 16 KB
 };
 __host__ __device__ inline PtLayout pt_layout(int hd)
 {
 	PtLayout L;
 	L.halves = (uint32_t)(hd / 64);
-	L.stage_bytes = 2 * L.halves * kPtAtom; // K then V
+	L.tile_bytes = L.halves * kPtAtom;
 	L.q = 0;
-	L.kv = L.q + (size_t)L.halves * kPtAtom;
-	L.p = L.kv + (size_t)kPtStages * L.stage_bytes;
-	L.bars = L.p + 2 * (size_t)kPtAtom;
-	L.total = L.bars + 128;
+	L.k = L.q + L.tile_bytes;
+	L.v = L.k + (size_t)kPtStages * L.tile_bytes;
+	L.p = L.v + (size_t)kPtStages * L.tile_bytes;
+	L.bars = L.p + 2 * (size_t)2 * kPtAtom; // two P buffers of [128 rows x 128 keys]
+	L.total = L.bars + 256;
 	return L;
 }
 inline size_t attn_prefill_tc_smem_bytes(int hd) { return 1024 + pt_layout(hd).total; }
 
+__device__ __forceinline__ float ex2_approx(float x)
+{
+	float y;
+	asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+	return y;
+}
+
+// Largest growth of the running max (log2 units) absorbed without rescaling O: P values up to
+// 2^8 stay exact enough in bf16 and fp32, and O / l is unchanged in exact arithmetic.
+constexpr float kPtRescaleLog2 = 8.0f;
+
 __global__ void __launch_bounds__(kPtThreads, 1)
-    k_attn_prefill_tc(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+    k_attn_prefill_tc(const __grid_constant__ CUtensorMap tm_k8, const __grid_constant__ CUtensorMap tm_k1,
+                      const __grid_constant__ CUtensorMap tm_v8, const __grid_constant__ CUtensorMap tm_v1,
                       const AttnPrefillArgs a)
 {
 	extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -90,21 +132,27 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 	const int hd = a.hd, G = a.H / a.KV, blk = a.blk;
 	const PtLayout Ly = pt_layout(hd);
 	uint8_t* q_s = smem + Ly.q;
-	uint8_t* kv_s = smem + Ly.kv;
+	uint8_t* k_s = smem + Ly.k;
+	uint8_t* v_s = smem + Ly.v;
 	uint8_t* p_s = smem + Ly.p;
-	uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + Ly.bars);
-	uint64_t* kv_empty = kv_full + kPtStages;
-	uint64_t* bar_s = kv_empty + kPtStages;  // S ready (MMA -> softmax)
-	uint64_t* bar_p = bar_s + 1;             // P written, S consumed (softmax -> MMA), 128 arrivals
-	uint64_t* bar_o = bar_p + 1;             // P.V done (MMA -> softmax)
-	uint64_t* bar_q = bar_o + 1;             // Q staged, 128 arrivals
-	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + 1);
+	uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly.bars);
+	uint64_t* k_full = bars;       // [2] TMA -> MMA
+	uint64_t* k_empty = bars + 2;  // [2] S MMA done with the K tile
+	uint64_t* v_full = bars + 4;   // [2]
+	uint64_t* v_empty = bars + 6;  // [2] P.V MMA done with the V tile
+	uint64_t* s_full = bars + 8;   // [2] S buffer b ready (MMA -> softmax)
+	uint64_t* p_free = bars + 10;  // [2] P buffer b read by its P.V MMA
+	uint64_t* bar_p = bars + 12;   // P of tile j written, its S consumed (128 arrivals)
+	uint64_t* bar_o = bars + 13;   // P.V of tile j done
+	uint64_t* bar_q = bars + 14;   // Q staged (128 arrivals)
+	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 	volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int kvh = blockIdx.x;
 	const int tq_per = kPtRows / G;
-	const int t0 = blockIdx.y * tq_per;
+	// causal work grows with the token index: the last tokens' tiles are scheduled first
+	const int t0 = (gridDim.y - 1 - blockIdx.y) * tq_per;
 	const int n_tok = min(tq_per, a.T - t0);
 	const int slot = a.tok_slot[t0];
 	const int last_pos = a.tok_pos[t0 + n_tok - 1];
@@ -112,11 +160,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 	const int pages_tile = kPtKeys / blk;
 
 	if (threadIdx.x == 0) {
-		for (int s = 0; s < kPtStages; ++s) {
-			mbar_init(&kv_full[s], 1);
-			mbar_init(&kv_empty[s], 1);
-		}
-		mbar_init(bar_s, 1);
+		for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
 		mbar_init(bar_p, 128);
 		mbar_init(bar_o, 1);
 		mbar_init(bar_q, 128);
@@ -125,7 +169,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 	}
 	if (warp == 1) {
 		asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-		             "r"(256)
+		             "r"(512)
 		             : "memory");
 		asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 	}
@@ -133,26 +177,32 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 	__syncthreads();
 	tc_fence_after();
 	const uint32_t tmem = *tmem_slot;
-	const uint32_t tmem_s = tmem, tmem_o = tmem + kPtKeys;
+	const uint32_t tmem_o = tmem + 2 * kPtKeys; // S buffers at columns 0 and 128
 	pdl_wait(); // queries and this chunk's keys come from the QKV kernel before it
 	pdl_trigger();
 
 	if (warp == 0) {
-		// ---------------- TMA producer: K and V pages of each tile
+		// ---------------- TMA producer: the K pages, then the V pages, of each tile
 		if (lane == 0) {
 			const uint64_t pol = policy_evict_last(); // the tile is re-read by the next query tiles
 			const int* bt = a.block_table + (size_t)slot * a.pages_per_seq;
 			int first = bt[0];
 			if (first < 0 || first >= a.max_pages) first = 0;
-			int issued = 0;
-			for (int j = 0; j < n_tiles; ++j) {
-				const int s = j % kPtStages;
-				if (j >= kPtStages && !mbar_wait(&kv_empty[s], (uint32_t)((j / kPtStages) - 1) & 1u, abort_flag, a.err)) break;
-				uint8_t* ks = kv_s + (size_t)s * Ly.stage_bytes;
-				uint8_t* vs = ks + (size_t)Ly.halves * kPtAtom;
-				mbar_arrive_expect_tx(&kv_full[s], Ly.stage_bytes);
+			// A tile whose pages have consecutive ids (a sequence prefilled into a fresh cache) is
+			// one box of pages_tile pages per 64 head dims; otherwise one box per page.
+			auto load = [&](const CUtensorMap* tm8, const CUtensorMap* tm1, uint8_t* dst, uint64_t* bar, int j) {
+				mbar_arrive_expect_tx(bar, Ly.tile_bytes);
+				const int p0 = j * pages_tile;
+				bool contig = p0 + pages_tile <= a.pages_per_seq;
+				const int id0 = contig ? bt[p0] : -1;
+				contig = contig && id0 >= 0 && id0 + pages_tile <= a.max_pages;
+				for (int pg = 1; contig && pg < pages_tile; ++pg) contig = bt[p0 + pg] == id0 + pg;
+				if (contig) {
+					for (uint32_t h = 0; h < Ly.halves; ++h) tma_load_4d(dst + h * kPtAtom, tm8, (int)h * 64, 0, kvh, id0, bar, pol);
+					return;
+				}
 				for (int pg = 0; pg < pages_tile; ++pg) {
-					const int pidx = j * pages_tile + pg;
+					const int pidx = p0 + pg;
 					int page = first; // pages past the context hold finite data that the mask drops
 					if (pidx * blk <= last_pos) {
 						page = bt[pidx];
@@ -161,63 +211,73 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 							page = first;
 						}
 					}
-					const int y = (page * a.KV + kvh) * blk;
-					for (uint32_t h = 0; h < Ly.halves; ++h) {
-						tma_load_2d(ks + h * kPtAtom + pg * blk * 128, &tm_k, (int)h * 64, y, &kv_full[s], pol);
-						tma_load_2d(vs + h * kPtAtom + pg * blk * 128, &tm_v, (int)h * 64, y, &kv_full[s], pol);
-					}
+					for (uint32_t h = 0; h < Ly.halves; ++h)
+						tma_load_4d(dst + h * kPtAtom + pg * blk * 128, tm1, (int)h * 64, 0, kvh, page, bar, pol);
 				}
-				++issued;
+			};
+			int kiss = 0, viss = 0;
+			for (int j = 0; j < n_tiles; ++j) {
+				const int s = j % kPtStages;
+				const uint32_t par = (uint32_t)((j / kPtStages) - 1) & 1u;
+				if (j >= kPtStages && !mbar_wait(&k_empty[s], par, abort_flag, a.err)) break;
+				load(&tm_k8, &tm_k1, k_s + (size_t)s * Ly.tile_bytes, &k_full[s], j);
+				++kiss;
+				if (j >= kPtStages && !mbar_wait(&v_empty[s], par, abort_flag, a.err)) break;
+				load(&tm_v8, &tm_v1, v_s + (size_t)s * Ly.tile_bytes, &v_full[s], j);
+				++viss;
 			}
-			for (int i = max(0, issued - kPtStages); i < issued; ++i) {
-				const uint64_t t0n = global_timer_ns();
-				while (!mbar_try_wait(&kv_full[i % kPtStages], (uint32_t)(i / kPtStages) & 1u))
-					if (global_timer_ns() - t0n > kWaitLimitNs) {
-						report_err(a.err, kDevTimeout);
-						break;
-					}
+			// never leave the CTA with copies in flight
+			for (int i = max(0, kiss - kPtStages); i < kiss; ++i) {
+				const uint64_t tw = global_timer_ns();
+				while (!mbar_try_wait(&k_full[i % kPtStages], (uint32_t)(i / kPtStages) & 1u))
+					if (global_timer_ns() - tw > kWaitLimitNs) break;
+			}
+			for (int i = max(0, viss - kPtStages); i < viss; ++i) {
+				const uint64_t tw = global_timer_ns();
+				while (!mbar_try_wait(&v_full[i % kPtStages], (uint32_t)(i / kPtStages) & 1u))
+					if (global_timer_ns() - tw > kWaitLimitNs) break;
 			}
 		}
 	} else if (warp == 1) {
-		// ---------------- MMA issuer
+		// ---------------- MMA issuer: S(j+2) runs while the softmax warps work on S(j+1)
 		if (lane == 0) {
 			const uint32_t idesc_s = umma_idesc_bf16(kPtRows, kPtKeys);
 			const uint32_t idesc_o = umma_idesc_bf16(kPtRows, hd) | (1u << 16); // B (V) MN-major
-			const uint32_t qa = smem_u32(q_s), pa = smem_u32(p_s);
+			const uint32_t qa = smem_u32(q_s);
 			const int ksteps_s = hd / 16;
-			bool ok = mbar_wait(bar_q, 0, abort_flag, a.err);
-			auto issue_s = [&](int j) {
-				const uint32_t ka = smem_u32(kv_s + (size_t)(j % kPtStages) * Ly.stage_bytes);
+			auto issue_s = [&](int j) -> bool {
+				const int s = j % kPtStages;
+				if (!mbar_wait(&k_full[s], (uint32_t)(j / kPtStages) & 1u, abort_flag, a.err)) return false;
+				tc_fence_after();
+				const uint32_t ka = smem_u32(k_s + (size_t)s * Ly.tile_bytes);
+				const uint32_t ts = tmem + (uint32_t)(j & 1) * kPtKeys;
 				for (int k = 0; k < ksteps_s; ++k) {
 					const uint32_t off = (uint32_t)(k >> 2) * kPtAtom + (uint32_t)(k & 3) * 32;
-					umma_bf16(tmem_s, umma_desc_sw128(qa + off), umma_desc_sw128(ka + off), idesc_s, k > 0 ? 1u : 0u);
+					umma_bf16(ts, umma_desc_sw128(qa + off), umma_desc_sw128(ka + off), idesc_s, k > 0 ? 1u : 0u);
 				}
-				umma_commit(bar_s);
+				umma_commit(&s_full[j & 1]);
+				umma_commit(&k_empty[s]);
+				return true;
 			};
-			if (ok && mbar_wait(&kv_full[0], 0, abort_flag, a.err)) {
-				tc_fence_after();
-				issue_s(0);
-			} else {
-				ok = false;
-			}
+			bool ok = mbar_wait(bar_q, 0, abort_flag, a.err);
+			ok = ok && issue_s(0);
+			if (ok && n_tiles > 1) ok = issue_s(1);
 			for (int j = 0; ok && j < n_tiles; ++j) {
 				if (!mbar_wait(bar_p, (uint32_t)j & 1u, abort_flag, a.err)) break;
+				const int s = j % kPtStages;
+				if (!mbar_wait(&v_full[s], (uint32_t)(j / kPtStages) & 1u, abort_flag, a.err)) break;
 				tc_fence_after();
-				const uint32_t va =
-				    smem_u32(kv_s + (size_t)(j % kPtStages) * Ly.stage_bytes + (size_t)Ly.halves * kPtAtom);
+				const uint32_t va = smem_u32(v_s + (size_t)s * Ly.tile_bytes);
+				const uint32_t pa = smem_u32(p_s + (size_t)(j & 1) * 2 * kPtAtom);
 				for (int k = 0; k < kPtKeys / 16; ++k) {
 					const uint32_t poff = (uint32_t)(k >> 2) * kPtAtom + (uint32_t)(k & 3) * 32;
 					umma_bf16(tmem_o, umma_desc_sw128(pa + poff), umma_desc_sw128_lbo(va + (uint32_t)k * 2048u, kPtAtom, 1024u),
 					          idesc_o, (j > 0 || k > 0) ? 1u : 0u);
 				}
 				umma_commit(bar_o);
-				umma_commit(&kv_empty[j % kPtStages]);
-				if (j + 1 < n_tiles) {
-					if (!mbar_wait(&kv_full[(j + 1) % kPtStages], (uint32_t)((j + 1) / kPtStages) & 1u, abort_flag, a.err))
-						break;
-					tc_fence_after();
-					issue_s(j + 1);
-				}
+				umma_commit(&p_free[j & 1]);
+				umma_commit(&v_empty[s]);
+				if (j + 2 < n_tiles && !issue_s(j + 2)) break;
 			}
 		}
 	} else {
@@ -245,68 +305,73 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 			const bool w = mbar_wait(bar, par, abort_flag, a.err);
 			return __all_sync(0xFFFFFFFFu, w);
 		};
-		float m = -INFINITY, l = 0.0f;
+		float m = -INFINITY, l = 0.0f; // m: the max the P values are taken against
 		bool ok = true;
 		for (int j = 0; j < n_tiles; ++j) {
-			if (!wait_all(bar_s, (uint32_t)j & 1u)) {
+			if (!wait_all(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) {
 				ok = false;
 				break;
 			}
 			tc_fence_after();
+			const uint32_t ts = tmem + (uint32_t)(j & 1) * kPtKeys + lane_off;
 			const int kbase = j * kPtKeys;
-			float mt = -INFINITY;
-#pragma unroll 1
-			for (int c = 0; c < kPtKeys; c += 32) {
-				float v[32];
-				tmem_ld_32cols(tmem_s + lane_off + (uint32_t)c, v);
+			const bool masked = kbase + kPtKeys - 1 > pos; // the diagonal tile (or an invalid row)
+			float v[kPtKeys];
 #pragma unroll
-				for (int i = 0; i < 32; ++i)
-					if (kbase + c + i <= pos) mt = fmaxf(mt, v[i] * sl2);
+			for (int c = 0; c < kPtKeys; c += 32) tmem_ld_32cols_nowait(ts + (uint32_t)c, v + c);
+			asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+			float mt = -INFINITY;
+#pragma unroll
+			for (int i = 0; i < kPtKeys; ++i) {
+				v[i] *= sl2;
+				if (masked && kbase + i > pos) v[i] = -INFINITY;
+				mt = fmaxf(mt, v[i]);
 			}
-			const float mn = fmaxf(m, mt);
-			const float alpha = (m == -INFINITY) ? 1.0f : exp2f(m - mn);
-			// P.V of the previous tile has to finish before P is overwritten and O rescaled
-			if (j > 0) {
+			// rescale only when the max grows by more than 2^8 (or on the first finite max)
+			const bool grow = mt > m + kPtRescaleLog2 || (m == -INFINITY && mt != -INFINITY);
+			const float mn = grow ? mt : m;
+			if (__any_sync(0xFFFFFFFFu, grow) && j > 0) {
+				// O must hold every earlier P.V before it is rescaled
 				if (!wait_all(bar_o, (uint32_t)(j - 1) & 1u)) {
 					ok = false;
 					break;
 				}
 				tc_fence_after();
-				if (__any_sync(0xFFFFFFFFu, alpha != 1.0f)) {
+				const float alpha = grow && m != -INFINITY ? ex2_approx(m - mn) : 1.0f;
 #pragma unroll 1
-					for (int c = 0; c < hd; c += 32) {
-						float o[32];
-						tmem_ld_32cols(tmem_o + lane_off + (uint32_t)c, o);
+				for (int c = 0; c < hd; c += 32) {
+					float o[32];
+					tmem_ld_32cols(tmem_o + lane_off + (uint32_t)c, o);
 #pragma unroll
-						for (int i = 0; i < 32; ++i) o[i] *= alpha;
-						tmem_st_32cols(tmem_o + lane_off + (uint32_t)c, o);
-					}
+					for (int i = 0; i < 32; ++i) o[i] *= alpha;
+					tmem_st_32cols(tmem_o + lane_off + (uint32_t)c, o);
 				}
+				l *= alpha;
 			}
-			float sum = 0.0f;
-#pragma unroll 1
-			for (int c = 0; c < kPtKeys; c += 32) {
-				float v[32];
-				tmem_ld_32cols(tmem_s + lane_off + (uint32_t)c, v);
-				uint32_t pk[16];
-#pragma unroll
-				for (int i = 0; i < 32; i += 2) {
-					const float p0 = (kbase + c + i <= pos && mn != -INFINITY) ? exp2f(v[i] * sl2 - mn) : 0.0f;
-					const float p1 = (kbase + c + i + 1 <= pos && mn != -INFINITY) ? exp2f(v[i + 1] * sl2 - mn) : 0.0f;
-					const uint32_t b0 = f32_to_bf16_bits(p0), b1 = f32_to_bf16_bits(p1);
-					// the sum uses the rounded values, the ones the MMA sees
-					sum += __uint_as_float(b0 << 16) + __uint_as_float(b1 << 16);
-					pk[i >> 1] = b0 | (b1 << 16);
-				}
-				uint8_t* blkp = p_s + (size_t)(c >> 6) * kPtAtom;
-				const int c0 = (c & 63) >> 3;
-#pragma unroll
-				for (int u = 0; u < 4; ++u)
-					*reinterpret_cast<uint4*>(blkp + sw128_off(r, c0 + u)) =
-					    make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-			}
-			l = l * alpha + sum;
 			m = mn;
+			// P buffer j&1 was last read by the P.V of tile j-2
+			if (j >= 2 && !wait_all(&p_free[j & 1], (uint32_t)((j >> 1) - 1) & 1u)) {
+				ok = false;
+				break;
+			}
+			uint8_t* pb = p_s + (size_t)(j & 1) * 2 * kPtAtom;
+			float sum = 0.0f;
+#pragma unroll
+			for (int c = 0; c < kPtKeys; c += 8) {
+				uint32_t pk[4];
+#pragma unroll
+				for (int i = 0; i < 8; i += 2) {
+					const float p0 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i] - m);
+					const float p1 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i + 1] - m);
+					const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
+					// the row sum adds the rounded values, the weights the MMA applies
+					sum += __low2float(b) + __high2float(b);
+					pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&b);
+				}
+				*reinterpret_cast<uint4*>(pb + (size_t)(c >> 6) * kPtAtom + sw128_off(r, (c & 63) >> 3)) =
+				    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+			}
+			l += sum;
 			asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 			tc_fence_before();
 			mbar_arrive(bar_p);
@@ -336,12 +401,12 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 	if (warp == 1) {
 		if (*abort_flag) {
 			// let every issued MMA finish before TMEM is freed
-			const uint64_t t0n = global_timer_ns();
+			const uint64_t tw = global_timer_ns();
 			while (!mbar_try_wait(bar_o, (uint32_t)(n_tiles - 1) & 1u))
-				if (global_timer_ns() - t0n > kWaitLimitNs) break;
+				if (global_timer_ns() - tw > kWaitLimitNs) break;
 		}
 		tc_fence_after();
-		asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+		asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
 	}
 }
 
