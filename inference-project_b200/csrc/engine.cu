@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "k_attn_decode.cuh"
+#include "k_attn_decode_stream.cuh"
 #include "k_attn_cluster.cuh"
 #include "k_gemv.cuh"
 #include "k_attn_prefill.cuh"
@@ -82,6 +83,7 @@ struct InfEngine {
 	int attn_max_pages_split_batch = 1;
 	float* logits_p = nullptr;    // [max_batch][Vl] batched-decode logits
 	uint32_t* argmax_p = nullptr; // [max_batch]
+	unsigned long long* batch_keys = nullptr; // [max_batch] argmax keys, zero between steps
 	unsigned* attn_counters = nullptr;
 	int* err = nullptr;
 	uint32_t* d_ids = nullptr; // staged ids [max_seq]
@@ -89,6 +91,9 @@ struct InfEngine {
 	int attn_splits = 1;
 	int attn_max_pages_split = 1;
 	bool pf_tc = false;           // prefill attention on the tensor cores (k_attn_prefill_tc.cuh)
+	float* gemm_part = nullptr;   // split-K shares of the tensor-core GEMM
+	u64 gemm_part_bytes = 0;
+	bool gemm_split = false;      // split-K allowed (batched decode; prefill keeps one K pass per tile)
 	int attn_cl_splits = 0;       // batch-1 decode attention as one cluster per KV head (0: split-K)
 	int attn_cl_pages = 0;
 	// multi-token (prefill) buffers, prefill_chunk rows each
@@ -468,6 +473,7 @@ Error_t enqueue_step(InfEngine* e)
 }
 
 // --------------------------------------------------------------------------- prefill
+constexpr u64 kGemmPartBytes = 16ull << 20; // split-K scratch of the tensor-core GEMM
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 Error_t tensor_map_2d(CUtensorMap* m, const void* base, u64 rows, u64 cols, u32 box_rows)
@@ -517,7 +523,25 @@ Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
 	const size_t smem = gemm_tc_smem_bytes();
 	INF_CUDA_TRY(set_smem(k_gemm_tc, smem));
 	a.err = e->err;
-	const dim3 grid((a.N + kTcBN - 1) / kTcBN, (a.T + kTcBM - 1) / kTcBM);
+	dim3 grid((a.N + kTcBN - 1) / kTcBN, (a.T + kTcBM - 1) / kTcBM);
+	// too few output tiles to stream the weights on every SM: split K across CTAs
+	const int tiles = (int)(grid.x * grid.y), n_kb = (a.K + kTcBK - 1) / kTcBK;
+	int splits = 1;
+	if (e->gemm_split && e->gemm_part && tiles * 2 <= e->sm_count) {
+		splits = std::min(e->sm_count / tiles, n_kb / 2);
+		const u64 per_split = (u64)a.T * a.N * 4;
+		splits = (int)std::min<u64>((u64)splits, e->gemm_part_bytes / std::max<u64>(per_split, 1));
+	}
+	if (splits >= 2) {
+		a.k_splits = splits;
+		a.partial = e->gemm_part;
+		grid.z = splits;
+		INF_CUDA_TRY(launch(e, k_gemm_tc, grid, dim3(kTcThreads), smem, tx, tw, a));
+		const int groups = a.T * ((a.N + 31) / 32);
+		INF_CUDA_TRY(launch(e, k_gemm_splitk_reduce, dim3((groups + 7) / 8), dim3(256), 0, a));
+		return Success;
+	}
+	a.k_splits = 1;
 	INF_CUDA_TRY(launch(e, k_gemm_tc, grid, dim3(kTcThreads), smem, tx, tw, a));
 	return Success;
 }
@@ -737,15 +761,14 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 			a.hd = hd;
 			a.blk = (int)c.kv_block;
 			a.n_splits = e->attn_splits_batch;
-			a.max_pages_split = e->attn_max_pages_split_batch;
+			a.max_pages_split = 0;
 			a.scale = (float)(1.0 / std::sqrt((double)hd));
 			a.part = e->attn_part;
 			a.counters = e->attn_counters;
 			a.out = e->attn_p;
 			a.err = e->err;
-			const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2,
-			                                           e->attn_max_pages_split_batch, e->attn_splits_batch);
-			const AttnKernel<bf16> ak = attn_decode_kernel<bf16>(e->Hl / e->KVl, hd);
+			const size_t smem = attn_stream_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2);
+			const AttnKernel<bf16> ak = attn_decode_stream_kernel<bf16>(e->Hl / e->KVl, hd);
 			if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
 			INF_CUDA_TRY(set_smem(ak, smem));
 			INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAttnThreads), smem, a));
@@ -771,12 +794,14 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 	INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
 	                    (bf16*)e->xhat_p, B, d, (const bf16*)e->final_norm, c.norm_eps));
 	{
-		TcArgs a = tc_base(e, B, e->Vl, d, kTcStoreF32);
+		// logits and the greedy argmax of every row in the GEMM's epilogue
+		TcArgs a = tc_base(e, B, e->Vl, d, kTcLogitsArgmax);
 		a.out = e->logits_p;
+		a.best_keys = e->batch_keys;
+		a.col_base = (uint32_t)(c.tp_rank * (u32)e->Vl);
 		INF_TRY(launch_gemm_tc(e, e->xhat_p, e->lm_head, a));
 	}
-	INF_CUDA_TRY(launch(e, k_argmax_rows, dim3(B), dim3(256), 0, (const float*)e->logits_p, e->Vl,
-	                    (uint32_t)(c.tp_rank * (u32)e->Vl), e->argmax_p));
+	INF_CUDA_TRY(launch(e, k_keys_to_ids, dim3((B + 255) / 256), dim3(256), 0, e->batch_keys, B, e->argmax_p));
 	return Success;
 }
 
@@ -1021,12 +1046,12 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	e->n_pages = c.kv_pages ? (int)c.kv_pages : (int)(c.max_batch * (u32)e->pages_per_seq);
 	e->max_out = (int)c.max_seq;
 	const int G = e->Hl / e->KVl;
-	// split-K attention: about one CTA per SM over the KV heads of the tokens, each split
-	// within the shared-memory budget
+	// split-K attention at batch 1: about one CTA per SM over the KV heads, each split within
+	// the shared-memory budget; batches stream their pages (a few CTAs per SM over the batch)
 	attn_decode_plan(e->sm_count, e->KVl, 1, e->pages_per_seq, (int)c.kv_block, (int)hd, e->esz, &e->attn_splits,
 	                 &e->attn_max_pages_split);
-	attn_decode_plan(e->sm_count, e->KVl, (int)c.max_batch, e->pages_per_seq, (int)c.kv_block, (int)hd, e->esz,
-	                 &e->attn_splits_batch, &e->attn_max_pages_split_batch);
+	e->attn_splits_batch = attn_stream_splits(e->sm_count, e->KVl, (int)c.max_batch, e->pages_per_seq);
+	e->attn_max_pages_split_batch = 0;
 	// batch-1 decode: one cluster per KV head when the longest context fits its shared memory
 	// and the GPU can place a cluster of that size
 	INF_TRY(attn_cl_choose(e, G, (int)hd));
@@ -1044,8 +1069,8 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	const u64 comm = c.tp_size > 1 ? (2ull * c.tp_size * d * 8 + 2ull * c.tp_size * kTpMaxCtas * 4 + 64ull * c.tp_size +
 	                                   (e->chunk > 0 ? 2ull * (u64)(c.prefill_chunk ? c.prefill_chunk : 4096) * d * 4 : 0) + 8 * 256)
 	                                : 0;
-	const u64 batch_bufs = c.max_batch > 1 ? (u64)c.max_batch * ((u64)e->Vl * 4 + 4) + 512 : 0;
-	const u64 act = comm + batch_bufs + d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + part_floats * 4 +
+	const u64 batch_bufs = c.max_batch > 1 ? (u64)c.max_batch * ((u64)e->Vl * 4 + 4 + 8) + 768 : 0;
+	const u64 act = comm + batch_bufs + (c.dtype == InfBF16 ? kGemmPartBytes + 256 : 0) + d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + part_floats * 4 +
 	                (u64)e->chunk * (d * 4 + d * es + 2ull * e->Hl * hd * es + (u64)e->Fl * es + 8) + 16 * 256;
 	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024;
 	const u64 total = w_total + kv_total + act + (u64)c.max_seq * hd * 4 + (u64)c.max_batch * e->pages_per_seq * 4 +
@@ -1088,9 +1113,14 @@ Error_t engine_build(InfEngine* e, u64 seed)
 	P.push(&e->d_ids, (u64)c.max_seq * 4);
 	P.push(&e->attn_part, part_floats * 4);
 	P.push(&e->attn_counters, (u64)c.max_batch * e->KVl * 4);
+	if (c.dtype == InfBF16) {
+		e->gemm_part_bytes = kGemmPartBytes;
+		P.push(&e->gemm_part, kGemmPartBytes);
+	}
 	if (c.max_batch > 1) {
 		P.push(&e->logits_p, (u64)c.max_batch * e->Vl * 4);
 		P.push(&e->argmax_p, (u64)c.max_batch * 4);
+		P.push(&e->batch_keys, (u64)c.max_batch * 8);
 	}
 	if (e->chunk > 0) {
 		P.push(&e->resid_p, (u64)e->chunk * d * 4);
@@ -1365,7 +1395,10 @@ Error_t inf_forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const 
 	INF_CUDA_TRY(cudaMemcpyAsync(e->d_ids, e->h_pin, sizeof(u32) * n_seqs, cudaMemcpyHostToDevice, e->stream));
 	INF_CUDA_TRY(cudaMemcpyAsync(e->tok_pos, e->h_tok, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, e->stream));
 	INF_CUDA_TRY(cudaMemcpyAsync(e->tok_slot, e->h_tok + e->chunk, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, e->stream));
-	INF_TRY(enqueue_decode_batch(e, (int)n_seqs));
+	e->gemm_split = true;
+	const Error_t eb = enqueue_decode_batch(e, (int)n_seqs);
+	e->gemm_split = false;
+	INF_TRY(eb);
 	if (logits_out) INF_TRY(copy_out(e, logits_out, e->logits_p, sizeof(float) * e->Vl * n_seqs));
 	if (argmax_out) INF_TRY(copy_out(e, argmax_out, e->argmax_p, sizeof(u32) * n_seqs));
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));

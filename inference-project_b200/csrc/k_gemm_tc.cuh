@@ -30,7 +30,7 @@ constexpr uint32_t kTcStageB = kTcBN * kTcBK * 2;
 constexpr uint32_t kTcStageBytes = kTcStageA + kTcStageB;
 constexpr int kTcTmemCols = 256;
 
-enum TcEpi : int { kTcStore = 0, kTcStoreF32 = 1, kTcResid = 2, kTcQkv = 3, kTcSwiglu = 4 };
+enum TcEpi : int { kTcStore = 0, kTcStoreF32 = 1, kTcResid = 2, kTcQkv = 3, kTcSwiglu = 4, kTcLogitsArgmax = 5 };
 
 struct TcArgs {
 	int T, N, K;
@@ -47,6 +47,15 @@ struct TcArgs {
 	const float* rope_sin;
 	int head_dim, n_q_heads, n_kv_heads, kv_block;
 	int* err;
+	// split-K (few output tiles, e.g. a 64-token batch): CTA z of k_splits sums its share of
+	// the K blocks into partial [k_splits][T][N] fp32; k_gemm_splitk_reduce adds the shares
+	// in z order and runs the epilogue
+	int k_splits;
+	float* partial;
+	// kTcLogitsArgmax: f32 logits to out and, per row, the max (value, column + col_base) key
+	// folded into best_keys[row] with a 64-bit atomicMax (ties -> lowest column)
+	unsigned long long* best_keys;
+	uint32_t col_base;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy)
@@ -116,11 +125,17 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, float (&v)[32])
 // Epilogue for one token row and 32 consecutive output columns n0 .. n0+31.
 __device__ __forceinline__ void tc_epilogue_row(const TcArgs& a, int t, int n0, const float (&v)[32])
 {
-	if (a.epi == kTcStoreF32) {
+	if (a.epi == kTcStoreF32 || a.epi == kTcLogitsArgmax) {
 		float* o = reinterpret_cast<float*>(a.out) + (size_t)t * a.N;
+		unsigned long long best = 0ull;
 #pragma unroll
 		for (int i = 0; i < 32; ++i)
-			if (n0 + i < a.N) o[n0 + i] = v[i];
+			if (n0 + i < a.N) {
+				o[n0 + i] = v[i];
+				const unsigned long long k = argmax_key(v[i], (uint32_t)(n0 + i) + a.col_base);
+				best = k > best ? k : best;
+			}
+		if (a.epi == kTcLogitsArgmax) atomicMax(a.best_keys + t, best);
 	} else if (a.epi == kTcStore) {
 		bf16* o = reinterpret_cast<bf16*>(a.out) + (size_t)t * a.N;
 #pragma unroll
@@ -187,7 +202,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-	const int n_kb = (a.K + kTcBK - 1) / kTcBK;
+	const int n_kb_all = (a.K + kTcBK - 1) / kTcBK;
+	const int S = a.k_splits > 1 ? a.k_splits : 1;
+	const int kb0 = (int)(((long long)blockIdx.z * n_kb_all) / S);
+	const int n_kb = (int)(((long long)(blockIdx.z + 1) * n_kb_all) / S) - kb0;
 
 	if (threadIdx.x == 0) {
 		for (int s = 0; s < kTcStages; ++s) {
@@ -221,8 +239,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 				if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort_flag, a.err)) break;
 				uint8_t* sa = tiles + (size_t)s * kTcStageBytes;
 				mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-				tma_load_2d(sa, &tm_x, kb * kTcBK, m_tile * kTcBM, &full[s], pol_x);
-				tma_load_2d(sa + kTcStageA, &tm_w, kb * kTcBK, n_tile * kTcBN, &full[s], pol_w);
+				tma_load_2d(sa, &tm_x, (kb0 + kb) * kTcBK, m_tile * kTcBM, &full[s], pol_x);
+				tma_load_2d(sa + kTcStageA, &tm_w, (kb0 + kb) * kTcBK, n_tile * kTcBN, &full[s], pol_w);
 				++issued;
 			}
 			for (int i = max(0, issued - kTcStages); i < issued; ++i) {
@@ -264,7 +282,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 				if (n0 >= a.N) break;
 				float v[32];
 				tmem_ld_32cols(tmem_d + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
-				if (t < a.T) tc_epilogue_row(a, t, n0, v);
+				if (t < a.T) {
+					if (S > 1) {
+						float* pp = a.partial + ((size_t)blockIdx.z * a.T + t) * a.N;
+#pragma unroll
+						for (int i = 0; i < 32; ++i)
+							if (n0 + i < a.N) pp[n0 + i] = v[i];
+					} else {
+						tc_epilogue_row(a, t, n0, v);
+					}
+				}
 			}
 		}
 	}
@@ -279,6 +306,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 		}
 		tc_fence_after();
 		asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kTcTmemCols) : "memory");
+	}
+}
+
+// Sum of the split-K shares in split order, then the GEMM's epilogue.  A warp takes one
+// (token row, 32 columns) group: lane i sums column n0 + i over the splits (coalesced), and
+// lane 0 runs the epilogue on the 32 sums.
+__global__ void __launch_bounds__(256) k_gemm_splitk_reduce(const TcArgs a)
+{
+	pdl_wait();
+	pdl_trigger();
+	__shared__ float st[8][32];
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int groups = (a.N + 31) / 32;
+	const int gw = blockIdx.x * 8 + warp;
+	if (gw >= a.T * groups) return;
+	const int t = gw / groups, n0 = (gw % groups) * 32;
+	float v = 0.0f;
+	if (n0 + lane < a.N)
+		for (int z = 0; z < a.k_splits; ++z) v += a.partial[((size_t)z * a.T + t) * a.N + n0 + lane];
+	st[warp][lane] = v;
+	__syncwarp();
+	if (lane == 0) {
+		float vals[32];
+#pragma unroll
+		for (int i = 0; i < 32; ++i) vals[i] = st[warp][i];
+		tc_epilogue_row(a, t, n0, vals);
+	}
+}
+
+// token ids from the argmax keys of kTcLogitsArgmax; the keys are cleared for the next use
+__global__ void k_keys_to_ids(unsigned long long* keys, int n, uint32_t* ids)
+{
+	pdl_wait();
+	pdl_trigger();
+	const int i = blockIdx.x * blockDim.x + threadIdx.x;
+	if (i < n) {
+		ids[i] = argmax_key_index(keys[i]);
+		keys[i] = 0ull;
 	}
 }
 
