@@ -267,6 +267,172 @@ def run_ours(args, rank: int, world: int, dist):
     eng.close()
 
 
+def linear_params(cfg, world: int) -> int:
+    """Projection weights of one layer on one rank (QKV, O, gate/up, down)."""
+    d, hd = cfg.dim, cfg.head_dim
+    H, KV, F = cfg.n_heads // world, cfg.n_kv_heads // world, cfg.ffn_dim // world
+    return (H + 2 * KV) * hd * d + H * hd * d + 2 * F * d + F * d
+
+
+def run_workload(args, rank: int, world: int, dist):
+    """The long-prefill (32768-token prompt) and batched-decode (64 sequences) workloads."""
+    import numpy as np
+    import torch
+
+    import infb200 as I
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    preset = 5 if args.workload == "prefill" else 4
+    cfg = I.preset(preset, n_layers=args.layers, tp_rank=rank if world > 1 else 0, tp_size=world)
+    eng = I.Engine(cfg, seed=0)
+    if world > 1:
+        gloo = dist.new_group(backend="gloo")
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.tp_export(), group=gloo)
+        eng.tp_connect(handles)
+    stream = torch.cuda.ExternalStream(eng.stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    L = cfg.n_layers
+    bf16_peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        bf16_peak, peak_kind = float(p["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        bf16_peak, peak_kind = 1400.0, "fallback (sustained)"
+    hbm_peak, hbm_kind = load_peaks()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    if args.workload == "prefill":
+        T = 32768 if args.prompt == PROMPT else args.prompt
+        prompt = I.synth_ids(3, T, cfg.vocab_size)  # seed-3 uniform ids
+        for _ in range(args.warmup):
+            eng.reset(0)
+            eng.forward(prompt, 0, want_logits=False)
+        torch.cuda.synchronize()
+        barrier()
+        l0 = eng.launches
+        with ClockSampler(local) as clk:
+            ms = 0.0
+            wall = 0.0
+            for _ in range(args.steps):
+                eng.reset(0)
+                torch.cuda.synchronize()
+                w0 = time.perf_counter()
+                ev0.record(stream)
+                _, first = eng.forward(prompt, 0, want_logits=False)
+                ev1.record(stream)
+                torch.cuda.synchronize()
+                wall += time.perf_counter() - w0
+                ms += ev0.elapsed_time(ev1)
+        launches = eng.launches - l0
+        barrier()
+        ms, wall = max_over_ranks(ms), max_over_ranks(wall)
+        # FLOPs of one rank: projections of every token + causal attention (QK and PV)
+        H = cfg.n_heads // world
+        flop = 2.0 * L * linear_params(cfg, world) * T + 4.0 * L * H * cfg.head_dim * T * (T + 1) / 2
+        achieved = flop / (ms / args.steps * 1e-3) / 1e12
+        tok_s = args.steps * T / (ms * 1e-3)
+        # decode after the long prefill: 128 steps at context ~32k (reported, not the metric)
+        dec_steps = 128 if T + 128 <= cfg.max_seq else 0
+        dec = None
+        if dec_steps:
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            eng.decode(first, T, dec_steps, want_ids=False)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            dec = max_over_ranks(dec_steps / (ev0.elapsed_time(ev1) * 1e-3))
+        if rank == 0:
+            print(json.dumps({
+                "metric": "prefill tokens/s (Llama-3-8B shape, bf16, 32768-token prompt), TP 1/2/4/8",
+                "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (Philox seed-0 N(0,0.02) weights, seed-3 uniform prompt ids)",
+                "config": {"workload": f"llama3-8b-shape prefill of {T} tokens (one sequence), then {dec_steps} decode steps",
+                           "model": "llama-3-8b-shape" if L == 32 else f"llama-3-8b-shape-{L}-layers",
+                           "global_batch": 1, "seq_len": T, "parallelism": f"tp{world}",
+                           "l2": "no flush: a step streams 16 GB of weights and writes 4 GB of K/V",
+                           "flop_per_step": flop, "decode_tokens_per_s_at_32k": dec},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
+                             "frac": achieved / bf16_peak, "traffic": None,
+                             "kernel": "whole prefill pass (tcgen05 GEMMs + tcgen05 causal attention)",
+                             "peak_kind": peak_kind},
+                "e2e": {"value": args.steps * T / wall, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T,
+                        "d2h_bytes_per_step": 4},
+                "gpu_launches": launches, "clocks": clk.summary(),
+            }), flush=True)
+    else:
+        B = cfg.max_batch
+        lens = I.synth_uniform(2, I.STREAM_CTX_LEN, B, 512, 4096)  # seed-2 context lengths
+        cur = []
+        t0 = time.time()
+        for i in range(B):
+            _, am = eng.forward(I.synth_ids(100 + i, int(lens[i]), cfg.vocab_size), 0, slot=i, want_logits=False)
+            cur.append(am)
+        fill_s = time.time() - t0
+        slots = np.arange(B, dtype=np.uint32)
+        pos = lens.astype(np.uint32).copy()
+        cur = np.asarray(cur, np.uint32)
+        if int(pos.max()) + args.warmup + args.steps > cfg.max_seq:
+            raise SystemExit("--steps/--warmup beyond max_seq")
+        for _ in range(args.warmup):
+            _, cur = eng.forward_batch(slots, cur, pos)
+            pos += 1
+        torch.cuda.synchronize()
+        barrier()
+        l0 = eng.launches
+        with ClockSampler(local) as clk:
+            w0 = time.perf_counter()
+            ev0.record(stream)
+            for _ in range(args.steps):
+                _, cur = eng.forward_batch(slots, cur, pos)
+                pos += 1
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            wall = time.perf_counter() - w0
+        launches = eng.launches - l0
+        barrier()
+        ms, wall = max_over_ranks(ev0.elapsed_time(ev1)), max_over_ranks(wall)
+        avg_ctx = float(lens.mean()) + args.warmup + (args.steps - 1) / 2
+        # bytes of one step on one rank: every weight once + every sequence's K/V
+        step_bytes = I.decode_bytes(cfg, 0) + B * (I.decode_bytes(cfg, int(avg_ctx)) - I.decode_bytes(cfg, 0))
+        achieved = step_bytes / (ms / args.steps * 1e-3) / 1e9
+        if rank == 0:
+            print(json.dumps({
+                "metric": "batched decode tokens/s (Llama-3-8B shape, bf16, 64 sequences, contexts 512-4096), TP 1/2/4/8",
+                "value": B * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (Philox seed-0 N(0,0.02) weights, seed-2 context lengths, per-sequence uniform ids)",
+                "config": {"workload": f"llama3-8b-shape batched greedy decode, {B} sequences, paged KV (16-token pages)",
+                           "model": "llama-3-8b-shape" if L == 32 else f"llama-3-8b-shape-{L}-layers",
+                           "global_batch": B, "seq_len": int(lens.max()), "parallelism": f"tp{world}",
+                           "l2": "no flush: a step streams ~34 GB (> 126 MB L2)", "fill_s": fill_s,
+                           "step_bytes": step_bytes},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": achieved / hbm_peak, "traffic": None,
+                             "kernel": "whole batched step (tcgen05 projections, split-K attention)",
+                             "peak_kind": hbm_kind},
+                "e2e": {"value": B * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 12 * B,
+                        "d2h_bytes_per_step": 4 * B},
+                "gpu_launches": launches, "clocks": clk.summary(),
+            }), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -277,6 +443,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs use a short one)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch"],
+                    help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence decode")
     args = ap.parse_args()
     globals()["PROMPT"] = args.prompt
     if args.warmup < 3:
@@ -298,6 +466,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.workload != "decode":
+            run_workload(args, rank, world, dist)
         else:
             run_ours(args, rank, world, dist)
     finally:
