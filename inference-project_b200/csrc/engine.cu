@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "k_attn_decode.cuh"
 #include "k_attn_decode_stream.cuh"
+#include "k_attn_decode_mma.cuh"
 #include "k_attn_cluster.cuh"
 #include "k_gemv.cuh"
 #include "k_attn_prefill.cuh"
@@ -767,11 +768,19 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 			a.counters = e->attn_counters;
 			a.out = e->attn_p;
 			a.err = e->err;
-			const size_t smem = attn_stream_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2);
-			const AttnKernel<bf16> ak = attn_decode_stream_kernel<bf16>(e->Hl / e->KVl, hd);
-			if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
-			INF_CUDA_TRY(set_smem(ak, smem));
-			INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAttnThreads), smem, a));
+			// tensor-core (mma) scores and P.V where the shape allows, else the SIMT streaming kernel
+			const AttnKernel<bf16> am = attn_decode_mma_kernel(e->Hl / e->KVl, hd);
+			if (am) {
+				const size_t smem = attn_mma_smem_bytes(hd, (int)c.kv_block, e->pages_per_seq);
+				INF_CUDA_TRY(set_smem(am, smem));
+				INF_CUDA_TRY(launch(e, am, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAmThreads), smem, a));
+			} else {
+				const size_t smem = attn_stream_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2);
+				const AttnKernel<bf16> ak = attn_decode_stream_kernel<bf16>(e->Hl / e->KVl, hd);
+				if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+				INF_CUDA_TRY(set_smem(ak, smem));
+				INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAttnThreads), smem, a));
+			}
 		}
 		{
 			TcArgs a = tc_base(e, B, d, e->Hl * hd, kTcResid);

@@ -1,0 +1,308 @@
+// Decode attention for batches of tokens on the tensor cores (bf16, head_dim 64 or 128).
+//
+// The same decomposition as the streaming kernel (k_attn_decode_stream.cuh): grid
+// (kv_heads, splits, tokens), a CTA streams its pages through a ring of shared-memory chunks
+// of 64 positions.  The arithmetic moves to warp-level mma.m16n8k16 (bf16 in, fp32 out): the
+// G query heads of the KV head are the rows of a 16-row A tile (rows >= G are zero), each of
+// the four warps takes 16 positions of a chunk, computes S = Q.K^T (2 x head_dim/16 MMAs),
+// keeps a per-row running max / sum (online softmax on the accumulator fragments), turns
+// its S fragments into the bf16 A fragments of P (the C layout of two 8-column tiles is the
+// A layout of one 16-deep step) and accumulates O += P.V (head_dim/8 MMAs).  At the end the
+// four warps' (max, sum, O) are merged through shared memory into the split's partial, and the
+// last CTA of each (token, KV head) combines the splits (atomic ticket, no spinning).
+// P is rounded to bf16 for the P.V product (the SIMT kernels keep it in fp32).
+#pragma once
+
+#include "common.cuh"
+#include "k_attn_decode.cuh"        // AttnDecodeArgs, AttnKernel, attn_vpl
+#include "k_attn_decode_stream.cuh" // kStChunkPages, kStBufs, attn_stream_splits
+
+namespace inf {
+
+constexpr int kAmThreads = 128; // 4 warps x 16 positions = one 64-position chunk
+
+__host__ __device__ inline size_t attn_mma_region_bytes(int hd, int blk)
+{
+	const size_t ring = (size_t)kStBufs * 2 * kStChunkPages * blk * hd * 2;
+	const size_t merge = (size_t)4 * 16 * hd * 4 + 4 * 16 * 2 * 4; // O, then (m, l) of every warp
+	return ((ring > merge ? ring : merge) + 127) & ~(size_t)127;
+}
+// region, the split's page ids (at most pages_per_seq), the chunk mbarriers
+inline size_t attn_mma_smem_bytes(int hd, int blk, int pages_per_seq)
+{
+	return attn_mma_region_bytes(hd, blk) + (((size_t)pages_per_seq * 4 + 15) & ~(size_t)15) + kStBufs * sizeof(uint64_t);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+	asm volatile(
+	    "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+	    : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+	    : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
+{
+	const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+	return *reinterpret_cast<const uint32_t*>(&b);
+}
+__device__ __forceinline__ uint32_t pack_raw_bf16(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
+
+template <int G, int HD>
+__global__ void __launch_bounds__(kAmThreads) k_attn_decode_mma(const AttnDecodeArgs a)
+{
+	static_assert(G >= 1 && G <= 16 && (HD == 64 || HD == 128), "rows / head_dim");
+	extern __shared__ __align__(128) uint8_t sm_raw[];
+	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+	const int blk = a.blk;
+	const int CT = kStChunkPages * blk;
+	const size_t blk_bytes = (size_t)blk * HD * 2;
+	const size_t chunk_bytes = (size_t)kStChunkPages * blk_bytes;
+	uint8_t* kbuf = sm_raw;
+	uint8_t* vbuf = kbuf + (size_t)kStBufs * chunk_bytes;
+	int* pg_s = reinterpret_cast<int*>(sm_raw + attn_mma_region_bytes(HD, blk)); // this split's page ids
+	uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(pg_s) + (((size_t)a.pages_per_seq * 4 + 15) & ~(size_t)15));
+	__shared__ int abort_flag;
+	__shared__ int last_flag;
+
+	const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+	const int gr = lane >> 2, gc = (lane & 3) * 2; // fragment row (and row + 8), column pair
+	pdl_wait();
+	pdl_trigger();
+	const int slot = a.tok_slot[b];
+	const int pos = a.tok_pos[b];
+	const int ctx = pos + 1;
+	const int n_pages = (ctx + blk - 1) / blk;
+	const int pps = (n_pages + a.n_splits - 1) / a.n_splits;
+	const int p_begin = split * pps;
+	const int np = max(0, min(n_pages, p_begin + pps) - p_begin);
+	const int n_chunks = (np + kStChunkPages - 1) / kStChunkPages;
+
+	if (tid == 0) {
+		abort_flag = 0;
+		for (int i = 0; i < kStBufs; ++i) mbar_init(&bars[i], 1);
+		mbar_fence_init();
+	}
+	// page ids once into shared memory (invalid ids as -1): the chunk issue and the mask read them
+	for (int q = tid; q < np; q += kAmThreads) {
+		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p_begin + q];
+		pg_s[q] = (page >= 0 && page < a.max_pages) ? page : -1;
+	}
+	__syncthreads();
+	auto issue = [&](int c) {
+		const int buf = c % kStBufs;
+		const int q0 = c * kStChunkPages, q1 = min(np, q0 + kStChunkPages);
+		uint32_t bytes = 0;
+		for (int q = q0; q < q1; ++q)
+			if (pg_s[q] >= 0) bytes += (uint32_t)(2 * blk_bytes);
+		mbar_arrive_expect_tx(&bars[buf], bytes);
+		const uint64_t pol = policy_evict_first();
+		for (int q = q0; q < q1; ++q) {
+			const int page = pg_s[q];
+			if (page < 0 || page >= a.max_pages) {
+				report_err(a.err, kDevKvRange);
+				continue; // masked below
+			}
+			const size_t off = (((size_t)page * a.KV + kvh) * blk) * HD;
+			bulk_g2s(kbuf + (size_t)buf * chunk_bytes + (size_t)(q - q0) * blk_bytes, reinterpret_cast<const bf16*>(a.kpool) + off,
+			         (uint32_t)blk_bytes, &bars[buf], pol);
+			bulk_g2s(vbuf + (size_t)buf * chunk_bytes + (size_t)(q - q0) * blk_bytes, reinterpret_cast<const bf16*>(a.vpool) + off,
+			         (uint32_t)blk_bytes, &bars[buf], pol);
+		}
+	};
+	if (tid == 0)
+		for (int c = 0; c < min(n_chunks, kStBufs); ++c) issue(c);
+
+	// Q as A fragments (rows gr and gr + 8; rows >= G are zero)
+	uint32_t qa[HD / 16][4];
+	{
+		const uint16_t* qb = reinterpret_cast<const uint16_t*>(a.q) + (size_t)b * a.H * HD + (size_t)kvh * G * HD;
+#pragma unroll
+		for (int ks = 0; ks < HD / 16; ++ks) {
+			const int c0 = ks * 16 + gc;
+			const uint16_t* r0 = qb + (size_t)gr * HD;
+			const uint16_t* r1 = qb + (size_t)(gr + 8) * HD;
+			const bool v0 = gr < G, v1 = gr + 8 < G;
+			qa[ks][0] = v0 ? pack_raw_bf16(r0[c0], r0[c0 + 1]) : 0u;
+			qa[ks][1] = v1 ? pack_raw_bf16(r1[c0], r1[c0 + 1]) : 0u;
+			qa[ks][2] = v0 ? pack_raw_bf16(r0[c0 + 8], r0[c0 + 9]) : 0u;
+			qa[ks][3] = v1 ? pack_raw_bf16(r1[c0 + 8], r1[c0 + 9]) : 0u;
+		}
+	}
+	float o[HD / 8][4];
+#pragma unroll
+	for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+	float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f; // rows gr, gr + 8 (l: this thread's share)
+	const float sl2 = a.scale * 1.4426950408889634f;
+
+	for (int c = 0; c < n_chunks; ++c) {
+		const int buf = c % kStBufs;
+		if (!abort_flag && !mbar_wait(&bars[buf], (uint32_t)(c / kStBufs) & 1u, (volatile int*)&abort_flag, a.err))
+			abort_flag = 1;
+		const int q0 = c * kStChunkPages;
+		const int n_tok = (min(np, q0 + kStChunkPages) - q0) * blk;
+		const int kb = warp * 16; // this warp's 16 positions of the chunk
+		if (kb < n_tok && !abort_flag) {
+			const uint16_t* kc = reinterpret_cast<const uint16_t*>(kbuf + (size_t)buf * chunk_bytes);
+			const uint16_t* vc = reinterpret_cast<const uint16_t*>(vbuf + (size_t)buf * chunk_bytes);
+			// S = Q.K^T for 16 positions (two 8-position tiles)
+			float s[2][4];
+#pragma unroll
+			for (int nt = 0; nt < 2; ++nt) {
+				s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+				const uint16_t* kr = kc + (size_t)(kb + nt * 8 + gr) * HD;
+#pragma unroll
+				for (int ks = 0; ks < HD / 16; ++ks) {
+					const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + gc);
+					const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + gc + 8);
+					mma_bf16_16816(s[nt], qa[ks], b0, b1);
+				}
+			}
+			// scale (log2 units) and mask positions past the context or on invalid pages
+			const int tok0 = (p_begin + q0) * blk;
+			float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+			for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+				for (int j = 0; j < 2; ++j) {
+					const int t = kb + nt * 8 + gc + j;
+					const bool ok = tok0 + t < ctx && pg_s[q0 + t / blk] >= 0;
+					s[nt][j] = ok ? s[nt][j] * sl2 : -INFINITY;
+					s[nt][2 + j] = ok ? s[nt][2 + j] * sl2 : -INFINITY;
+					mx0 = fmaxf(mx0, s[nt][j]);
+					mx1 = fmaxf(mx1, s[nt][2 + j]);
+				}
+			// the row's max over the quad (the four lanes that hold one row)
+			mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 1));
+			mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 2));
+			mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 1));
+			mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 2));
+			const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+			const float al0 = (m0 == -INFINITY) ? 0.0f : exp2f(m0 - n0);
+			const float al1 = (m1 == -INFINITY) ? 0.0f : exp2f(m1 - n1);
+			m0 = n0;
+			m1 = n1;
+			float ps[2][4];
+			float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+			for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+				for (int j = 0; j < 2; ++j) {
+					ps[nt][j] = (n0 == -INFINITY) ? 0.0f : exp2f(s[nt][j] - n0);
+					ps[nt][2 + j] = (n1 == -INFINITY) ? 0.0f : exp2f(s[nt][2 + j] - n1);
+				}
+			uint32_t pa[4];
+			pa[0] = pack_bf16(ps[0][0], ps[0][1]);
+			pa[1] = pack_bf16(ps[0][2], ps[0][3]);
+			pa[2] = pack_bf16(ps[1][0], ps[1][1]);
+			pa[3] = pack_bf16(ps[1][2], ps[1][3]);
+			// the sums add the rounded values, the weights the MMA applies
+#pragma unroll
+			for (int i = 0; i < 4; i += 2) {
+				sum0 += __uint_as_float(pa[i] << 16) + __uint_as_float(pa[i] & 0xFFFF0000u);
+				sum1 += __uint_as_float(pa[i + 1] << 16) + __uint_as_float(pa[i + 1] & 0xFFFF0000u);
+			}
+			l0 = l0 * al0 + sum0;
+			l1 = l1 * al1 + sum1;
+			// O = O * alpha + P.V
+#pragma unroll
+			for (int dt = 0; dt < HD / 8; ++dt) {
+				o[dt][0] *= al0;
+				o[dt][1] *= al0;
+				o[dt][2] *= al1;
+				o[dt][3] *= al1;
+				const int dim = dt * 8 + gr;
+				const uint16_t* v0 = vc + (size_t)(kb + gc) * HD + dim;
+				const uint32_t b0 = pack_raw_bf16(v0[0], v0[HD]);
+				const uint32_t b1 = pack_raw_bf16(v0[8 * HD], v0[9 * HD]);
+				mma_bf16_16816(o[dt], pa, b0, b1);
+			}
+		}
+		__syncthreads(); // every warp is done with the chunk's buffer
+		if (tid == 0 && c + kStBufs < n_chunks) issue(c + kStBufs);
+	}
+
+	// merge the four warps: (m, l, O) per row through shared memory (the ring is idle now)
+	float* mo = reinterpret_cast<float*>(sm_raw);       // [warps][16][HD]
+	float* ml = mo + 4 * 16 * HD;                        // [warps][16][2]
+	l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 1);
+	l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 2);
+	l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
+	l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 2);
+#pragma unroll
+	for (int dt = 0; dt < HD / 8; ++dt) {
+		float* r0 = mo + ((size_t)warp * 16 + gr) * HD + dt * 8 + gc;
+		float* r1 = mo + ((size_t)warp * 16 + gr + 8) * HD + dt * 8 + gc;
+		r0[0] = o[dt][0];
+		r0[1] = o[dt][1];
+		r1[0] = o[dt][2];
+		r1[1] = o[dt][3];
+	}
+	if ((lane & 3) == 0) {
+		ml[((size_t)warp * 16 + gr) * 2 + 0] = m0;
+		ml[((size_t)warp * 16 + gr) * 2 + 1] = l0;
+		ml[((size_t)warp * 16 + gr + 8) * 2 + 0] = m1;
+		ml[((size_t)warp * 16 + gr + 8) * 2 + 1] = l1;
+	}
+	__syncthreads();
+	// split partial: acc (unnormalised, against the max M in natural-log units), M, L
+	const int hd2 = HD + 2;
+	const float ln2 = 0.6931471805599453f;
+	for (int e = tid; e < G * HD; e += kAmThreads) {
+		const int g = e / HD, i = e % HD;
+		float M = -INFINITY;
+#pragma unroll
+		for (int w = 0; w < 4; ++w) M = fmaxf(M, ml[((size_t)w * 16 + g) * 2]);
+		float v = 0.0f, L = 0.0f;
+#pragma unroll
+		for (int w = 0; w < 4; ++w) {
+			const float mw = ml[((size_t)w * 16 + g) * 2];
+			const float wgt = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+			v = fmaf(wgt, mo[((size_t)w * 16 + g) * HD + i], v);
+			L = fmaf(wgt, ml[((size_t)w * 16 + g) * 2 + 1], L);
+		}
+		float* pr = a.part + (((size_t)b * a.H + kvh * G + g) * a.n_splits + split) * hd2;
+		pr[i] = v;
+		if (i == 0) {
+			pr[HD] = M == -INFINITY ? -INFINITY : M * ln2; // the combine works in natural-log units
+			pr[HD + 1] = L;
+		}
+	}
+	__threadfence();
+	__syncthreads();
+	if (tid == 0) {
+		const unsigned t = atomicAdd(&a.counters[b * a.KV + kvh], 1u);
+		last_flag = (t == (unsigned)a.n_splits - 1);
+	}
+	__syncthreads();
+	if (!last_flag) return;
+	__threadfence();
+	bf16* ob = reinterpret_cast<bf16*>(a.out) + (size_t)b * a.H * HD;
+	for (int e = tid; e < G * HD; e += kAmThreads) {
+		const int g = e / HD, i = e % HD;
+		const float* ph = a.part + ((size_t)b * a.H + kvh * G + g) * a.n_splits * hd2;
+		float M = -INFINITY;
+		for (int s = 0; s < a.n_splits; ++s) M = fmaxf(M, __ldcg(ph + (size_t)s * hd2 + HD));
+		float L = 0.0f, v = 0.0f;
+		for (int s = 0; s < a.n_splits; ++s) {
+			const float ms = __ldcg(ph + (size_t)s * hd2 + HD);
+			const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+			L = fmaf(w, __ldcg(ph + (size_t)s * hd2 + HD + 1), L);
+			v = fmaf(w, __ldcg(ph + (size_t)s * hd2 + i), v);
+		}
+		Store<bf16>::put(ob + (size_t)(kvh * G + g) * HD + i, L > 0.0f ? v / L : 0.0f);
+	}
+	if (tid == 0) a.counters[b * a.KV + kvh] = 0u;
+}
+
+// the instantiation for GQA group G (<= 8) and head_dim 64 / 128 (nullptr otherwise)
+inline AttnKernel<bf16> attn_decode_mma_kernel(int G, int hd)
+{
+#define INF_AM_CASE(g)                                               \
+	if (G == g && hd == 64) return k_attn_decode_mma<g, 64>;     \
+	if (G == g && hd == 128) return k_attn_decode_mma<g, 128>;
+	INF_AM_CASE(1) INF_AM_CASE(2) INF_AM_CASE(4) INF_AM_CASE(8)
+#undef INF_AM_CASE
+	return nullptr;
+}
+
+} // namespace inf

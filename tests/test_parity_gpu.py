@@ -188,12 +188,14 @@ def test_forward_batch_matches_single(cuda):
             assert a1 == am[i] or top[-1] - top[-2] < 2 * DRIFT_TINYLLAMA_2
 
 
-def test_batched_decode_ragged_contexts_steps(cuda):
+@pytest.mark.parametrize("preset", [2, 3])
+def test_batched_decode_ragged_contexts_steps(cuda, preset):
     """16 sequences with context lengths spread over [20, 400], four batched decode steps
-    (tensor-core projections, one attention launch for all tokens, LM-head GEMM + row argmax)
-    against stepping every sequence alone through the batch-1 path on a second engine with
-    the same prompts; both sides are fed the same tokens."""
-    cfg = I.preset(2, n_layers=2, max_seq=512, max_batch=16)
+    (tensor-core projections, one attention launch for all tokens, LM-head GEMM with the row
+    argmax in its epilogue) against stepping every sequence alone through the batch-1 path on
+    a second engine with the same prompts; both sides are fed the same tokens.  TinyLlama
+    (GQA 8, head_dim 64) and Llama-3-8B (GQA 4, head_dim 128) shapes."""
+    cfg = I.preset(preset, n_layers=2, max_seq=512, max_batch=16)
     B = 16
     lens = I.synth_uniform(2, I.STREAM_CTX_LEN, B, 20, 400)
     prompts = [I.synth_ids(100 + i, int(lens[i]), cfg.vocab_size) for i in range(B)]
@@ -205,7 +207,7 @@ def test_batched_decode_ragged_contexts_steps(cuda):
             assert am == am2
             cur.append(am)
         pos = lens.astype(np.uint32).copy()
-        bound = 2 * DRIFT_TINYLLAMA_2
+        bound = 2 * (DRIFT_TINYLLAMA_2 if preset == 2 else DRIFT_LLAMA3[2])
         for step in range(4):
             lg, am = eb.forward_batch(np.arange(B), np.array(cur, np.uint32), pos, want_logits=True)
             for i in range(B):
