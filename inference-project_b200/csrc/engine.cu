@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <unordered_map>
 #include <utility>
@@ -873,6 +874,9 @@ Error_t release_pages(InfEngine* e, u32 slot)
 {
 	std::vector<int>& pg = e->seq_pages[slot];
 	for (int p : pg) e->free_pages.push_back(p);
+	// lowest ids are handed out first, so a sequence gets consecutive pages again (the prefill
+	// attention loads a tile of consecutive pages with one copy)
+	std::sort(e->free_pages.begin(), e->free_pages.end(), std::greater<int>());
 	pg.clear();
 	std::fill(e->h_block_table.begin() + (size_t)slot * e->pages_per_seq,
 	          e->h_block_table.begin() + (size_t)(slot + 1) * e->pages_per_seq, -1);
