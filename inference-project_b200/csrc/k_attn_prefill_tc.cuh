@@ -26,7 +26,7 @@ namespace inf {
 constexpr int kPtRows = 128;       // query rows per CTA (MMA M)
 constexpr int kPtKeys = 128;       // keys per tile (MMA N of S, K of P.V)
 constexpr int kPtStages = 2;
-constexpr int kPtThreads = 192;
+constexpr int kPtThreads = 320; // TMA warp, MMA warp, 8 softmax warps
 constexpr uint32_t kPtAtom = 128 * 64 * 2; // one [128 x 64] bf16 SWIZZLE_128B block: 16 KB
 
 // shared-memory descriptor with explicit leading / stride byte offsets (SWIZZLE_128B)
@@ -106,7 +106,7 @@ __host__ __device__ inline PtLayout pt_layout(int hd)
 	L.v = L.k + (size_t)kPtStages * L.tile_bytes;
 	L.p = L.v + (size_t)kPtStages * L.tile_bytes;
 	L.bars = L.p + 2 * (size_t)2 * kPtAtom; // two P buffers of [128 rows x 128 keys]
-	L.total = L.bars + 256;
+	L.total = L.bars + 256 + 2 * 128 * 4; // barriers, flags, the halves' row maxima [2][128]
 	return L;
 }
 inline size_t attn_prefill_tc_smem_bytes(int hd) { return 1024 + pt_layout(hd).total; }
@@ -142,9 +142,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 	uint64_t* v_empty = bars + 6;  // [2] P.V MMA done with the V tile
 	uint64_t* s_full = bars + 8;   // [2] S buffer b ready (MMA -> softmax)
 	uint64_t* p_free = bars + 10;  // [2] P buffer b read by its P.V MMA
-	uint64_t* bar_p = bars + 12;   // P of tile j written, its S consumed (128 arrivals)
+	uint64_t* bar_p = bars + 12;   // P of tile j written, its S consumed (256 arrivals)
 	uint64_t* bar_o = bars + 13;   // P.V of tile j done
-	uint64_t* bar_q = bars + 14;   // Q staged (128 arrivals)
+	uint64_t* bar_q = bars + 14;   // Q staged (256 arrivals)
 	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 	volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -161,9 +161,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 
 	if (threadIdx.x == 0) {
 		for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
-		mbar_init(bar_p, 128);
+		mbar_init(bar_p, 256);
 		mbar_init(bar_o, 1);
-		mbar_init(bar_q, 128);
+		mbar_init(bar_q, 256);
 		*abort_flag = 0;
 		mbar_fence_init();
 	}
@@ -281,18 +281,26 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 			}
 		}
 	} else {
-		// ---------------- softmax / epilogue: TMEM lane quarter = warp % 4, one row per thread
-		const int quarter = warp & 3;
+		// ---------------- softmax / epilogue: eight warps, two per TMEM lane quarter; a row's
+		// 128 scores are split in halves (warps 2-5: keys 0-63, warps 6-9: keys 64-127), the
+		// halves exchange their maxima through shared memory, and each half rescales and
+		// stores its half of the O columns
+		const int quarter = warp & 3, half = (warp - 2) >> 2;
 		const int r = quarter * 32 + lane;
 		const int tq = r / G, g = r % G;
 		const bool valid = tq < n_tok;
 		const int pos = valid ? a.tok_pos[t0 + tq] : -1;
 		const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-		// Q row -> shared memory, swizzled (K-major SWIZZLE_128B, one block per 64 head dims)
+		float* xmax = reinterpret_cast<float*>(smem + Ly.bars + 256); // [2 halves][128 rows]
+		constexpr int kHalfKeys = kPtKeys / 2;
+		const int hd_half = hd / 2;
+		// Q row -> shared memory, swizzled (K-major SWIZZLE_128B, one block per 64 head dims);
+		// each half loads half of the row's 16-byte chunks
 		{
 			const uint4* src = reinterpret_cast<const uint4*>(
 			    reinterpret_cast<const bf16*>(a.q) + ((size_t)(t0 + (valid ? tq : 0)) * a.H + kvh * G + g) * hd);
-			for (int c = 0; c < hd / 8; ++c) {
+			const int nc = hd / 8;
+			for (int c = half * (nc / 2); c < (half + 1) * (nc / 2); ++c) {
 				const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
 				*reinterpret_cast<uint4*>(q_s + (size_t)(c >> 3) * kPtAtom + sw128_off(r, c & 7)) = v;
 			}
@@ -305,83 +313,89 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 			const bool w = mbar_wait(bar, par, abort_flag, a.err);
 			return __all_sync(0xFFFFFFFFu, w);
 		};
-		float m = -INFINITY, l = 0.0f; // m: the max the P values are taken against
+		float m = -INFINITY, l = 0.0f; // m: the max the P values are taken against; l: this half's sum
 		bool ok = true;
+		// every softmax thread reaches both named barriers of every tile (no early exit)
 		for (int j = 0; j < n_tiles; ++j) {
-			if (!wait_all(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) {
-				ok = false;
-				break;
-			}
-			tc_fence_after();
-			const uint32_t ts = tmem + (uint32_t)(j & 1) * kPtKeys + lane_off;
-			const int kbase = j * kPtKeys;
-			const bool masked = kbase + kPtKeys - 1 > pos; // the diagonal tile (or an invalid row)
-			float v[kPtKeys];
-#pragma unroll
-			for (int c = 0; c < kPtKeys; c += 32) tmem_ld_32cols_nowait(ts + (uint32_t)c, v + c);
-			asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+			ok = ok && wait_all(&s_full[j & 1], (uint32_t)(j >> 1) & 1u);
+			const int kbase = j * kPtKeys + half * kHalfKeys;
+			float v[kHalfKeys];
 			float mt = -INFINITY;
+			if (ok) {
+				tc_fence_after();
+				const uint32_t ts = tmem + (uint32_t)(j & 1) * kPtKeys + (uint32_t)(half * kHalfKeys) + lane_off;
+				const bool masked = kbase + kHalfKeys - 1 > pos; // the diagonal tile (or an invalid row)
 #pragma unroll
-			for (int i = 0; i < kPtKeys; ++i) {
-				v[i] *= sl2;
-				if (masked && kbase + i > pos) v[i] = -INFINITY;
-				mt = fmaxf(mt, v[i]);
+				for (int c = 0; c < kHalfKeys; c += 32) tmem_ld_32cols_nowait(ts + (uint32_t)c, v + c);
+				asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+				for (int i = 0; i < kHalfKeys; ++i) {
+					v[i] *= sl2;
+					if (masked && kbase + i > pos) v[i] = -INFINITY;
+					mt = fmaxf(mt, v[i]);
+				}
 			}
-			// rescale only when the max grows by more than 2^8 (or on the first finite max)
+			xmax[half * kPtRows + r] = mt;
+			named_bar_sync(1, 256);
+			mt = fmaxf(mt, xmax[(half ^ 1) * kPtRows + r]);
+			named_bar_sync(1, 256); // both halves have read before the next tile's writes
+			// rescale only when the max grows by more than 2^8 (or on the first finite max);
+			// both halves of a row take the same decision
 			const bool grow = mt > m + kPtRescaleLog2 || (m == -INFINITY && mt != -INFINITY);
 			const float mn = grow ? mt : m;
-			if (__any_sync(0xFFFFFFFFu, grow) && j > 0) {
+			if (ok && __any_sync(0xFFFFFFFFu, grow) && j > 0) {
 				// O must hold every earlier P.V before it is rescaled
-				if (!wait_all(bar_o, (uint32_t)(j - 1) & 1u)) {
-					ok = false;
-					break;
-				}
-				tc_fence_after();
-				const float alpha = grow && m != -INFINITY ? ex2_approx(m - mn) : 1.0f;
+				ok = wait_all(bar_o, (uint32_t)(j - 1) & 1u);
+				if (ok) {
+					tc_fence_after();
+					const float alpha = grow && m != -INFINITY ? ex2_approx(m - mn) : 1.0f;
 #pragma unroll 1
-				for (int c = 0; c < hd; c += 32) {
-					float o[32];
-					tmem_ld_32cols(tmem_o + lane_off + (uint32_t)c, o);
+					for (int c = half * hd_half; c < (half + 1) * hd_half; c += 32) {
+						float o[32];
+						tmem_ld_32cols(tmem_o + lane_off + (uint32_t)c, o);
 #pragma unroll
-					for (int i = 0; i < 32; ++i) o[i] *= alpha;
-					tmem_st_32cols(tmem_o + lane_off + (uint32_t)c, o);
+						for (int i = 0; i < 32; ++i) o[i] *= alpha;
+						tmem_st_32cols(tmem_o + lane_off + (uint32_t)c, o);
+					}
 				}
-				l *= alpha;
 			}
+			if (grow && m != -INFINITY) l *= ex2_approx(m - mn);
 			m = mn;
 			// P buffer j&1 was last read by the P.V of tile j-2
-			if (j >= 2 && !wait_all(&p_free[j & 1], (uint32_t)((j >> 1) - 1) & 1u)) {
-				ok = false;
-				break;
-			}
-			uint8_t* pb = p_s + (size_t)(j & 1) * 2 * kPtAtom;
-			float sum = 0.0f;
+			if (ok && j >= 2) ok = wait_all(&p_free[j & 1], (uint32_t)((j >> 1) - 1) & 1u);
+			if (ok) {
+				uint8_t* pb = p_s + (size_t)(j & 1) * 2 * kPtAtom + (size_t)half * kPtAtom; // this half's 64 keys
+				float sum = 0.0f;
 #pragma unroll
-			for (int c = 0; c < kPtKeys; c += 8) {
-				uint32_t pk[4];
+				for (int c = 0; c < kHalfKeys; c += 8) {
+					uint32_t pk[4];
 #pragma unroll
-				for (int i = 0; i < 8; i += 2) {
-					const float p0 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i] - m);
-					const float p1 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i + 1] - m);
-					const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
-					// the row sum adds the rounded values, the weights the MMA applies
-					sum += __low2float(b) + __high2float(b);
-					pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&b);
+					for (int i = 0; i < 8; i += 2) {
+						const float p0 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i] - m);
+						const float p1 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i + 1] - m);
+						const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
+						// the row sum adds the rounded values, the weights the MMA applies
+						sum += __low2float(b) + __high2float(b);
+						pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&b);
+					}
+					*reinterpret_cast<uint4*>(pb + sw128_off(r, c >> 3)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 				}
-				*reinterpret_cast<uint4*>(pb + (size_t)(c >> 6) * kPtAtom + sw128_off(r, (c & 63) >> 3)) =
-				    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+				l += sum;
+				asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+				tc_fence_before();
+				mbar_arrive(bar_p);
 			}
-			l += sum;
-			asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-			tc_fence_before();
-			mbar_arrive(bar_p);
 		}
+		// the row's sum: both halves
+		xmax[half * kPtRows + r] = l;
+		named_bar_sync(1, 256);
+		const float lt = l + xmax[(half ^ 1) * kPtRows + r];
 		if (ok && wait_all(bar_o, (uint32_t)(n_tiles - 1) & 1u)) {
 			tc_fence_after();
-			const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+			const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
 			bf16* dst = reinterpret_cast<bf16*>(a.out) + (size_t)(t0 + (valid ? tq : 0)) * a.H * hd + (size_t)(kvh * G + g) * hd;
 #pragma unroll 1
-			for (int c = 0; c < hd; c += 32) {
+			for (int c = half * hd_half; c < (half + 1) * hd_half; c += 32) {
 				float o[32];
 				tmem_ld_32cols(tmem_o + lane_off + (uint32_t)c, o);
 				if (valid) {
