@@ -770,11 +770,14 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 			a.out = e->attn_p;
 			a.err = e->err;
 			// tensor-core (mma) scores and P.V where the shape allows, else the SIMT streaming kernel
-			const AttnKernel<bf16> am = attn_decode_mma_kernel(e->Hl / e->KVl, hd);
-			if (am) {
+			const AttnMmaKernel am = attn_decode_mma_kernel(e->Hl / e->KVl, hd);
+			if (am && c.kv_block == 16) { // 64-position chunks = 8 KB per 64 head dims
 				const size_t smem = attn_mma_smem_bytes(hd, (int)c.kv_block, e->pages_per_seq);
+				CUtensorMap tk, tv; // one page (blk positions x 64 head dims) per box
+				INF_TRY(tensor_map_kv(&tk, L.kpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
+				INF_TRY(tensor_map_kv(&tv, L.vpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
 				INF_CUDA_TRY(set_smem(am, smem));
-				INF_CUDA_TRY(launch(e, am, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAmThreads), smem, a));
+				INF_CUDA_TRY(launch(e, am, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAmThreads), smem, tk, tv, a));
 			} else {
 				const size_t smem = attn_stream_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2);
 				const AttnKernel<bf16> ak = attn_decode_stream_kernel<bf16>(e->Hl / e->KVl, hd);

@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "k_attn_decode.cuh"        // AttnDecodeArgs, AttnKernel, attn_vpl
 #include "k_attn_decode_stream.cuh" // kStChunkPages, kStBufs, attn_stream_splits
+#include "k_attn_prefill_tc.cuh"    // tma_load_4d (4-D boxes of the paged K/V pool)
 
 namespace inf {
 
@@ -30,7 +31,7 @@ __host__ __device__ inline size_t attn_mma_region_bytes(int hd, int blk)
 // region, the split's page ids (at most pages_per_seq), the chunk mbarriers
 inline size_t attn_mma_smem_bytes(int hd, int blk, int pages_per_seq)
 {
-	return attn_mma_region_bytes(hd, blk) + (((size_t)pages_per_seq * 4 + 15) & ~(size_t)15) + kStBufs * sizeof(uint64_t);
+	return 1024 + attn_mma_region_bytes(hd, blk) + (((size_t)pages_per_seq * 4 + 15) & ~(size_t)15) + kStBufs * sizeof(uint64_t);
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
@@ -47,11 +48,33 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
 }
 __device__ __forceinline__ uint32_t pack_raw_bf16(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3)
+{
+	asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+	             : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+	             : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3)
+{
+	asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+	             : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+	             : "r"(addr));
+}
+// A chunk of K or V in shared memory: [head_dim / 64 halves][64 positions][128 bytes], each
+// half in SWIZZLE_128B atoms (8 positions x 128 bytes) as the TMA boxes write it.
+__device__ __forceinline__ uint32_t kv_sw_addr(uint32_t base, int r, int c16, int half)
+{
+	return base + (uint32_t)half * 8192u + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c16 ^ (r & 7)) << 4));
+}
+
 template <int G, int HD>
-__global__ void __launch_bounds__(kAmThreads) k_attn_decode_mma(const AttnDecodeArgs a)
+__global__ void __launch_bounds__(kAmThreads)
+    k_attn_decode_mma(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const AttnDecodeArgs a)
 {
 	static_assert(G >= 1 && G <= 16 && (HD == 64 || HD == 128), "rows / head_dim");
-	extern __shared__ __align__(128) uint8_t sm_raw[];
+	extern __shared__ __align__(1024) uint8_t sm_base[];
+	// 1024-byte aligned: the TMA boxes are SWIZZLE_128B atoms
+	uint8_t* sm_raw = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_base) + 1023) & ~(uintptr_t)1023);
 	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
 	const int blk = a.blk;
 	const int CT = kStChunkPages * blk;
@@ -102,11 +125,13 @@ __global__ void __launch_bounds__(kAmThreads) k_attn_decode_mma(const AttnDecode
 				report_err(a.err, kDevKvRange);
 				continue; // masked below
 			}
-			const size_t off = (((size_t)page * a.KV + kvh) * blk) * HD;
-			bulk_g2s(kbuf + (size_t)buf * chunk_bytes + (size_t)(q - q0) * blk_bytes, reinterpret_cast<const bf16*>(a.kpool) + off,
-			         (uint32_t)blk_bytes, &bars[buf], pol);
-			bulk_g2s(vbuf + (size_t)buf * chunk_bytes + (size_t)(q - q0) * blk_bytes, reinterpret_cast<const bf16*>(a.vpool) + off,
-			         (uint32_t)blk_bytes, &bars[buf], pol);
+			// one box of blk positions x 64 head dims per half, swizzled for ldmatrix
+			for (int h = 0; h < HD / 64; ++h) {
+				tma_load_4d(kbuf + (size_t)buf * chunk_bytes + (size_t)h * 8192 + (size_t)(q - q0) * blk * 128, &tm_k, h * 64, 0,
+				            kvh, page, &bars[buf], pol);
+				tma_load_4d(vbuf + (size_t)buf * chunk_bytes + (size_t)h * 8192 + (size_t)(q - q0) * blk * 128, &tm_v, h * 64, 0,
+				            kvh, page, &bars[buf], pol);
+			}
 		}
 	};
 	if (tid == 0)
@@ -142,20 +167,22 @@ __global__ void __launch_bounds__(kAmThreads) k_attn_decode_mma(const AttnDecode
 		const int n_tok = (min(np, q0 + kStChunkPages) - q0) * blk;
 		const int kb = warp * 16; // this warp's 16 positions of the chunk
 		if (kb < n_tok && !abort_flag) {
-			const uint16_t* kc = reinterpret_cast<const uint16_t*>(kbuf + (size_t)buf * chunk_bytes);
-			const uint16_t* vc = reinterpret_cast<const uint16_t*>(vbuf + (size_t)buf * chunk_bytes);
-			// S = Q.K^T for 16 positions (two 8-position tiles)
+			const uint32_t kc = smem_u32(kbuf + (size_t)buf * chunk_bytes);
+			const uint32_t vc = smem_u32(vbuf + (size_t)buf * chunk_bytes);
+			// S = Q.K^T for 16 positions (two 8-position tiles); ldmatrix x4: matrices
+			// (tile 0, dims +0..7), (tile 0, +8..15), (tile 1, +0..7), (tile 1, +8..15)
 			float s[2][4];
 #pragma unroll
-			for (int nt = 0; nt < 2; ++nt) {
-				s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-				const uint16_t* kr = kc + (size_t)(kb + nt * 8 + gr) * HD;
+			for (int nt = 0; nt < 2; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+			const int mi = lane >> 3, mr = lane & 7; // the matrix and row this lane addresses
+			const int krow = kb + (mi >> 1) * 8 + mr;
 #pragma unroll
-				for (int ks = 0; ks < HD / 16; ++ks) {
-					const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + gc);
-					const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + gc + 8);
-					mma_bf16_16816(s[nt], qa[ks], b0, b1);
-				}
+			for (int ks = 0; ks < HD / 16; ++ks) {
+				const int c16 = (ks & 3) * 2 + (mi & 1);
+				uint32_t b00, b01, b10, b11;
+				ldsm_x4(kv_sw_addr(kc, krow, c16, ks >> 2), b00, b01, b10, b11);
+				mma_bf16_16816(s[0], qa[ks], b00, b01);
+				mma_bf16_16816(s[1], qa[ks], b10, b11);
 			}
 			// scale (log2 units) and mask positions past the context or on invalid pages
 			const int tok0 = (p_begin + q0) * blk;
@@ -204,17 +231,23 @@ __global__ void __launch_bounds__(kAmThreads) k_attn_decode_mma(const AttnDecode
 			l0 = l0 * al0 + sum0;
 			l1 = l1 * al1 + sum1;
 			// O = O * alpha + P.V
+			// ldmatrix x4 trans: matrices (positions +0..7, dims dt), (+8..15, dt), (+0..7, dt+1),
+			// (+8..15, dt+1) are the B fragments of two 8-dim output tiles
+			const int vrow = kb + (mi & 1) * 8 + mr;
 #pragma unroll
-			for (int dt = 0; dt < HD / 8; ++dt) {
-				o[dt][0] *= al0;
-				o[dt][1] *= al0;
-				o[dt][2] *= al1;
-				o[dt][3] *= al1;
-				const int dim = dt * 8 + gr;
-				const uint16_t* v0 = vc + (size_t)(kb + gc) * HD + dim;
-				const uint32_t b0 = pack_raw_bf16(v0[0], v0[HD]);
-				const uint32_t b1 = pack_raw_bf16(v0[8 * HD], v0[9 * HD]);
+			for (int dt = 0; dt < HD / 8; dt += 2) {
+#pragma unroll
+				for (int u = 0; u < 2; ++u) {
+					o[dt + u][0] *= al0;
+					o[dt + u][1] *= al0;
+					o[dt + u][2] *= al1;
+					o[dt + u][3] *= al1;
+				}
+				const int d16 = dt + (mi >> 1); // 8-dim chunk index over head_dim
+				uint32_t b0, b1, c0, c1;
+				ldsm_x4_trans(kv_sw_addr(vc, vrow, d16 & 7, d16 >> 3), b0, b1, c0, c1);
 				mma_bf16_16816(o[dt], pa, b0, b1);
+				mma_bf16_16816(o[dt + 1], pa, c0, c1);
 			}
 		}
 		__syncthreads(); // every warp is done with the chunk's buffer
@@ -294,8 +327,10 @@ __global__ void __launch_bounds__(kAmThreads) k_attn_decode_mma(const AttnDecode
 	if (tid == 0) a.counters[b * a.KV + kvh] = 0u;
 }
 
+typedef void (*AttnMmaKernel)(CUtensorMap, CUtensorMap, AttnDecodeArgs);
+
 // the instantiation for GQA group G (<= 8) and head_dim 64 / 128 (nullptr otherwise)
-inline AttnKernel<bf16> attn_decode_mma_kernel(int G, int hd)
+inline AttnMmaKernel attn_decode_mma_kernel(int G, int hd)
 {
 #define INF_AM_CASE(g)                                               \
 	if (G == g && hd == 64) return k_attn_decode_mma<g, 64>;     \
