@@ -9,10 +9,12 @@
 //   warp 1      allocates TMEM (S: 128 columns, O: head_dim columns) and issues, from one
 //               thread, S = Q.K^T (both operands K-major) and O += P.V (P K-major from shared
 //               memory, V MN-major: the page rows are keys, contiguous along head_dim);
-//   warps 2..5  load Q once (swizzled by hand), then per tile read their row of S from TMEM,
-//               mask keys past the row's position, keep the running max and sum, write
-//               P = exp(S - max) as bf16 in the swizzled K-major layout, and rescale O in TMEM
-//               when the max grows; at the end O / sum is stored as bf16.
+//   warps 2..9  load Q once (swizzled by hand), then per tile read S from TMEM -- two warps
+//               per TMEM lane quarter, each on half of a row's 128 scores, the halves' maxima
+//               exchanged through shared memory -- mask keys past the row's position, keep the
+//               running max and sum, write P = exp(S - max) as bf16 in the swizzled K-major
+//               layout, and rescale their half of O in TMEM when the max grows by more than
+//               2^8; at the end O / sum is stored as bf16.
 // Rounding: S and O accumulate in fp32, P is rounded to bf16 for the second MMA (the SIMT
 // kernel k_attn_prefill.cuh keeps P in fp32).  Every wait is bounded; on a timeout the
 // kernel records kDevTimeout, lets its copies and MMAs drain, frees TMEM and returns.
