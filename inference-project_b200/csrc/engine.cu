@@ -716,8 +716,9 @@ Error_t run_prefill(InfEngine* e, u32 n, u32 start, u32 slot)
 bool use_tc_prefill(const InfEngine* e, u32 n) { return e->cfg.dtype == InfBF16 && e->chunk > 0 && n > 1; }
 
 // One decode token for each of B sequences (ids in d_ids, slots/positions in tok_slot/tok_pos):
-// the projections run once for all B tokens on the tensor cores, attention is the split-K
-// decode kernel with one grid slice per token, the LM head is a GEMM plus a row argmax.
+// the projections run once for all B tokens on the tensor cores (split-K when there are few
+// output tiles), attention is the streaming mma kernel with one grid slice per token, the LM
+// head is a GEMM whose epilogue folds the greedy argmax of every row.
 Error_t enqueue_decode_batch(InfEngine* e, int B)
 {
 	const InfConfig& c = e->cfg;

@@ -5,7 +5,10 @@
 // that share it (GQA), so every K/V page is read once for the whole group -- and a
 // contiguous range of at most max_pages_split pages of the token's context.
 //
-// At batch 1 a layer's KV is a few MB, so the kernel is built for latency:
+// It serves batch-1 decode when the context is too long for the cluster kernel
+// (k_attn_cluster.cuh) and the stand-alone inf_attn_decode / inf_attn_decode_noalloc entry
+// points; batches run the streaming tensor-core kernel (k_attn_decode_mma.cuh).  A layer's
+// KV of one token is a few MB, so the kernel is built for latency:
 //   * every page of the split is fetched at once with a 1-D bulk copy per K and V block,
 //     each page on its own mbarrier; pages older than the current token's page are issued
 //     before griddepcontrol.wait (earlier steps wrote them), overlapping the QKV kernel that
