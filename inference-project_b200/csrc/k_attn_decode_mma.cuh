@@ -2,7 +2,11 @@
 //
 // The same decomposition as the streaming kernel (k_attn_decode_stream.cuh): grid
 // (kv_heads, splits, tokens), a CTA streams its pages through a ring of shared-memory chunks
-// of 64 positions.  The arithmetic moves to warp-level mma.m16n8k16 (bf16 in, fp32 out): the
+// of 64 positions.  Thread 0 reads the split's page ids into shared memory once and loads each
+// page of K and V with 4-D TMA boxes (64 head dims x 16 positions x 1 head x 1 page,
+// SWIZZLE_128B), one box per 64-dim half, so the K and V fragments come from ldmatrix (.x4 for
+// K, .x4.trans for V) without bank conflicts; pages of 16 positions only.
+// The arithmetic moves to warp-level mma.m16n8k16 (bf16 in, fp32 out): the
 // G query heads of the KV head are the rows of a 16-row A tile (rows >= G are zero), each of
 // the four warps takes 16 positions of a chunk, computes S = Q.K^T (2 x head_dim/16 MMAs),
 // keeps a per-row running max / sum (online softmax on the accumulator fragments), turns

@@ -1,6 +1,8 @@
-// Decode attention for batches of tokens with long contexts: the K/V pages of a split are
-// streamed through a ring of shared-memory chunks with an online softmax, so a split may
-// cover any number of pages and the grid stays a few CTAs per SM.
+// Decode attention for batches of tokens (SIMT): the K/V pages of a split are streamed through
+// a ring of shared-memory chunks with an online softmax, so a split may cover any number of
+// pages and the grid stays a few CTAs per SM.  Batches run the tensor-core kernel of the same
+// decomposition (k_attn_decode_mma.cuh) when the pages hold 16 positions and the GQA group and
+// head size have an instance there; this kernel serves the other shapes.
 //
 // Grid (kv_heads, splits, tokens); a CTA owns one KV head of one token (its G query heads)
 // and a contiguous range of the token's pages, read in chunks of kStChunkPages pages

@@ -9,7 +9,11 @@
 //               frees each stage and finally signals the accumulator
 //   warps 2..5  epilogue: tcgen05.ld 32x32b (row = TMEM lane = token) and the same fused
 //               epilogues as the decode GEMV (store, residual add, RoPE + KV-cache write,
-//               SwiGLU) on adjacent column pairs
+//               SwiGLU) on adjacent column pairs, or fp32 logits with a per-row greedy
+//               argmax folded in (atomicMax of a (value, column) key)
+// When the output has too few tiles to fill the SMs (a batch of decode tokens), blockIdx.z
+// splits the K blocks; each split writes fp32 partials and k_gemm_splitk_reduce sums them
+// and runs the epilogue.
 // Every wait is bounded; on a timeout the kernel records kDevTimeout, lets its copies and
 // MMAs drain, frees TMEM and returns.
 #pragma once
