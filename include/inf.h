@@ -206,7 +206,11 @@ Error_t inf_attn_decode_noalloc(const void* d_q, const void* d_kpool, const void
  * 5 Llama-3-8B 32k prefill. */
 Error_t inf_config_preset(u32 preset, InfConfig* out);
 /* model_build (src/main.cu:200-352).  weights_path NULL: synthetic weights N(0, init_std)
- * from `seed` (Philox4x32-10), gains 1.0.  Creates *ctx if it is NULL. */
+ * from `seed` (Philox4x32-10), gains 1.0.  Otherwise a safetensors checkpoint (one file, a
+ * *.safetensors.index.json of shards, or a directory holding model.safetensors.index.json or
+ * model.safetensors), checked as inf_safetensors_check does before any device memory is
+ * taken, then copied to the device through pinned staging buffers; seed is unused.
+ * Creates *ctx if it is NULL. */
 Error_t inf_model_build(ExecCtx** ctx, Model* model, const InfConfig* config, const char* weights_path, u64 seed);
 /* model_destroy (src/main.cu:354-358) */
 Error_t inf_model_destroy(ExecCtx** ctx, Model* model);
@@ -240,6 +244,51 @@ Error_t inf_tp_export(Model* model, void* handle_out, u64 handle_bytes); /* 64-b
 Error_t inf_tp_connect(Model* model, const void* handles, u32 n_ranks);
 /* Release the KV pages of a sequence slot. */
 Error_t inf_seq_reset(Model* model, u32 seq_slot);
+
+/* ---- checkpoints ------------------------------------------------------------------ */
+/* model_parse_config (src/main.cu:120-157): reads a Hugging Face config.json -- its
+ * "text_config" object when there is one (as the reference does), else the top level -- into
+ * *inout: hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
+ * num_key_value_heads (default num_attention_heads), head_dim (default hidden_size /
+ * num_attention_heads), vocab_size, rms_norm_eps, rope_theta and torch_dtype ("bfloat16" or
+ * "float32").  A field the file lacks keeps its value; max_seq, max_batch, the KV paging and the
+ * tensor-parallel fields are never taken from the file.  ErrorIo if the file cannot be read,
+ * ErrorInvalidValue for malformed JSON or a field of the wrong type or range. */
+Error_t inf_config_from_json(const char* config_path, InfConfig* inout);
+
+/* The checkpoint checks of model_build without a GPU.  Every tensor the decoder of `config`
+ * needs must be present under its Hugging Face Llama name, "model." or
+ * "model.language_model." + embed_tokens.weight, norm.weight and
+ * layers.<i>.{input_layernorm, post_attention_layernorm}.weight,
+ * layers.<i>.self_attn.{q,k,v,o}_proj.weight, layers.<i>.mlp.{gate,up,down}_proj.weight, plus
+ * lm_head.weight (absent: the embedding is the LM head), in dtype BF16 or F32 (converted to
+ * config->dtype, bf16 by round-to-nearest-even) and with the shape config implies.  The file
+ * itself must follow the safetensors format: an 8-byte little-endian header length, a JSON
+ * header of at most 100,000,000 bytes, offsets relative to the byte buffer after the header
+ * (the reference adds them to the file start, defect D7), sizes equal to shape x dtype size,
+ * and a buffer indexed without holes or overlaps.
+ * ErrorIo: a file cannot be opened or mapped.  ErrorInvalidValue: malformed header, offsets or
+ * index, or a missing tensor.  ErrorBadConfig: a shape that does not match config.
+ * ErrorUnsupported: a needed tensor in another dtype. */
+Error_t inf_safetensors_check(const char* weights_path, const InfConfig* config);
+
+/* Weights of the decoder, by their place in the device layout. */
+typedef enum InfWeightKind {
+	InfWEmbed     = 0,  /* [vocab_size x dim] */
+	InfWLmHead    = 1,  /* [vocab_size / tp x dim], rank's vocabulary rows */
+	InfWFinalNorm = 2,  /* [1 x dim] */
+	InfWQkv       = 8,  /* [(H + 2 KV) / tp * head_dim x dim]: q, k, v heads, rows (i, i + head_dim/2) paired */
+	InfWO         = 11, /* [dim x H / tp * head_dim], rank's columns */
+	InfWGateUp    = 12, /* [2 ffn_dim / tp x dim], rows gate_0, up_0, gate_1, ... */
+	InfWDown      = 14, /* [dim x ffn_dim / tp], rank's columns */
+	InfWAttnNorm  = 15, /* [1 x dim] */
+	InfWFfnNorm   = 16, /* [1 x dim] */
+} InfWeightKind;
+/* One weight of `layer` (ignored for embed, LM head and final norm) as inf_model_build writes
+ * it to rank config->tp_rank's device memory, read from the checkpoint into host memory `out`
+ * (out_bytes at least rows x cols x the dtype's size).  Host only, no device work. */
+Error_t inf_safetensors_read(const char* weights_path, const InfConfig* config, u32 layer, u32 kind, void* out,
+                             u64 out_bytes);
 
 /* Synthetic inputs: n integers uniform in [lo, hi_inclusive] from Philox4x32-10 keyed by
  * SplitMix64(SplitMix64(seed) ^ stream), counter i, Lemire multiply-shift.  Prompt ids use

@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstring>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <utility>
@@ -27,6 +28,7 @@
 #include "k_attn_prefill_tc.cuh"
 #include "k_gemm_tc.cuh"
 #include "k_small.cuh"
+#include "loader.h"
 #include "runtime.h"
 #include "synth.cuh"
 
@@ -1041,12 +1043,13 @@ void rope_tables(const InfConfig& c, std::vector<float>& cs, std::vector<float>&
 		}
 }
 
-Error_t engine_build(InfEngine* e, u64 seed)
+Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 {
 	InfConfig& c = e->cfg;
 	if (c.kv_block == 0) c.kv_block = 16;
 	if (c.tp_size == 0) c.tp_size = 1;
 	INF_TRY(validate(c));
+	if (ck) INF_TRY(checkpoint_check(*ck, c)); // every tensor present, dtypes and shapes, before the device is touched
 	INF_CUDA_TRY(cudaGetDevice(&e->device));
 	INF_CUDA_TRY(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, e->device));
 	INF_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
@@ -1181,8 +1184,27 @@ Error_t engine_build(InfEngine* e, u64 seed)
 
 	INF_CUDA_TRY(cudaMemsetAsync(e->ctx->dev_arena._d_ptr + w_begin + e->weight_bytes, 0,
 	                             arena_dev_pos_get(&e->ctx->dev_arena) - w_begin - e->weight_bytes, e->stream));
-	if (c.dtype == InfBF16) INF_TRY(generate_weights<bf16>(e, seed));
-	else INF_TRY(generate_weights<float>(e, seed));
+	if (ck) {
+		std::vector<WeightDst> w;
+		w.push_back({0, InfWEmbed, e->embed});
+		for (u32 l = 0; l < L; ++l) {
+			const LayerW& Ly = e->layers[l];
+			const int li = (int)l;
+			w.push_back({li, InfWQkv, Ly.wqkv});
+			w.push_back({li, InfWO, Ly.wo});
+			w.push_back({li, InfWGateUp, Ly.wgu});
+			w.push_back({li, InfWDown, Ly.wd});
+			w.push_back({li, InfWAttnNorm, Ly.attn_norm});
+			w.push_back({li, InfWFfnNorm, Ly.ffn_norm});
+		}
+		w.push_back({0, InfWFinalNorm, e->final_norm});
+		w.push_back({0, InfWLmHead, e->lm_head});
+		INF_TRY(checkpoint_upload(*ck, c, w, e->stream));
+	} else if (c.dtype == InfBF16) {
+		INF_TRY(generate_weights<bf16>(e, seed));
+	} else {
+		INF_TRY(generate_weights<float>(e, seed));
+	}
 
 	std::vector<float> cs, sn;
 	rope_tables(c, cs, sn);
@@ -1325,12 +1347,17 @@ Error_t inf_config_preset(u32 preset, InfConfig* out)
 Error_t inf_model_build(ExecCtx** ctx, Model* model, const InfConfig* config, const char* weights_path, u64 seed)
 {
 	if (!ctx || !model || !config) return fail(ErrorInvalidValue, "inf_model_build: NULL argument");
-	if (weights_path) return fail(ErrorUnsupported, "checkpoint loading is not built; pass NULL for synthetic weights");
+	std::unique_ptr<Checkpoint> ck;
+	if (weights_path) { // opened and indexed before any device work
+		ck.reset(new (std::nothrow) Checkpoint());
+		if (!ck) return fail(ErrorMemoryAllocation, "checkpoint");
+		INF_TRY(checkpoint_open(weights_path, ck.get()));
+	}
 	InfEngine* e = new (std::nothrow) InfEngine();
 	if (!e) return fail(ErrorMemoryAllocation, "engine");
 	e->cfg = *config;
 	e->ctx = *ctx;
-	Error_t r = engine_build(e, seed);
+	Error_t r = engine_build(e, seed, ck.get());
 	if (r != Success) {
 		ExecCtx* c = e->ctx;
 		engine_free(e);
@@ -1344,6 +1371,43 @@ Error_t inf_model_build(ExecCtx** ctx, Model* model, const InfConfig* config, co
 	model->model_bsize = e->weight_bytes;
 	model->engine = e;
 	return Success;
+}
+
+Error_t inf_config_from_json(const char* config_path, InfConfig* inout) { return config_from_json(config_path, inout); }
+
+// the config as engine_build sees it: defaults filled in, shape rules checked
+static Error_t checkpoint_config(const InfConfig* config, InfConfig* c)
+{
+	if (!config) return fail(ErrorInvalidValue, "NULL config");
+	*c = *config;
+	if (c->kv_block == 0) c->kv_block = 16;
+	if (c->tp_size == 0) c->tp_size = 1;
+	return validate(*c);
+}
+
+Error_t inf_safetensors_check(const char* weights_path, const InfConfig* config)
+{
+	InfConfig c;
+	INF_TRY(checkpoint_config(config, &c));
+	Checkpoint ck;
+	INF_TRY(checkpoint_open(weights_path, &ck));
+	return checkpoint_check(ck, c);
+}
+
+Error_t inf_safetensors_read(const char* weights_path, const InfConfig* config, u32 layer, u32 kind, void* out, u64 out_bytes)
+{
+	InfConfig c;
+	INF_TRY(checkpoint_config(config, &c));
+	if (!out) return fail(ErrorInvalidValue, "inf_safetensors_read: NULL out");
+	const bool per_layer = kind != InfWEmbed && kind != InfWLmHead && kind != InfWFinalNorm;
+	if (per_layer && layer >= c.n_layers) return fail(ErrorInvalidValue, "layer %u of %u", layer, c.n_layers);
+	u64 rows, cols;
+	weight_dims(c, kind, &rows, &cols);
+	const u64 need = rows * cols * (c.dtype == InfBF16 ? 2 : 4);
+	if (out_bytes < need) return fail(ErrorInvalidValue, "out holds %llu bytes, the weight needs %llu", (unsigned long long)out_bytes, (unsigned long long)need);
+	Checkpoint ck;
+	INF_TRY(checkpoint_open(weights_path, &ck));
+	return weight_rows(ck, c, per_layer ? (int)layer : 0, kind, 0, rows, out);
 }
 
 Error_t inf_model_destroy(ExecCtx** ctx, Model* model)

@@ -81,7 +81,6 @@ __global__ void __launch_bounds__(kAmThreads)
 	uint8_t* sm_raw = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_base) + 1023) & ~(uintptr_t)1023);
 	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
 	const int blk = a.blk;
-	const int CT = kStChunkPages * blk;
 	const size_t blk_bytes = (size_t)blk * HD * 2;
 	const size_t chunk_bytes = (size_t)kStChunkPages * blk_bytes;
 	uint8_t* kbuf = sm_raw;

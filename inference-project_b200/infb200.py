@@ -29,6 +29,9 @@ ERRORS = {
 F32, BF16 = 0, 1
 PREFILL_ATTN_AUTO, PREFILL_ATTN_SIMT = 0, 1  # InfPrefillAttention
 KERNEL_KINDS = ["embed", "qkv", "attn", "o_proj", "gate_up", "down", "lm_head"]
+# InfWeightKind: the weights in their device layout
+W_EMBED, W_LM_HEAD, W_FINAL_NORM = 0, 1, 2
+W_QKV, W_O, W_GATE_UP, W_DOWN, W_ATTN_NORM, W_FFN_NORM = 8, 11, 12, 14, 15, 16
 
 
 class InfError(RuntimeError):
@@ -81,7 +84,8 @@ EXPORTS = [
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
-    "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc",
+    "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
+    "inf_safetensors_read",
 ]
 
 _lib = None
@@ -142,6 +146,9 @@ def lib():
         "inf_tp_export": (E, [C.POINTER(Model), vp, u64]),
         "inf_attn_decode_noalloc": (E, [vp, vp, vp, vp, u32, u32, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp]),
         "inf_tp_connect": (E, [C.POINTER(Model), vp, u32]),
+        "inf_config_from_json": (E, [C.c_char_p, C.POINTER(InfConfig)]),
+        "inf_safetensors_check": (E, [C.c_char_p, C.POINTER(InfConfig)]),
+        "inf_safetensors_read": (E, [C.c_char_p, C.POINTER(InfConfig), u32, u32, vp, u64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -176,6 +183,38 @@ def config_from_dict(d: dict) -> InfConfig:
     return c
 
 
+def config_from_json(path: str, base: InfConfig | None = None) -> InfConfig:
+    """inf_config_from_json: a Hugging Face config.json over `base` (fields the file lacks keep
+    base's values: max_seq, max_batch, KV paging, tensor parallelism)."""
+    c = InfConfig()
+    if base is not None:
+        C.memmove(C.byref(c), C.byref(base), C.sizeof(InfConfig))
+    check(lib().inf_config_from_json(os.fsencode(path), C.byref(c)), "inf_config_from_json")
+    return c
+
+
+def safetensors_check(path: str, cfg: InfConfig) -> None:
+    check(lib().inf_safetensors_check(os.fsencode(path), C.byref(cfg)), "inf_safetensors_check")
+
+
+def weight_shape(cfg: InfConfig, kind: int) -> tuple:
+    """Rows and columns of one weight in the device layout of rank cfg.tp_rank."""
+    tp = max(1, cfg.tp_size)
+    d, hd = cfg.dim, cfg.head_dim
+    return {W_EMBED: (cfg.vocab_size, d), W_LM_HEAD: (cfg.vocab_size // tp, d), W_FINAL_NORM: (1, d),
+            W_QKV: ((cfg.n_heads + 2 * cfg.n_kv_heads) // tp * hd, d), W_O: (d, cfg.n_heads // tp * hd),
+            W_GATE_UP: (2 * cfg.ffn_dim // tp, d), W_DOWN: (d, cfg.ffn_dim // tp), W_ATTN_NORM: (1, d),
+            W_FFN_NORM: (1, d)}[kind]
+
+
+def safetensors_read(path: str, cfg: InfConfig, layer: int, kind: int) -> np.ndarray:
+    """inf_safetensors_read: one weight as the device holds it (uint16 bf16 bits or float32)."""
+    out = np.empty(weight_shape(cfg, kind), dtype=np.uint16 if cfg.dtype == BF16 else np.float32)
+    check(lib().inf_safetensors_read(os.fsencode(path), C.byref(cfg), layer, kind, _ptr(out), out.nbytes),
+          "inf_safetensors_read")
+    return out
+
+
 def oracle_dict(c: InfConfig) -> dict:
     """The same model as a dict for oracle/oracle.py (tests only)."""
     return dict(vocab=c.vocab_size, dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads, n_kv_heads=c.n_kv_heads,
@@ -190,11 +229,13 @@ def _ptr(a: np.ndarray):
 class Engine:
     """One model on the current CUDA device (one context per GPU)."""
 
-    def __init__(self, cfg: InfConfig, seed: int = 0):
+    def __init__(self, cfg: InfConfig, seed: int = 0, weights_path: str | None = None):
+        """Synthetic weights from `seed`, or a safetensors checkpoint (file, index or directory)."""
         self.cfg = cfg
         self.ctx = C.POINTER(ExecCtx)()
         self.model = Model()
-        check(lib().inf_model_build(C.byref(self.ctx), C.byref(self.model), C.byref(cfg), None, seed),
+        path = os.fsencode(weights_path) if weights_path is not None else None
+        check(lib().inf_model_build(C.byref(self.ctx), C.byref(self.model), C.byref(cfg), path, seed),
               "inf_model_build")
         self.V = cfg.vocab_size // max(1, cfg.tp_size)
 
