@@ -439,6 +439,59 @@ def run_workload(args, rank: int, world: int, dist):
     eng.close()
 
 
+def run_tokenize(args):
+    """Host tokenizer encode throughput (no GPU): inf_tokenizer_encode against the reference's
+    own tokenizer_encode (oracle/_ref/libref_tokenizer.so, built from src/tokenizer.c) on the
+    synthetic BPE tokenizer.json of the tests and a seeded corpus of space-separated words drawn
+    from its vocabulary (64 documents of 64 KB).  One thread each."""
+    import numpy as np
+
+    import infb200 as I
+    tok_path = os.path.join(ROOT, "tests", "golden", "tokenizer_synth.json")
+    with open(tok_path, encoding="utf-8") as f:
+        vocab = json.load(f)["model"]["vocab"]
+    words = [p.replace("\u2581", "") for p in vocab if not p.startswith("<")]
+    words = [w for w in words if w]
+    rng = np.random.default_rng(5)
+    zipf = np.array([1.0 / (i + 1) for i in range(len(words))])
+    zipf /= zipf.sum()
+    docs = []
+    for _ in range(64):
+        d = " ".join(words[i] for i in rng.choice(len(words), size=40000, p=zipf))
+        docs.append(d.encode()[:65536].decode("utf-8", errors="ignore").rstrip(" "))
+    n_bytes = sum(len(d.encode()) for d in docs)
+    tok = I.Tokenizer(tok_path)
+    for _ in range(args.warmup):
+        n_tok = sum(tok.encode(d).size for d in docs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for d in docs:
+            tok.encode(d)
+    dt = (time.perf_counter() - t0) / args.steps
+    tok.close()
+    line = {"metric": "tokenizer encode throughput (synthetic BPE tokenizer.json, 700 merges)", "value": round(n_tok / dt, 1),
+            "unit": "tokens/s", "mb_per_s": round(n_bytes / dt / 1e6, 2), "n_gpus": 0, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "utf-8", "data": "synthetic",
+            "config": {"workload": f"encode {len(docs)} documents, {n_bytes} bytes, {n_tok} tokens per step"},
+            "roofline": None, "gpu_launches": 0}
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libref_tokenizer.so")
+    if os.path.exists(ref_lib):
+        sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+        from gen_tokenizer import RefTokenizer
+        ref = RefTokenizer(tok_path, ref_lib)
+        t0 = time.perf_counter()
+        done, n_ref = 0, 0
+        while done < len(docs) and time.perf_counter() - t0 < args.cpu_budget:
+            n_ref += len(ref.encode(docs[done]))
+            done += 1
+        rdt = time.perf_counter() - t0
+        ref.close()
+        line["cpu_baseline"] = {"value": round(n_ref / rdt, 1), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                                "sample": f"{done} of the {len(docs)} documents, reference tokenizer_encode"}
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -449,13 +502,16 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs use a short one)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch"],
-                    help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence decode")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch", "tokenize"],
+                    help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence "
+                         "decode; tokenize: host tokenizer encode (no GPU)")
     args = ap.parse_args()
     globals()["PROMPT"] = args.prompt
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 
+    if args.workload == "tokenize":
+        return run_tokenize(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     dist = None

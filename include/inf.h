@@ -290,6 +290,35 @@ typedef enum InfWeightKind {
 Error_t inf_safetensors_read(const char* weights_path, const InfConfig* config, u32 layer, u32 kind, void* out,
                              u64 out_bytes);
 
+/* ---- tokenizer (src/tokenizer.h:13-38) ------------------------------------------- */
+typedef struct InfTokenizer InfTokenizer;
+/* tokenizer_build (src/tokenizer.c:186-262): the BPE model of a Hugging Face tokenizer.json,
+ * "model": {"vocab": {piece: id}, "merges": [[left, right], ...] or ["left right", ...],
+ * "byte_fallback", "unk_token"}; a merge's rank is its position in the list.  "added_tokens"
+ * are decoded too.  ErrorIo if the file cannot be read; ErrorInvalidValue if it is malformed. */
+Error_t inf_tokenizer_build(const char* tokenizer_json_path, InfTokenizer** out);
+/* tokenizer_destroy (src/tokenizer.c:264-278) */
+Error_t inf_tokenizer_destroy(InfTokenizer** tok);
+/* One past the largest id that has a piece. */
+u32     inf_tokenizer_vocab_size(const InfTokenizer* tok);
+/* tokenizer_encode (src/tokenizer.c:39-183), the reference's segmentation: words split at
+ * ' ' (two spaces make an empty word, a trailing space ends the text), every word after the
+ * first prefixed with U+2581, characters by the reference's UTF-8 lead-byte rule (clamped to
+ * the word), then per round the pair of lowest merge rank merged at all its non-overlapping
+ * occurrences, left to right, until no adjacent pair has a rank.  A final piece outside the
+ * vocabulary becomes its bytes as <0xXX> tokens (byte_fallback), else the unk token, else
+ * ErrorInvalidValue (the reference drops it and still counts it, defect D13).  A text that
+ * starts with a space starts with an empty word that yields nothing (the reference reads out
+ * of bounds there).  *n_ids is the number of ids; ids NULL counts only; more than max_ids:
+ * ErrorInvalidValue. */
+Error_t inf_tokenizer_encode(const InfTokenizer* tok, const char* text, u32* ids, u64 max_ids, u64* n_ids);
+/* tokenizer_decode (declared at src/tokenizer.h:38, never defined by the reference): the
+ * pieces of ids concatenated, U+2581 -> ' ', <0xXX> -> that byte (byte_fallback models).
+ * Writes a NUL-terminated string of *out_len bytes; out NULL gives the length only; out_bytes
+ * below *out_len + 1: ErrorInvalidValue; an id without a piece: ErrorTokenOutOfRange. */
+Error_t inf_tokenizer_decode(const InfTokenizer* tok, const u32* ids, u64 n_ids, char* out, u64 out_bytes,
+                             u64* out_len);
+
 /* Synthetic inputs: n integers uniform in [lo, hi_inclusive] from Philox4x32-10 keyed by
  * SplitMix64(SplitMix64(seed) ^ stream), counter i, Lemire multiply-shift.  Prompt ids use
  * stream 0x1000000 + sequence, context lengths 0x2000000.  Host memory, no device work. */

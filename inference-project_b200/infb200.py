@@ -85,7 +85,8 @@ EXPORTS = [
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
     "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
-    "inf_safetensors_read",
+    "inf_safetensors_read", "inf_tokenizer_build", "inf_tokenizer_destroy", "inf_tokenizer_vocab_size",
+    "inf_tokenizer_encode", "inf_tokenizer_decode",
 ]
 
 _lib = None
@@ -149,6 +150,11 @@ def lib():
         "inf_config_from_json": (E, [C.c_char_p, C.POINTER(InfConfig)]),
         "inf_safetensors_check": (E, [C.c_char_p, C.POINTER(InfConfig)]),
         "inf_safetensors_read": (E, [C.c_char_p, C.POINTER(InfConfig), u32, u32, vp, u64]),
+        "inf_tokenizer_build": (E, [C.c_char_p, C.POINTER(vp)]),
+        "inf_tokenizer_destroy": (E, [C.POINTER(vp)]),
+        "inf_tokenizer_vocab_size": (u32, [vp]),
+        "inf_tokenizer_encode": (E, [vp, C.c_char_p, vp, u64, C.POINTER(u64)]),
+        "inf_tokenizer_decode": (E, [vp, vp, u64, C.c_char_p, u64, C.POINTER(u64)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -213,6 +219,57 @@ def safetensors_read(path: str, cfg: InfConfig, layer: int, kind: int) -> np.nda
     check(lib().inf_safetensors_read(os.fsencode(path), C.byref(cfg), layer, kind, _ptr(out), out.nbytes),
           "inf_safetensors_read")
     return out
+
+
+class Tokenizer:
+    """inf_tokenizer_*: BPE encode / decode of a Hugging Face tokenizer.json."""
+
+    def __init__(self, path: str):
+        self.h = vp()
+        check(lib().inf_tokenizer_build(os.fsencode(path), C.byref(self.h)), "inf_tokenizer_build")
+
+    @property
+    def vocab_size(self) -> int:
+        return int(lib().inf_tokenizer_vocab_size(self.h))
+
+    def encode(self, text) -> np.ndarray:
+        raw = text.encode() if isinstance(text, str) else bytes(text)
+        n = u64()
+        out = np.empty(len(raw) + 8, dtype=np.uint32)  # enough unless byte fallback splits "▁"
+        rc = lib().inf_tokenizer_encode(self.h, raw, _ptr(out), out.size, C.byref(n))
+        if rc == 4 and n.value > out.size:
+            out = np.empty(n.value, dtype=np.uint32)
+            rc = lib().inf_tokenizer_encode(self.h, raw, _ptr(out), out.size, C.byref(n))
+        check(rc, "inf_tokenizer_encode")
+        return out[:n.value]
+
+    def decode_bytes(self, ids) -> bytes:
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        n = u64()
+        check(lib().inf_tokenizer_decode(self.h, _ptr(ids), ids.size, None, 0, C.byref(n)), "inf_tokenizer_decode")
+        buf = C.create_string_buffer(n.value + 1)
+        check(lib().inf_tokenizer_decode(self.h, _ptr(ids), ids.size, buf, n.value + 1, C.byref(n)),
+              "inf_tokenizer_decode")
+        return buf.raw[:n.value]
+
+    def decode(self, ids) -> str:
+        return self.decode_bytes(ids).decode("utf-8", errors="replace")
+
+    def close(self):
+        if self.h:
+            check(lib().inf_tokenizer_destroy(C.byref(self.h)), "inf_tokenizer_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def oracle_dict(c: InfConfig) -> dict:
