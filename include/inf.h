@@ -245,6 +245,25 @@ Error_t inf_tp_connect(Model* model, const void* handles, u32 n_ranks);
 /* Release the KV pages of a sequence slot. */
 Error_t inf_seq_reset(Model* model, u32 seq_slot);
 
+/* ---- sampling ----------------------------------------------------------------------- */
+typedef struct InfSampling {
+	f32 temperature; /* 0: greedy argmax (the default) */
+	f32 top_p;       /* (0, 1]; 1 keeps every token */
+	u32 top_k;       /* 0 keeps every token */
+	u32 reserved;
+	u64 seed;
+} InfSampling;
+/* Temperature / top-k / top-p sampling for every token the model chooses from then on
+ * (inf_generate, inf_decode, and the id inf_forward reports).  With m the largest logit, each
+ * token weighs q = min(floor(expf((logit - m) / temperature) * 2^32), 2^32 - 1); top-k keeps the
+ * tokens at or above the k-th largest q, top-p then the fewest of those (ties kept) whose q sum to
+ * at least ceil(top_p * their total); the token is the first, in id order, whose running sum of
+ * kept q exceeds floor(r * total / 2^64), r the 64-bit Philox4x32-10 draw keyed by
+ * SplitMix64(SplitMix64(seed) ^ 0x3000000) at counter (position, slot << 32).  Deterministic
+ * for a seed.  Batch-1 decode on one GPU only (ErrorUnsupported under tensor parallelism);
+ * inf_forward_batch stays greedy. */
+Error_t inf_set_sampling(Model* model, const InfSampling* sampling);
+
 /* ---- checkpoints ------------------------------------------------------------------ */
 /* model_parse_config (src/main.cu:120-157): reads a Hugging Face config.json -- its
  * "text_config" object when there is one (as the reference does), else the top level -- into
@@ -333,6 +352,7 @@ typedef enum InfBuffer {
 	InfBufLogits = 4, /* logits of the last token [vocab_size] */
 	InfBufK      = 5, /* K the cache holds for (layer, slot, pos) [n_kv_heads * head_dim] */
 	InfBufV      = 6, /* V the cache holds for (layer, slot, pos) */
+	InfBufSampleQ = 7, /* the sampler's fixed-point weights of the last step [vocab_size], raw u32 bits */
 } InfBuffer;
 /* Copy one engine buffer to host floats (bf16 widened).  For test and debugging; the
  * reference's equivalent is print_dev_buf_bf16 (src/main.cu:44-61). */

@@ -27,6 +27,7 @@
 #include "k_attn_prefill.cuh"
 #include "k_attn_prefill_tc.cuh"
 #include "k_gemm_tc.cuh"
+#include "k_sample.cuh"
 #include "k_small.cuh"
 #include "loader.h"
 #include "runtime.h"
@@ -115,6 +116,9 @@ struct InfEngine {
 	int* h_ctl = nullptr;      // [2 * kCtlWords]: staging in, staging out
 	// decode graph
 	cudaGraphExec_t decode_exec = nullptr;
+	InfSampling samp = {};      // temperature 0: greedy
+	bool sampling = false;
+	uint32_t* sample_q = nullptr; // [Vl] fixed-point weights of the sampler
 	int graph_kernels = 0;
 	u64 launches = 0;
 	bool profiling = false;
@@ -331,6 +335,8 @@ Error_t prof_end(InfEngine* e, int kind)
 	return Success;
 }
 
+Error_t enqueue_sample(InfEngine* e);
+
 template <typename T>
 Error_t enqueue_decode_step(InfEngine* e)
 {
@@ -465,6 +471,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 		a.max_out = e->max_out;
 		INF_TRY(prof_begin(e));
 		INF_TRY((launch_gemv<T, kEpiLogits>(e, a)));
+		INF_TRY(enqueue_sample(e)); // timed with the LM head when profiling
 		INF_TRY(prof_end(e, InfKLmHead));
 	}
 	e->graph_kernels = (int)e->launches - kernels_before;
@@ -669,8 +676,31 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 	return Success;
 }
 
+// With sampling on, replaces the id the LM head chose (greedy) by a draw from the
+// temperature / top-k / top-p distribution of its logits (k_sample.cuh).
+Error_t enqueue_sample(InfEngine* e)
+{
+	if (!e->sampling) return Success;
+	SampleArgs a;
+	a.logits = e->logits;
+	a.q = e->sample_q;
+	a.V = e->Vl;
+	a.inv_temp = (float)(1.0 / (double)e->samp.temperature);
+	a.top_p = e->samp.top_p;
+	a.top_k = e->samp.top_k;
+	a.key = stream_key(e->samp.seed, kSampleStream);
+	a.cur_id = e->cur_id;
+	a.out_ids = e->out_ids;
+	a.step = e->step;
+	a.pos = e->pos;
+	a.slot = e->slot;
+	a.max_out = e->max_out;
+	INF_CUDA_TRY(launch(e, k_sample, dim3(1), dim3(kSampleThreads), 0, a));
+	return Success;
+}
+
 // Final norm + LM head + argmax of one residual row (the decode GEMV); advances the ctl
-// block exactly like a decode step (pos += 1, id = argmax).
+// block exactly like a decode step (pos += 1, id = argmax, or the sampled id).
 Error_t enqueue_lm_head_row(InfEngine* e, const float* resid_row)
 {
 	GemvArgs a = gemv_base(e, e->lm_head, e->Vl, (int)e->cfg.dim);
@@ -685,7 +715,8 @@ Error_t enqueue_lm_head_row(InfEngine* e, const float* resid_row)
 	a.step = e->step;
 	a.pos_rw = e->pos;
 	a.max_out = e->max_out;
-	return e->cfg.dtype == InfBF16 ? launch_gemv<bf16, kEpiLogits>(e, a) : launch_gemv<float, kEpiLogits>(e, a);
+	INF_TRY((e->cfg.dtype == InfBF16 ? launch_gemv<bf16, kEpiLogits>(e, a) : launch_gemv<float, kEpiLogits>(e, a)));
+	return enqueue_sample(e);
 }
 
 // Prefill of n tokens (already in d_ids) of one slot from start: chunks of e->chunk tokens
@@ -1129,6 +1160,7 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	P.push(&e->ctl, kCtlWords * sizeof(int));
 	P.push(&e->best, 16);
 	P.push(&e->lm_counter, 16);
+	P.push(&e->sample_q, (u64)e->Vl * 4);
 	P.push(&e->out_ids, (u64)e->max_out * 4);
 	P.push(&e->d_ids, (u64)c.max_seq * 4);
 	P.push(&e->attn_part, part_floats * 4);
@@ -1646,6 +1678,27 @@ Error_t inf_tp_connect(Model* model, const void* handles, u32 n_ranks)
 	return build_decode_graph(e);
 }
 
+Error_t inf_set_sampling(Model* model, const InfSampling* s)
+{
+	if (!model || !model->engine || !s) return fail(ErrorInvalidValue, "inf_set_sampling: NULL argument");
+	InfEngine* e = model->engine;
+	if (!(s->temperature >= 0.0f) || !std::isfinite(s->temperature)) return fail(ErrorInvalidValue, "temperature %g", (double)s->temperature);
+	if (!(s->top_p > 0.0f && s->top_p <= 1.0f)) return fail(ErrorInvalidValue, "top_p %g outside (0, 1]", (double)s->top_p);
+	const bool on = s->temperature > 0.0f;
+	if (on && e->cfg.tp_size > 1) return fail(ErrorUnsupported, "sampling with the vocabulary split across ranks");
+	if (on && 1.0 / (double)s->temperature > 3.0e38) return fail(ErrorInvalidValue, "temperature %g too small", (double)s->temperature);
+	e->samp = *s;
+	if (on == e->sampling && !on) return Success;
+	e->sampling = on;
+	// the decode graph holds the sampler's arguments: rebuild it
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	if (e->decode_exec) {
+		cudaGraphExecDestroy(e->decode_exec);
+		e->decode_exec = nullptr;
+	}
+	return build_decode_graph(e);
+}
+
 Error_t inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 pos, f32* out, u64 n_out)
 {
 	if (!model || !model->engine || !out) return fail(ErrorInvalidValue, "inf_debug_read: bad arguments");
@@ -1663,6 +1716,7 @@ Error_t inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 po
 	case InfBufAttn: src = e->attn; n = (u64)e->Hl * hd; break;
 	case InfBufH: src = e->h; n = (u64)e->Fl; break;
 	case InfBufLogits: src = e->logits; n = (u64)e->Vl; is_f32 = true; break;
+	case InfBufSampleQ: src = e->sample_q; n = (u64)e->Vl; is_f32 = true; break; // raw u32 bits
 	case InfBufK:
 	case InfBufV: {
 		if (layer >= c.n_layers || seq_slot >= c.max_batch || pos >= c.max_seq)

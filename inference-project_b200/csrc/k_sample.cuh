@@ -1,0 +1,203 @@
+// Sampling beyond greedy for the decode loop: temperature, top-k and top-p over the logits
+// the LM head wrote, one CTA of 1024 threads, after the LM head in the decode step.
+//
+// Definition (the oracle restates it exactly; everything after the exponential is integer):
+//   m    = max_i logits_i
+//   w_i  = expf((logits_i - m) * inv_temp)                   fp32, in (0, 1]
+//   q_i  = min(floor(w_i * 2^32), 2^32 - 1)                  32-bit fixed-point weight
+//   t_k  = largest t with #{q_i >= t} >= top_k               (top_k 0 or >= V: t_k = 0)
+//   Z_k  = sum of q_i over q_i >= t_k
+//   t_p  = largest t with sum{q_i : q_i >= t, q_i >= t_k} >= ceil(top_p * Z_k)   (in double)
+//   kept = {i : q_i >= t_p},  Z = sum of kept q_i
+//   r    = 64-bit Philox4x32-10 draw (words y:x) keyed by SplitMix64(SplitMix64(seed) ^ 0x3000000)
+//          at counter (position of the new token, sequence slot)
+//   s    = floor(r * Z / 2^64);  id = the first kept index (ascending) whose inclusive prefix
+//          sum of kept q exceeds s
+// Ties at a threshold are all kept.  Both thresholds come from a 4-pass radix select on 8-bit
+// digits with shared-memory histograms of counts or 64-bit masses: integer atomics, so the
+// result does not depend on the order threads add.  The weights q are kept in global scratch
+// (L2-resident: 4 bytes x V) between passes.
+#pragma once
+
+#include "common.cuh"
+#include "synth.cuh"
+
+namespace inf {
+
+constexpr int kSampleThreads = 1024;
+constexpr uint64_t kSampleStream = 0x3000000;
+
+struct SampleArgs {
+	const float* logits; // [V]
+	uint32_t* q;         // [V] scratch: fixed-point weights
+	int V;
+	float inv_temp;
+	float top_p;
+	uint32_t top_k;
+	PhiloxKey key;
+	uint32_t* cur_id;    // overwritten with the sampled id
+	uint32_t* out_ids;   // out_ids[*step - 1] overwritten (the LM head already advanced step)
+	const uint32_t* step;
+	const int* pos;      // position of the new token (already advanced by the LM head)
+	const int* slot;
+	int max_out;
+};
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v)
+{
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+	return v;
+}
+
+// Largest t such that the weight of {i : q_i >= t, q_i >= floor_t} reaches target, where an
+// element weighs 1 (by_mass false) or q_i.  Every thread returns the same t.
+__device__ uint32_t sample_radix_select(const SampleArgs& a, uint32_t floor_t, bool by_mass, uint64_t target,
+                                        unsigned long long* hist, unsigned long long* sh_acc, uint32_t* sh_prefix)
+{
+	const int tid = threadIdx.x;
+	uint32_t prefix = 0;
+	uint64_t acc = 0; // weight of the elements above the current bucket
+	for (int shift = 24; shift >= 0; shift -= 8) {
+		for (int b = tid; b < 256; b += kSampleThreads) hist[b] = 0ull;
+		__syncthreads();
+		const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+		for (int i = tid; i < a.V; i += kSampleThreads) {
+			const uint32_t q = a.q[i];
+			if (q < floor_t || (q & hi_mask) != (prefix & hi_mask)) continue;
+			atomicAdd(&hist[(q >> shift) & 255u], by_mass ? (unsigned long long)q : 1ull);
+		}
+		__syncthreads();
+		if (tid == 0) {
+			int d = 255;
+			uint64_t c = acc;
+			for (; d > 0; --d) {
+				if (c + hist[d] >= target) break;
+				c += hist[d];
+			}
+			*sh_prefix = prefix | ((uint32_t)d << shift);
+			*sh_acc = c;
+		}
+		__syncthreads();
+		prefix = *sh_prefix;
+		acc = *sh_acc;
+		__syncthreads();
+	}
+	return prefix;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
+{
+	pdl_wait();
+	pdl_trigger();
+	__shared__ unsigned long long hist[256];
+	__shared__ unsigned long long red[kSampleThreads / 32];
+	__shared__ float redf[kSampleThreads / 32];
+	__shared__ unsigned long long sh_acc;
+	__shared__ uint32_t sh_prefix;
+	const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+	// max logit
+	float m = -INFINITY;
+	for (int i = tid; i < a.V; i += kSampleThreads) m = fmaxf(m, a.logits[i]);
+	m = warp_max(m);
+	if (lane == 0) redf[warp] = m;
+	__syncthreads();
+	if (warp == 0) {
+		float v = redf[lane];
+		v = warp_max(v);
+		if (lane == 0) redf[0] = v;
+	}
+	__syncthreads();
+	m = redf[0];
+
+	// fixed-point weights
+	for (int i = tid; i < a.V; i += kSampleThreads) {
+		const float w = expf((a.logits[i] - m) * a.inv_temp);
+		const float s = w * 4294967296.0f; // exact: a power-of-two scale
+		a.q[i] = s >= 4294967295.0f ? 0xFFFFFFFFu : (uint32_t)s;
+	}
+	__syncthreads(); // q is read back by other threads (global, same CTA)
+
+	// top-k threshold, then the mass it keeps
+	uint32_t tk = 0;
+	if (a.top_k > 0 && a.top_k < (uint32_t)a.V) tk = sample_radix_select(a, 0u, false, a.top_k, hist, &sh_acc, &sh_prefix);
+	uint64_t zk = 0;
+	for (int i = tid; i < a.V; i += kSampleThreads) {
+		const uint32_t q = a.q[i];
+		if (q >= tk) zk += q;
+	}
+	zk = warp_sum_u64(zk);
+	if (lane == 0) red[warp] = zk;
+	__syncthreads();
+	if (tid == 0) {
+		uint64_t z = 0;
+		for (int w = 0; w < kSampleThreads / 32; ++w) z += red[w];
+		sh_acc = z;
+	}
+	__syncthreads();
+	zk = sh_acc;
+	__syncthreads();
+
+	// top-p threshold
+	uint32_t tp = tk;
+	if (a.top_p < 1.0f && zk > 0) {
+		double tgt = ceil((double)a.top_p * (double)zk);
+		if (tgt < 1.0) tgt = 1.0;
+		if (tgt > (double)zk) tgt = (double)zk;
+		tp = sample_radix_select(a, tk, true, (uint64_t)tgt, hist, &sh_acc, &sh_prefix);
+		if (tp < tk) tp = tk;
+	}
+
+	// the draw: first kept index whose inclusive prefix mass exceeds s
+	const int chunk = (a.V + kSampleThreads - 1) / kSampleThreads;
+	const int i0 = min(a.V, tid * chunk), i1 = min(a.V, i0 + chunk);
+	uint64_t mine = 0;
+	for (int i = i0; i < i1; ++i) {
+		const uint32_t q = a.q[i];
+		if (q >= tp) mine += q;
+	}
+	// exclusive scan of the threads' masses in thread order
+	uint64_t incl = mine;
+#pragma unroll
+	for (int o = 1; o < 32; o <<= 1) {
+		const uint64_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+		if (lane >= o) incl += v;
+	}
+	if (lane == 31) red[warp] = incl;
+	__syncthreads();
+	if (warp == 0) {
+		uint64_t v = red[lane];
+		uint64_t s = v;
+#pragma unroll
+		for (int o = 1; o < 32; o <<= 1) {
+			const uint64_t u = __shfl_up_sync(0xFFFFFFFFu, s, o);
+			if (lane >= o) s += u;
+		}
+		red[lane] = s - v; // exclusive prefix of the warps
+		if (lane == 31) sh_acc = s; // total kept mass
+	}
+	__syncthreads();
+	const uint64_t total = sh_acc;
+	const uint64_t base = red[warp] + incl - mine;
+	const uint64_t ctr = (uint64_t)(uint32_t)*a.pos | ((uint64_t)(uint32_t)*a.slot << 32);
+	const uint4 wds = philox10(ctr, a.key);
+	const uint64_t r = ((uint64_t)wds.y << 32) | wds.x;
+	const uint64_t s = __umul64hi(r, total);
+	if (total > 0 && s >= base && s < base + mine) {
+		uint64_t c = base;
+		for (int i = i0; i < i1; ++i) {
+			const uint32_t q = a.q[i];
+			if (q < tp) continue;
+			c += q;
+			if (c > s) {
+				*a.cur_id = (uint32_t)i;
+				const uint32_t st = *a.step;
+				if (st >= 1 && (int)(st - 1) < a.max_out) a.out_ids[st - 1] = (uint32_t)i;
+				break;
+			}
+		}
+	}
+}
+
+} // namespace inf

@@ -54,6 +54,10 @@ class InfConfig(C.Structure):
         return d
 
 
+class InfSampling(C.Structure):
+    _fields_ = [("temperature", f32), ("top_p", f32), ("top_k", u32), ("reserved", u32), ("seed", u64)]
+
+
 class HostArena(C.Structure):
     _fields_ = [("reserve_size", u64), ("commit_size", u64), ("commit_pos", u64), ("pos", u64)]
 
@@ -86,7 +90,7 @@ EXPORTS = [
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
     "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
     "inf_safetensors_read", "inf_tokenizer_build", "inf_tokenizer_destroy", "inf_tokenizer_vocab_size",
-    "inf_tokenizer_encode", "inf_tokenizer_decode",
+    "inf_tokenizer_encode", "inf_tokenizer_decode", "inf_set_sampling",
 ]
 
 _lib = None
@@ -155,6 +159,7 @@ def lib():
         "inf_tokenizer_vocab_size": (u32, [vp]),
         "inf_tokenizer_encode": (E, [vp, C.c_char_p, vp, u64, C.POINTER(u64)]),
         "inf_tokenizer_decode": (E, [vp, vp, u64, C.c_char_p, u64, C.POINTER(u64)]),
+        "inf_set_sampling": (E, [C.POINTER(Model), C.POINTER(InfSampling)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -375,7 +380,7 @@ class Engine:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         check(lib().inf_tp_connect(C.byref(self.model), buf, len(handles)), "inf_tp_connect")
 
-    BUFFERS = {"resid": 0, "q": 1, "attn": 2, "h": 3, "logits": 4, "k": 5, "v": 6}
+    BUFFERS = {"resid": 0, "q": 1, "attn": 2, "h": 3, "logits": 4, "k": 5, "v": 6, "sample_q": 7}
 
     def debug_read(self, name: str, layer: int = 0, slot: int = 0, pos: int = 0) -> np.ndarray:
         n = max(self.cfg.dim, self.cfg.ffn_dim, self.V, self.cfg.n_heads * self.cfg.head_dim)
@@ -385,8 +390,15 @@ class Engine:
         tp = max(1, self.cfg.tp_size)
         sizes = {"resid": self.cfg.dim, "q": self.cfg.n_heads // tp * self.cfg.head_dim,
                  "attn": self.cfg.n_heads // tp * self.cfg.head_dim, "h": self.cfg.ffn_dim // tp, "logits": self.V,
-                 "k": self.cfg.n_kv_heads // tp * self.cfg.head_dim, "v": self.cfg.n_kv_heads // tp * self.cfg.head_dim}
-        return out[:sizes[name]].copy()
+                 "k": self.cfg.n_kv_heads // tp * self.cfg.head_dim, "v": self.cfg.n_kv_heads // tp * self.cfg.head_dim,
+                 "sample_q": self.V}
+        r = out[:sizes[name]].copy()
+        return r.view(np.uint32) if name == "sample_q" else r
+
+    def set_sampling(self, temperature: float, top_p: float = 1.0, top_k: int = 0, seed: int = 0):
+        """inf_set_sampling; temperature 0 restores greedy decoding."""
+        s = InfSampling(temperature=temperature, top_p=top_p, top_k=top_k, reserved=0, seed=seed)
+        check(lib().inf_set_sampling(C.byref(self.model), C.byref(s)), "inf_set_sampling")
 
     def reset(self, slot: int = 0):
         check(lib().inf_seq_reset(C.byref(self.model), slot), "inf_seq_reset")

@@ -255,6 +255,74 @@ uint32_t orc_argmax(const float* x, uint64_t n)
 }
 
 /* ------------------------------------------------------------------------- */
+/* sampling (the library's inf_set_sampling rule; it has no reference code)   */
+/* ------------------------------------------------------------------------- */
+
+void orc_sample_weights(const float* logits, uint64_t n, float inv_temp, uint32_t* q)
+{
+	float m = -INFINITY;
+	for (uint64_t i = 0; i < n; ++i) m = logits[i] > m ? logits[i] : m;
+	for (uint64_t i = 0; i < n; ++i) {
+		const float w = expf((logits[i] - m) * inv_temp);
+		const float s = w * 4294967296.0f;
+		q[i] = s >= 4294967295.0f ? 0xFFFFFFFFu : (uint32_t)s;
+	}
+}
+
+static int cmp_u32_desc(const void* a, const void* b)
+{
+	const uint32_t x = *(const uint32_t*)a, y = *(const uint32_t*)b;
+	return x < y ? 1 : x > y ? -1 : 0;
+}
+
+uint32_t orc_sample_select(const uint32_t* q, uint64_t n, float top_p, uint32_t top_k, uint64_t seed, uint64_t counter)
+{
+	uint32_t* s = (uint32_t*)malloc(n * sizeof *s);
+	if (!s) return 0xFFFFFFFFu;
+	memcpy(s, q, n * sizeof *s);
+	qsort(s, n, sizeof *s, cmp_u32_desc);
+	/* top-k: the k-th largest weight (ties kept) */
+	const uint32_t tk = (top_k > 0 && top_k < n) ? s[top_k - 1] : 0u;
+	uint64_t zk = 0;
+	for (uint64_t i = 0; i < n; ++i)
+		if (q[i] >= tk) zk += q[i];
+	/* top-p: walking down the distinct weights, the first whose running sum (all its ties
+	 * included) reaches ceil(top_p * zk) */
+	uint32_t tp = tk;
+	if (top_p < 1.0f && zk > 0) {
+		double tgt = ceil((double)top_p * (double)zk);
+		if (tgt < 1.0) tgt = 1.0;
+		if (tgt > (double)zk) tgt = (double)zk;
+		uint64_t c = 0;
+		for (uint64_t i = 0; i < n && s[i] >= tk;) {
+			const uint32_t v = s[i];
+			while (i < n && s[i] == v) c += s[i++];
+			if ((double)c >= tgt) {
+				tp = v;
+				break;
+			}
+		}
+	}
+	free(s);
+	uint64_t total = 0;
+	for (uint64_t i = 0; i < n; ++i)
+		if (q[i] >= tp) total += q[i];
+	uint32_t key[2], w[4];
+	const uint32_t ctr[4] = { (uint32_t)counter, (uint32_t)(counter >> 32), 0u, 0u };
+	orc_stream_key(seed, 0x3000000u, key);
+	orc_philox4x32_10(ctr, key, w);
+	const uint64_t r = ((uint64_t)w[1] << 32) | w[0];
+	const uint64_t target = (uint64_t)(((unsigned __int128)r * total) >> 64);
+	uint64_t c = 0;
+	for (uint64_t i = 0; i < n; ++i) {
+		if (q[i] < tp) continue;
+		c += q[i];
+		if (c > target) return (uint32_t)i;
+	}
+	return 0xFFFFFFFFu;
+}
+
+/* ------------------------------------------------------------------------- */
 /* model                                                                      */
 /* ------------------------------------------------------------------------- */
 

@@ -91,6 +91,12 @@ uint32_t orc_argmax(const float* x, uint64_t n);
 /* 1: accumulate projections in float (to measure the drift between two fp32 orders) */
 void     orc_set_accum_f32(int on);
 
+/* Sampling as the library defines it (inf_set_sampling, include/inf.h): the fixed-point
+ * weights q_i = min(floor(expf((logit_i - max) * inv_temp) * 2^32), 2^32 - 1), and the integer
+ * selection from q (top-k, top-p, Philox draw at `counter`).  Sorting, not a radix select. */
+void     orc_sample_weights(const float* logits, uint64_t n, float inv_temp, uint32_t* q);
+uint32_t orc_sample_select(const uint32_t* q, uint64_t n, float top_p, uint32_t top_k, uint64_t seed, uint64_t counter);
+
 #ifdef __cplusplus
 }
 #endif

@@ -87,6 +87,10 @@ def lib():
         L.orc_set_accum_f32.argtypes = [C.c_int]
         L.orc_argmax.restype = u32
         L.orc_argmax.argtypes = [vp, u64]
+        L.orc_sample_weights.argtypes = [vp, u64, f32, vp]
+        L.orc_sample_weights.restype = None
+        L.orc_sample_select.argtypes = [vp, u64, f32, u32, u64, u64]
+        L.orc_sample_select.restype = u32
         _lib = L
     return _lib
 
@@ -117,6 +121,18 @@ def gen_ids(seed: int, n: int, vocab: int, stream: int = STREAM_PROMPT) -> np.nd
 
 def uniform_u32(seed: int, stream: int, idx: int, lo: int, hi: int) -> int:
     return int(lib().orc_uniform_u32(seed, stream, idx, lo, hi))
+
+
+def sample_weights(logits: np.ndarray, inv_temp: float) -> np.ndarray:
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    q = np.empty(x.size, dtype=np.uint32)
+    lib().orc_sample_weights(_p(x), x.size, inv_temp, _p(q))
+    return q
+
+
+def sample_select(q: np.ndarray, top_p: float, top_k: int, seed: int, counter: int) -> int:
+    q = np.ascontiguousarray(q, dtype=np.uint32)
+    return int(lib().orc_sample_select(_p(q), q.size, top_p, top_k, seed, counter))
 
 
 def tensor_stream(layer: int, kind: int) -> int:
