@@ -264,6 +264,36 @@ typedef struct InfSampling {
  * inf_forward_batch stays greedy. */
 Error_t inf_set_sampling(Model* model, const InfSampling* sampling);
 
+/* ---- continuous batching ------------------------------------------------------------ */
+typedef struct InfServer InfServer;
+/* A request queue in front of the model's max_batch sequence slots (at most max_active of them
+ * in use, 0: all).  Each inf_server_step admits waiting requests first come first served into
+ * free slots (pages released, prompt prefilled with inf_forward, its greedy next token the
+ * first output), advances every sequence admitted in an earlier step by one token with one
+ * inf_forward_batch call, and retires sequences that produced eos_id, reached max_new tokens or
+ * ran out of positions, releasing their pages.  Greedy only (ErrorUnsupported at admission
+ * while sampling is on).  A request whose prefill fails is retired with that error and the
+ * others go on; a failing batched step returns its error.  Not thread-safe. */
+Error_t inf_server_create(Model* model, u32 max_active, InfServer** out);
+/* The same scheduler over a host-only stand-in model (next id = a hash of the sequence's
+ * previous id and position) that checks every sequence is fed its own positions in order: for
+ * testing the scheduling without a GPU. */
+Error_t inf_server_create_synthetic(u32 n_slots, u32 max_seq, u32 vocab, u32 max_active, InfServer** out);
+Error_t inf_server_destroy(InfServer** server);
+/* Queue a request; n_prompt < max_seq.  eos_id 0xFFFFFFFF: none. */
+Error_t inf_server_submit(InfServer* server, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id,
+                          u64* request_id);
+/* One scheduling step; *n_finished (may be NULL) = requests retired in it. */
+Error_t inf_server_step(InfServer* server, u32* n_finished);
+/* The ids a request has produced so far (out_ids NULL: count only), *done = 1 once retired,
+ * *status = the error that retired it (Success if none).  done and status may be NULL. */
+Error_t inf_server_result(InfServer* server, u64 request_id, u32* out_ids, u32 cap, u32* n_out, u32* done,
+                          Error_t* status);
+/* Forget a retired request. */
+Error_t inf_server_release(InfServer* server, u64 request_id);
+Error_t inf_server_stats(const InfServer* server, u32* n_waiting, u32* n_active, u64* batched_steps,
+                         u64* batched_tokens);
+
 /* ---- checkpoints ------------------------------------------------------------------ */
 /* model_parse_config (src/main.cu:120-157): reads a Hugging Face config.json -- its
  * "text_config" object when there is one (as the reference does), else the top level -- into

@@ -1342,6 +1342,8 @@ Error_t forward_one(InfEngine* e, u32 id, u32 pos, u32 slot, f32* logits_out, u3
 } // namespace
 
 // =============================================================================== C ABI
+bool inf::model_sampling_on(const Model* m) { return m && m->engine && m->engine->sampling; }
+
 extern "C" {
 
 Error_t inf_config_preset(u32 preset, InfConfig* out)

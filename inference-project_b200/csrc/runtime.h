@@ -28,4 +28,7 @@ Error_t fail(Error_t err, const char* fmt, ...);
 
 bool is_device_ptr(const void* p);
 
+// Whether inf_set_sampling turned sampling on for this model (false for NULL).
+bool model_sampling_on(const Model* m);
+
 } // namespace inf

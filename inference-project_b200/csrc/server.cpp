@@ -1,0 +1,315 @@
+// Continuous batching over the paged KV cache: a request queue in front of the model's
+// sequence slots.  Host code only.
+//
+// Every inf_server_step:
+//   1. admits waiting requests, first come first served, into free slots (at most max_active
+//      sequences at once): the slot's pages are released, the prompt is prefilled with
+//      inf_forward and its greedy next token is the request's first output;
+//   2. advances every other active sequence by one token with one inf_forward_batch call
+//      (the projections of all of them in one pass over the weights, per-sequence attention
+//      over each one's pages);
+//   3. retires sequences that produced their end-of-sequence id, reached max_new tokens or
+//      the end of the slot's positions, and releases their pages for the next admissions.
+// A request admitted in step s contributes its first token in step s and joins the batched
+// decode from step s + 1.  The reference has no serving loop (it stops after one RMSNorm,
+// src/main.cu:396-412); this is the scheduler a caller would otherwise write around
+// inf_forward_batch.
+#include <algorithm>
+#include <deque>
+#include <memory>
+#include <unordered_map>
+#include <vector>
+
+#include "runtime.h"
+
+using namespace inf;
+
+namespace {
+
+// The model calls the scheduler makes; the device model or the host stand-in below.
+struct Backend {
+	virtual ~Backend() = default;
+	virtual u32 slots() const = 0;
+	virtual u32 max_seq() const = 0;
+	virtual Error_t release(u32 slot) = 0;
+	virtual Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) = 0;
+	virtual Error_t decode(u32 n, const u32* slots, const u32* ids, const u32* pos, u32* next) = 0;
+};
+
+struct ModelBackend final : Backend {
+	Model* m;
+	explicit ModelBackend(Model* model) : m(model) {}
+	u32 slots() const override { return m->config.max_batch; }
+	u32 max_seq() const override { return m->config.max_seq; }
+	Error_t release(u32 slot) override { return inf_seq_reset(m, slot); }
+	Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) override
+	{
+		// the batched decode is greedy; a sampled first token would mix two rules in one sequence
+		if (model_sampling_on(m)) return fail(ErrorUnsupported, "the server decodes greedily; turn sampling off");
+		return inf_forward(m, ids, n, 0, slot, nullptr, next);
+	}
+	Error_t decode(u32 n, const u32* s, const u32* ids, const u32* pos, u32* next) override
+	{
+		return inf_forward_batch(m, n, s, ids, pos, nullptr, next);
+	}
+};
+
+// Host stand-in: the next id is a hash of the sequence's previous id and position only, so a
+// sequence's outputs cannot depend on what else shares its batch.  Tracks which positions each
+// slot has written, to check the scheduler feeds every sequence its own positions in order.
+struct SyntheticBackend final : Backend {
+	u32 n_slots, seq, vocab;
+	std::vector<u32> filled; // positions written per slot
+	SyntheticBackend(u32 s, u32 ms, u32 v) : n_slots(s), seq(ms), vocab(v), filled(s, 0) {}
+	u32 slots() const override { return n_slots; }
+	u32 max_seq() const override { return seq; }
+	static u32 mix(u64 x)
+	{
+		x ^= x >> 33;
+		x *= 0xff51afd7ed558ccdull;
+		x ^= x >> 33;
+		x *= 0xc4ceb9fe1a85ec53ull;
+		return (u32)(x ^ (x >> 33));
+	}
+	Error_t release(u32 slot) override
+	{
+		if (slot >= n_slots) return fail(ErrorInvalidValue, "slot %u", slot);
+		filled[slot] = 0;
+		return Success;
+	}
+	Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) override
+	{
+		if (slot >= n_slots || n == 0 || n > seq) return fail(ErrorInvalidValue, "prefill slot %u n %u", slot, n);
+		if (filled[slot] != 0) return fail(ErrorInvalidValue, "prefill into a slot that holds %u positions", filled[slot]);
+		u64 h = 0;
+		for (u32 i = 0; i < n; ++i) h = mix(h * 31 + ids[i]);
+		filled[slot] = n;
+		*next = mix(h ^ ((u64)n << 40)) % vocab;
+		return Success;
+	}
+	Error_t decode(u32 n, const u32* s, const u32* ids, const u32* pos, u32* next) override
+	{
+		for (u32 i = 0; i < n; ++i) {
+			if (s[i] >= n_slots || pos[i] >= seq) return fail(ErrorKvOutOfRange, "slot %u position %u", s[i], pos[i]);
+			if (pos[i] != filled[s[i]]) return fail(ErrorInvalidValue, "slot %u fed position %u after %u", s[i], pos[i], filled[s[i]]);
+			for (u32 j = 0; j < i; ++j)
+				if (s[j] == s[i]) return fail(ErrorInvalidValue, "slot %u twice in one batch", s[i]);
+		}
+		for (u32 i = 0; i < n; ++i) {
+			filled[s[i]] = pos[i] + 1;
+			next[i] = mix(((u64)ids[i] << 32) ^ pos[i]) % vocab;
+		}
+		return Success;
+	}
+};
+
+struct Request {
+	u64 id;
+	std::vector<u32> prompt;
+	u32 max_new, eos;
+	std::vector<u32> out;
+	int slot = -1;
+	u32 pos = 0;      // position of the last output token (the next one fed)
+	u64 admitted = 0; // the step that prefilled it
+	bool done = false;
+	Error_t err = Success;
+};
+
+} // namespace
+
+struct InfServer {
+	std::unique_ptr<Backend> be;
+	u32 max_active = 0;
+	u64 next_id = 1;
+	u64 steps = 0;
+	std::unordered_map<u64, Request> reqs;
+	std::deque<u64> waiting;
+	std::vector<u64> active;
+	std::vector<u32> free_slots;
+	u64 batched_steps = 0, batched_tokens = 0;
+};
+
+namespace {
+
+Error_t retire(InfServer* s, Request& r)
+{
+	r.done = true;
+	if (r.slot >= 0) {
+		const u32 slot = (u32)r.slot;
+		r.slot = -1;
+		s->free_slots.push_back(slot);
+		return s->be->release(slot);
+	}
+	return Success;
+}
+
+bool finished(const InfServer* s, const Request& r)
+{
+	return r.out.size() >= r.max_new || (!r.out.empty() && r.out.back() == r.eos) || r.pos >= s->be->max_seq();
+}
+
+Error_t create(std::unique_ptr<Backend> be, u32 max_active, InfServer** out)
+{
+	if (!out) return fail(ErrorInvalidValue, "inf_server_create: NULL out");
+	*out = nullptr;
+	const u32 n = be->slots();
+	if (n == 0) return fail(ErrorInvalidValue, "the model has no sequence slots");
+	InfServer* s = new (std::nothrow) InfServer();
+	if (!s) return fail(ErrorMemoryAllocation, "server");
+	s->be = std::move(be);
+	s->max_active = max_active == 0 ? n : std::min(max_active, n);
+	for (u32 k = n; k-- > 0;) s->free_slots.push_back(k); // slot 0 first
+	for (u32 k = 0; k < n; ++k) {
+		const Error_t e = s->be->release(k);
+		if (e != Success) {
+			delete s;
+			return e;
+		}
+	}
+	*out = s;
+	return Success;
+}
+
+} // namespace
+
+extern "C" {
+
+Error_t inf_server_create(Model* model, u32 max_active, InfServer** out)
+{
+	if (!model || !model->engine) return fail(ErrorInvalidValue, "inf_server_create: no model");
+	return create(std::unique_ptr<Backend>(new ModelBackend(model)), max_active, out);
+}
+
+Error_t inf_server_create_synthetic(u32 n_slots, u32 max_seq, u32 vocab, u32 max_active, InfServer** out)
+{
+	if (n_slots == 0 || max_seq < 2 || vocab == 0) return fail(ErrorInvalidValue, "inf_server_create_synthetic: sizes");
+	return create(std::unique_ptr<Backend>(new SyntheticBackend(n_slots, max_seq, vocab)), max_active, out);
+}
+
+Error_t inf_server_destroy(InfServer** s)
+{
+	if (!s || !*s) return fail(ErrorInvalidValue, "inf_server_destroy: no server");
+	delete *s;
+	*s = nullptr;
+	return Success;
+}
+
+Error_t inf_server_submit(InfServer* s, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id, u64* request_id)
+{
+	if (!s || !prompt || !request_id || n_prompt == 0 || max_new == 0) return fail(ErrorInvalidValue, "inf_server_submit: arguments");
+	if (n_prompt >= s->be->max_seq()) return fail(ErrorKvOutOfRange, "prompt of %u tokens, %u positions per slot", n_prompt, s->be->max_seq());
+	Request r;
+	r.id = s->next_id++;
+	r.prompt.assign(prompt, prompt + n_prompt);
+	r.max_new = max_new;
+	r.eos = eos_id;
+	s->waiting.push_back(r.id);
+	*request_id = r.id;
+	s->reqs.emplace(r.id, std::move(r));
+	return Success;
+}
+
+Error_t inf_server_step(InfServer* s, u32* n_finished)
+{
+	if (!s) return fail(ErrorInvalidValue, "inf_server_step: no server");
+	const u64 step = ++s->steps;
+	u32 fin = 0;
+	// 1. admissions: prefill and the first token
+	while (!s->waiting.empty() && !s->free_slots.empty() && s->active.size() < s->max_active) {
+		Request& r = s->reqs.at(s->waiting.front());
+		s->waiting.pop_front();
+		r.slot = (int)s->free_slots.back();
+		s->free_slots.pop_back();
+		r.admitted = step;
+		u32 first = 0;
+		const Error_t e = s->be->prefill(r.prompt.data(), (u32)r.prompt.size(), (u32)r.slot, &first);
+		if (e != Success) { // this request fails alone; the others go on
+			r.err = e;
+			INF_TRY(retire(s, r));
+			++fin;
+			continue;
+		}
+		r.out.push_back(first);
+		r.pos = (u32)r.prompt.size();
+		if (finished(s, r)) {
+			INF_TRY(retire(s, r));
+			++fin;
+		} else {
+			s->active.push_back(r.id);
+		}
+	}
+	// 2. one batched decode step for the sequences admitted before this step
+	std::vector<u32> slots, ids, pos;
+	std::vector<u64> batch;
+	for (u64 id : s->active) {
+		const Request& r = s->reqs.at(id);
+		if (r.admitted == step) continue;
+		batch.push_back(id);
+		slots.push_back((u32)r.slot);
+		ids.push_back(r.out.back());
+		pos.push_back(r.pos);
+	}
+	if (!batch.empty()) {
+		std::vector<u32> next(batch.size());
+		INF_TRY(s->be->decode((u32)batch.size(), slots.data(), ids.data(), pos.data(), next.data()));
+		++s->batched_steps;
+		s->batched_tokens += batch.size();
+		for (size_t i = 0; i < batch.size(); ++i) {
+			Request& r = s->reqs.at(batch[i]);
+			r.out.push_back(next[i]);
+			r.pos += 1;
+		}
+	}
+	// 3. retire
+	std::vector<u64> keep;
+	for (u64 id : s->active) {
+		Request& r = s->reqs.at(id);
+		if (finished(s, r)) {
+			INF_TRY(retire(s, r));
+			++fin;
+		} else {
+			keep.push_back(id);
+		}
+	}
+	s->active.swap(keep);
+	if (n_finished) *n_finished = fin;
+	return Success;
+}
+
+Error_t inf_server_result(InfServer* s, u64 request_id, u32* out_ids, u32 cap, u32* n_out, u32* done, Error_t* status)
+{
+	if (!s || !n_out) return fail(ErrorInvalidValue, "inf_server_result: arguments");
+	const auto it = s->reqs.find(request_id);
+	if (it == s->reqs.end()) return fail(ErrorInvalidValue, "no request %llu", (unsigned long long)request_id);
+	const Request& r = it->second;
+	*n_out = (u32)r.out.size();
+	if (done) *done = r.done ? 1u : 0u;
+	if (status) *status = r.err;
+	if (out_ids) {
+		if (cap < r.out.size()) return fail(ErrorInvalidValue, "%zu ids, room for %u", r.out.size(), cap);
+		std::copy(r.out.begin(), r.out.end(), out_ids);
+	}
+	return Success;
+}
+
+Error_t inf_server_release(InfServer* s, u64 request_id)
+{
+	if (!s) return fail(ErrorInvalidValue, "inf_server_release: no server");
+	const auto it = s->reqs.find(request_id);
+	if (it == s->reqs.end()) return fail(ErrorInvalidValue, "no request %llu", (unsigned long long)request_id);
+	if (!it->second.done) return fail(ErrorInvalidValue, "request %llu is still running", (unsigned long long)request_id);
+	s->reqs.erase(it);
+	return Success;
+}
+
+Error_t inf_server_stats(const InfServer* s, u32* n_waiting, u32* n_active, u64* batched_steps, u64* batched_tokens)
+{
+	if (!s) return fail(ErrorInvalidValue, "inf_server_stats: no server");
+	if (n_waiting) *n_waiting = (u32)s->waiting.size();
+	if (n_active) *n_active = (u32)s->active.size();
+	if (batched_steps) *batched_steps = s->batched_steps;
+	if (batched_tokens) *batched_tokens = s->batched_tokens;
+	return Success;
+}
+
+} // extern "C"

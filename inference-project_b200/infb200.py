@@ -90,7 +90,9 @@ EXPORTS = [
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
     "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
     "inf_safetensors_read", "inf_tokenizer_build", "inf_tokenizer_destroy", "inf_tokenizer_vocab_size",
-    "inf_tokenizer_encode", "inf_tokenizer_decode", "inf_set_sampling",
+    "inf_tokenizer_encode", "inf_tokenizer_decode", "inf_set_sampling", "inf_server_create",
+    "inf_server_create_synthetic", "inf_server_destroy", "inf_server_submit", "inf_server_step", "inf_server_result",
+    "inf_server_release", "inf_server_stats",
 ]
 
 _lib = None
@@ -160,6 +162,14 @@ def lib():
         "inf_tokenizer_encode": (E, [vp, C.c_char_p, vp, u64, C.POINTER(u64)]),
         "inf_tokenizer_decode": (E, [vp, vp, u64, C.c_char_p, u64, C.POINTER(u64)]),
         "inf_set_sampling": (E, [C.POINTER(Model), C.POINTER(InfSampling)]),
+        "inf_server_create": (E, [C.POINTER(Model), u32, C.POINTER(vp)]),
+        "inf_server_create_synthetic": (E, [u32, u32, u32, u32, C.POINTER(vp)]),
+        "inf_server_destroy": (E, [C.POINTER(vp)]),
+        "inf_server_submit": (E, [vp, vp, u32, u32, u32, C.POINTER(u64)]),
+        "inf_server_step": (E, [vp, C.POINTER(u32)]),
+        "inf_server_result": (E, [vp, u64, vp, u32, C.POINTER(u32), C.POINTER(u32), C.POINTER(C.c_int)]),
+        "inf_server_release": (E, [vp, u64]),
+        "inf_server_stats": (E, [vp, C.POINTER(u32), C.POINTER(u32), C.POINTER(u64), C.POINTER(u64)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -263,6 +273,67 @@ class Tokenizer:
     def close(self):
         if self.h:
             check(lib().inf_tokenizer_destroy(C.byref(self.h)), "inf_tokenizer_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+NO_EOS = 0xFFFFFFFF
+
+
+class Server:
+    """inf_server_*: continuous batching over a model's sequence slots (or, with engine None,
+    over the host-only stand-in model of inf_server_create_synthetic)."""
+
+    def __init__(self, engine=None, max_active: int = 0, synthetic: tuple | None = None):
+        self.h = vp()
+        if engine is not None:
+            check(lib().inf_server_create(C.byref(engine.model), max_active, C.byref(self.h)), "inf_server_create")
+        else:
+            n_slots, max_seq, vocab = synthetic
+            check(lib().inf_server_create_synthetic(n_slots, max_seq, vocab, max_active, C.byref(self.h)),
+                  "inf_server_create_synthetic")
+
+    def submit(self, prompt, max_new: int, eos: int = NO_EOS) -> int:
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        rid = u64()
+        check(lib().inf_server_submit(self.h, _ptr(p), p.size, max_new, eos, C.byref(rid)), "inf_server_submit")
+        return rid.value
+
+    def step(self) -> int:
+        n = u32()
+        check(lib().inf_server_step(self.h, C.byref(n)), "inf_server_step")
+        return n.value
+
+    def result(self, rid: int):
+        """(ids so far, done, error code that retired it or 0)."""
+        n, done, status = u32(), u32(), C.c_int()
+        check(lib().inf_server_result(self.h, rid, None, 0, C.byref(n), None, None), "inf_server_result")
+        out = np.empty(n.value, dtype=np.uint32)
+        check(lib().inf_server_result(self.h, rid, _ptr(out), out.size, C.byref(n), C.byref(done), C.byref(status)),
+              "inf_server_result")
+        return out, bool(done.value), status.value
+
+    def release(self, rid: int):
+        check(lib().inf_server_release(self.h, rid), "inf_server_release")
+
+    def stats(self) -> dict:
+        w, a, bs, bt = u32(), u32(), u64(), u64()
+        check(lib().inf_server_stats(self.h, C.byref(w), C.byref(a), C.byref(bs), C.byref(bt)), "inf_server_stats")
+        return dict(waiting=w.value, active=a.value, batched_steps=bs.value, batched_tokens=bt.value)
+
+    def close(self):
+        if self.h:
+            check(lib().inf_server_destroy(C.byref(self.h)), "inf_server_destroy")
 
     def __enter__(self):
         return self

@@ -1,0 +1,125 @@
+"""Continuous batching (inf_server_*) scheduling on the host-only stand-in model
+(inf_server_create_synthetic): its next id depends only on the sequence's own previous id and
+position, and it rejects a batch that feeds a slot out of order or twice, so the tests check
+admission order, the max_active bound, retirement (eos, max_new, end of positions), slot and page
+reuse, and that a request's output does not depend on what shares its batch."""
+import numpy as np
+import pytest
+
+import infb200 as I
+
+
+def synthetic_next(prev, pos, vocab):
+    M = (1 << 64) - 1
+
+    def mix(x):
+        x &= M
+        x ^= x >> 33
+        x = (x * 0xff51afd7ed558ccd) & M
+        x ^= x >> 33
+        x = (x * 0xc4ceb9fe1a85ec53) & M
+        return (x ^ (x >> 33)) & 0xFFFFFFFF
+    return mix((prev << 32) ^ pos) % vocab
+
+
+def run_all(server, reqs, arrivals=None):
+    """Submit (prompt, max_new, eos) at their arrival steps, step until all retire."""
+    arrivals = arrivals or [0] * len(reqs)
+    ids = [None] * len(reqs)
+    step = 0
+    while True:
+        for i, (p, m, e) in enumerate(reqs):
+            if arrivals[i] == step:
+                ids[i] = server.submit(p, m, e)
+        server.step()
+        step += 1
+        if step > max(arrivals) and all(ids[i] is not None and server.result(ids[i])[1] for i in range(len(reqs))):
+            break
+        assert step < 10_000
+    return [server.result(r) for r in ids], step
+
+
+def requests(rng, n, vocab, max_seq):
+    out = []
+    for _ in range(n):
+        lp = int(rng.integers(1, max_seq // 2))
+        out.append((rng.integers(0, vocab, lp, dtype=np.uint32), int(rng.integers(1, 40)), I.NO_EOS))
+    return out
+
+
+def test_outputs_do_not_depend_on_the_batch():
+    rng = np.random.default_rng(1)
+    reqs = requests(rng, 30, 1000, 128)
+    arrivals = list(rng.integers(0, 40, len(reqs)))
+    with I.Server(synthetic=(6, 128, 1000)) as s:
+        together, _ = run_all(s, reqs, arrivals)
+        st = s.stats()
+        assert st["waiting"] == 0 and st["active"] == 0 and st["batched_steps"] > 0
+    for (p, m, e), (out, done, rc) in zip(reqs, together):
+        with I.Server(synthetic=(1, 128, 1000)) as alone:
+            (solo, _, _), = run_all(alone, [(p, m, e)])[0]
+        assert done and rc == 0
+        np.testing.assert_array_equal(out, solo)
+        assert out.size == m
+        # each token after the first follows from the one before at its position
+        for k in range(1, out.size):
+            assert out[k] == synthetic_next(int(out[k - 1]), len(p) + k - 1, 1000)
+
+
+def test_max_active_and_fifo_admission():
+    rng = np.random.default_rng(2)
+    reqs = [(rng.integers(0, 50, 5, dtype=np.uint32), 10, I.NO_EOS) for _ in range(7)]
+    with I.Server(synthetic=(8, 64, 50), max_active=3) as s:
+        rids = [s.submit(*r) for r in reqs]
+        s.step()
+        st = s.stats()
+        assert st["active"] == 3 and st["waiting"] == 4
+        started = [s.result(r)[0].size > 0 for r in rids]
+        assert started == [True] * 3 + [False] * 4  # first come, first served
+        while not all(s.result(r)[1] for r in rids):
+            s.step()
+            assert s.stats()["active"] <= 3
+
+
+def test_eos_and_end_of_positions():
+    with I.Server(synthetic=(2, 16, 7)) as s:
+        # a vocabulary of 7 ids: some id repeats quickly; use the second output as eos
+        probe = s.submit(np.array([1, 2, 3], np.uint32), 5)
+        while not s.result(probe)[1]:
+            s.step()
+        out, _, _ = s.result(probe)
+        eos = int(out[1])
+        r = s.submit(np.array([1, 2, 3], np.uint32), 50, eos)
+        while not s.result(r)[1]:
+            s.step()
+        got = s.result(r)[0]
+        assert got[-1] == eos and eos not in got[:-1].tolist()
+        # max_seq 16: a 10-token prompt leaves positions 10..15 to feed -> 7 outputs at most
+        r = s.submit(np.arange(10, dtype=np.uint32) % 7, 100)
+        while not s.result(r)[1]:
+            s.step()
+        assert s.result(r)[0].size == 7
+
+
+def test_slots_are_reused_and_requests_released():
+    with I.Server(synthetic=(2, 32, 100)) as s:
+        rids = [s.submit(np.array([i + 1], np.uint32), 3) for i in range(10)]
+        steps = 0
+        while not all(s.result(r)[1] for r in rids):
+            s.step()
+            steps += 1
+        assert steps <= 20  # two slots turn over five times
+        for r in rids:
+            s.release(r)
+        with pytest.raises(I.InfError):
+            s.result(rids[0])
+
+
+def test_submit_checks():
+    with I.Server(synthetic=(2, 16, 100)) as s:
+        for bad in ((np.array([], np.uint32), 3), (np.arange(16, dtype=np.uint32), 3), (np.array([1], np.uint32), 0)):
+            with pytest.raises(I.InfError):
+                s.submit(*bad)
+        r = s.submit(np.array([1], np.uint32), 5)
+        with pytest.raises(I.InfError):
+            s.release(r)  # still running
