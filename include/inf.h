@@ -270,7 +270,8 @@ typedef struct InfServer InfServer;
  * in use, 0: all).  Each inf_server_step admits waiting requests first come first served into
  * free slots (pages released, prompt prefilled with inf_forward, its greedy next token the
  * first output), advances every sequence admitted in an earlier step by one token with one
- * inf_forward_batch call, and retires sequences that produced eos_id, reached max_new tokens or
+ * batched decode step (the tensor-core batch path even for a lone sequence, so a request's ids
+ * do not depend on the load), and retires sequences that produced eos_id, reached max_new tokens or
  * ran out of positions, releasing their pages.  Greedy only (ErrorUnsupported at admission
  * while sampling is on).  A request whose prefill fails is retired with that error and the
  * others go on; a failing batched step returns its error.  Not thread-safe. */

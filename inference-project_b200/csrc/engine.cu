@@ -1478,13 +1478,21 @@ Error_t inf_forward(Model* model, const u32* ids, u32 n_tokens, u32 start_pos, u
 Error_t inf_forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const u32* ids, const u32* positions,
                           f32* logits_out, u32* argmax_out)
 {
+	return forward_batch(model, n_seqs, seq_slots, ids, positions, logits_out, argmax_out, false);
+}
+
+} // extern "C"
+
+Error_t inf::forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const u32* ids, const u32* positions,
+                           f32* logits_out, u32* argmax_out, bool single_batched)
+{
 	if (!model || !model->engine || !seq_slots || !ids || !positions || n_seqs == 0)
 		return fail(ErrorInvalidValue, "inf_forward_batch: bad arguments");
 	InfEngine* e = model->engine;
 	const InfConfig& c = e->cfg;
 	const bool host_args = !is_device_ptr(seq_slots) && !is_device_ptr(ids) && !is_device_ptr(positions);
-	const bool batched = host_args && c.dtype == InfBF16 && c.tp_size <= 1 && n_seqs > 1 && n_seqs <= c.max_batch &&
-	                     (int)n_seqs <= e->chunk && e->logits_p;
+	const bool batched = host_args && c.dtype == InfBF16 && c.tp_size <= 1 && (n_seqs > 1 || single_batched) &&
+	                     n_seqs <= c.max_batch && (int)n_seqs <= e->chunk && e->logits_p;
 	if (!batched) {
 		for (u32 i = 0; i < n_seqs; ++i) {
 			f32* lo = logits_out ? logits_out + (size_t)i * e->Vl : nullptr;
@@ -1519,6 +1527,8 @@ Error_t inf_forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const 
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
 	return check_dev_err(e);
 }
+
+extern "C" {
 
 Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u32* out_ids, InfStats* stats)
 {

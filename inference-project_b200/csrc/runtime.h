@@ -31,4 +31,10 @@ bool is_device_ptr(const void* p);
 // Whether inf_set_sampling turned sampling on for this model (false for NULL).
 bool model_sampling_on(const Model* m);
 
+// inf_forward_batch; single_batched runs even one sequence through the batched tensor-core
+// step (inf_forward_batch gives a lone sequence the batch-1 decode kernels instead), so a
+// sequence's results do not depend on how many others share the step.
+Error_t forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const u32* ids, const u32* positions,
+                      f32* logits_out, u32* argmax_out, bool single_batched);
+
 } // namespace inf

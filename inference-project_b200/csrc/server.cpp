@@ -5,9 +5,10 @@
 //   1. admits waiting requests, first come first served, into free slots (at most max_active
 //      sequences at once): the slot's pages are released, the prompt is prefilled with
 //      inf_forward and its greedy next token is the request's first output;
-//   2. advances every other active sequence by one token with one inf_forward_batch call
-//      (the projections of all of them in one pass over the weights, per-sequence attention
-//      over each one's pages);
+//   2. advances every other active sequence by one token with one batched decode step (the
+//      projections of all of them in one pass over the weights on the tensor cores,
+//      per-sequence attention over each one's pages) -- the batched step even for a lone
+//      sequence, so that a request's ids never depend on how many others are running;
 //   3. retires sequences that produced their end-of-sequence id, reached max_new tokens or
 //      the end of the slot's positions, and releases their pages for the next admissions.
 // A request admitted in step s contributes its first token in step s and joins the batched
@@ -50,7 +51,7 @@ struct ModelBackend final : Backend {
 	}
 	Error_t decode(u32 n, const u32* s, const u32* ids, const u32* pos, u32* next) override
 	{
-		return inf_forward_batch(m, n, s, ids, pos, nullptr, next);
+		return forward_batch(m, n, s, ids, pos, nullptr, next, true);
 	}
 };
 

@@ -1,9 +1,10 @@
 """Continuous batching on the B200 (inf_server_* over the engine): requests arriving over time
 share batched decode steps, slots and pages turn over, and every request's ids equal the ids it
-gets when it runs alone.  That holds bit for bit because nothing a sequence computes depends on
-its batch neighbours: each row of the tensor-core projections accumulates on its own (one
-128-row tile, the same K split for 1 and 8 rows), the attention split count is fixed per model,
-and the LM head's argmax is per row.  The first id of each request is the batch-1 prefill's."""
+gets when it runs alone.  That holds bit for bit because the server runs even a lone sequence
+through the batched tensor-core step and nothing a sequence computes there depends on its batch
+neighbours: each row of the projections accumulates on its own (one 128-row tile, the same K
+split for 1 and 8 rows), the attention split count is fixed per model, and the LM head's argmax
+is per row.  The first id of each request is the batch-1 prefill's."""
 import numpy as np
 import pytest
 
