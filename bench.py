@@ -173,6 +173,11 @@ def run_ours(args, rank: int, world: int, dist):
     t0 = time.time()
     _, first = eng.forward(prompt, 0)
     prefill_s = time.time() - t0
+    sampling = None
+    if args.sample:
+        t_, p_, k_ = (float(x) for x in args.sample.split(","))
+        sampling = {"temperature": t_, "top_p": p_, "top_k": int(k_), "seed": 7}
+        eng.set_sampling(t_, p_, int(k_), seed=7)
     eng.decode(first, PROMPT, warmup)
 
     def barrier():
@@ -244,7 +249,9 @@ def run_ours(args, rank: int, world: int, dist):
             "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (Philox seed-0 N(0,0.02) weights, seed-1 uniform prompt ids)",
-            "config": {"workload": "llama3-8b-shape batch-1 greedy decode, prompt 2048, timed positions 2048..2048+K-1",
+            "config": {"workload": "llama3-8b-shape batch-1 " + ("sampled" if sampling else "greedy")
+                                   + " decode, prompt 2048, timed positions 2048..2048+K-1",
+                       "sampling": sampling,
                        "model": "llama-3-8b-shape" if args.layers == 32 else f"llama-3-8b-shape-{args.layers}-layers",
                        "global_batch": 1, "seq_len": PROMPT,
                        "parallelism": f"tp{world}",
@@ -277,7 +284,8 @@ def linear_params(cfg, world: int) -> int:
 
 
 def run_workload(args, rank: int, world: int, dist):
-    """The long-prefill (32768-token prompt) and batched-decode (64 sequences) workloads."""
+    """The long-prefill (32768-token prompt), batched-decode (64 sequences) and continuous-batching
+    (192 requests through inf_server into 64 slots) workloads."""
     import numpy as np
     import torch
 
@@ -378,6 +386,57 @@ def run_workload(args, rank: int, world: int, dist):
                         "d2h_bytes_per_step": 4},
                 "gpu_launches": launches, "clocks": clk.summary(),
             }), flush=True)
+    elif args.workload == "serve":
+        if world > 1:
+            raise SystemExit("--workload serve runs on one GPU")
+        B = cfg.max_batch
+        n_req = 3 * B
+        rng = np.random.default_rng(6)
+        lens = rng.integers(128, 1025, n_req)
+        news = rng.integers(32, 257, n_req)
+        prompts = [I.synth_ids(200 + i, int(lens[i]), cfg.vocab_size) for i in range(n_req)]
+        for _ in range(args.warmup):  # short requests through a server of their own
+            with I.Server(eng) as s:
+                for i in range(8):
+                    s.submit(prompts[i][:64], 4)
+                while s.stats()["waiting"] or s.stats()["active"]:
+                    s.step()
+        torch.cuda.synchronize()
+        l0 = eng.launches
+        with ClockSampler(local) as clk:
+            with I.Server(eng) as s:
+                torch.cuda.nvtx.range_push("timed")
+                w0 = time.perf_counter()
+                rids = [s.submit(p, int(m)) for p, m in zip(prompts, news)]
+                steps = 0
+                while True:
+                    s.step()
+                    steps += 1
+                    st = s.stats()
+                    if st["waiting"] == 0 and st["active"] == 0:
+                        break
+                wall = time.perf_counter() - w0
+                torch.cuda.nvtx.range_pop()
+                outs = [s.result(r) for r in rids]
+        launches = eng.launches - l0
+        out_tok = int(sum(o[0].size for o in outs))
+        assert all(o[1] and o[2] == 0 for o in outs)
+        print(json.dumps({
+            "metric": "continuous-batching output tokens/s (Llama-3-8B shape, bf16, 192 requests into 64 slots)",
+            "value": out_tok / wall, "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": wall * 1e3 / steps, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (Philox seed-0 N(0,0.02) weights, per-request uniform ids, "
+                                     "prompt lengths 128-1024 and 32-256 new tokens from numpy seed 6)",
+            "config": {"workload": f"{n_req} requests submitted at once to inf_server over {B} slots; greedy; "
+                                   "every step: admissions (prefill), one batched decode step, retirements",
+                       "model": "llama-3-8b-shape" if L == 32 else f"llama-3-8b-shape-{L}-layers",
+                       "global_batch": B, "prompt_tokens": int(lens.sum()), "output_tokens": out_tok,
+                       "mean_decode_batch": st["batched_tokens"] / max(1, st["batched_steps"]),
+                       "timing": "host wall clock: the server synchronizes with the device every step"},
+            "roofline": None,
+            "e2e": {"value": out_tok / wall, "unit": "tokens/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
+            "gpu_launches": launches, "clocks": clk.summary(),
+        }), flush=True)
     else:
         B = cfg.max_batch
         lens = I.synth_uniform(2, I.STREAM_CTX_LEN, B, 512, 4096)  # seed-2 context lengths
@@ -502,9 +561,10 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs use a short one)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch", "tokenize"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch", "serve", "tokenize"],
                     help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence "
-                         "decode; tokenize: host tokenizer encode (no GPU)")
+                         "decode; serve: continuous batching of 192 requests; tokenize: host tokenizer encode (no GPU)")
+    ap.add_argument("--sample", default="", help="decode workload with sampling: temperature,top_p,top_k")
     args = ap.parse_args()
     globals()["PROMPT"] = args.prompt
     if args.warmup < 3:
