@@ -695,7 +695,8 @@ Error_t enqueue_sample(InfEngine* e)
 	a.pos = e->pos;
 	a.slot = e->slot;
 	a.max_out = e->max_out;
-	INF_CUDA_TRY(launch(e, k_sample, dim3(1), dim3(kSampleThreads), 0, a));
+	INF_CUDA_TRY(set_smem(k_sample, kSampleSmem));
+	INF_CUDA_TRY(launch(e, k_sample, dim3(1), dim3(kSampleThreads), kSampleSmem, a));
 	return Success;
 }
 

@@ -14,8 +14,8 @@
 //   s    = floor(r * Z / 2^64);  id = the first kept index (ascending) whose inclusive prefix
 //          sum of kept q exceeds s
 // Ties at a threshold are all kept.  Both thresholds come from a 4-pass radix select on 8-bit
-// digits with shared-memory histograms of counts or 64-bit masses: integer atomics, so the
-// result does not depend on the order threads add.  The weights q are kept in global scratch
+// digits with per-warp shared-memory histograms of counts or 64-bit masses: integer atomics, so
+// the result does not depend on the order threads add.  The weights q are kept in global scratch
 // (L2-resident: 4 bytes x V) between passes.
 #pragma once
 
@@ -25,6 +25,9 @@
 namespace inf {
 
 constexpr int kSampleThreads = 1024;
+constexpr int kSampleWarps = kSampleThreads / 32;
+constexpr int kSampleSubStride = 257; // u64 per warp histogram: 256 bins + 1 to skew banks across warps
+constexpr size_t kSampleSmem = (size_t)kSampleWarps * kSampleSubStride * sizeof(unsigned long long);
 constexpr uint64_t kSampleStream = 0x3000000;
 
 struct SampleArgs {
@@ -51,21 +54,43 @@ __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v)
 }
 
 // Largest t such that the weight of {i : q_i >= t, q_i >= floor_t} reaches target, where an
-// element weighs 1 (by_mass false) or q_i.  Every thread returns the same t.
+// element weighs 1 (by_mass false) or q_i.  Every thread returns the same t.  Each warp counts
+// into its own histogram in `sub` (logits put most tokens in a few bins, and one shared
+// histogram serialised every update on them), and a thread adds runs of equal bins in a
+// register before it touches shared memory; the warp histograms are then summed per bin.
 __device__ uint32_t sample_radix_select(const SampleArgs& a, uint32_t floor_t, bool by_mass, uint64_t target,
-                                        unsigned long long* hist, unsigned long long* sh_acc, uint32_t* sh_prefix)
+                                        unsigned long long* hist, unsigned long long* sub, unsigned long long* sh_acc,
+                                        uint32_t* sh_prefix)
 {
 	const int tid = threadIdx.x;
+	unsigned long long* mine = sub + (size_t)(tid >> 5) * kSampleSubStride;
 	uint32_t prefix = 0;
 	uint64_t acc = 0; // weight of the elements above the current bucket
 	for (int shift = 24; shift >= 0; shift -= 8) {
-		for (int b = tid; b < 256; b += kSampleThreads) hist[b] = 0ull;
+		for (int b = tid; b < kSampleWarps * kSampleSubStride; b += kSampleThreads) sub[b] = 0ull;
 		__syncthreads();
 		const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+		uint32_t cb = 0xFFFFFFFFu; // the bin of the run in the register
+		unsigned long long cw = 0ull;
 		for (int i = tid; i < a.V; i += kSampleThreads) {
 			const uint32_t q = a.q[i];
 			if (q < floor_t || (q & hi_mask) != (prefix & hi_mask)) continue;
-			atomicAdd(&hist[(q >> shift) & 255u], by_mass ? (unsigned long long)q : 1ull);
+			const uint32_t bin = (q >> shift) & 255u;
+			const unsigned long long w = by_mass ? (unsigned long long)q : 1ull;
+			if (bin == cb) {
+				cw += w;
+			} else {
+				if (cw) atomicAdd(&mine[cb], cw);
+				cb = bin;
+				cw = w;
+			}
+		}
+		if (cw) atomicAdd(&mine[cb], cw);
+		__syncthreads();
+		for (int b = tid; b < 256; b += kSampleThreads) {
+			unsigned long long h = 0ull;
+			for (int w = 0; w < kSampleWarps; ++w) h += sub[(size_t)w * kSampleSubStride + b];
+			hist[b] = h;
 		}
 		__syncthreads();
 		if (tid == 0) {
@@ -90,6 +115,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 {
 	pdl_wait();
 	pdl_trigger();
+	extern __shared__ unsigned long long sub[]; // [kSampleWarps][kSampleSubStride]
 	__shared__ unsigned long long hist[256];
 	__shared__ unsigned long long red[kSampleThreads / 32];
 	__shared__ float redf[kSampleThreads / 32];
@@ -121,7 +147,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 
 	// top-k threshold, then the mass it keeps
 	uint32_t tk = 0;
-	if (a.top_k > 0 && a.top_k < (uint32_t)a.V) tk = sample_radix_select(a, 0u, false, a.top_k, hist, &sh_acc, &sh_prefix);
+	if (a.top_k > 0 && a.top_k < (uint32_t)a.V) tk = sample_radix_select(a, 0u, false, a.top_k, hist, sub, &sh_acc, &sh_prefix);
 	uint64_t zk = 0;
 	for (int i = tid; i < a.V; i += kSampleThreads) {
 		const uint32_t q = a.q[i];
@@ -145,7 +171,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 		double tgt = ceil((double)a.top_p * (double)zk);
 		if (tgt < 1.0) tgt = 1.0;
 		if (tgt > (double)zk) tgt = (double)zk;
-		tp = sample_radix_select(a, tk, true, (uint64_t)tgt, hist, &sh_acc, &sh_prefix);
+		tp = sample_radix_select(a, tk, true, (uint64_t)tgt, hist, sub, &sh_acc, &sh_prefix);
 		if (tp < tk) tp = tk;
 	}
 
