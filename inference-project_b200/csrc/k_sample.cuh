@@ -53,6 +53,29 @@ __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v)
 	return v;
 }
 
+// Calls f(q_i) for the indices this thread owns in a strided pass over [0, V): 16-byte loads,
+// two in flight per thread (one CTA makes every pass, so each pass is load-latency bound), then
+// the ragged tail one by one.  p must be 16-byte aligned.
+template <typename T, typename F>
+__device__ __forceinline__ void sample_visit(const T* p, int V, F f)
+{
+	static_assert(sizeof(T) == 4, "4-byte elements");
+	const int n4 = V >> 2;
+	const uint4* p4 = reinterpret_cast<const uint4*>(p);
+	int i = threadIdx.x;
+	for (; i + kSampleThreads < n4; i += 2 * kSampleThreads) {
+		const uint4 x = p4[i], y = p4[i + kSampleThreads];
+		f(i * 4 + 0, x.x); f(i * 4 + 1, x.y); f(i * 4 + 2, x.z); f(i * 4 + 3, x.w);
+		const int j = (i + kSampleThreads) * 4;
+		f(j + 0, y.x); f(j + 1, y.y); f(j + 2, y.z); f(j + 3, y.w);
+	}
+	if (i < n4) {
+		const uint4 x = p4[i];
+		f(i * 4 + 0, x.x); f(i * 4 + 1, x.y); f(i * 4 + 2, x.z); f(i * 4 + 3, x.w);
+	}
+	for (int k = n4 * 4 + (int)threadIdx.x; k < V; k += kSampleThreads) f(k, reinterpret_cast<const uint32_t*>(p)[k]);
+}
+
 // Largest t such that the weight of {i : q_i >= t, q_i >= floor_t} reaches target, where an
 // element weighs 1 (by_mass false) or q_i.  Every thread returns the same t.  Each warp counts
 // into its own histogram in `sub` (logits put most tokens in a few bins, and one shared
@@ -72,9 +95,8 @@ __device__ uint32_t sample_radix_select(const SampleArgs& a, uint32_t floor_t, b
 		const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
 		uint32_t cb = 0xFFFFFFFFu; // the bin of the run in the register
 		unsigned long long cw = 0ull;
-		for (int i = tid; i < a.V; i += kSampleThreads) {
-			const uint32_t q = a.q[i];
-			if (q < floor_t || (q & hi_mask) != (prefix & hi_mask)) continue;
+		sample_visit(a.q, a.V, [&](int, uint32_t q) {
+			if (q < floor_t || (q & hi_mask) != (prefix & hi_mask)) return;
 			const uint32_t bin = (q >> shift) & 255u;
 			const unsigned long long w = by_mass ? (unsigned long long)q : 1ull;
 			if (bin == cb) {
@@ -84,7 +106,7 @@ __device__ uint32_t sample_radix_select(const SampleArgs& a, uint32_t floor_t, b
 				cb = bin;
 				cw = w;
 			}
-		}
+		});
 		if (cw) atomicAdd(&mine[cb], cw);
 		__syncthreads();
 		for (int b = tid; b < 256; b += kSampleThreads) {
@@ -125,7 +147,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 
 	// max logit
 	float m = -INFINITY;
-	for (int i = tid; i < a.V; i += kSampleThreads) m = fmaxf(m, a.logits[i]);
+	sample_visit(a.logits, a.V, [&](int, uint32_t bits) { m = fmaxf(m, __uint_as_float(bits)); });
 	m = warp_max(m);
 	if (lane == 0) redf[warp] = m;
 	__syncthreads();
@@ -138,21 +160,20 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 	m = redf[0];
 
 	// fixed-point weights
-	for (int i = tid; i < a.V; i += kSampleThreads) {
-		const float w = expf((a.logits[i] - m) * a.inv_temp);
+	sample_visit(a.logits, a.V, [&](int i, uint32_t bits) {
+		const float w = expf((__uint_as_float(bits) - m) * a.inv_temp);
 		const float s = w * 4294967296.0f; // exact: a power-of-two scale
 		a.q[i] = s >= 4294967295.0f ? 0xFFFFFFFFu : (uint32_t)s;
-	}
+	});
 	__syncthreads(); // q is read back by other threads (global, same CTA)
 
 	// top-k threshold, then the mass it keeps
 	uint32_t tk = 0;
 	if (a.top_k > 0 && a.top_k < (uint32_t)a.V) tk = sample_radix_select(a, 0u, false, a.top_k, hist, sub, &sh_acc, &sh_prefix);
 	uint64_t zk = 0;
-	for (int i = tid; i < a.V; i += kSampleThreads) {
-		const uint32_t q = a.q[i];
+	sample_visit(a.q, a.V, [&](int, uint32_t q) {
 		if (q >= tk) zk += q;
-	}
+	});
 	zk = warp_sum_u64(zk);
 	if (lane == 0) red[warp] = zk;
 	__syncthreads();
@@ -176,12 +197,23 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 	}
 
 	// the draw: first kept index whose inclusive prefix mass exceeds s
-	const int chunk = (a.V + kSampleThreads - 1) / kSampleThreads;
+	// each thread owns a contiguous range of a multiple of 4 elements (16-byte aligned)
+	const int chunk = (((a.V + 3) / 4 + kSampleThreads - 1) / kSampleThreads) * 4;
 	const int i0 = min(a.V, tid * chunk), i1 = min(a.V, i0 + chunk);
 	uint64_t mine = 0;
-	for (int i = i0; i < i1; ++i) {
-		const uint32_t q = a.q[i];
-		if (q >= tp) mine += q;
+	{
+		int i = i0;
+		for (; i + 4 <= i1; i += 4) {
+			const uint4 x = *reinterpret_cast<const uint4*>(a.q + i);
+			mine += (x.x >= tp ? x.x : 0u);
+			mine += (x.y >= tp ? x.y : 0u);
+			mine += (x.z >= tp ? x.z : 0u);
+			mine += (x.w >= tp ? x.w : 0u);
+		}
+		for (; i < i1; ++i) {
+			const uint32_t q = a.q[i];
+			if (q >= tp) mine += q;
+		}
 	}
 	// exclusive scan of the threads' masses in thread order
 	uint64_t incl = mine;
