@@ -115,15 +115,37 @@ __device__ uint32_t sample_radix_select(const SampleArgs& a, uint32_t floor_t, b
 			hist[b] = h;
 		}
 		__syncthreads();
-		if (tid == 0) {
-			int d = 255;
-			uint64_t c = acc;
-			for (; d > 0; --d) {
-				if (c + hist[d] >= target) break;
-				c += hist[d];
+		if (tid < 32) {
+			// the highest bin d whose weight, added to everything above it, reaches target (bin 0
+			// if none does): lane l holds bins 255 - 8l .. 248 - 8l, a scan over the lanes gives
+			// the weight above each lane's bins, the first lane to reach target takes it
+			const int lane = tid;
+			unsigned long long h[8], own = 0ull;
+#pragma unroll
+			for (int j = 0; j < 8; ++j) {
+				h[j] = hist[255 - 8 * lane - j];
+				own += h[j];
 			}
-			*sh_prefix = prefix | ((uint32_t)d << shift);
-			*sh_acc = c;
+			unsigned long long incl = own;
+#pragma unroll
+			for (int o = 1; o < 32; o <<= 1) {
+				const unsigned long long v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+				if (lane >= o) incl += v;
+			}
+			unsigned long long c = acc + (incl - own);
+			int hit = -1;
+#pragma unroll
+			for (int j = 0; j < 8; ++j) {
+				if (hit < 0) {
+					if (c + h[j] >= target || (lane == 31 && j == 7)) hit = j;
+					else c += h[j];
+				}
+			}
+			const unsigned first = __ffs(__ballot_sync(0xFFFFFFFFu, hit >= 0)) - 1;
+			if (lane == (int)first) {
+				*sh_prefix = prefix | ((uint32_t)(255 - 8 * lane - hit) << shift);
+				*sh_acc = c;
+			}
 		}
 		__syncthreads();
 		prefix = *sh_prefix;
