@@ -218,65 +218,82 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 		if (tp < tk) tp = tk;
 	}
 
-	// the draw: first kept index whose inclusive prefix mass exceeds s
-	// each thread owns a contiguous range of a multiple of 4 elements (16-byte aligned)
-	const int chunk = (((a.V + 3) / 4 + kSampleThreads - 1) / kSampleThreads) * 4;
-	const int i0 = min(a.V, tid * chunk), i1 = min(a.V, i0 + chunk);
-	uint64_t mine = 0;
-	{
-		int i = i0;
-		for (; i + 4 <= i1; i += 4) {
+	// the draw: first kept index whose inclusive prefix mass exceeds s.  Warp w owns the
+	// contiguous elements [w * E, (w + 1) * E), read in rows of 128 (one 16-byte load per lane,
+	// coalesced); the warp holding s then walks its rows with warp scans.
+	const int rows = (a.V + kSampleWarps * 128 - 1) / (kSampleWarps * 128);
+	const int wbase = warp * rows * 128;
+	auto lane_row = [&](int r, uint32_t (&v)[4]) { // this lane's 4 elements of row r (0 past V)
+		const int i = wbase + r * 128 + lane * 4;
+		if (i + 4 <= a.V) {
 			const uint4 x = *reinterpret_cast<const uint4*>(a.q + i);
-			mine += (x.x >= tp ? x.x : 0u);
-			mine += (x.y >= tp ? x.y : 0u);
-			mine += (x.z >= tp ? x.z : 0u);
-			mine += (x.w >= tp ? x.w : 0u);
-		}
-		for (; i < i1; ++i) {
-			const uint32_t q = a.q[i];
-			if (q >= tp) mine += q;
-		}
-	}
-	// exclusive scan of the threads' masses in thread order
-	uint64_t incl = mine;
+			v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+		} else {
 #pragma unroll
-	for (int o = 1; o < 32; o <<= 1) {
-		const uint64_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-		if (lane >= o) incl += v;
+			for (int k = 0; k < 4; ++k) v[k] = i + k < a.V ? a.q[i + k] : 0u;
+		}
+#pragma unroll
+		for (int k = 0; k < 4; ++k) v[k] = (v[k] >= tp && i + k < a.V) ? v[k] : 0u; // kept mass only
+	};
+	uint64_t mine = 0;
+	for (int r = 0; r < rows; ++r) {
+		uint32_t v[4];
+		lane_row(r, v);
+		mine += (uint64_t)v[0] + v[1] + v[2] + v[3];
 	}
-	if (lane == 31) red[warp] = incl;
+	mine = warp_sum_u64(mine);
+	if (lane == 0) red[warp] = mine;
 	__syncthreads();
 	if (warp == 0) {
-		uint64_t v = red[lane];
-		uint64_t s = v;
+		const uint64_t v = red[lane];
+		uint64_t t = v;
 #pragma unroll
 		for (int o = 1; o < 32; o <<= 1) {
-			const uint64_t u = __shfl_up_sync(0xFFFFFFFFu, s, o);
-			if (lane >= o) s += u;
+			const uint64_t u = __shfl_up_sync(0xFFFFFFFFu, t, o);
+			if (lane >= o) t += u;
 		}
-		red[lane] = s - v; // exclusive prefix of the warps
-		if (lane == 31) sh_acc = s; // total kept mass
+		red[lane] = t - v;          // exclusive prefix of the warps
+		if (lane == 31) sh_acc = t; // total kept mass
 	}
 	__syncthreads();
 	const uint64_t total = sh_acc;
-	const uint64_t base = red[warp] + incl - mine;
 	const uint64_t ctr = (uint64_t)(uint32_t)*a.pos | ((uint64_t)(uint32_t)*a.slot << 32);
 	const uint4 wds = philox10(ctr, a.key);
-	const uint64_t r = ((uint64_t)wds.y << 32) | wds.x;
-	const uint64_t s = __umul64hi(r, total);
-	if (total > 0 && s >= base && s < base + mine) {
-		uint64_t c = base;
-		for (int i = i0; i < i1; ++i) {
-			const uint32_t q = a.q[i];
-			if (q < tp) continue;
-			c += q;
-			if (c > s) {
-				*a.cur_id = (uint32_t)i;
-				const uint32_t st = *a.step;
-				if (st >= 1 && (int)(st - 1) < a.max_out) a.out_ids[st - 1] = (uint32_t)i;
-				break;
+	const uint64_t r64 = ((uint64_t)wds.y << 32) | wds.x;
+	const uint64_t s = __umul64hi(r64, total);
+	uint64_t c = red[warp];
+	if (total == 0 || s < c || s >= c + mine) return; // another warp's range (warp-uniform)
+	for (int r = 0; r < rows; ++r) {
+		uint32_t v[4];
+		lane_row(r, v);
+		const uint64_t own = (uint64_t)v[0] + v[1] + v[2] + v[3];
+		uint64_t incl = own;
+#pragma unroll
+		for (int o = 1; o < 32; o <<= 1) {
+			const uint64_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+			if (lane >= o) incl += u;
+		}
+		const uint64_t row = __shfl_sync(0xFFFFFFFFu, incl, 31);
+		if (c + row <= s) {
+			c += row;
+			continue;
+		}
+		const unsigned hit = __ballot_sync(0xFFFFFFFFu, c + incl > s);
+		if (lane == (int)(__ffs(hit) - 1)) {
+			uint64_t cc = c + incl - own;
+#pragma unroll
+			for (int k = 0; k < 4; ++k) {
+				cc += v[k];
+				if (cc > s) {
+					const uint32_t id = (uint32_t)(wbase + r * 128 + lane * 4 + k);
+					*a.cur_id = id;
+					const uint32_t st = *a.step;
+					if (st >= 1 && (int)(st - 1) < a.max_out) a.out_ids[st - 1] = id;
+					break;
+				}
 			}
 		}
+		break;
 	}
 }
 
