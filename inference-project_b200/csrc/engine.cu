@@ -1442,7 +1442,7 @@ Error_t inf_safetensors_read(const char* weights_path, const InfConfig* config, 
 	if (out_bytes < need) return fail(ErrorInvalidValue, "out holds %llu bytes, the weight needs %llu", (unsigned long long)out_bytes, (unsigned long long)need);
 	Checkpoint ck;
 	INF_TRY(checkpoint_open(weights_path, &ck));
-	return weight_rows(ck, c, per_layer ? (int)layer : 0, kind, 0, rows, out);
+	return weight_rows_parallel(ck, c, per_layer ? (int)layer : 0, kind, 0, rows, out);
 }
 
 Error_t inf_model_destroy(ExecCtx** ctx, Model* model)

@@ -23,6 +23,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <thread>
 #include <unordered_set>
 
 #include "loader.h"
@@ -662,6 +663,33 @@ Error_t weight_rows(const Checkpoint& ck, const InfConfig& c, int l, uint32_t ki
 	return Success;
 }
 
+Error_t weight_rows_parallel(const Checkpoint& ck, const InfConfig& c, int l, uint32_t kind, uint64_t row0, uint64_t n,
+                             void* dst)
+{
+	uint64_t rows, cols;
+	weight_dims(c, kind, &rows, &cols);
+	const uint64_t row_bytes = cols * (c.dtype == InfBF16 ? 2 : 4);
+	const unsigned hw = std::thread::hardware_concurrency();
+	const int threads = (int)std::min<uint64_t>(std::min(16u, hw ? hw : 1u), n * row_bytes / (1u << 20) + 1); // >= 1 MB each
+	if (threads <= 1) return weight_rows(ck, c, l, kind, row0, n, dst);
+	const uint64_t per = (n + threads - 1) / threads;
+	std::vector<Error_t> err((size_t)threads, Success);
+	std::vector<std::thread> pool;
+	for (int t = 0; t < threads; ++t) {
+		const uint64_t a = (uint64_t)t * per;
+		if (a >= n) break;
+		const uint64_t m = std::min(per, n - a);
+		pool.emplace_back([&, t, a, m] { err[(size_t)t] = weight_rows(ck, c, l, kind, row0 + a, m, (unsigned char*)dst + a * row_bytes); });
+	}
+	for (std::thread& th : pool) th.join();
+	for (int t = 0; t < (int)pool.size(); ++t)
+		if (err[(size_t)t] != Success) { // again on this thread, for the error detail
+			const uint64_t a = (uint64_t)t * per;
+			return weight_rows(ck, c, l, kind, row0 + a, std::min(per, n - a), (unsigned char*)dst + a * row_bytes);
+		}
+	return Success;
+}
+
 Error_t checkpoint_upload(const Checkpoint& ck, const InfConfig& c, const std::vector<WeightDst>& dsts, cudaStream_t stream)
 {
 	constexpr uint64_t kStage = 64ull << 20;
@@ -687,7 +715,7 @@ Error_t checkpoint_upload(const Checkpoint& ck, const InfConfig& c, const std::v
 			const uint64_t n = std::min(per, rows - r0);
 			if (used[b]) ok = cu(cudaEventSynchronize(ev[b]), "cudaEventSynchronize"); // its previous copy is done
 			if (!ok) break;
-			const Error_t e = weight_rows(ck, c, dsts[w].layer, dsts[w].kind, r0, n, buf[b]);
+			const Error_t e = weight_rows_parallel(ck, c, dsts[w].layer, dsts[w].kind, r0, n, buf[b]);
 			if (e != Success) {
 				r = e;
 				ok = false;

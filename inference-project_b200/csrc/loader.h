@@ -79,6 +79,11 @@ void weight_dims(const InfConfig& c, uint32_t kind, uint64_t* rows, uint64_t* co
 Error_t weight_rows(const Checkpoint& ck, const InfConfig& c, int layer, uint32_t kind, uint64_t row0, uint64_t n,
                     void* dst);
 
+// weight_rows split over up to 16 host threads (page faults of the mapping and the copies run
+// in parallel; one thread assembles about 3.5 GB/s).
+Error_t weight_rows_parallel(const Checkpoint& ck, const InfConfig& c, int layer, uint32_t kind, uint64_t row0, uint64_t n,
+                             void* dst);
+
 // One weight and where it goes on the device.
 struct WeightDst {
 	int layer;
