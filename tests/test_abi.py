@@ -104,3 +104,27 @@ def test_library_id_generator_matches_oracle():
     lens = I.synth_uniform(2, I.STREAM_CTX_LEN, 64, 512, 4096)
     want = [O.uniform_u32(2, O.STREAM_CTX_LEN, i, 512, 4096) for i in range(64)]
     np.testing.assert_array_equal(lens, np.array(want, np.uint32))
+
+
+def test_new_entry_points_reject_null_arguments_without_a_device():
+    """Checkpoint, tokenizer, server and sampling entry points fail with ErrorInvalidValue (4) on
+    missing arguments before touching anything."""
+    L = I.lib()
+    c = I.preset(1)
+    n = I.u64()
+    assert L.inf_safetensors_check(None, C.byref(c)) == 4
+    assert L.inf_safetensors_check(b"x", None) == 4
+    assert L.inf_config_from_json(None, C.byref(c)) == 4
+    assert L.inf_tokenizer_build(None, None) == 4
+    assert L.inf_tokenizer_destroy(None) == 4
+    assert L.inf_tokenizer_encode(None, b"a", None, 0, C.byref(n)) == 4
+    assert L.inf_tokenizer_decode(None, None, 0, None, 0, C.byref(n)) == 4
+    assert L.inf_tokenizer_vocab_size(None) == 0
+    assert L.inf_server_create(None, 0, C.byref(I.vp())) == 4
+    assert L.inf_server_create_synthetic(0, 16, 10, 0, C.byref(I.vp())) == 4
+    assert L.inf_server_step(None, None) == 4
+    assert L.inf_server_destroy(None) == 4
+    assert L.inf_server_stats(None, None, None, None, None) == 4
+    assert L.inf_set_sampling(None, None) == 4
+    s = I.InfSampling(temperature=1.0, top_p=1.0)
+    assert L.inf_set_sampling(C.byref(I.Model()), C.byref(s)) == 4  # no engine
