@@ -78,3 +78,21 @@ def test_sampling_argument_checks(eng):
         with pytest.raises(I.InfError) as ei:
             eng.set_sampling(**bad)
         assert ei.value.code == 4
+
+
+def test_ragged_vocabulary(cuda):
+    """A vocabulary that is not a multiple of 4 (50257) exercises the sampler's scalar tails."""
+    cfg = I.preset(2, n_layers=1, max_seq=128, vocab_size=50257)
+    with I.Engine(cfg, seed=0) as e:
+        prompt = O.gen_ids(3, 12, e.V)
+        _, tok = e.forward(prompt, 0)
+        e.set_sampling(1.1, 0.97, 0, seed=9)
+        pos = prompt.size
+        for _ in range(12):
+            ids, _ = e.decode(tok, pos, 1)
+            q = e.debug_read("sample_q")
+            assert int(ids[0]) == O.sample_select(q, 0.97, 0, 9, pos + 1)
+            tok, pos = int(ids[0]), pos + 1
+        e.set_sampling(0.7, 1.0, 50257 - 3, seed=9)  # top-k just below the vocabulary
+        ids, _ = e.decode(tok, pos, 1)
+        assert int(ids[0]) == O.sample_select(e.debug_read("sample_q"), 1.0, 50257 - 3, 9, pos + 1)
