@@ -303,7 +303,9 @@ Error_t inf_server_stats(const InfServer* server, u32* n_waiting, u32* n_active,
  * num_attention_heads), vocab_size, rms_norm_eps, rope_theta and torch_dtype ("bfloat16" or
  * "float32").  A field the file lacks keeps its value; max_seq, max_batch, the KV paging and the
  * tensor-parallel fields are never taken from the file.  ErrorIo if the file cannot be read,
- * ErrorInvalidValue for malformed JSON or a field of the wrong type or range. */
+ * ErrorInvalidValue for malformed JSON or a field of the wrong type or range, ErrorUnsupported
+ * for what this decoder does not compute (a model_type other than "llama", an activation other
+ * than SiLU, attention or MLP biases, RoPE scaling). */
 Error_t inf_config_from_json(const char* config_path, InfConfig* inout);
 
 /* The checkpoint checks of model_build without a GPU.  Every tensor the decoder of `config`
@@ -319,7 +321,9 @@ Error_t inf_config_from_json(const char* config_path, InfConfig* inout);
  * and a buffer indexed without holes or overlaps.
  * ErrorIo: a file cannot be opened or mapped.  ErrorInvalidValue: malformed header, offsets or
  * index, or a missing tensor.  ErrorBadConfig: a shape that does not match config.
- * ErrorUnsupported: a needed tensor in another dtype. */
+ * ErrorUnsupported: a needed tensor in another dtype, or a tensor under the decoder's prefix
+ * that this decoder does not use (q/k norms, extra norms, biases, per-layer embeddings: the
+ * checkpoint is another model family). */
 Error_t inf_safetensors_check(const char* weights_path, const InfConfig* config);
 
 /* Weights of the decoder, by their place in the device layout. */

@@ -589,12 +589,47 @@ void convert_row(const unsigned char* src, bool src_f32, bool dst_bf16, uint64_t
 
 } // namespace
 
+// A tensor under the decoder's prefix that this decoder does not use changes the model's
+// function (q/k norms, extra norms, biases, per-layer embeddings of other families): refuse
+// it rather than run a different model.  Buffers that carry no weights are allowed.
+bool decoder_tensor_known(const std::string& rest)
+{
+	static const char* const top[] = {"embed_tokens.weight", "norm.weight"};
+	for (const char* t : top)
+		if (rest == t) return true;
+	if (rest.compare(0, 7, "layers.") != 0) return false;
+	size_t k = 7;
+	while (k < rest.size() && rest[k] >= '0' && rest[k] <= '9') ++k;
+	if (k == 7 || k >= rest.size() || rest[k] != '.') return false;
+	const std::string leaf = rest.substr(k + 1);
+	static const char* const used[] = {
+	    "input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight", "self_attn.k_proj.weight",
+	    "self_attn.v_proj.weight", "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
+	    "mlp.down_proj.weight", "self_attn.rotary_emb.inv_freq", // a RoPE buffer some exports keep: no weights
+	};
+	for (const char* u : used)
+		if (leaf == u) return true;
+	return false;
+}
+
 Error_t checkpoint_check(const Checkpoint& ck, const InfConfig& c)
 {
 	Need s[3];
 	for (uint32_t k : kModelKinds) INF_TRY(sources(ck, c, 0, k, s));
 	for (uint32_t l = 0; l < c.n_layers; ++l)
 		for (uint32_t k : kLayerKinds) INF_TRY(sources(ck, c, (int)l, k, s));
+	// the prefix the embedding was found under is the decoder's
+	std::string emb;
+	find_model(ck, "embed_tokens.weight", &emb);
+	const std::string prefix = emb.substr(0, emb.size() - strlen("embed_tokens.weight"));
+	for (const auto& t : ck.tensors) {
+		const std::string& n = t.first;
+		if (n.compare(0, prefix.size(), prefix) != 0) continue; // another component (vision tower, ...)
+		if (prefix == "model." && n.compare(0, 21, "model.language_model.") == 0) continue;
+		if (!decoder_tensor_known(n.substr(prefix.size())))
+			return fail(ErrorUnsupported, "%s: a tensor this Llama decoder does not implement (its model would compute "
+			            "something else)", n.c_str());
+	}
 	return Success;
 }
 
@@ -792,8 +827,13 @@ Error_t config_from_json(const char* path, InfConfig* c)
 		else return fail(ErrorUnsupported, "%s: torch_dtype %s (bfloat16 or float32)", path, dt->s.c_str());
 	}
 	// what the decoder does not implement is refused, not ignored
-	const JVal* act = m.get("hidden_act");
-	if (act && act->kind == JVal::Str && act->s != "silu") return fail(ErrorUnsupported, "%s: hidden_act %s (silu)", path, act->s.c_str());
+	const JVal* mt = m.get("model_type");
+	if (mt && mt->kind == JVal::Str && mt->s != "llama")
+		return fail(ErrorUnsupported, "%s: model_type %s (the Llama decoder only)", path, mt->s.c_str());
+	for (const char* key : {"hidden_act", "hidden_activation"}) {
+		const JVal* act = m.get(key);
+		if (act && act->kind == JVal::Str && act->s != "silu") return fail(ErrorUnsupported, "%s: %s %s (silu)", path, key, act->s.c_str());
+	}
 	for (const char* k : {"attention_bias", "mlp_bias"}) {
 		const JVal* v = m.get(k);
 		if (v && v->kind == JVal::Bool && v->b) return fail(ErrorUnsupported, "%s: %s (projections have no bias)", path, k);

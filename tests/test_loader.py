@@ -179,12 +179,31 @@ def test_any_tensor_order(tmp_path):
     """Defect D8: tensors in any order (here reversed) and unrelated tensors of other dtypes."""
     t = bf16_tensors(6)
     items = [(n, "BF16", t[(k, l)]) for n, k, l in hf_names(TINY["n_layers"])][::-1]
-    items.insert(3, ("model.vision_tower.patch.weight", "I32", np.arange(12, dtype=np.int32).reshape(3, 4)))
+    items.insert(3, ("vision_tower.patch.weight", "I32", np.arange(12, dtype=np.int32).reshape(3, 4)))
     path = str(tmp_path / "rev.safetensors")
     write_safetensors(path, items, metadata={"format": "pt"})
     c = cfg_of()
     I.safetensors_check(path, c)
     np.testing.assert_array_equal(I.safetensors_read(path, c, 1, I.W_DOWN), expected(t, c, 1, I.W_DOWN))
+
+
+@pytest.mark.parametrize("extra,ok", [
+    ("model.layers.0.self_attn.rotary_emb.inv_freq", True),   # a buffer, no weights
+    ("model.layers.0.self_attn.q_norm.weight", False),         # q/k norms (Gemma 3, Qwen 3)
+    ("model.layers.1.pre_feedforward_layernorm.weight", False),
+    ("model.layers.0.self_attn.q_proj.bias", False),           # biases (Qwen 2)
+    ("model.embed_tokens_per_layer.weight", False),            # per-layer embeddings (Gemma 3n / 4)
+])
+def test_tensors_of_other_families_are_refused(tmp_path, extra, ok):
+    t = bf16_tensors(10)
+    items = [(n, "BF16", t[(k, l)]) for n, k, l in hf_names(TINY["n_layers"])]
+    items.append((extra, "F32", np.ones(8, np.float32)))
+    path = str(tmp_path / "x.safetensors")
+    write_safetensors(path, items)
+    if ok:
+        I.safetensors_check(path, cfg_of())
+    else:
+        check_code(E_UNSUPPORTED, I.safetensors_check, path, cfg_of(), match=extra)
 
 
 def test_sharded_index_and_directory(tmp_path):
@@ -434,6 +453,8 @@ def test_config_text_config_and_defaults(tmp_path):
     ({"hidden_act": "gelu"}, E_UNSUPPORTED),
     ({"attention_bias": True}, E_UNSUPPORTED),
     ({"rope_scaling": {"rope_type": "llama3", "factor": 8.0}}, E_UNSUPPORTED),
+    ({"model_type": "gemma3_text"}, E_UNSUPPORTED),
+    ({"hidden_activation": "gelu_pytorch_tanh"}, E_UNSUPPORTED),
     ({"hidden_size": 100, "num_attention_heads": 3}, E_INVALID),
     ("[" * 70 + "]" * 70, E_INVALID),
 ])
