@@ -349,7 +349,9 @@ typedef struct InfTokenizer InfTokenizer;
 /* tokenizer_build (src/tokenizer.c:186-262): the BPE model of a Hugging Face tokenizer.json,
  * "model": {"vocab": {piece: id}, "merges": [[left, right], ...] or ["left right", ...],
  * "byte_fallback", "unk_token"}; a merge's rank is its position in the list.  "added_tokens"
- * are decoded too.  ErrorIo if the file cannot be read; ErrorInvalidValue if it is malformed. */
+ * are decoded too.  ErrorIo if the file cannot be read; ErrorInvalidValue if it is malformed;
+ * ErrorUnsupported for another model type or a byte-level BPE (GPT-2 / Llama-3 style, whose
+ * regex pre-tokenizer this segmentation does not implement). */
 Error_t inf_tokenizer_build(const char* tokenizer_json_path, InfTokenizer** out);
 /* tokenizer_destroy (src/tokenizer.c:264-278) */
 Error_t inf_tokenizer_destroy(InfTokenizer** tok);

@@ -218,6 +218,23 @@ Error_t build(const char* path, InfTokenizer* t)
 	if (!model || model->kind != JVal::Obj) return fail(ErrorInvalidValue, "%s: no \"model\" object", path);
 	const JVal* type = model->get("type");
 	if (type && type->kind == JVal::Str && type->s != "BPE") return fail(ErrorUnsupported, "%s: model type %s (BPE)", path, type->s.c_str());
+	// byte-level BPE (GPT-2 / Llama-3 style) maps bytes to printable characters and splits text
+	// with a regex first; this segmentation is the reference's SentencePiece-style one, so such
+	// a tokenizer would give other ids: refuse it
+	auto byte_level = [](const JVal* v) {
+		if (!v || v->kind != JVal::Obj) return false;
+		const JVal* t = v->get("type");
+		if (t && t->kind == JVal::Str && t->s == "ByteLevel") return true;
+		const JVal* seq = v->get("pretokenizers");
+		if (seq && seq->kind == JVal::Arr)
+			for (const JVal& x : seq->arr) {
+				const JVal* tt = x.get("type");
+				if (tt && tt->kind == JVal::Str && tt->s == "ByteLevel") return true;
+			}
+		return false;
+	};
+	if (byte_level(root.get("pre_tokenizer")) || byte_level(root.get("decoder")))
+		return fail(ErrorUnsupported, "%s: a byte-level BPE tokenizer (its regex pre-tokenizer is not implemented)", path);
 	const JVal* vocab = model->get("vocab");
 	if (!vocab || vocab->kind != JVal::Obj) return fail(ErrorInvalidValue, "%s: no \"model\".\"vocab\" object", path);
 	const JVal* merges = model->get("merges");

@@ -177,6 +177,10 @@ def test_added_tokens_decode(tok, spec):
     ({"model": {"vocab": {"a": 0}, "merges": [["a"]]}}, E_INVALID),
     ({"model": {"vocab": {"a": 0}, "merges": ["ab"]}}, E_INVALID),
     ({"model": {"type": "Unigram", "vocab": {"a": 0}, "merges": []}}, E_UNSUPPORTED),
+    ({"pre_tokenizer": {"type": "ByteLevel", "add_prefix_space": False},
+      "model": {"type": "BPE", "vocab": {"a": 0}, "merges": []}}, E_UNSUPPORTED),
+    ({"pre_tokenizer": {"type": "Sequence", "pretokenizers": [{"type": "Split"}, {"type": "ByteLevel"}]},
+      "model": {"type": "BPE", "vocab": {"a": 0}, "merges": []}}, E_UNSUPPORTED),
 ])
 def test_malformed_tokenizer_json(tmp_path, doc, code):
     with pytest.raises(I.InfError) as ei:
