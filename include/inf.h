@@ -368,6 +368,11 @@ u32     inf_tokenizer_vocab_size(const InfTokenizer* tok);
  * of bounds there).  *n_ids is the number of ids; ids NULL counts only; more than max_ids:
  * ErrorInvalidValue. */
 Error_t inf_tokenizer_encode(const InfTokenizer* tok, const char* text, u32* ids, u64 max_ids, u64* n_ids);
+/* inf_tokenizer_encode after cutting out the added tokens marked "special" (longest match at
+ * the earliest position, e.g. "<start_of_turn>"): each special becomes its id and every piece of
+ * text between them is encoded as a whole text (its first word without U+2581).  The
+ * reference has no special tokens; this is for chat templates. */
+Error_t inf_tokenizer_encode_special(const InfTokenizer* tok, const char* text, u32* ids, u64 max_ids, u64* n_ids);
 /* tokenizer_decode (declared at src/tokenizer.h:38, never defined by the reference): the
  * pieces of ids concatenated, U+2581 -> ' ', <0xXX> -> that byte (byte_fallback models).
  * Writes a NUL-terminated string of *out_len bytes; out NULL gives the length only; out_bytes

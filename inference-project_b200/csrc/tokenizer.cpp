@@ -45,6 +45,9 @@ struct InfTokenizer {
 	int64_t byte_id[256];
 	bool byte_fallback = false;
 	int64_t unk_id = -1;
+	// added tokens marked "special", by first byte, longest first (inf_tokenizer_encode_special)
+	std::vector<std::pair<std::string, uint32_t>> specials;
+	std::vector<std::vector<uint32_t>> special_by_byte = std::vector<std::vector<uint32_t>>(256);
 
 	uint32_t intern(const std::string& s)
 	{
@@ -288,9 +291,17 @@ Error_t build(const char* path, InfTokenizer* t)
 		for (const JVal& a : added->arr) {
 			const JVal* id = a.get("id");
 			const JVal* content = a.get("content");
-			if (id && id->kind == JVal::Num && id->is_uint && id->u <= 0x7FFFFFFFull && content && content->kind == JVal::Str)
+			if (id && id->kind == JVal::Num && id->is_uint && id->u <= 0x7FFFFFFFull && content && content->kind == JVal::Str) {
 				set_piece(id->u, content->s);
+				const JVal* sp = a.get("special");
+				if (sp && sp->kind == JVal::Bool && sp->b && !content->s.empty())
+					t->specials.emplace_back(content->s, (uint32_t)id->u);
+			}
 		}
+	for (uint32_t k = 0; k < t->specials.size(); ++k)
+		t->special_by_byte[(unsigned char)t->specials[k].first[0]].push_back(k);
+	for (auto& v : t->special_by_byte)
+		std::sort(v.begin(), v.end(), [&](uint32_t x, uint32_t y) { return t->specials[x].first.size() > t->specials[y].first.size(); });
 	return Success;
 }
 
@@ -323,26 +334,44 @@ Error_t inf_tokenizer_destroy(InfTokenizer** tok)
 
 u32 inf_tokenizer_vocab_size(const InfTokenizer* tok) { return tok ? (u32)tok->piece.size() : 0; }
 
-Error_t inf_tokenizer_encode(const InfTokenizer* tok, const char* text, u32* ids, u64 max_ids, u64* n_ids)
-{
-	if (!tok || !text || !n_ids) return fail(ErrorInvalidValue, "inf_tokenizer_encode: NULL argument");
+} // extern "C"
+
+namespace {
+
+// One encode call's state: the ids so far and, because words repeat (natural text is
+// Zipf-distributed), the ids of short words already encoded.
+struct Encoder {
+	const InfTokenizer& tok;
 	std::vector<uint32_t> out;
 	Work W;
-	// words repeat (natural text is Zipf-distributed): the ids of short words are kept for the
-	// rest of the call
 	std::unordered_map<std::string, std::pair<uint32_t, uint32_t>> seen; // word -> (first id in out, count)
-	constexpr size_t kMemoWord = 48, kMemoWords = 1 << 16;
 	std::string w;
-	const char* p = text;
+	explicit Encoder(const InfTokenizer& t) : tok(t) {}
+
+	// text[p, end) as a whole text: words split at ' ', "▁" before every word but the first
+	Error_t text(const char* p, const char* end);
+	Error_t finish(u32* ids, u64 max_ids, u64* n_ids) const
+	{
+		*n_ids = out.size();
+		if (!ids) return Success;
+		if (out.size() > max_ids) return fail(ErrorInvalidValue, "%zu ids, room for %llu", out.size(), (unsigned long long)max_ids);
+		std::copy(out.begin(), out.end(), ids);
+		return Success;
+	}
+};
+
+Error_t Encoder::text(const char* p, const char* end)
+{
+	constexpr size_t kMemoWord = 48, kMemoWords = 1 << 16;
 	bool first = true;
-	while (*p) {
+	while (p < end) {
 		const char* l = p;
-		while (*p && *p != ' ') ++p;
+		while (p < end && *p != ' ') ++p;
 		w.clear();
 		if (!first) w = kSpaceMark;
 		w.append(l, (size_t)(p - l));
 		first = false;
-		if (*p == ' ') ++p;
+		if (p < end && *p == ' ') ++p;
 		if (w.size() <= kMemoWord) {
 			const auto it = seen.find(w);
 			if (it != seen.end()) {
@@ -352,19 +381,56 @@ Error_t inf_tokenizer_encode(const InfTokenizer* tok, const char* text, u32* ids
 			}
 		}
 		const size_t at = out.size();
-		bpe_word(*tok, w, W);
+		bpe_word(tok, w, W);
 		for (const Node& n : W.pieces)
-			if (!emit(*tok, w, n, out))
+			if (!emit(tok, w, n, out))
 				return fail(ErrorInvalidValue, "piece \"%s\" is not in the vocabulary and the model has neither byte fallback nor an unk token",
 				            w.substr(n.begin, n.end - n.begin).c_str());
 		if (w.size() <= kMemoWord && seen.size() < kMemoWords && at <= 0xFFFFFFFFull)
 			seen.emplace(w, std::make_pair((uint32_t)at, (uint32_t)(out.size() - at)));
 	}
-	*n_ids = out.size();
-	if (!ids) return Success;
-	if (out.size() > max_ids) return fail(ErrorInvalidValue, "%zu ids, room for %llu", out.size(), (unsigned long long)max_ids);
-	std::copy(out.begin(), out.end(), ids);
 	return Success;
+}
+
+} // namespace
+
+extern "C" {
+
+Error_t inf_tokenizer_encode(const InfTokenizer* tok, const char* text, u32* ids, u64 max_ids, u64* n_ids)
+{
+	if (!tok || !text || !n_ids) return fail(ErrorInvalidValue, "inf_tokenizer_encode: NULL argument");
+	Encoder E(*tok);
+	INF_TRY(E.text(text, text + strlen(text)));
+	return E.finish(ids, max_ids, n_ids);
+}
+
+Error_t inf_tokenizer_encode_special(const InfTokenizer* tok, const char* text, u32* ids, u64 max_ids, u64* n_ids)
+{
+	if (!tok || !text || !n_ids) return fail(ErrorInvalidValue, "inf_tokenizer_encode_special: NULL argument");
+	Encoder E(*tok);
+	const char* end = text + strlen(text);
+	const char* seg = text;
+	for (const char* p = text; p < end;) {
+		const std::vector<uint32_t>& cand = tok->special_by_byte[(unsigned char)*p];
+		const std::pair<std::string, uint32_t>* hit = nullptr;
+		for (uint32_t k : cand) { // longest first
+			const std::string& c = tok->specials[k].first;
+			if ((size_t)(end - p) >= c.size() && memcmp(p, c.data(), c.size()) == 0) {
+				hit = &tok->specials[k];
+				break;
+			}
+		}
+		if (!hit) {
+			++p;
+			continue;
+		}
+		INF_TRY(E.text(seg, p));
+		E.out.push_back(hit->second);
+		p += hit->first.size();
+		seg = p;
+	}
+	INF_TRY(E.text(seg, end));
+	return E.finish(ids, max_ids, n_ids);
 }
 
 Error_t inf_tokenizer_decode(const InfTokenizer* tok, const u32* ids, u64 n_ids, char* out, u64 out_bytes, u64* out_len)

@@ -90,7 +90,7 @@ EXPORTS = [
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
     "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
     "inf_safetensors_read", "inf_tokenizer_build", "inf_tokenizer_destroy", "inf_tokenizer_vocab_size",
-    "inf_tokenizer_encode", "inf_tokenizer_decode", "inf_set_sampling", "inf_server_create",
+    "inf_tokenizer_encode", "inf_tokenizer_encode_special", "inf_tokenizer_decode", "inf_set_sampling", "inf_server_create",
     "inf_server_create_synthetic", "inf_server_destroy", "inf_server_submit", "inf_server_step", "inf_server_result",
     "inf_server_release", "inf_server_stats",
 ]
@@ -160,6 +160,7 @@ def lib():
         "inf_tokenizer_destroy": (E, [C.POINTER(vp)]),
         "inf_tokenizer_vocab_size": (u32, [vp]),
         "inf_tokenizer_encode": (E, [vp, C.c_char_p, vp, u64, C.POINTER(u64)]),
+        "inf_tokenizer_encode_special": (E, [vp, C.c_char_p, vp, u64, C.POINTER(u64)]),
         "inf_tokenizer_decode": (E, [vp, vp, u64, C.c_char_p, u64, C.POINTER(u64)]),
         "inf_set_sampling": (E, [C.POINTER(Model), C.POINTER(InfSampling)]),
         "inf_server_create": (E, [C.POINTER(Model), u32, C.POINTER(vp)]),
@@ -247,14 +248,16 @@ class Tokenizer:
     def vocab_size(self) -> int:
         return int(lib().inf_tokenizer_vocab_size(self.h))
 
-    def encode(self, text) -> np.ndarray:
+    def encode(self, text, special: bool = False) -> np.ndarray:
+        """The reference's encoding; special=True first cuts out added special tokens."""
+        fn = lib().inf_tokenizer_encode_special if special else lib().inf_tokenizer_encode
         raw = text.encode() if isinstance(text, str) else bytes(text)
         n = u64()
         out = np.empty(len(raw) + 8, dtype=np.uint32)  # enough unless byte fallback splits "▁"
-        rc = lib().inf_tokenizer_encode(self.h, raw, _ptr(out), out.size, C.byref(n))
+        rc = fn(self.h, raw, _ptr(out), out.size, C.byref(n))
         if rc == 4 and n.value > out.size:
             out = np.empty(n.value, dtype=np.uint32)
-            rc = lib().inf_tokenizer_encode(self.h, raw, _ptr(out), out.size, C.byref(n))
+            rc = fn(self.h, raw, _ptr(out), out.size, C.byref(n))
         check(rc, "inf_tokenizer_encode")
         return out[:n.value]
 

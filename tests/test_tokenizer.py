@@ -204,3 +204,18 @@ def test_long_unspaced_text_is_fast(tok, spec):
     ids = tok.encode(s)
     assert time.perf_counter() - t0 < 5.0
     assert tok.decode(ids) == s
+
+
+def test_special_tokens_are_cut_out_when_asked(tok, spec):
+    """inf_tokenizer_encode_special: added tokens marked special match whole (longest first) and
+    each text piece between them encodes as a whole text; the plain encode (the reference's)
+    splits them into characters."""
+    added = {a["content"]: a["id"] for a in spec["added_tokens"]}
+    sot, bos = added["<start_of_turn>"], added["<bos>"]
+    text = "<bos><start_of_turn>the end<start_of_turn> a b"
+    got = list(tok.encode(text, special=True))
+    want = [bos, sot] + list(tok.encode("the end")) + [sot] + list(tok.encode(" a b"))
+    assert got == want
+    assert sot not in list(tok.encode(text))  # the reference's encoding has no special tokens
+    assert list(tok.encode("no specials here", special=True)) == list(tok.encode("no specials here"))
+    assert tok.decode(got) == text
