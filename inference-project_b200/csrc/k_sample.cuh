@@ -16,7 +16,10 @@
 // Ties at a threshold are all kept.  Both thresholds come from a 4-pass radix select on 8-bit
 // digits with per-warp shared-memory histograms of counts or 64-bit masses: integer atomics, so
 // the result does not depend on the order threads add.  The weights q are kept in global scratch
-// (L2-resident: 4 bytes x V) between passes.
+// (L2-resident: 4 bytes x V) between passes; every pass reads them with 16-byte loads, two in
+// flight per thread, and the draw gives each warp a contiguous range that the warp holding s
+// searches row by row with warp scans.  One CTA makes every pass, so the kernel is bound by its
+// own instruction stream (about 0.2 ms per token at V = 128256).
 #pragma once
 
 #include "common.cuh"
