@@ -4,7 +4,9 @@ and gate/up rows column-parallel, O and down columns row-parallel, LM-head vocab
 its half of one decoder layer in float64, and the two partial sums after O and after down are
 added with all_reduce -- the exchanges the projection kernels do over NVLink peer memory -- and
 the LM head's argmax is taken across the vocabulary shards (ties to the lowest id).  The result
-must equal the single-process computation on the canonical tensors."""
+must equal the single-process computation on the canonical tensors.  And a rank that dies
+between steps: the survivor's exchange ends with an error within its short process-group
+timeout instead of waiting for good."""
 import os
 import socket
 
@@ -142,3 +144,41 @@ def test_tp2_layer_matches_single_process(tmp_path):
     ref_path = str(tmp_path / "ref.npz")
     np.savez(ref_path, x=x, r2=r2, argmax=am)
     mp.spawn(rank_main, args=(path, free_port(), ref_path), nprocs=WORLD, join=True)
+
+
+def failing_rank_main(rank, port, q):
+    """Rank 1 dies before the exchange; rank 0's all-reduce must end with an error, not hang."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=WORLD,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # a rank that stops between steps
+    t0 = time.time()
+    try:
+        dist.all_reduce(torch.ones(4))
+        q.put(("no error", time.time() - t0))
+    except Exception as e:  # noqa: BLE001 -- any error is the detection
+        q.put(("error", time.time() - t0, type(e).__name__))
+
+
+def test_rank_failure_is_detected_not_hung():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=failing_rank_main, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    try:
+        res = q.get(timeout=120)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert res[0] == "error" and res[1] < 60, res
+    assert procs[1].exitcode == 3
