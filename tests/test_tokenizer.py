@@ -140,9 +140,9 @@ def test_merge_order_is_rank_not_frequency(tmp_path):
         with I.Tokenizer(write_spec(__import__("pathlib").Path(d), spec)) as t:
             enc = lambda s: [list(vocab)[i] for i in t.encode(s)]
             assert enc("abc") == ["abc"]          # (b,c) rank 1 before (a,b) rank 2, then (a,bc)
-            assert enc("aaa") == ["aaa"]          # round 1: (a,a) at 0 only -> aa a; round 2: (aa,a)
+            assert enc("aaa") == ["aaa"]          # first merge pass: (a,a) at 0 only -> aa a; second: (aa,a)
             assert enc("aaaa") == ["aaaa"]        # (a,a) twice in one round, then (aa,aa)
-            assert enc("aaaaa") == ["aaaa", "a"]  # round 1: aa aa a; round 2: (aa,aa) rank 4 < (aa,a) rank 5
+            assert enc("aaaaa") == ["aaaa", "a"]  # first pass: aa aa a; second: (aa,aa) rank 4 < (aa,a) rank 5
 
 
 def test_buffers_and_counts(tok):
