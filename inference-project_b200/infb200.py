@@ -182,7 +182,7 @@ def lib():
 
 def check(rc: int, where: str) -> None:
     if rc != 0:
-        raise InfError(rc, where, lib().inf_last_error_detail().decode())
+        raise InfError(rc, where, lib().inf_last_error_detail().decode(errors="replace"))  # details quote file bytes
 
 
 def preset(n: int, **overrides) -> InfConfig:
