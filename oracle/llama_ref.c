@@ -88,7 +88,7 @@ float orc_normal_value(uint64_t seed, uint64_t stream, uint64_t idx, float scale
 }
 
 /* round-to-nearest-even on the fp32 bit pattern */
-uint16_t orc_f32_to_bf16(float x)
+static inline uint16_t f2bf(float x)
 {
 	uint32_t u;
 	memcpy(&u, &x, 4);
@@ -97,7 +97,11 @@ uint16_t orc_f32_to_bf16(float x)
 	return (uint16_t)(u >> 16);
 }
 
-float orc_bf16_to_f32(uint16_t h)
+uint16_t orc_f32_to_bf16(float x) { return f2bf(x); }
+
+/* the exported conversions are not inlined into the loops below under -fPIC (they could be
+ * interposed); these static copies are */
+static inline float bf16f(uint16_t h)
 {
 	const uint32_t u = (uint32_t)h << 16;
 	float f;
@@ -105,9 +109,11 @@ float orc_bf16_to_f32(uint16_t h)
 	return f;
 }
 
+float orc_bf16_to_f32(uint16_t h) { return bf16f(h); }
+
 static inline float round_store(float x, int bf16)
 {
-	return bf16 ? orc_bf16_to_f32(orc_f32_to_bf16(x)) : x;
+	return bf16 ? bf16f(f2bf(x)) : x;
 }
 
 void orc_fill_tensor(uint64_t seed, uint64_t stream, uint64_t n, float std, int bf16, void* out)
@@ -120,7 +126,7 @@ void orc_fill_tensor(uint64_t seed, uint64_t stream, uint64_t n, float std, int 
 		uint32_t ctr[4] = { (uint32_t)i, (uint32_t)((uint64_t)i >> 32), 0u, 0u }, w[4];
 		orc_philox4x32_10(ctr, key, w);
 		const float v = normal_from_words(w, scale);
-		if (bf16) ((uint16_t*)out)[i] = orc_f32_to_bf16(v);
+		if (bf16) ((uint16_t*)out)[i] = f2bf(v);
 		else ((float*)out)[i] = v;
 	}
 }
@@ -164,7 +170,7 @@ void orc_rope_table(uint32_t max_seq, uint32_t head_dim, float theta, float* cos
 
 static inline float wval(const void* W, int bf16, uint64_t i)
 {
-	return bf16 ? orc_bf16_to_f32(((const uint16_t*)W)[i]) : ((const float*)W)[i];
+	return bf16 ? bf16f(((const uint16_t*)W)[i]) : ((const float*)W)[i];
 }
 
 void orc_embed_gather(const uint32_t* ids, uint64_t n, uint32_t dim, const void* table, int bf16, float* out)
@@ -183,10 +189,10 @@ static inline double dot_bf16_f(const uint16_t* w, const float* x, uint64_t n)
 	float acc[16] = { 0 };
 	uint64_t i = 0;
 	for (; i + 16 <= n; i += 16)
-		for (int j = 0; j < 16; ++j) acc[j] += orc_bf16_to_f32(w[i + j]) * x[i + j];
+		for (int j = 0; j < 16; ++j) acc[j] += bf16f(w[i + j]) * x[i + j];
 	float s = 0.f;
 	for (int j = 0; j < 16; ++j) s += acc[j];
-	for (; i < n; ++i) s += orc_bf16_to_f32(w[i]) * x[i];
+	for (; i < n; ++i) s += bf16f(w[i]) * x[i];
 	return s;
 }
 
@@ -217,10 +223,10 @@ static inline double dot_bf16_d(const uint16_t* w, const float* x, uint64_t n)
 	double acc[8] = { 0 };
 	uint64_t i = 0;
 	for (; i + 8 <= n; i += 8)
-		for (int j = 0; j < 8; ++j) acc[j] += (double)orc_bf16_to_f32(w[i + j]) * (double)x[i + j];
+		for (int j = 0; j < 8; ++j) acc[j] += (double)bf16f(w[i + j]) * (double)x[i + j];
 	double s = 0.0;
 	for (int j = 0; j < 8; ++j) s += acc[j];
-	for (; i < n; ++i) s += (double)orc_bf16_to_f32(w[i]) * (double)x[i];
+	for (; i < n; ++i) s += (double)bf16f(w[i]) * (double)x[i];
 	return s;
 }
 
@@ -347,8 +353,7 @@ struct OrcModel {
 	float*    rope_sin;
 	float*    kcache; /* [slot][layer][pos][kv][hd] */
 	float*    vcache;
-	/* scratch */
-	float *r, *xh, *q, *k, *v, *att, *o, *tmp, *gate, *up, *h, *scores, *logits;
+	float*    logits; /* last token's logits */
 	/* layer-0 stage outputs of the last token, for stage tests */
 	float *dbg_q, *dbg_k, *dbg_v, *dbg_att, *dbg_h, *dbg_r;
 };
@@ -439,19 +444,6 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 	const uint64_t kv_elems = (uint64_t)cfg->n_slots * L * cfg->max_seq * KV * hd;
 	m->kcache = (float*)calloc(kv_elems, sizeof(float));
 	m->vcache = (float*)calloc(kv_elems, sizeof(float));
-	const uint64_t big = (F > d ? F : d);
-	m->r = (float*)calloc(d, 4);
-	m->xh = (float*)calloc(d, 4);
-	m->q = (float*)calloc(H * hd, 4);
-	m->k = (float*)calloc(KV * hd, 4);
-	m->v = (float*)calloc(KV * hd, 4);
-	m->att = (float*)calloc(H * hd, 4);
-	m->o = (float*)calloc(d, 4);
-	m->tmp = (float*)calloc(big, 4);
-	m->gate = (float*)calloc(F, 4);
-	m->up = (float*)calloc(F, 4);
-	m->h = (float*)calloc(F, 4);
-	m->scores = (float*)calloc(H * (uint64_t)cfg->max_seq, 4);
 	m->logits = (float*)calloc(V, 4);
 	m->dbg_q = (float*)calloc(H * hd, 4);
 	m->dbg_k = (float*)calloc(KV * hd, 4);
@@ -459,7 +451,7 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 	m->dbg_att = (float*)calloc(H * hd, 4);
 	m->dbg_h = (float*)calloc(F, 4);
 	m->dbg_r = (float*)calloc(d, 4);
-	if (!m->embed || !m->lm_head || !m->kcache || !m->vcache || !m->scores || !m->logits) {
+	if (!m->embed || !m->lm_head || !m->kcache || !m->vcache || !m->logits) {
 		orc_model_destroy(m);
 		return NULL;
 	}
@@ -484,8 +476,7 @@ void orc_model_destroy(OrcModel* m)
 		free(m->layers);
 	}
 	free(m->rope_cos); free(m->rope_sin); free(m->kcache); free(m->vcache);
-	free(m->r); free(m->xh); free(m->q); free(m->k); free(m->v); free(m->att); free(m->o); free(m->tmp);
-	free(m->gate); free(m->up); free(m->h); free(m->scores); free(m->logits);
+	free(m->logits);
 	free(m->dbg_q); free(m->dbg_k); free(m->dbg_v); free(m->dbg_att); free(m->dbg_h); free(m->dbg_r);
 	free(m);
 }
@@ -510,88 +501,211 @@ static void rope_inplace(float* x, uint32_t n_heads, uint32_t hd, const float* c
 	}
 }
 
-/* one token through the model at position pos (KV for pos written) */
-static void forward_token(OrcModel* m, uint32_t slot, uint32_t id, uint32_t pos, float* logits_out)
+/* Y[t][r] = W[r,:] . X[t,:] for T rows of X: each weight row is read once per block and every
+ * (row, token) dot product is the same computation orc_matvec does, so a block gives the
+ * per-token results bit for bit. */
+/* dot_bf16_d of one weight row with four vectors at once (each sum in the same order as
+ * dot_bf16_d, so the results are identical; the row is converted once for all four) */
+static inline void dot4_bf16_d(const uint16_t* w, const float* x0, const float* x1, const float* x2, const float* x3,
+                               uint64_t n, double out[4])
+{
+	double a0[8] = { 0 }, a1[8] = { 0 }, a2[8] = { 0 }, a3[8] = { 0 };
+	uint64_t i = 0;
+	for (; i + 8 <= n; i += 8)
+		for (int j = 0; j < 8; ++j) {
+			const double wv = (double)bf16f(w[i + j]);
+			a0[j] += wv * (double)x0[i + j];
+			a1[j] += wv * (double)x1[i + j];
+			a2[j] += wv * (double)x2[i + j];
+			a3[j] += wv * (double)x3[i + j];
+		}
+	double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+	for (int j = 0; j < 8; ++j) {
+		s0 += a0[j];
+		s1 += a1[j];
+		s2 += a2[j];
+		s3 += a3[j];
+	}
+	for (; i < n; ++i) {
+		const double wv = (double)bf16f(w[i]);
+		s0 += wv * (double)x0[i];
+		s1 += wv * (double)x1[i];
+		s2 += wv * (double)x2[i];
+		s3 += wv * (double)x3[i];
+	}
+	out[0] = s0;
+	out[1] = s1;
+	out[2] = s2;
+	out[3] = s3;
+}
+
+/* Y[t][r] = W[r,:] . X[t,:] for T rows of X: each weight row is read once per block and every
+ * (row, token) dot product is the same computation orc_matvec does, so a block gives the
+ * per-token results bit for bit. */
+static void matmat(const void* W, int bf16, uint64_t rows, uint64_t cols, const float* X, uint32_t T, float* Y)
+{
+#pragma omp parallel for schedule(static)
+	for (int64_t r = 0; r < (int64_t)rows; ++r) {
+		uint32_t t = 0;
+		if (bf16 && !g_accum_f32)
+			for (; t + 4 <= T; t += 4) {
+				double v[4];
+				const float* x = X + (uint64_t)t * cols;
+				dot4_bf16_d((const uint16_t*)W + (uint64_t)r * cols, x, x + cols, x + 2 * cols, x + 3 * cols, cols, v);
+				for (int u = 0; u < 4; ++u) Y[(uint64_t)(t + u) * rows + r] = (float)v[u];
+			}
+		for (; t < T; ++t) {
+			const float* x = X + (uint64_t)t * cols;
+			const double v = bf16 ? (g_accum_f32 ? dot_bf16_f((const uint16_t*)W + (uint64_t)r * cols, x, cols)
+			                                     : dot_bf16_d((const uint16_t*)W + (uint64_t)r * cols, x, cols))
+			                      : dot_f32_d((const float*)W + (uint64_t)r * cols, x, cols);
+			Y[(uint64_t)t * rows + r] = (float)v;
+		}
+	}
+}
+
+enum { kOrcBlock = 64 }; /* tokens per block of a multi-token forward */
+
+typedef struct OrcBlockBufs {
+	uint32_t cap;
+	float *r, *xh, *q, *k, *v, *att, *o, *gate, *up, *h, *scores;
+	int n_scores;
+} OrcBlockBufs;
+
+static void block_free(OrcBlockBufs* b)
+{
+	free(b->r); free(b->xh); free(b->q); free(b->k); free(b->v); free(b->att); free(b->o);
+	free(b->gate); free(b->up); free(b->h); free(b->scores);
+	memset(b, 0, sizeof *b);
+}
+
+static int block_alloc(const OrcConfig* c, uint32_t T, OrcBlockBufs* b)
+{
+	memset(b, 0, sizeof *b);
+	const uint64_t d = c->dim, Hh = (uint64_t)c->n_heads * c->head_dim, KVh = (uint64_t)c->n_kv_heads * c->head_dim,
+	               F = c->ffn;
+	b->cap = T;
+	b->r = (float*)malloc(4 * T * d);
+	b->xh = (float*)malloc(4 * T * d);
+	b->q = (float*)malloc(4 * T * Hh);
+	b->k = (float*)malloc(4 * T * KVh);
+	b->v = (float*)malloc(4 * T * KVh);
+	b->att = (float*)malloc(4 * T * Hh);
+	b->o = (float*)malloc(4 * T * d);
+	b->gate = (float*)malloc(4 * T * F);
+	b->up = (float*)malloc(4 * T * F);
+	b->h = (float*)malloc(4 * T * F);
+	b->n_scores = omp_get_max_threads();
+	b->scores = (float*)malloc(4 * (uint64_t)b->n_scores * c->max_seq);
+	if (!b->r || !b->xh || !b->q || !b->k || !b->v || !b->att || !b->o || !b->gate || !b->up || !b->h || !b->scores) {
+		block_free(b);
+		return -5;
+	}
+	return 0;
+}
+
+/* Tokens ids[0..T) at positions pos0.. through the model (KV of every position written), one
+ * layer at a time for the whole block; token t attends positions 0..pos0+t.  logits_all
+ * [T][vocab] (may be NULL) receives every token's logits, logits_last (may be NULL) the last
+ * token's.  Per token this is the decode step's arithmetic exactly. */
+static int forward_block(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t T, uint32_t pos0, float* logits_all,
+                         float* logits_last)
 {
 	const OrcConfig* c = &m->cfg;
 	const int bf = (int)c->bf16;
 	const uint32_t d = c->dim, H = c->n_heads, KV = c->n_kv_heads, hd = c->head_dim, F = c->ffn;
 	const uint32_t group = H / KV, half = hd / 2;
 	const float attn_scale = (float)(1.0 / sqrt((double)hd));
-	const float* cs = m->rope_cos + (uint64_t)pos * half;
-	const float* sn = m->rope_sin + (uint64_t)pos * half;
+	OrcBlockBufs B;
+	const int rc = block_alloc(c, T, &B);
+	if (rc) return rc;
 
-	orc_embed_gather(&id, 1, d, m->embed, bf, m->r);
+	orc_embed_gather(ids, T, d, m->embed, bf, B.r);
 	for (uint32_t l = 0; l < c->n_layers; ++l) {
 		const OrcLayer* Ly = &m->layers[l];
-		orc_rmsnorm(m->r, 1, d, Ly->attn_norm, bf, c->eps, m->xh);
-		orc_matvec(Ly->wq, bf, (uint64_t)H * hd, d, m->xh, m->q);
-		orc_matvec(Ly->wk, bf, (uint64_t)KV * hd, d, m->xh, m->k);
-		orc_matvec(Ly->wv, bf, (uint64_t)KV * hd, d, m->xh, m->v);
-		rope_inplace(m->q, H, hd, cs, sn);
-		rope_inplace(m->k, KV, hd, cs, sn);
-		for (uint32_t i = 0; i < H * hd; ++i) m->q[i] = round_store(m->q[i], bf);
-		for (uint32_t i = 0; i < KV * hd; ++i) {
-			m->k[i] = round_store(m->k[i], bf);
-			m->v[i] = round_store(m->v[i], bf);
+		orc_rmsnorm(B.r, T, d, Ly->attn_norm, bf, c->eps, B.xh);
+		matmat(Ly->wq, bf, (uint64_t)H * hd, d, B.xh, T, B.q);
+		matmat(Ly->wk, bf, (uint64_t)KV * hd, d, B.xh, T, B.k);
+		matmat(Ly->wv, bf, (uint64_t)KV * hd, d, B.xh, T, B.v);
+		for (uint32_t t = 0; t < T; ++t) {
+			const uint32_t pos = pos0 + t;
+			const float* cs = m->rope_cos + (uint64_t)pos * half;
+			const float* sn = m->rope_sin + (uint64_t)pos * half;
+			float* q = B.q + (uint64_t)t * H * hd;
+			float* k = B.k + (uint64_t)t * KV * hd;
+			float* v = B.v + (uint64_t)t * KV * hd;
+			rope_inplace(q, H, hd, cs, sn);
+			rope_inplace(k, KV, hd, cs, sn);
+			for (uint32_t i = 0; i < H * hd; ++i) q[i] = round_store(q[i], bf);
+			for (uint32_t i = 0; i < KV * hd; ++i) {
+				k[i] = round_store(k[i], bf);
+				v[i] = round_store(v[i], bf);
+			}
+			memcpy(kv_at(m, m->kcache, slot, l, pos), k, sizeof(float) * KV * hd);
+			memcpy(kv_at(m, m->vcache, slot, l, pos), v, sizeof(float) * KV * hd);
 		}
-		memcpy(kv_at(m, m->kcache, slot, l, pos), m->k, sizeof(float) * KV * hd);
-		memcpy(kv_at(m, m->vcache, slot, l, pos), m->v, sizeof(float) * KV * hd);
-		const uint32_t ctx = pos + 1;
-#pragma omp parallel for schedule(static)
-		for (int32_t h = 0; h < (int32_t)H; ++h) {
-			const uint32_t g = (uint32_t)h / group;
-			const float* qh = m->q + (uint64_t)h * hd;
-			float* sc = m->scores + (uint64_t)h * c->max_seq;
+#pragma omp parallel for schedule(dynamic, 1)
+		for (int64_t th = 0; th < (int64_t)T * H; ++th) {
+			const uint32_t t = (uint32_t)(th / H), h = (uint32_t)(th % H);
+			const uint32_t g = h / group, ctx = pos0 + t + 1;
+			const float* qh = B.q + (uint64_t)t * H * hd + (uint64_t)h * hd;
+			float* sc = B.scores + (uint64_t)omp_get_thread_num() * c->max_seq;
 			double mx = -INFINITY;
-			for (uint32_t t = 0; t < ctx; ++t) {
-				const float* kt = kv_at(m, m->kcache, slot, l, t) + (uint64_t)g * hd;
+			for (uint32_t p = 0; p < ctx; ++p) {
+				const float* kt = kv_at(m, m->kcache, slot, l, p) + (uint64_t)g * hd;
 				const float s = (float)dot_f32_d(kt, qh, hd) * attn_scale;
-				sc[t] = s;
+				sc[p] = s;
 				if (s > mx) mx = s;
 			}
 			double den = 0.0;
-			for (uint32_t t = 0; t < ctx; ++t) {
-				sc[t] = (float)exp((double)sc[t] - mx);
-				den += sc[t];
+			for (uint32_t p = 0; p < ctx; ++p) {
+				sc[p] = (float)exp((double)sc[p] - mx);
+				den += sc[p];
 			}
 			double acc[512];
 			for (uint32_t i = 0; i < hd; ++i) acc[i] = 0.0;
-			for (uint32_t t = 0; t < ctx; ++t) {
-				const float* vt = kv_at(m, m->vcache, slot, l, t) + (uint64_t)g * hd;
-				for (uint32_t i = 0; i < hd; ++i) acc[i] += (double)sc[t] * (double)vt[i];
+			for (uint32_t p = 0; p < ctx; ++p) {
+				const float* vt = kv_at(m, m->vcache, slot, l, p) + (uint64_t)g * hd;
+				for (uint32_t i = 0; i < hd; ++i) acc[i] += (double)sc[p] * (double)vt[i];
 			}
-			float* oh = m->att + (uint64_t)h * hd;
+			float* oh = B.att + (uint64_t)t * H * hd + (uint64_t)h * hd;
 			for (uint32_t i = 0; i < hd; ++i) oh[i] = round_store((float)(acc[i] / den), bf);
 		}
 		if (l == 0) {
-			memcpy(m->dbg_q, m->q, sizeof(float) * H * hd);
-			memcpy(m->dbg_k, m->k, sizeof(float) * KV * hd);
-			memcpy(m->dbg_v, m->v, sizeof(float) * KV * hd);
-			memcpy(m->dbg_att, m->att, sizeof(float) * H * hd);
+			const uint32_t t = T - 1;
+			memcpy(m->dbg_q, B.q + (uint64_t)t * H * hd, sizeof(float) * H * hd);
+			memcpy(m->dbg_k, B.k + (uint64_t)t * KV * hd, sizeof(float) * KV * hd);
+			memcpy(m->dbg_v, B.v + (uint64_t)t * KV * hd, sizeof(float) * KV * hd);
+			memcpy(m->dbg_att, B.att + (uint64_t)t * H * hd, sizeof(float) * H * hd);
 		}
-		orc_matvec(Ly->wo, bf, d, (uint64_t)H * hd, m->att, m->o);
-		for (uint32_t i = 0; i < d; ++i) m->r[i] += m->o[i];
+		matmat(Ly->wo, bf, d, (uint64_t)H * hd, B.att, T, B.o);
+		for (uint64_t i = 0; i < (uint64_t)T * d; ++i) B.r[i] += B.o[i];
 
-		orc_rmsnorm(m->r, 1, d, Ly->ffn_norm, bf, c->eps, m->xh);
-		orc_matvec(Ly->wg, bf, F, d, m->xh, m->gate);
-		orc_matvec(Ly->wu, bf, F, d, m->xh, m->up);
-		for (uint32_t j = 0; j < F; ++j) {
-			const double gt = m->gate[j];
+		orc_rmsnorm(B.r, T, d, Ly->ffn_norm, bf, c->eps, B.xh);
+		matmat(Ly->wg, bf, F, d, B.xh, T, B.gate);
+		matmat(Ly->wu, bf, F, d, B.xh, T, B.up);
+		for (uint64_t j = 0; j < (uint64_t)T * F; ++j) {
+			const double gt = B.gate[j];
 			const double s = gt / (1.0 + exp(-gt));
-			m->h[j] = round_store((float)(s * (double)m->up[j]), bf);
+			B.h[j] = round_store((float)(s * (double)B.up[j]), bf);
 		}
-		orc_matvec(Ly->wd, bf, d, F, m->h, m->o);
-		for (uint32_t i = 0; i < d; ++i) m->r[i] += m->o[i];
+		matmat(Ly->wd, bf, d, F, B.h, T, B.o);
+		for (uint64_t i = 0; i < (uint64_t)T * d; ++i) B.r[i] += B.o[i];
 		if (l == 0) {
-			memcpy(m->dbg_h, m->h, sizeof(float) * F);
-			memcpy(m->dbg_r, m->r, sizeof(float) * d);
+			memcpy(m->dbg_h, B.h + (uint64_t)(T - 1) * F, sizeof(float) * F);
+			memcpy(m->dbg_r, B.r + (uint64_t)(T - 1) * d, sizeof(float) * d);
 		}
 	}
-	if (logits_out) {
-		orc_rmsnorm(m->r, 1, d, m->final_norm, bf, c->eps, m->xh);
-		orc_matvec(m->lm_head, bf, c->vocab, d, m->xh, logits_out);
+	if (logits_all) {
+		orc_rmsnorm(B.r, T, d, m->final_norm, bf, c->eps, B.xh);
+		matmat(m->lm_head, bf, c->vocab, d, B.xh, T, logits_all);
+		if (logits_last) memcpy(logits_last, logits_all + (uint64_t)(T - 1) * c->vocab, sizeof(float) * c->vocab);
+	} else if (logits_last) {
+		orc_rmsnorm(B.r + (uint64_t)(T - 1) * d, 1, d, m->final_norm, bf, c->eps, B.xh);
+		orc_matvec(m->lm_head, bf, c->vocab, d, B.xh, logits_last);
 	}
+	block_free(&B);
+	return 0;
 }
 
 int orc_forward(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t n, uint32_t start_pos,
@@ -602,14 +716,16 @@ int orc_forward(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t n, uin
 	if ((uint64_t)start_pos + n > c->max_seq) return -2;
 	for (uint32_t t = 0; t < n; ++t)
 		if (ids[t] >= c->vocab) return -3;
-	for (uint32_t t = 0; t < n; ++t) {
-		const int last = (t + 1 == n);
-		float* lo = logits_all ? logits_all + (uint64_t)t * c->vocab : (last ? m->logits : NULL);
-		forward_token(m, slot, ids[t], start_pos + t, lo);
-		if (last && lo) {
-			if (logits_last && logits_last != lo) memcpy(logits_last, lo, sizeof(float) * c->vocab);
-			if (argmax_last) *argmax_last = orc_argmax(lo, c->vocab);
-		}
+	for (uint32_t t0 = 0; t0 < n; t0 += kOrcBlock) {
+		const uint32_t T = (n - t0 < (uint32_t)kOrcBlock) ? n - t0 : (uint32_t)kOrcBlock;
+		const int last = (t0 + T == n);
+		float* la = logits_all ? logits_all + (uint64_t)t0 * c->vocab : NULL;
+		const int rc = forward_block(m, slot, ids + t0, T, start_pos + t0, la, last ? m->logits : NULL);
+		if (rc) return rc;
+	}
+	if (n > 0) {
+		if (logits_last) memcpy(logits_last, m->logits, sizeof(float) * c->vocab);
+		if (argmax_last) *argmax_last = orc_argmax(m->logits, c->vocab);
 	}
 	return 0;
 }

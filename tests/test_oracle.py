@@ -119,11 +119,19 @@ def test_oracle_rejects_bad_inputs():
         m.forward([1, 2], 63)         # beyond max_seq
 
 
-def test_prefill_equals_tokenwise():
-    m = O.OracleModel(dict(TINY, dtype="bf16"), seed=0)
-    ids = O.gen_ids(5, 10, 512)
+@pytest.mark.parametrize("dtype,n", [("bf16", 10), ("bf16", 150), ("fp32", 70)])
+def test_prefill_equals_tokenwise(dtype, n):
+    """A multi-token forward runs the prompt in blocks of 64 tokens, one layer at a time for the
+    block; every logit and every K/V entry equals feeding the tokens one at a time."""
+    cfg = dict(TINY, dtype=dtype, max_seq=160)
+    m = O.OracleModel(cfg, seed=0)
+    ids = O.gen_ids(5, n, 512)
     la, _ = m.forward(ids, 0, all_logits=True)
-    m2 = O.OracleModel(dict(TINY, dtype="bf16"), seed=0)
-    for t in range(10):
+    m2 = O.OracleModel(cfg, seed=0)
+    for t in range(n):
         lt, _ = m2.forward(ids[t:t + 1], t)
         np.testing.assert_array_equal(lt, la[t])
+    for layer in range(cfg["n_layers"]):
+        for t in range(0, n, 7):
+            for a, b in zip(m.kv(layer, t), m2.kv(layer, t)):
+                np.testing.assert_array_equal(a, b)
