@@ -148,11 +148,28 @@ void    arena_dev_pop(DevArena* const arena, u64 bsize);
 void    arena_dev_pop_at(DevArena* const arena, u64 pos);
 u64     arena_dev_pos_get(const DevArena* const arena);
 
-/* ---- checked copies: src/cuda/api/cuda_mem_wrapper.cuh:12-16 ------------------------ */
+/* ---- CUDA memory wrappers: src/cuda/api/cuda_mem_wrapper.cuh:10-16 -------------------
+ * Same names and return types as the reference: the b32 functions return 1 on success and 0
+ * on failure, the Error_t ones Success or a code; none aborts (the reference's CHECK_CUDA does),
+ * and inf_last_error_detail() describes every failure.  `stream` is a cudaStream_t passed as
+ * void* (the same pointer at the C ABI). */
+/* cuda_mem_wrapper.cuh:10.  Takes the address of the caller's pointer, which receives the
+ * allocation (the reference takes the pointer by value, so its allocation is lost: defect D10;
+ * a reference caller passing &ptr gets the fixed behaviour). */
+b32     cu_malloc(void** dev_ptr, const u64 bsize);
+/* cuda_mem_wrapper.cuh:11.  0 if dev_ptr is not device memory. */
+b32     cu_free(void* dev_ptr);
+/* cuda_mem_wrapper.cuh:12.  ErrorInvalidDevPtr if dst is not device memory. */
 Error_t cu_memcpy_htd(void* dst, const void* src, const u64 bsize);
-Error_t cu_memcpy_htd_async(void* dst, const void* src, const u64 bsize, void* stream);
+/* cuda_mem_wrapper.cuh:13.  0 if dst is not device memory. */
+b32     cu_memcpy_htd_async(void* dst, const void* src, const u64 bsize, void* stream);
+/* cuda_mem_wrapper.cuh:14.  ErrorInvalidHostPtr if src is not device memory (the reference's code). */
 Error_t cu_memcpy_dth(void* dst, const void* src, const u64 bsize);
-Error_t cu_memset(void* s, i32 c, u64 n);
+/* cuda_mem_wrapper.cuh:15.  Page-locks host memory for reading by the device (cudaHostRegister
+ * with cudaHostRegisterReadOnly); 0 for a device pointer. */
+b32     cu_host_register_read_only(void* ptr, const u64 bsize);
+/* cuda_mem_wrapper.cuh:16.  0 if s is not device memory. */
+b32     cu_memset(void* s, i32 c, u64 n);
 
 /* ---- stand-alone kernels ----------------------------------------------------------- */
 /* Replaces k_fetch_input_embeddings (src/cuda/kernels/input_embeddings.cuh:20-24) and its
@@ -173,29 +190,63 @@ Error_t inf_rmsnorm(const void* d_x, void* d_y, u32 rows, u32 dim, const void* d
  * (src/model.cuh:44-50 declares wq/wk/wv/wo only). */
 Error_t inf_gemm_bf16(const void* d_x, const void* d_w, void* d_y, u32 T, u32 N, u32 K, u32 out_f32, void* stream);
 
-/* Decode attention over a paged KV cache for n_tokens query tokens (one per sequence), the
- * kernel the decode step runs (no reference counterpart: src/model.cuh:44-50 stops at the
- * projection weights).  q, out: [n_tokens][n_heads*head_dim]; kpool, vpool:
- * [n_pages][n_kv_heads][kv_block][head_dim]; block_table: [slots][pages_per_seq] i32;
- * tok_slot, tok_pos: [n_tokens] i32 -- token i attends positions 0..tok_pos[i] of its slot.
- * dtype: InfDtype of q, K/V and out.  d_scratch: device memory of at least
- * inf_attn_decode_scratch_bytes(...) bytes (split partials, tickets, error word), 16-byte
- * aligned; its contents on entry do not matter.  Synchronous. */
+/* Decode attention over a paged KV cache for n_tokens query tokens (one per sequence), with
+ * the kernel the model's decode step runs for that shape (no reference counterpart:
+ * src/model.cuh:44-50 stops at the projection weights).  q, out: [n_tokens][n_heads*head_dim];
+ * kpool, vpool: [n_pages][n_kv_heads][kv_block][head_dim]; block_table: [slots][pages_per_seq]
+ * i32; tok_slot, tok_pos: [n_tokens] i32 -- token i attends positions 0..tok_pos[i] of its
+ * slot.  dtype: InfDtype of q, K/V and out.  d_scratch: device memory of at least
+ * inf_attn_decode_scratch_bytes(...) bytes (split partials, tickets, error word; enough for
+ * every kernel of InfAttnKernel), 16-byte aligned; its contents on entry do not matter.
+ * Synchronous. */
 u64     inf_attn_decode_scratch_bytes(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
                                       u32 pages_per_seq, u32 dtype);
 Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
                         u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos, u32 n_tokens,
                         u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype, void* d_out,
                         void* d_scratch, u64 scratch_bytes, void* stream);
+
+/* The decode attention kernels.  A kernel's split plan depends on pages_per_seq (the longest
+ * context a sequence may reach) exactly as in the model, whose pages_per_seq is
+ * ceil(max_seq / kv_block). */
+typedef enum InfAttnKernel {
+	InfAttnAuto    = 0, /* what the decode step picks: InfAttnCluster for one token when it fits, else
+	                       InfAttnMma for several tokens where it applies, else InfAttnSplitK */
+	InfAttnSplitK  = 1, /* CTAs per (token, KV head, split), partials combined through the scratch by
+	                       the last CTA of each (token, KV head) */
+	InfAttnCluster = 2, /* one thread-block cluster of 8 or 16 CTAs per (token, KV head), the split
+	                       combine in distributed shared memory; pages_per_seq up to 16 per CTA */
+	InfAttnMma     = 3, /* the batched step's tensor-core kernel (mma.m16n8k16, TMA page loads): bf16,
+	                       kv_block 16, head_dim 64 or 128 */
+} InfAttnKernel;
+/* inf_attn_decode with the kernel chosen by the caller (InfAttnKernel); ErrorUnsupported when
+ * that kernel cannot serve the shape.  For tests and measurements of one kernel. */
+Error_t inf_attn_decode_with(u32 kernel, const void* d_q, const void* d_kpool, const void* d_vpool,
+                             const i32* d_block_table, u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot,
+                             const i32* d_tok_pos, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
+                             u32 dtype, void* d_out, void* d_scratch, u64 scratch_bytes, void* stream);
+/* Causal attention of one prefill pass, the kernel the model's prefill runs (no reference
+ * counterpart): n_tokens consecutive tokens of one sequence, token t at position tok_pos[t]
+ * attending positions 0..tok_pos[t] of slot tok_slot[t], whose K/V (this pass's tokens
+ * included) are already in the cache.  bf16 only; q, out: [n_tokens][n_heads*head_dim], the
+ * other arguments as for inf_attn_decode.  kernel: InfPrefillAttention (Auto: the tcgen05/TMEM
+ * kernel for head_dim 64 or 128, GQA groups dividing 128 and kv_block a multiple of 8 dividing
+ * 128; else the SIMT kernel).  Synchronous. */
+Error_t inf_attn_prefill(u32 kernel, const void* d_q, const void* d_kpool, const void* d_vpool,
+                         const i32* d_block_table, u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot,
+                         const i32* d_tok_pos, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
+                         void* d_out, void* stream);
 /* inf_attn_decode for callers that cannot allocate device memory -- a serving loop that must
- * not call cudaMalloc/cudaFree mid-step (they synchronize the device), or a runtime whose
- * device memory is all committed to a pre-sized arena.  No counterpart in the reference.
- * The scratch is a 4 MiB array built into the library (held on every GPU that loads it
- * until the process exits); shapes needing more return ErrorInvalidValue.  The first call
- * on each device looks up the array's device address (cudaGetSymbolAddress); make that
- * first call before any stream capture.  All calls share the array: calls whose work
- * overlaps on the GPU race and must be ordered by the caller (same stream, or events).
- * Allocates nothing.  Synchronous. */
+ * not call cudaMalloc/cudaFree mid-step (they synchronize the device), or a runtime whose device
+ * memory is all committed to a pre-sized arena.  No counterpart in the reference.  The scratch is
+ * a 4 MiB array built into the library (held on every GPU that loads it until the process
+ * exits); shapes needing more return ErrorInvalidValue, shapes the attention cannot serve the
+ * error inf_attn_decode gives for them.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress) and keeps it; make that first call before any stream
+ * capture, and do not use the library on a device after cudaDeviceReset.  The call waits for its
+ * stream before returning (it reads the kernel's error word).  All calls share the array, so calls
+ * issued from other host threads, or on other streams, must not run at the same time as this
+ * one: the caller orders them.  Allocates nothing. */
 Error_t inf_attn_decode_noalloc(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
                                 u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos,
                                 u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype,
@@ -272,16 +323,24 @@ typedef struct InfServer InfServer;
  * first output), advances every sequence admitted in an earlier step by one token with one
  * batched decode step (the tensor-core batch path even for a lone sequence, so a request's ids
  * do not depend on the load), and retires sequences that produced eos_id, reached max_new tokens or
- * ran out of positions, releasing their pages.  Greedy only (ErrorUnsupported at admission
- * while sampling is on).  A request whose prefill fails is retired with that error and the
- * others go on; a failing batched step returns its error.  Not thread-safe. */
+ * ran out of positions, releasing their pages.  A request is admitted only when the KV pool can
+ * hold every position it may write (prompt + max_new - 1, at most max_seq) on top of what the
+ * running requests reserved; until then it waits at the head of the queue.  Greedy only
+ * (ErrorUnsupported at admission while sampling is on).  A request whose prefill fails is retired
+ * with that error and the others go on; a failing batched step retires the requests of its batch
+ * with its error and returns it.  Not thread-safe. */
 Error_t inf_server_create(Model* model, u32 max_active, InfServer** out);
 /* The same scheduler over a host-only stand-in model (next id = a hash of the sequence's
- * previous id and position) that checks every sequence is fed its own positions in order: for
- * testing the scheduling without a GPU. */
-Error_t inf_server_create_synthetic(u32 n_slots, u32 max_seq, u32 vocab, u32 max_active, InfServer** out);
+ * previous id and position) that checks every sequence is fed its own positions in order and
+ * holds kv_pages pages of 16 positions (0: enough for every slot's max_seq), failing with
+ * ErrorArenaOutOfMemory like the device cache when they run out: for testing the scheduling
+ * without a GPU.  A prompt that starts with id vocab - 1 makes the first batched step its
+ * sequence joins fail with ErrorGeneric. */
+Error_t inf_server_create_synthetic(u32 n_slots, u32 max_seq, u32 vocab, u32 kv_pages, u32 max_active,
+                                    InfServer** out);
 Error_t inf_server_destroy(InfServer** server);
-/* Queue a request; n_prompt < max_seq.  eos_id 0xFFFFFFFF: none. */
+/* Queue a request; n_prompt < max_seq.  eos_id 0xFFFFFFFF: none.  ErrorArenaOutOfMemory if its
+ * positions need more KV pages than the whole pool holds. */
 Error_t inf_server_submit(InfServer* server, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id,
                           u64* request_id);
 /* One scheduling step; *n_finished (may be NULL) = requests retired in it. */

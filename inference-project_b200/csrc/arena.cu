@@ -227,7 +227,46 @@ void arena_dev_pop_at(DevArena* const arena, u64 pos)
 
 u64 arena_dev_pos_get(const DevArena* const arena) { return arena ? arena->pos : 0; }
 
-/* ---- checked copies ------------------------------------------------------------------ */
+/* ---- CUDA memory wrappers (src/cuda/api/cuda_mem_wrapper.cu:10-87) --------------------
+ * Same names and return conventions as the reference: the b32 wrappers return 1 on success
+ * and 0 on failure, the Error_t ones Success or a code.  Unlike the reference nothing aborts: a
+ * failing CUDA call returns 0 (or ErrorCuda) and inf_last_error_detail() says which call and
+ * why, as does a rejected pointer. */
+
+b32 cu_malloc(void** dev_ptr, const u64 bsize)
+{
+	// The reference takes the pointer by value and checks that it is already device memory
+	// before allocating, so the allocation never reaches its caller (defect D10).  Here the
+	// caller's pointer receives the allocation.
+	if (!dev_ptr) {
+		(void)fail(ErrorInvalidValue, "cu_malloc: NULL out pointer");
+		return 0;
+	}
+	*dev_ptr = nullptr;
+	const cudaError_t e = cudaMalloc(dev_ptr, bsize);
+	if (e != cudaSuccess) {
+		(void)cudaGetLastError();
+		*dev_ptr = nullptr;
+		(void)fail(ErrorMemoryAllocation, "cu_malloc: cudaMalloc(%llu): %s", (unsigned long long)bsize,
+		           cudaGetErrorString(e));
+		return 0;
+	}
+	return 1;
+}
+
+b32 cu_free(void* dev_ptr)
+{
+	if (!inf::is_device_ptr(dev_ptr)) {
+		(void)fail(ErrorInvalidDevPtr, "cu_free: not device memory");
+		return 0;
+	}
+	const cudaError_t e = cudaFree(dev_ptr);
+	if (e != cudaSuccess) {
+		(void)fail(ErrorCuda, "cu_free: %s", cudaGetErrorString(e));
+		return 0;
+	}
+	return 1;
+}
 
 Error_t cu_memcpy_htd(void* dst, const void* src, const u64 bsize)
 {
@@ -236,25 +275,56 @@ Error_t cu_memcpy_htd(void* dst, const void* src, const u64 bsize)
 	return Success;
 }
 
-Error_t cu_memcpy_htd_async(void* dst, const void* src, const u64 bsize, void* stream)
+b32 cu_memcpy_htd_async(void* dst, const void* src, const u64 bsize, void* stream)
 {
-	if (!inf::is_device_ptr(dst)) return fail(ErrorInvalidDevPtr, "cu_memcpy_htd_async: dst is not device memory");
-	INF_CUDA_TRY(cudaMemcpyAsync(dst, src, bsize, cudaMemcpyHostToDevice, (cudaStream_t)stream));
-	return Success;
+	if (!inf::is_device_ptr(dst)) {
+		(void)fail(ErrorInvalidDevPtr, "cu_memcpy_htd_async: dst is not device memory");
+		return 0;
+	}
+	const cudaError_t e = cudaMemcpyAsync(dst, src, bsize, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+	if (e != cudaSuccess) {
+		(void)fail(ErrorCuda, "cu_memcpy_htd_async: %s", cudaGetErrorString(e));
+		return 0;
+	}
+	return 1;
 }
 
 Error_t cu_memcpy_dth(void* dst, const void* src, const u64 bsize)
 {
-	if (!inf::is_device_ptr(src)) return fail(ErrorInvalidDevPtr, "cu_memcpy_dth: src is not device memory");
+	// the reference answers a source that is not device memory with ErrorInvalidHostPtr
+	// (src/cuda/api/cuda_mem_wrapper.cu:65-67); kept, so its callers' checks still match
+	if (!inf::is_device_ptr(src)) return fail(ErrorInvalidHostPtr, "cu_memcpy_dth: src is not device memory");
 	INF_CUDA_TRY(cudaMemcpy(dst, src, bsize, cudaMemcpyDeviceToHost));
 	return Success;
 }
 
-Error_t cu_memset(void* s, i32 c, u64 n)
+b32 cu_host_register_read_only(void* ptr, const u64 bsize)
 {
-	if (!inf::is_device_ptr(s)) return fail(ErrorInvalidDevPtr, "cu_memset: not device memory");
-	INF_CUDA_TRY(cudaMemset(s, c, n));
-	return Success;
+	if (!ptr || inf::is_device_ptr(ptr)) {
+		(void)fail(ErrorInvalidHostPtr, "cu_host_register_read_only: not host memory");
+		return 0;
+	}
+	const cudaError_t e = cudaHostRegister(ptr, bsize, cudaHostRegisterReadOnly);
+	if (e != cudaSuccess) {
+		(void)cudaGetLastError();
+		(void)fail(ErrorCuda, "cu_host_register_read_only: %s", cudaGetErrorString(e));
+		return 0;
+	}
+	return 1;
+}
+
+b32 cu_memset(void* s, i32 c, u64 n)
+{
+	if (!inf::is_device_ptr(s)) {
+		(void)fail(ErrorInvalidDevPtr, "cu_memset: not device memory");
+		return 0;
+	}
+	const cudaError_t e = cudaMemset(s, c, n);
+	if (e != cudaSuccess) {
+		(void)fail(ErrorCuda, "cu_memset: %s", cudaGetErrorString(e));
+		return 0;
+	}
+	return 1;
 }
 
 } // extern "C"

@@ -28,7 +28,9 @@ void* g_scratch_addr[kNoAllocMaxDevices] = {};
 
 // Device address of g_attn_scratch on the current device.  In host code the array's name
 // is only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per
-// device, with that device current.
+// device, with that device current.  The address is kept for the life of the process: a
+// cudaDeviceReset (which unloads this module from the device) invalidates it, so the library
+// must not be used on a device after that device was reset.
 Error_t scratch_address(void** out)
 {
 	int dev = 0;
@@ -55,7 +57,6 @@ extern "C" Error_t inf_attn_decode_noalloc(const void* d_q, const void* d_kpool,
                                            void* stream)
 {
 	const u64 need = inf_attn_decode_scratch_bytes(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype);
-	if (need == 0) return inf::fail(ErrorInvalidValue, "inf_attn_decode_noalloc: unsupported shape");
 	if (need > kNoAllocScratchBytes)
 		return inf::fail(ErrorInvalidValue,
 		                 "inf_attn_decode_noalloc: this shape needs %llu bytes of scratch, above the built-in %llu; "
@@ -63,6 +64,8 @@ extern "C" Error_t inf_attn_decode_noalloc(const void* d_q, const void* d_kpool,
 		                 (unsigned long long)need, (unsigned long long)kNoAllocScratchBytes);
 	void* scratch = nullptr;
 	INF_TRY(scratch_address(&scratch));
+	// need == 0: a shape the attention cannot serve; inf_attn_decode's own checks report why
+	// (the same error the scratch-taking entry point gives), before anything is launched
 	// inf_attn_decode clears the tickets and the error word on the stream before the kernel,
 	// so what a previous call left in the array does not matter
 	return inf_attn_decode(d_q, d_kpool, d_vpool, d_block_table, pages_per_seq, n_pages, d_tok_slot, d_tok_pos, n_tokens,

@@ -247,17 +247,18 @@ GemvArgs gemv_base(InfEngine* e, const void* W, int N, int K)
 }
 
 // --------------------------------------------------------------------------- cluster attention
+// Whether a cluster of cs CTAs (mp pages each) of the batch-1 attention kernel fits one GPU.
 template <typename T>
-Error_t attn_cl_fit(InfEngine* e, int G, int hd, int cs, int mp, bool* ok)
+Error_t attn_cl_fit(int G, int hd, int blk, int kv_heads, int cs, int mp, bool* ok)
 {
 	*ok = false;
 	const AttnKernel<T> k = attn_decode_cl_kernel<T>(G, hd);
 	if (!k) return Success;
-	const size_t smem = attn_cl_layout(G, hd, (int)e->cfg.kv_block, sizeof(T), mp, cs).total;
+	const size_t smem = attn_cl_layout(G, hd, blk, sizeof(T), mp, cs).total;
 	INF_CUDA_TRY(set_smem(k, smem));
 	if (cs > 8) INF_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
 	cudaLaunchConfig_t lc = {};
-	lc.gridDim = dim3(cs, e->KVl, 1);
+	lc.gridDim = dim3(cs, kv_heads, 1);
 	lc.blockDim = dim3(kAttnThreads);
 	lc.dynamicSmemBytes = smem;
 	cudaLaunchAttribute attr[1];
@@ -276,22 +277,31 @@ Error_t attn_cl_fit(InfEngine* e, int G, int hd, int cs, int mp, bool* ok)
 	return Success;
 }
 
-Error_t attn_cl_choose(InfEngine* e, int G, int hd)
+// The batch-1 decode attention plan: one cluster per KV head, the largest cluster (16, then 8
+// CTAs) whose split of a pages_per_seq-page context fits the shared-memory budget and that the
+// GPU can place.  *splits = 0 when none does (the split-K kernel serves the shape).
+Error_t attn_cl_plan(int G, int hd, int blk, size_t esz, int pages_per_seq, int kv_heads, int* splits, int* pages)
 {
-	e->attn_cl_splits = 0;
-	e->attn_cl_pages = 0;
+	*splits = 0;
+	*pages = 0;
 	for (int cs = kAttnClMaxSplits; cs >= 8; cs >>= 1) {
-		const int mp = attn_cl_pages_per_split(cs, e->pages_per_seq, (int)e->cfg.kv_block, hd, e->esz, G);
+		const int mp = attn_cl_pages_per_split(cs, pages_per_seq, blk, hd, esz, G);
 		if (mp == 0) continue;
 		bool ok = false;
-		if (e->cfg.dtype == InfBF16) INF_TRY(attn_cl_fit<bf16>(e, G, hd, cs, mp, &ok));
-		else INF_TRY(attn_cl_fit<float>(e, G, hd, cs, mp, &ok));
+		if (esz == 2) INF_TRY(attn_cl_fit<bf16>(G, hd, blk, kv_heads, cs, mp, &ok));
+		else INF_TRY(attn_cl_fit<float>(G, hd, blk, kv_heads, cs, mp, &ok));
 		if (!ok) continue;
-		e->attn_cl_splits = cs;
-		e->attn_cl_pages = mp;
+		*splits = cs;
+		*pages = mp;
 		return Success;
 	}
 	return Success;
+}
+
+Error_t attn_cl_choose(InfEngine* e, int G, int hd)
+{
+	return attn_cl_plan(G, hd, (int)e->cfg.kv_block, e->esz, e->pages_per_seq, e->KVl, &e->attn_cl_splits,
+	                    &e->attn_cl_pages);
 }
 
 // launch with a cluster of cluster_x CTAs along x and the programmatic-dependency edge
@@ -1869,19 +1879,26 @@ Error_t inf_gemm_bf16(const void* d_x, const void* d_w, void* d_y, u32 T, u32 N,
 }
 
 // ---- stand-alone decode attention -------------------------------------------------------
+} // extern "C"
 
 namespace {
 struct AttnPlan {
-	int splits, max_pages_split;
+	int kernel;                   // InfAttnKernel that runs (never InfAttnAuto)
+	int splits, max_pages_split;  // of that kernel
 	size_t part_bytes, counter_bytes, smem;
 };
 
-Error_t attn_plan(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 pages_per_seq, u32 dtype,
-                  AttnPlan* p)
+// Every kernel's plan for the shape; scratch is sized for the largest, so any kernel can run in
+// a buffer of inf_attn_decode_scratch_bytes.  `kernel` resolves InfAttnAuto the way the model's
+// decode step does: the cluster kernel for single tokens when it fits, the tensor-core streaming
+// kernel for batches (bf16, 16-token pages, head_dim 64 or 128), else the split-K kernel.
+Error_t attn_plan(u32 kernel, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 pages_per_seq,
+                  u32 dtype, AttnPlan* p)
 {
 	if (n_tokens == 0 || n_heads == 0 || n_kv_heads == 0 || head_dim == 0 || head_dim % 2 || kv_block == 0 ||
 	    pages_per_seq == 0 || n_heads % n_kv_heads || (dtype != InfBF16 && dtype != InfF32) || n_tokens > 65535)
 		return fail(ErrorInvalidValue, "attention: bad shape");
+	if (kernel > InfAttnMma) return fail(ErrorInvalidValue, "attention: kernel %u", kernel);
 	const u32 G = n_heads / n_kv_heads;
 	if ((G != 1 && G != 2 && G != 4 && G != 8) || head_dim > 256 || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "attention: GQA group %u x head_dim %u", G, head_dim);
@@ -1889,57 +1906,116 @@ Error_t attn_plan(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 k
 	if ((kv_block * head_dim * esz) % 16) return fail(ErrorUnsupported, "attention: page block not a multiple of 16 bytes");
 	int sms = 148, dev = 0;
 	if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+	// split-K
+	int sk_splits = 1, sk_pages = 1;
 	attn_decode_plan(sms, (int)n_kv_heads, (int)n_tokens, (int)pages_per_seq, (int)kv_block, (int)head_dim, esz,
-	                 &p->splits, &p->max_pages_split);
-	p->part_bytes = (size_t)n_tokens * n_heads * p->splits * (head_dim + 2) * sizeof(float);
+	                 &sk_splits, &sk_pages);
+	// tensor-core streaming (the batched decode step's kernel)
+	const bool mma_ok = dtype == InfBF16 && kv_block == 16 && attn_decode_mma_kernel((int)G, (int)head_dim) != nullptr;
+	const int mma_splits = attn_stream_splits(sms, (int)n_kv_heads, (int)n_tokens, (int)pages_per_seq);
+	const size_t hd2 = head_dim + 2;
+	p->part_bytes = (size_t)n_tokens * n_heads * (size_t)std::max(sk_splits, mma_ok ? mma_splits : 1) * hd2 * sizeof(float);
 	p->counter_bytes = (size_t)n_tokens * n_kv_heads * sizeof(unsigned) + 16; // + error word
-	p->smem = attn_decode_smem_bytes((int)G, (int)head_dim, (int)kv_block, esz, p->max_pages_split, p->splits);
+	int k = (int)kernel;
+	int cl_splits = 0, cl_pages = 0;
+	if (k == InfAttnAuto || k == InfAttnCluster) {
+		if (n_tokens == 1 || k == InfAttnCluster)
+			INF_TRY(attn_cl_plan((int)G, (int)head_dim, (int)kv_block, esz, (int)pages_per_seq, (int)n_kv_heads, &cl_splits,
+			                     &cl_pages));
+		if (k == InfAttnCluster && cl_splits == 0)
+			return fail(ErrorUnsupported, "attention: %u pages per sequence do not fit one cluster", pages_per_seq);
+	}
+	if (k == InfAttnMma && !mma_ok)
+		return fail(ErrorUnsupported, "attention: the tensor-core kernel needs bf16, 16-token pages and head_dim 64 or 128");
+	if (k == InfAttnAuto) k = cl_splits > 0 ? InfAttnCluster : (n_tokens > 1 && mma_ok) ? InfAttnMma : InfAttnSplitK;
+	p->kernel = k;
+	if (k == InfAttnCluster) {
+		p->splits = cl_splits;
+		p->max_pages_split = cl_pages;
+		p->smem = attn_cl_layout((int)G, (int)head_dim, (int)kv_block, esz, cl_pages, cl_splits).total;
+	} else if (k == InfAttnMma) {
+		p->splits = mma_splits;
+		p->max_pages_split = 0;
+		p->smem = attn_mma_smem_bytes((int)head_dim, (int)kv_block, (int)pages_per_seq);
+	} else {
+		p->splits = sk_splits;
+		p->max_pages_split = sk_pages;
+		p->smem = attn_decode_smem_bytes((int)G, (int)head_dim, (int)kv_block, esz, sk_pages, sk_splits);
+	}
 	return Success;
 }
 
-Error_t attn_launch(const AttnPlan& P, AttnDecodeArgs a, u32 n_tokens, u32 dtype, cudaStream_t st)
+template <typename T>
+Error_t attn_launch_t(const AttnPlan& P, const AttnDecodeArgs& a, u32 n_tokens, u32 n_pages, cudaStream_t st)
 {
-	a.n_splits = P.splits;
-	a.max_pages_split = P.max_pages_split;
-	const dim3 g((unsigned)a.KV, (unsigned)P.splits, n_tokens);
 	const int G = a.H / a.KV;
-	if (dtype == InfBF16) {
-		const AttnKernel<bf16> k = attn_decode_kernel<bf16>(G, a.hd);
+	if (P.kernel == InfAttnCluster) {
+		const AttnKernel<T> k = attn_decode_cl_kernel<T>(G, a.hd);
 		if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
 		INF_CUDA_TRY(set_smem(k, P.smem));
-		k<<<g, kAttnThreads, P.smem, st>>>(a);
-	} else {
-		const AttnKernel<float> k = attn_decode_kernel<float>(G, a.hd);
-		if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
-		INF_CUDA_TRY(set_smem(k, P.smem));
-		k<<<g, kAttnThreads, P.smem, st>>>(a);
+		if (P.splits > 8) INF_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+		cudaLaunchConfig_t lc = {};
+		lc.gridDim = dim3((unsigned)P.splits, (unsigned)a.KV, n_tokens);
+		lc.blockDim = dim3(kAttnThreads);
+		lc.dynamicSmemBytes = P.smem;
+		lc.stream = st;
+		cudaLaunchAttribute attr[1];
+		attr[0].id = cudaLaunchAttributeClusterDimension;
+		attr[0].val.clusterDim.x = (unsigned)P.splits;
+		attr[0].val.clusterDim.y = 1;
+		attr[0].val.clusterDim.z = 1;
+		lc.attrs = attr;
+		lc.numAttrs = 1;
+		INF_CUDA_TRY(cudaLaunchKernelEx(&lc, k, a));
+		return Success;
 	}
+	if constexpr (sizeof(T) == 2) {
+		if (P.kernel == InfAttnMma) {
+			const AttnMmaKernel k = attn_decode_mma_kernel(G, a.hd);
+			if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
+			CUtensorMap tk, tv; // one page (blk positions x 64 head dims) per box
+			INF_TRY(tensor_map_kv(&tk, a.kpool, (u32)a.hd, (u32)a.blk, (u32)a.KV, n_pages, 1));
+			INF_TRY(tensor_map_kv(&tv, a.vpool, (u32)a.hd, (u32)a.blk, (u32)a.KV, n_pages, 1));
+			INF_CUDA_TRY(set_smem(k, P.smem));
+			k<<<dim3((unsigned)a.KV, (unsigned)P.splits, n_tokens), kAmThreads, P.smem, st>>>(tk, tv, a);
+			INF_CUDA_TRY(cudaGetLastError());
+			return Success;
+		}
+	}
+	const AttnKernel<T> k = attn_decode_kernel<T>(G, a.hd);
+	if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
+	INF_CUDA_TRY(set_smem(k, P.smem));
+	k<<<dim3((unsigned)a.KV, (unsigned)P.splits, n_tokens), kAttnThreads, P.smem, st>>>(a);
 	INF_CUDA_TRY(cudaGetLastError());
 	return Success;
 }
 } // namespace
 
+extern "C" {
+
 u64 inf_attn_decode_scratch_bytes(u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
                                   u32 pages_per_seq, u32 dtype)
 {
 	AttnPlan P = {};
-	if (attn_plan(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P) != Success) return 0;
+	if (attn_plan(InfAttnSplitK, n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P) != Success)
+		return 0;
 	return (u64)(P.part_bytes + P.counter_bytes);
 }
 
-Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
-                        u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos, u32 n_tokens,
-                        u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype, void* d_out,
-                        void* d_scratch, u64 scratch_bytes, void* stream)
+Error_t inf_attn_decode_with(u32 kernel, const void* d_q, const void* d_kpool, const void* d_vpool,
+                             const i32* d_block_table, u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot,
+                             const i32* d_tok_pos, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
+                             u32 dtype, void* d_out, void* d_scratch, u64 scratch_bytes, void* stream)
 {
 	if (!d_q || !d_kpool || !d_vpool || !d_block_table || !d_tok_slot || !d_tok_pos || !d_out || !d_scratch)
 		return fail(ErrorInvalidValue, "inf_attn_decode: NULL pointer");
 	AttnPlan P;
-	INF_TRY(attn_plan(n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P));
+	INF_TRY(attn_plan(kernel, n_tokens, n_heads, n_kv_heads, head_dim, kv_block, pages_per_seq, dtype, &P));
 	if (scratch_bytes < P.part_bytes + P.counter_bytes)
 		return fail(ErrorInvalidValue, "inf_attn_decode: scratch needs %zu bytes", P.part_bytes + P.counter_bytes);
 	if (((uintptr_t)d_scratch & 15) || ((uintptr_t)d_kpool & 15) || ((uintptr_t)d_vpool & 15))
 		return fail(ErrorInvalidValue, "inf_attn_decode: 16-byte alignment");
+	if (n_pages == 0) return fail(ErrorInvalidValue, "inf_attn_decode: no pages");
 	const cudaStream_t st = (cudaStream_t)stream;
 	uint8_t* scr = (uint8_t*)d_scratch;
 	unsigned* counters = (unsigned*)(scr + P.part_bytes);
@@ -1959,15 +2035,101 @@ Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpoo
 	a.KV = (int)n_kv_heads;
 	a.hd = (int)head_dim;
 	a.blk = (int)kv_block;
+	a.n_splits = P.splits;
+	a.max_pages_split = P.max_pages_split;
 	a.scale = (float)(1.0 / std::sqrt((double)head_dim));
 	a.part = (float*)scr;
 	a.counters = counters;
 	a.out = d_out;
 	a.err = err;
-	INF_TRY(attn_launch(P, a, n_tokens, dtype, st));
+	if (dtype == InfBF16) INF_TRY(attn_launch_t<bf16>(P, a, n_tokens, n_pages, st));
+	else INF_TRY(attn_launch_t<float>(P, a, n_tokens, n_pages, st));
 	int h_err = 0;
 	INF_CUDA_TRY(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
 	INF_CUDA_TRY(cudaStreamSynchronize(st));
+	return map_dev_err(h_err);
+}
+
+Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpool, const i32* d_block_table,
+                        u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot, const i32* d_tok_pos, u32 n_tokens,
+                        u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block, u32 dtype, void* d_out,
+                        void* d_scratch, u64 scratch_bytes, void* stream)
+{
+	return inf_attn_decode_with(InfAttnAuto, d_q, d_kpool, d_vpool, d_block_table, pages_per_seq, n_pages, d_tok_slot,
+	                            d_tok_pos, n_tokens, n_heads, n_kv_heads, head_dim, kv_block, dtype, d_out, d_scratch,
+	                            scratch_bytes, stream);
+}
+
+Error_t inf_attn_prefill(u32 kernel, const void* d_q, const void* d_kpool, const void* d_vpool,
+                         const i32* d_block_table, u32 pages_per_seq, u32 n_pages, const i32* d_tok_slot,
+                         const i32* d_tok_pos, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 head_dim, u32 kv_block,
+                         void* d_out, void* stream)
+{
+	if (!d_q || !d_kpool || !d_vpool || !d_block_table || !d_tok_slot || !d_tok_pos || !d_out)
+		return fail(ErrorInvalidValue, "inf_attn_prefill: NULL pointer");
+	if (n_tokens == 0 || n_heads == 0 || n_kv_heads == 0 || n_heads % n_kv_heads || head_dim == 0 || head_dim % 2 ||
+	    kv_block == 0 || pages_per_seq == 0 || n_pages == 0 || kernel > InfPrefillAttnSimt || n_tokens > 65535u * 16u)
+		return fail(ErrorInvalidValue, "inf_attn_prefill: bad shape");
+	if (((uintptr_t)d_kpool | (uintptr_t)d_vpool | (uintptr_t)d_q) & 15)
+		return fail(ErrorInvalidValue, "inf_attn_prefill: 16-byte alignment");
+	const int G = (int)(n_heads / n_kv_heads), hd = (int)head_dim, blk = (int)kv_block;
+	if (G * hd * kPfTq > kPfThreads * kPfMaxAcc || (G != 1 && G != 2 && G != 4 && G != 8) || hd > 256)
+		return fail(ErrorUnsupported, "inf_attn_prefill: GQA group %d x head_dim %d", G, hd);
+	const bool tc = kernel == InfPrefillAttnAuto && (hd == 64 || hd == 128) && kPtRows % G == 0 && blk % 8 == 0 &&
+	                kPtKeys % blk == 0;
+	const cudaStream_t st = (cudaStream_t)stream;
+	int* d_err = nullptr;
+	INF_CUDA_TRY(cudaMallocAsync((void**)&d_err, sizeof(int), st));
+	INF_CUDA_TRY(cudaMemsetAsync(d_err, 0, sizeof(int), st));
+	AttnPrefillArgs a;
+	memset(&a, 0, sizeof a);
+	a.q = d_q;
+	a.kpool = d_kpool;
+	a.vpool = d_vpool;
+	a.block_table = d_block_table;
+	a.pages_per_seq = (int)pages_per_seq;
+	a.max_pages = (int)n_pages;
+	a.tok_pos = d_tok_pos;
+	a.tok_slot = d_tok_slot;
+	a.T = (int)n_tokens;
+	a.H = (int)n_heads;
+	a.KV = (int)n_kv_heads;
+	a.hd = hd;
+	a.blk = blk;
+	a.scale = (float)(1.0 / std::sqrt((double)hd));
+	a.out = d_out;
+	a.err = d_err;
+	Error_t r = Success;
+	if (tc) {
+		const size_t smem = attn_prefill_tc_smem_bytes(hd);
+		const u32 bp = kPtKeys / kv_block;
+		CUtensorMap tk8, tk1, tv8, tv1;
+		r = tensor_map_kv(&tk8, d_kpool, head_dim, kv_block, n_kv_heads, n_pages, bp);
+		if (r == Success) r = tensor_map_kv(&tk1, d_kpool, head_dim, kv_block, n_kv_heads, n_pages, 1);
+		if (r == Success) r = tensor_map_kv(&tv8, d_vpool, head_dim, kv_block, n_kv_heads, n_pages, bp);
+		if (r == Success) r = tensor_map_kv(&tv1, d_vpool, head_dim, kv_block, n_kv_heads, n_pages, 1);
+		cudaError_t ce = cudaSuccess;
+		if (r == Success) ce = set_smem(k_attn_prefill_tc, smem);
+		if (r == Success && ce == cudaSuccess) {
+			const int tq = kPtRows / G;
+			k_attn_prefill_tc<<<dim3(n_kv_heads, (n_tokens + tq - 1) / tq), kPtThreads, smem, st>>>(tk8, tk1, tv8, tv1, a);
+			ce = cudaGetLastError();
+		}
+		if (r == Success && ce != cudaSuccess) r = fail(ErrorCuda, "inf_attn_prefill: %s", cudaGetErrorString(ce));
+	} else {
+		const size_t smem = attn_prefill_smem_bytes(G, hd, blk);
+		cudaError_t ce = set_smem(k_attn_prefill<bf16>, smem);
+		if (ce == cudaSuccess) {
+			k_attn_prefill<bf16><<<dim3(n_kv_heads, (n_tokens + kPfTq - 1) / kPfTq), kPfThreads, smem, st>>>(a);
+			ce = cudaGetLastError();
+		}
+		if (ce != cudaSuccess) r = fail(ErrorCuda, "inf_attn_prefill: %s", cudaGetErrorString(ce));
+	}
+	int h_err = 0;
+	if (r == Success) INF_CUDA_TRY(cudaMemcpyAsync(&h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+	cudaFreeAsync(d_err, st);
+	INF_CUDA_TRY(cudaStreamSynchronize(st));
+	if (r != Success) return r;
 	return map_dev_err(h_err);
 }
 

@@ -82,9 +82,10 @@ class InfStats(C.Structure):
 EXPORTS = [
     "exec_ctx_create", "exec_ctx_destroy", "arena_host_create", "arena_host_destroy", "arena_host_push",
     "arena_host_pop", "arena_host_pop_at", "mem_arena_host_pos_get", "arena_dev_create", "arena_dev_destroy",
-    "arena_dev_push", "arena_dev_pop", "arena_dev_pop_at", "arena_dev_pos_get", "cu_memcpy_htd",
-    "cu_memcpy_htd_async", "cu_memcpy_dth", "cu_memset", "inf_fetch_input_embeddings", "inf_rmsnorm",
-    "inf_gemm_bf16", "inf_attn_decode_scratch_bytes", "inf_attn_decode",
+    "arena_dev_push", "arena_dev_pop", "arena_dev_pop_at", "arena_dev_pos_get", "cu_malloc", "cu_free",
+    "cu_memcpy_htd", "cu_memcpy_htd_async", "cu_memcpy_dth", "cu_host_register_read_only", "cu_memset",
+    "inf_fetch_input_embeddings", "inf_rmsnorm", "inf_gemm_bf16", "inf_attn_decode_scratch_bytes", "inf_attn_decode",
+    "inf_attn_decode_with", "inf_attn_prefill",
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
@@ -125,15 +126,21 @@ def lib():
         "arena_dev_pop": (None, [C.POINTER(DevArena), u64]),
         "arena_dev_pop_at": (None, [C.POINTER(DevArena), u64]),
         "arena_dev_pos_get": (u64, [C.POINTER(DevArena)]),
+        "cu_malloc": (i32, [C.POINTER(vp), u64]),
+        "cu_free": (i32, [vp]),
         "cu_memcpy_htd": (E, [vp, vp, u64]),
-        "cu_memcpy_htd_async": (E, [vp, vp, u64, vp]),
+        "cu_memcpy_htd_async": (i32, [vp, vp, u64, vp]),
         "cu_memcpy_dth": (E, [vp, vp, u64]),
-        "cu_memset": (E, [vp, i32, u64]),
+        "cu_host_register_read_only": (i32, [vp, u64]),
+        "cu_memset": (i32, [vp, i32, u64]),
         "inf_fetch_input_embeddings": (E, [vp, u64, u32, u32, vp, vp, u32, vp]),
         "inf_rmsnorm": (E, [vp, vp, u32, u32, vp, f32, u32, vp]),
         "inf_gemm_bf16": (E, [vp, vp, vp, u32, u32, u32, u32, vp]),
         "inf_attn_decode_scratch_bytes": (u64, [u32, u32, u32, u32, u32, u32, u32]),
         "inf_attn_decode": (E, [vp, vp, vp, vp, u32, u32, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, u64, vp]),
+        "inf_attn_decode_with": (E, [u32, vp, vp, vp, vp, u32, u32, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, u64,
+                                     vp]),
+        "inf_attn_prefill": (E, [u32, vp, vp, vp, vp, u32, u32, vp, vp, u32, u32, u32, u32, u32, vp, vp]),
         "inf_config_preset": (E, [u32, C.POINTER(InfConfig)]),
         "inf_model_build": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model), C.POINTER(InfConfig), C.c_char_p, u64]),
         "inf_model_destroy": (E, [C.POINTER(C.POINTER(ExecCtx)), C.POINTER(Model)]),
@@ -164,7 +171,7 @@ def lib():
         "inf_tokenizer_decode": (E, [vp, vp, u64, C.c_char_p, u64, C.POINTER(u64)]),
         "inf_set_sampling": (E, [C.POINTER(Model), C.POINTER(InfSampling)]),
         "inf_server_create": (E, [C.POINTER(Model), u32, C.POINTER(vp)]),
-        "inf_server_create_synthetic": (E, [u32, u32, u32, u32, C.POINTER(vp)]),
+        "inf_server_create_synthetic": (E, [u32, u32, u32, u32, u32, C.POINTER(vp)]),
         "inf_server_destroy": (E, [C.POINTER(vp)]),
         "inf_server_submit": (E, [vp, vp, u32, u32, u32, C.POINTER(u64)]),
         "inf_server_step": (E, [vp, C.POINTER(u32)]),
@@ -302,8 +309,9 @@ class Server:
         if engine is not None:
             check(lib().inf_server_create(C.byref(engine.model), max_active, C.byref(self.h)), "inf_server_create")
         else:
-            n_slots, max_seq, vocab = synthetic
-            check(lib().inf_server_create_synthetic(n_slots, max_seq, vocab, max_active, C.byref(self.h)),
+            n_slots, max_seq, vocab = synthetic[:3]
+            kv_pages = synthetic[3] if len(synthetic) > 3 else 0
+            check(lib().inf_server_create_synthetic(n_slots, max_seq, vocab, kv_pages, max_active, C.byref(self.h)),
                   "inf_server_create_synthetic")
 
     def submit(self, prompt, max_new: int, eos: int = NO_EOS) -> int:
@@ -527,6 +535,29 @@ def attn_decode(d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_to
     check(lib().inf_attn_decode(vp(d_q), vp(d_k), vp(d_v), vp(d_bt), pages_per_seq, n_pages, vp(d_slot), vp(d_pos),
                                 n_tokens, n_heads, n_kv_heads, head_dim, kv_block, dtype, vp(d_out), vp(d_scratch),
                                 scratch_bytes, vp(stream) if stream else None), "inf_attn_decode")
+
+
+ATTN_AUTO, ATTN_SPLITK, ATTN_CLUSTER, ATTN_MMA = 0, 1, 2, 3  # InfAttnKernel
+
+
+def attn_decode_with(kernel, d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_tokens, n_heads,
+                     n_kv_heads, head_dim, kv_block, dtype, d_out, d_scratch, scratch_bytes, stream=0) -> None:
+    """inf_attn_decode with one kernel of InfAttnKernel forced."""
+    check(lib().inf_attn_decode_with(kernel, vp(d_q), vp(d_k), vp(d_v), vp(d_bt), pages_per_seq, n_pages, vp(d_slot),
+                                     vp(d_pos), n_tokens, n_heads, n_kv_heads, head_dim, kv_block, dtype, vp(d_out),
+                                     vp(d_scratch), scratch_bytes, vp(stream) if stream else None),
+          "inf_attn_decode_with")
+
+
+PREFILL_AUTO, PREFILL_SIMT = 0, 1  # InfPrefillAttention
+
+
+def attn_prefill(kernel, d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_tokens, n_heads, n_kv_heads,
+                 head_dim, kv_block, d_out, stream=0) -> None:
+    """Causal attention of one prefill pass over the paged cache (bf16)."""
+    check(lib().inf_attn_prefill(kernel, vp(d_q), vp(d_k), vp(d_v), vp(d_bt), pages_per_seq, n_pages, vp(d_slot),
+                                 vp(d_pos), n_tokens, n_heads, n_kv_heads, head_dim, kv_block, vp(d_out),
+                                 vp(stream) if stream else None), "inf_attn_prefill")
 
 
 def attn_decode_noalloc(d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_tokens, n_heads, n_kv_heads,

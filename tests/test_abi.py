@@ -121,10 +121,28 @@ def test_new_entry_points_reject_null_arguments_without_a_device():
     assert L.inf_tokenizer_decode(None, None, 0, None, 0, C.byref(n)) == 4
     assert L.inf_tokenizer_vocab_size(None) == 0
     assert L.inf_server_create(None, 0, C.byref(I.vp())) == 4
-    assert L.inf_server_create_synthetic(0, 16, 10, 0, C.byref(I.vp())) == 4
+    assert L.inf_server_create_synthetic(0, 16, 10, 0, 0, C.byref(I.vp())) == 4
     assert L.inf_server_step(None, None) == 4
     assert L.inf_server_destroy(None) == 4
     assert L.inf_server_stats(None, None, None, None, None) == 4
     assert L.inf_set_sampling(None, None) == 4
     s = I.InfSampling(temperature=1.0, top_p=1.0)
     assert L.inf_set_sampling(C.byref(I.Model()), C.byref(s)) == 4  # no engine
+
+
+def test_memory_wrappers_keep_the_reference_return_conventions_without_a_device():
+    """src/cuda/api/cuda_mem_wrapper.cuh:10-16: the b32 wrappers answer 1 for success and 0 for
+    failure, cu_memcpy_htd / cu_memcpy_dth return Error_t.  Without a GPU every pointer is rejected
+    (or the CUDA call fails) and each wrapper says so without aborting."""
+    L = I.lib()
+    buf = (C.c_uint8 * 64)()
+    p = I.vp(1234)
+    assert L.cu_malloc(None, 16) == 0
+    assert L.cu_malloc(C.byref(p), 16) == 0 and not p.value  # no device to allocate on
+    assert L.cu_free(buf) == 0
+    assert L.cu_memset(buf, 0, 64) == 0
+    assert L.cu_memcpy_htd_async(buf, buf, 64, None) == 0
+    assert L.cu_memcpy_htd(buf, buf, 64) == 6   # ErrorInvalidDevPtr: dst is host memory
+    assert L.cu_memcpy_dth(buf, buf, 64) == 5   # ErrorInvalidHostPtr, as the reference answers
+    assert L.cu_host_register_read_only(None, 64) == 0
+    assert b"cu_host_register_read_only" in I.lib().inf_last_error_detail()

@@ -105,3 +105,59 @@ def test_rope_positions_far_into_the_cache(cuda):
     orc.forward(ids, start)
     for t in range(24):
         assert_bf16_close(got[t], orc.kv(0, start + t)[0], f"k[{start + t}]")
+
+
+def test_headline_decode_plan_stages(cuda):
+    """The batch-1 decode step as the headline runs it: the Llama-3-8B shape at its default
+    max_seq 3072 (192 pages per sequence, so the decode graph's attention is the 16-CTA cluster
+    kernel with 12 pages per CTA), one layer, vocabulary 8192 to keep the oracle cheap.  A
+    2048-token prompt goes through the tensor-core prefill, then 16 tokens through the decode
+    graph at positions 2048..2063.  At every step:
+    * the attention output is the correctly rounded value (within one bf16 ulp, measured 0.5) of
+      attention computed in float64 from the step's q over the engine's own cache (every K/V row
+      read back): the kernel, its split plan and the current row it patches in after the
+      dependency wait are exact;
+    * q, the new K/V row, the attention output, the SwiGLU product and the logits match the
+      oracle, which ran the same ids from its own prefill.  The prompt's K/V rows came from the
+      tensor-core prefill's fp32 sums, a rounding-boundary flip away from the oracle's double sums
+      at a few percent of entries, so the attention output and what follows it carry an absolute
+      allowance of 0.4% of the vector's largest value."""
+    torch = cuda
+    cfg = I.preset(3, n_layers=1, vocab_size=8192)
+    assert cfg.max_seq == 3072
+    n, steps = 2048, 16
+    prompt = I.synth_ids(21, n, cfg.vocab_size)
+    ids = I.synth_ids(22, steps, cfg.vocab_size)
+    H, KV, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    got = []
+    with I.Engine(cfg) as eng:
+        eng.forward(prompt, 0, want_logits=False)
+        for s in range(steps):
+            lg, am = eng.forward(ids[s:s + 1], n + s)
+            got.append({k: eng.debug_read(k) for k in ("q", "attn", "h")} | {"logits": lg, "am": am})
+        K = np.stack([eng.debug_read("k", 0, 0, t) for t in range(n + steps)]).reshape(-1, KV, hd)
+        V = np.stack([eng.debug_read("v", 0, 0, t) for t in range(n + steps)]).reshape(-1, KV, hd)
+    Kt = torch.from_numpy(K).double().permute(1, 0, 2)  # [KV, pos, hd], the bf16 values widened
+    Vt = torch.from_numpy(V).double().permute(1, 0, 2)
+    for s in range(steps):
+        p = n + s
+        q = torch.from_numpy(got[s]["q"]).double().view(KV, H // KV, hd)
+        sc = torch.einsum("kgd,knd->kgn", q, Kt[:, :p + 1]) / hd ** 0.5
+        ref = torch.einsum("kgn,knd->kgd", torch.softmax(sc, -1), Vt[:, :p + 1]).reshape(-1).numpy()
+        assert_bf16_close(got[s]["attn"], ref, f"attention at {p} over the engine's cache", min_exact=0.0,
+                          abs_frac=1e-6)
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0)
+    orc.forward(prompt, 0)
+    for s in range(steps):
+        p = n + s
+        o_lg, o_am = orc.forward(ids[s:s + 1], p)
+        q, k, v, att = orc.layer0()
+        h, _ = orc.layer0_mlp()
+        g = got[s]
+        assert_bf16_close(g["q"], q, f"q at {p}")
+        assert_bf16_close(K[p].reshape(-1), k, f"k at {p}")
+        assert_bf16_close(V[p].reshape(-1), v, f"v at {p}")
+        assert_bf16_close(g["attn"], att, f"attention at {p}", min_exact=0.85, abs_frac=4e-3)
+        assert_bf16_close(g["h"], h, f"swiglu at {p}", min_exact=0.85, abs_frac=4e-3)
+        assert float(np.abs(g["logits"] - o_lg).max()) <= 2e-2, f"logits at {p}"
+        assert g["am"] == o_am or np.sort(o_lg)[-1] - np.sort(o_lg)[-2] < 2e-2

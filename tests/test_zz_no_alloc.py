@@ -5,7 +5,8 @@ device mid-step, or a runtime whose device memory is all committed to a pre-size
 Instead of caller-provided scratch it uses an array built into libinf.so, shared by every
 call.  These tests call it through the C ABI twice in a row (the second call finds the first
 call's leftovers in the shared array) and compare each result with the scratch-taking entry
-point inf_attn_decode, at the tolerance of the attention kernel tests.  The file runs last so
+point inf_attn_decode: both run the same kernel with the same split plan, so the outputs must
+be bit-identical, whatever the shared array held before.  The file runs last so
 that a failure here leaves every other test already run; it also passes on its own in a
 fresh process (the first call sets up the array's device address).
 """
@@ -58,7 +59,7 @@ def test_no_alloc_attention_matches_scratch_entry_point_twice(cuda):
         want = _with_scratch(torch, c)
         got = _no_alloc(torch, c)
         torch.cuda.synchronize()
-        torch.testing.assert_close(got.float(), want.float(), rtol=2 ** -7, atol=2e-3)
+        assert torch.equal(got, want)
 
 
 def test_no_alloc_attention_rejects_shapes_beyond_its_scratch(cuda):
@@ -67,3 +68,18 @@ def test_no_alloc_attention_rejects_shapes_beyond_its_scratch(cuda):
     with pytest.raises(I.InfError) as e:
         _no_alloc(torch, c)
     assert e.value.code == 4 and "above the built-in" in str(e.value)
+
+
+def test_no_alloc_attention_reports_unsupported_shapes_like_the_scratch_entry_point(cuda):
+    torch = cuda
+    c = _case(torch, 24, 8, 128, [100], seed=4)  # GQA group 3: no kernel serves it
+    with pytest.raises(I.InfError) as a:
+        _no_alloc(torch, c)
+    scratch = torch.empty(256, dtype=torch.uint8, device="cuda")  # the shape's scratch size is 0: unsupported
+    out = torch.empty_like(c["q"])
+    with pytest.raises(I.InfError) as b:
+        I.attn_decode(c["q"].data_ptr(), c["kp"].data_ptr(), c["vp"].data_ptr(), c["bt"].data_ptr(), c["pps"],
+                      c["n_pages"], c["slots"].data_ptr(), c["pos"].data_ptr(), c["n"], 24, 8, 128, 16, I.BF16,
+                      out.data_ptr(), scratch.data_ptr(), 256)
+    assert a.value.code == b.value.code == 15
+    assert I.attn_decode_scratch_bytes(1, 24, 8, 128, 16, c["pps"], I.BF16) == 0
