@@ -11,6 +11,10 @@
 //      sequence, so that a request's ids never depend on how many others are running;
 //   3. retires sequences that produced their end-of-sequence id, reached max_new tokens or
 //      the end of the slot's positions, and releases their pages for the next admissions.
+// KV pages are accounted for at admission: a request reserves the pages of every position it
+// can write before it retires (its prompt plus max_new - 1 fed tokens, at most max_seq), and
+// waits -- keeping its place in the queue -- while the pool cannot cover that, so a batched
+// step never runs out of pages halfway through a sequence.
 // A request admitted in step s contributes its first token in step s and joins the batched
 // decode from step s + 1.  The reference has no serving loop (it stops after one RMSNorm,
 // src/main.cu:396-412); this is the scheduler a caller would otherwise write around
@@ -32,6 +36,8 @@ struct Backend {
 	virtual ~Backend() = default;
 	virtual u32 slots() const = 0;
 	virtual u32 max_seq() const = 0;
+	virtual u32 kv_block() const = 0; // positions per KV page
+	virtual u32 kv_pages() const = 0; // pages in the pool, shared by all slots
 	virtual Error_t release(u32 slot) = 0;
 	virtual Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) = 0;
 	virtual Error_t decode(u32 n, const u32* slots, const u32* ids, const u32* pos, u32* next) = 0;
@@ -42,6 +48,12 @@ struct ModelBackend final : Backend {
 	explicit ModelBackend(Model* model) : m(model) {}
 	u32 slots() const override { return m->config.max_batch; }
 	u32 max_seq() const override { return m->config.max_seq; }
+	u32 kv_block() const override { return m->config.kv_block ? m->config.kv_block : 16; }
+	u32 kv_pages() const override
+	{
+		const InfConfig& c = m->config;
+		return c.kv_pages ? c.kv_pages : c.max_batch * ((c.max_seq + kv_block() - 1) / kv_block());
+	}
 	Error_t release(u32 slot) override { return inf_seq_reset(m, slot); }
 	Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) override
 	{
@@ -57,13 +69,22 @@ struct ModelBackend final : Backend {
 
 // Host stand-in: the next id is a hash of the sequence's previous id and position only, so a
 // sequence's outputs cannot depend on what else shares its batch.  Tracks which positions each
-// slot has written, to check the scheduler feeds every sequence its own positions in order.
+// slot has written, to check the scheduler feeds every sequence its own positions in order, and
+// holds a pool of 16-position pages that fails like the device cache when it runs out.  A prompt
+// that starts with id vocab - 1 makes the first batched step its sequence is in fail with
+// ErrorGeneric (to test how the scheduler handles a failing step).
 struct SyntheticBackend final : Backend {
-	u32 n_slots, seq, vocab;
-	std::vector<u32> filled; // positions written per slot
-	SyntheticBackend(u32 s, u32 ms, u32 v) : n_slots(s), seq(ms), vocab(v), filled(s, 0) {}
+	u32 n_slots, seq, vocab, pages;
+	std::vector<u32> filled;   // positions written per slot
+	std::vector<char> poison;  // slot's prompt started with vocab - 1
+	SyntheticBackend(u32 s, u32 ms, u32 v, u32 p)
+	    : n_slots(s), seq(ms), vocab(v), pages(p ? p : s * ((ms + 15) / 16)), filled(s, 0), poison(s, 0)
+	{
+	}
 	u32 slots() const override { return n_slots; }
 	u32 max_seq() const override { return seq; }
+	u32 kv_block() const override { return 16; }
+	u32 kv_pages() const override { return pages; }
 	static u32 mix(u64 x)
 	{
 		x ^= x >> 33;
@@ -72,19 +93,29 @@ struct SyntheticBackend final : Backend {
 		x *= 0xc4ceb9fe1a85ec53ull;
 		return (u32)(x ^ (x >> 33));
 	}
+	u32 pages_in_use(int except_slot, u32 positions_there) const
+	{
+		u32 n = 0;
+		for (u32 k = 0; k < n_slots; ++k) n += ((int)k == except_slot ? positions_there : filled[k]) / 16 +
+		                                        (((int)k == except_slot ? positions_there : filled[k]) % 16 != 0);
+		return n;
+	}
 	Error_t release(u32 slot) override
 	{
 		if (slot >= n_slots) return fail(ErrorInvalidValue, "slot %u", slot);
 		filled[slot] = 0;
+		poison[slot] = 0;
 		return Success;
 	}
 	Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) override
 	{
 		if (slot >= n_slots || n == 0 || n > seq) return fail(ErrorInvalidValue, "prefill slot %u n %u", slot, n);
 		if (filled[slot] != 0) return fail(ErrorInvalidValue, "prefill into a slot that holds %u positions", filled[slot]);
+		if (pages_in_use((int)slot, n) > pages) return fail(ErrorArenaOutOfMemory, "KV cache out of pages");
 		u64 h = 0;
 		for (u32 i = 0; i < n; ++i) h = mix(h * 31 + ids[i]);
 		filled[slot] = n;
+		poison[slot] = ids[0] == vocab - 1;
 		*next = mix(h ^ ((u64)n << 40)) % vocab;
 		return Success;
 	}
@@ -96,10 +127,14 @@ struct SyntheticBackend final : Backend {
 			for (u32 j = 0; j < i; ++j)
 				if (s[j] == s[i]) return fail(ErrorInvalidValue, "slot %u twice in one batch", s[i]);
 		}
-		for (u32 i = 0; i < n; ++i) {
-			filled[s[i]] = pos[i] + 1;
-			next[i] = mix(((u64)ids[i] << 32) ^ pos[i]) % vocab;
+		for (u32 i = 0; i < n; ++i)
+			if (poison[s[i]]) return fail(ErrorGeneric, "stand-in failure for slot %u", s[i]);
+		for (u32 i = 0; i < n; ++i) filled[s[i]] = pos[i] + 1;
+		if (pages_in_use(-1, 0) > pages) {
+			for (u32 i = 0; i < n; ++i) filled[s[i]] = pos[i];
+			return fail(ErrorArenaOutOfMemory, "KV cache out of pages");
 		}
+		for (u32 i = 0; i < n; ++i) next[i] = mix(((u64)ids[i] << 32) ^ pos[i]) % vocab;
 		return Success;
 	}
 };
@@ -112,6 +147,7 @@ struct Request {
 	int slot = -1;
 	u32 pos = 0;      // position of the last output token (the next one fed)
 	u64 admitted = 0; // the step that prefilled it
+	u32 pages = 0;    // KV pages reserved while it holds a slot
 	bool done = false;
 	Error_t err = Success;
 };
@@ -127,14 +163,26 @@ struct InfServer {
 	std::deque<u64> waiting;
 	std::vector<u64> active;
 	std::vector<u32> free_slots;
+	u32 pages_reserved = 0;
 	u64 batched_steps = 0, batched_tokens = 0;
 };
 
 namespace {
 
+// Pages of every position a request can write before it retires: the prompt, then one fed
+// token per output after the first, at most max_seq positions.
+u32 pages_needed(const InfServer* s, const Request& r)
+{
+	const u64 positions = std::min<u64>((u64)r.prompt.size() + r.max_new - 1, s->be->max_seq());
+	const u32 blk = s->be->kv_block();
+	return (u32)((positions + blk - 1) / blk);
+}
+
 Error_t retire(InfServer* s, Request& r)
 {
 	r.done = true;
+	s->pages_reserved -= r.pages;
+	r.pages = 0;
 	if (r.slot >= 0) {
 		const u32 slot = (u32)r.slot;
 		r.slot = -1;
@@ -181,10 +229,10 @@ Error_t inf_server_create(Model* model, u32 max_active, InfServer** out)
 	return create(std::unique_ptr<Backend>(new ModelBackend(model)), max_active, out);
 }
 
-Error_t inf_server_create_synthetic(u32 n_slots, u32 max_seq, u32 vocab, u32 max_active, InfServer** out)
+Error_t inf_server_create_synthetic(u32 n_slots, u32 max_seq, u32 vocab, u32 kv_pages, u32 max_active, InfServer** out)
 {
 	if (n_slots == 0 || max_seq < 2 || vocab == 0) return fail(ErrorInvalidValue, "inf_server_create_synthetic: sizes");
-	return create(std::unique_ptr<Backend>(new SyntheticBackend(n_slots, max_seq, vocab)), max_active, out);
+	return create(std::unique_ptr<Backend>(new SyntheticBackend(n_slots, max_seq, vocab, kv_pages)), max_active, out);
 }
 
 Error_t inf_server_destroy(InfServer** s)
@@ -200,10 +248,13 @@ Error_t inf_server_submit(InfServer* s, const u32* prompt, u32 n_prompt, u32 max
 	if (!s || !prompt || !request_id || n_prompt == 0 || max_new == 0) return fail(ErrorInvalidValue, "inf_server_submit: arguments");
 	if (n_prompt >= s->be->max_seq()) return fail(ErrorKvOutOfRange, "prompt of %u tokens, %u positions per slot", n_prompt, s->be->max_seq());
 	Request r;
-	r.id = s->next_id++;
 	r.prompt.assign(prompt, prompt + n_prompt);
 	r.max_new = max_new;
 	r.eos = eos_id;
+	const u32 need = pages_needed(s, r);
+	if (need > s->be->kv_pages())
+		return fail(ErrorArenaOutOfMemory, "request needs %u KV pages, the pool holds %u", need, s->be->kv_pages());
+	r.id = s->next_id++;
 	s->waiting.push_back(r.id);
 	*request_id = r.id;
 	s->reqs.emplace(r.id, std::move(r));
@@ -218,7 +269,11 @@ Error_t inf_server_step(InfServer* s, u32* n_finished)
 	// 1. admissions: prefill and the first token
 	while (!s->waiting.empty() && !s->free_slots.empty() && s->active.size() < s->max_active) {
 		Request& r = s->reqs.at(s->waiting.front());
+		const u32 need = pages_needed(s, r);
+		if (s->pages_reserved + need > s->be->kv_pages()) break; // first come first served: it waits for pages
 		s->waiting.pop_front();
+		r.pages = need;
+		s->pages_reserved += need;
 		r.slot = (int)s->free_slots.back();
 		s->free_slots.pop_back();
 		r.admitted = step;
@@ -252,7 +307,25 @@ Error_t inf_server_step(InfServer* s, u32* n_finished)
 	}
 	if (!batch.empty()) {
 		std::vector<u32> next(batch.size());
-		INF_TRY(s->be->decode((u32)batch.size(), slots.data(), ids.data(), pos.data(), next.data()));
+		const Error_t e = s->be->decode((u32)batch.size(), slots.data(), ids.data(), pos.data(), next.data());
+		if (e != Success) {
+			// the batch's requests end with the error (their pages and slots go back to the pool),
+			// so the next step does not retry the same failing batch
+			std::vector<u64> keep;
+			for (u64 id : s->active) {
+				Request& r = s->reqs.at(id);
+				if (std::find(batch.begin(), batch.end(), id) != batch.end()) {
+					r.err = e;
+					(void)retire(s, r);
+					++fin;
+				} else {
+					keep.push_back(id);
+				}
+			}
+			s->active.swap(keep);
+			if (n_finished) *n_finished = fin;
+			return e;
+		}
 		++s->batched_steps;
 		s->batched_tokens += batch.size();
 		for (size_t i = 0; i < batch.size(); ++i) {

@@ -123,3 +123,62 @@ def test_submit_checks():
         r = s.submit(np.array([1], np.uint32), 5)
         with pytest.raises(I.InfError):
             s.release(r)  # still running
+
+
+def test_overcommitted_page_pool_admits_only_what_fits():
+    """8 slots but pages for about two long requests at once: the scheduler admits a request
+    only when every position it may write fits beside the running requests' reservations (the
+    stand-in fails like the device cache if a step runs out of pages), keeps first-come order,
+    and every request still gets its solo output."""
+    rng = np.random.default_rng(4)
+    reqs = [(rng.integers(0, 500, 90, dtype=np.uint32), 60, I.NO_EOS) for _ in range(7)]  # 149 positions: 10 pages
+    with I.Server(synthetic=(8, 256, 500, 21)) as s:
+        rids = [s.submit(p, m, e) for p, m, e in reqs]
+        max_active = 0
+        while s.stats()["waiting"] or s.stats()["active"]:
+            s.step()
+            max_active = max(max_active, s.stats()["active"])
+        assert max_active == 2  # 21 pages hold two 10-page reservations
+        outs = [s.result(r) for r in rids]
+    for (p, m, e), (out, done, rc) in zip(reqs, outs):
+        assert done and rc == 0 and out.size == m
+        with I.Server(synthetic=(1, 256, 500)) as alone:
+            (solo, _, _), = run_all(alone, [(p, m, e)])[0]
+        np.testing.assert_array_equal(out, solo)
+
+
+def test_request_larger_than_the_pool_is_refused_at_submit():
+    with I.Server(synthetic=(4, 256, 500, 5)) as s:
+        with pytest.raises(I.InfError) as e:
+            s.submit(np.arange(70, dtype=np.uint32), 20)  # 89 positions: 6 pages of 16
+        assert e.value.code == 2
+        rid = s.submit(np.arange(60, dtype=np.uint32), 20)   # 79 positions: 5 pages
+        while s.stats()["waiting"] or s.stats()["active"]:
+            s.step()
+        out, done, rc = s.result(rid)
+        assert done and rc == 0 and out.size == 20
+
+
+def test_failing_batched_step_retires_its_requests():
+    """A batched step that fails (the stand-in fails every batch that holds a sequence whose
+    prompt starts with id vocab - 1) returns its error once and retires the requests of that
+    batch with it; their slots and pages go back to the pool, the server does not retry the same
+    batch, and requests admitted later run to completion."""
+    vocab = 500
+    with I.Server(synthetic=(4, 128, vocab, 12)) as s:
+        good0 = s.submit(np.arange(1, 20, dtype=np.uint32), 8)
+        bad = s.submit(np.array([vocab - 1, 3, 4], np.uint32), 8)
+        s.step()                            # both admitted (prefill only)
+        with pytest.raises(I.InfError) as e:
+            s.step()                        # their first batched step fails
+        assert e.value.code == 7
+        for rid in (good0, bad):
+            out, done, rc = s.result(rid)
+            assert done and rc == 7 and out.size == 1
+        assert s.stats()["active"] == 0
+        later = [s.submit(np.arange(5 + i, 40, dtype=np.uint32), 10) for i in range(3)]
+        while s.stats()["waiting"] or s.stats()["active"]:
+            s.step()
+        for rid in later:
+            out, done, rc = s.result(rid)
+            assert done and rc == 0 and out.size == 10
