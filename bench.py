@@ -1,13 +1,15 @@
 """Batch-1 decode throughput of the Llama-3-8B-shape decoder (bf16) on B200.
 
-Workload: Llama-3-8B shape (vocab 128256, d 4096, 32 layers, 32 q / 8 kv heads of 128,
-SwiGLU 14336, RoPE theta 5e5), weights N(0, 0.02) from seed 0, a 2048-token prompt of
-uniform ids from seed 1, then greedy decode.  A step is one decoded token at batch 1; the
-timed steps are decode positions 2048 .. 2048+K-1 (warm-up steps run at the same positions
+Workload (the default, --preset 3): Llama-3-8B shape (vocab 128256, d 4096, 32 layers, 32 q /
+8 kv heads of 128, SwiGLU 14336, RoPE theta 5e5), weights N(0, 0.02) from seed 0, a 2048-token
+prompt of uniform ids from seed 1, then greedy decode.  A step is one decoded token at batch 1;
+the timed steps are decode positions 2048 .. 2048+K-1 (warm-up steps run at the same positions
 first and are overwritten).  Every step streams ~15.3 GB of weights and KV, far above the
-126 MB L2, so no L2 flush is needed between steps.
+126 MB L2, so no L2 flush is needed between steps.  --preset 2 is the TinyLlama-1.1B shape
+(prompt 512, 512 steps, 2.09 GB per step); --preset 1 the tiny d288 fp32 model (prompt 16,
+240 steps), whose 61 MB of weights stay in L2, so it reports latency per step.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--preset 1|2|3]
 
 Prints one JSON line (rank 0).  `value` is device-timed (CUDA events on the library's
 stream, max over ranks); `e2e` times the per-token public call inf_forward() with the id
@@ -33,6 +35,23 @@ GATEUP_NCU_TRAFFIC = 238.34e6
 PROMPT = 2048
 DECODE_STEPS = 1024
 
+# The decode workloads as plain model dicts (the oracle's form), so that the reference arm runs
+# without loading the library under test; tests/test_bench_cpu.py checks them against the
+# library's presets.
+_LLAMA3 = dict(vocab=128256, dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, max_seq=3072,
+               eps=1e-5, rope_theta=500000.0, dtype="bf16", init_std=0.02)
+DECODE = {
+    1: dict(model=dict(vocab=32000, dim=288, n_layers=6, n_heads=6, n_kv_heads=6, head_dim=48, ffn=768, max_seq=256,
+                       eps=1e-5, rope_theta=10000.0, dtype="fp32", init_std=0.02),
+            prompt=16, steps=240, name="tiny-llama-d288-fp32",
+            metric="batch-1 greedy decode latency per step (tiny Llama d288, 6 layers, fp32; weights L2-resident)"),
+    2: dict(model=dict(vocab=32000, dim=2048, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64, ffn=5632,
+                       max_seq=1024, eps=1e-5, rope_theta=10000.0, dtype="bf16", init_std=0.02),
+            prompt=512, steps=512, name="tinyllama-1.1b-shape",
+            metric="batch-1 decode tokens/s and % of HBM roofline (TinyLlama-1.1B shape, bf16), 1 GPU"),
+    3: dict(model=_LLAMA3, prompt=2048, steps=1024, name="llama-3-8b-shape", metric=METRIC),
+}
+
 
 def load_peaks():
     try:
@@ -55,10 +74,16 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        """Starts nvidia-smi and returns once its first sample is in, so that starting the sampler
+        (a fork of this process and nvidia-smi's start-up) happens before the timed region's
+        barrier: under tensor parallelism a rank that started late would make the others' first
+        exchanges wait for it inside their timed regions."""
+        self.first = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.first.append(self.proc.stdout.readline())
         except Exception:
             self.proc = None
         return self
@@ -72,7 +97,7 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines = [l for l in self.first + out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], [], set()
@@ -123,27 +148,30 @@ def oracle_decode_rate(cfg_dict: dict, ctx: int, budget_s: float, warmup: int = 
 
 def run_reference(args, rank: int, world: int):
     """The reference arm: the oracle's CPU restatement of the decoder (the reference itself has
-    no forward pass), timed on the host cores on this workload's config."""
+    no forward pass), timed on the host cores on this workload's config.  It loads only the
+    oracle (oracle/libllama_ref.so), never the library under test."""
     if rank != 0:
         return
-    import infb200 as I
-    cfg = I.preset(3)
-    d = I.oracle_dict(cfg)
-    # each step is one decoded token at ctx 2048+; bounded so the run ends in a few minutes
+    w = DECODE[args.preset]
+    d = dict(w["model"])
+    prompt = w["prompt"] if args.prompt is None else args.prompt
+    # each step is one decoded token at ctx prompt+; bounded so the run ends in a few minutes
     budget = float(os.environ.get("INF_REF_BUDGET_S", "60"))
-    rate, n, el, threads, setup_s = oracle_decode_rate(d, PROMPT, budget, warmup=min(args.warmup, 1))
+    rate, n, el, threads, setup_s = oracle_decode_rate(d, prompt, budget, warmup=min(args.warmup, 1))
+    latency = args.preset == 1
     line = {
-        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s", "n_gpus": world,
-        "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": 1000.0 * el / n, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "llama3-8b-shape batch-1 decode at ctx 2048+", "model": "llama-3-8b-shape",
-                   "global_batch": 1, "seq_len": PROMPT, "parallelism": "cpu"},
+        "impl": "reference", "metric": w["metric"], "value": 1000.0 / rate if latency else rate,
+        "unit": "ms" if latency else "tokens/s", "n_gpus": world,
+        "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": 1000.0 * el / n, "higher_is_better": not latency,
+        "scaling": "strong", "vs_baseline": None, "dtype": d["dtype"], "data": "synthetic",
+        "config": {"workload": f"{w['name']} batch-1 decode at ctx {prompt}+", "model": w["name"],
+                   "global_batch": 1, "seq_len": prompt, "parallelism": "cpu"},
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{n} decode tokens at ctx {PROMPT}+ with a synthetic KV cache; "
+                         "sample": f"{n} decode tokens at ctx {prompt}+ with a synthetic KV cache; "
                                    f"CPU restatement (oracle/llama_ref.c, OpenMP), the reference has no forward pass; "
                                    f"setup {setup_s:.0f}s untimed"},
-        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    line["e2e"] = {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     print(json.dumps(line), flush=True)
 
 
@@ -153,13 +181,15 @@ def run_ours(args, rank: int, world: int, dist):
 
     import infb200 as I
 
+    w = DECODE[args.preset]
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    cfg = I.preset(3, n_layers=args.layers, tp_rank=rank if world > 1 else 0, tp_size=world)
-    steps, warmup = args.steps, args.warmup
-    if PROMPT + max(steps, warmup) > cfg.max_seq:
-        raise SystemExit(f"--steps/--warmup above {cfg.max_seq - PROMPT}")
-    prompt = I.synth_ids(1, PROMPT, cfg.vocab_size)  # seed-1 uniform prompt ids
+    cfg = I.preset(args.preset, n_layers=args.layers, tp_rank=rank if world > 1 else 0, tp_size=world)
+    prompt_len = w["prompt"] if args.prompt is None else args.prompt
+    steps, warmup = args.steps or w["steps"], args.warmup
+    if prompt_len + max(steps, warmup) > cfg.max_seq:
+        raise SystemExit(f"--steps/--warmup above {cfg.max_seq - prompt_len}")
+    prompt = I.synth_ids(1, prompt_len, cfg.vocab_size)  # seed-1 uniform prompt ids
 
     eng = I.Engine(cfg, seed=0)
     if world > 1:
@@ -178,97 +208,118 @@ def run_ours(args, rank: int, world: int, dist):
         t_, p_, k_ = (float(x) for x in args.sample.split(","))
         sampling = {"temperature": t_, "top_p": p_, "top_k": int(k_), "seed": 7}
         eng.set_sampling(t_, p_, int(k_), seed=7)
-    eng.decode(first, PROMPT, warmup)
+    eng.decode(first, prompt_len, warmup)
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
-    # ---- timed region: K decode steps chained on the device
-    torch.cuda.synchronize()
-    barrier()
+    def gather(x):
+        """x from every rank, in rank order (one float each)."""
+        if dist is None:
+            return [x]
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [float(v.item()) for v in out]
+
+    # ---- timed region: K decode steps chained on the device (one graph replay per step); the
+    # clock sampler is running before the barrier, so no rank starts late
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    l0 = eng.launches
     with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        l0 = eng.launches
         torch.cuda.nvtx.range_push("timed")  # lets ncu --nvtx-include "timed/" select these launches
         ev0.record(stream)
-        ids, st = eng.decode(first, PROMPT, steps, want_ids=False)
+        ids, st = eng.decode(first, prompt_len, steps, want_ids=True)  # ids: one 4-byte read per step, at the end
         ev1.record(stream)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
-    barrier()
-    launches = eng.launches - l0
-    ms = ev0.elapsed_time(ev1)
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        launches = eng.launches - l0
+        barrier()
+    rank_ms = gather(ev0.elapsed_time(ev1))
+    ms = max(rank_ms)
     ms_per_step = ms / steps
+    # every rank must have chosen the same ids (the cross-shard argmax is exchanged on the device)
+    checksum = int(np.bitwise_xor.reduce((ids.astype(np.uint64) * np.arange(1, steps + 1, dtype=np.uint64))
+                                         ^ np.arange(steps, dtype=np.uint64)))
+    sums = gather(float(checksum % (1 << 52)))
+    ranks_agree = all(v == sums[0] for v in sums)
 
     # ---- per-kernel durations of one eager step (events around each launch, same stream)
     prof = {}
     for _ in range(3):
-        for k, v in eng.profile_step(PROMPT + steps - 1, first).items():
+        for k, v in eng.profile_step(prompt_len + steps - 1, first).items():
             prof[k] = prof.get(k, 0.0) + v / 3
 
     # ---- e2e: the per-token public call with host buffers
     tid = first
+    e2e_ids = []
     torch.cuda.synchronize()
     barrier()
     e0 = time.perf_counter()
-    for s in range(steps):
-        _, tid = eng.forward([tid], PROMPT + s, want_logits=False)
-    e2e_s = time.perf_counter() - e0
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    for s_ in range(steps):
+        _, tid = eng.forward([tid], prompt_len + s_, want_logits=False)
+        e2e_ids.append(tid)
+    e2e_s = max(gather(time.perf_counter() - e0))
+    e2e_same = bool(np.array_equal(np.asarray(e2e_ids, np.uint32), ids)) if not sampling else None
 
     # ---- roofline of the dominant kernel (gate/up projection + SwiGLU)
     peak, peak_kind = load_peaks()
     L, d, F = cfg.n_layers, cfg.dim, cfg.ffn_dim
     Fl = F // world  # this rank's FFN shard
-    gu_bytes = 2 * Fl * d * 2 + d * 4 + Fl * 2
+    esz = 2 if cfg.dtype == I.BF16 else 4
+    gu_bytes = 2 * Fl * d * esz + d * 4 + Fl * esz
     gu_ms = prof.get("gate_up", 0.0) / L
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else None
-    avg_ctx = PROMPT + (steps - 1) / 2
+    avg_ctx = prompt_len + (steps - 1) / 2
     step_bytes = I.decode_bytes(cfg, int(avg_ctx))
     step_gbs = step_bytes / (ms_per_step * 1e-3) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
-        rate, n, el, threads, setup_s = oracle_decode_rate(I.oracle_dict(cfg), PROMPT, args.cpu_budget)
+        rate, n, el, threads, setup_s = oracle_decode_rate(dict(w["model"], n_layers=args.layers), prompt_len,
+                                                           args.cpu_budget)
         cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{n} decode tokens ({el:.1f}s) at ctx {PROMPT}+ with a synthetic KV cache, CPU restatement "
-                         f"(oracle/llama_ref.c, OpenMP); weight generation {setup_s:.0f}s untimed"}
+               "sample": f"{n} decode tokens ({el:.1f}s) at ctx {prompt_len}+ with a synthetic KV cache, CPU "
+                         f"restatement (oracle/llama_ref.c, OpenMP); weight generation {setup_s:.0f}s untimed"}
 
-    value = steps / (ms * 1e-3)  # tensor parallel: every rank works on the same tokens
+    latency = args.preset == 1  # weights in L2: latency per step is the figure of merit
+    value = ms_per_step if latency else steps / (ms * 1e-3)  # tensor parallel: every rank works on the same tokens
     if rank == 0:
+        model = w["name"] if args.layers == DECODE[args.preset]["model"]["n_layers"] else f"{w['name']}-{args.layers}-layers"
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": (achieved / peak) if achieved else None,
+                    "kernel": f"k_gemv gate/up+SwiGLU (per launch: 2*{Fl}*{d} weights)", "peak_kind": peak_kind}
+        if args.preset == 3:
+            # dram__bytes_read.sum + dram__bytes_write.sum of one full-width launch (ncu capture of the
+            # same kernel and shape), scaled to this rank's shard
+            roofline.update(traffic=GATEUP_NCU_TRAFFIC * Fl / F, traffic_unit="bytes per launch")
+        else:
+            roofline.update(traffic=None)
+        if latency:
+            roofline["note"] = "61 MB of weights stay in the 126 MB L2: the HBM figure is an upper bound, not the limit"
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
-            "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "metric": w["metric"], "value": value, "unit": "ms" if latency else "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": not latency,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if cfg.dtype == I.BF16 else "f32",
             "data": "synthetic (Philox seed-0 N(0,0.02) weights, seed-1 uniform prompt ids)",
-            "config": {"workload": "llama3-8b-shape batch-1 " + ("sampled" if sampling else "greedy")
-                                   + " decode, prompt 2048, timed positions 2048..2048+K-1",
-                       "sampling": sampling,
-                       "model": "llama-3-8b-shape" if args.layers == 32 else f"llama-3-8b-shape-{args.layers}-layers",
-                       "global_batch": 1, "seq_len": PROMPT,
+            "config": {"workload": f"{w['name']} batch-1 " + ("sampled" if sampling else "greedy")
+                                   + f" decode, prompt {prompt_len}, timed positions {prompt_len}..{prompt_len}+K-1",
+                       "sampling": sampling, "model": model, "global_batch": 1, "seq_len": prompt_len,
                        "parallelism": f"tp{world}",
-                       "l2": "no flush: each step streams 15.3 GB (> 126 MB L2)",
+                       "l2": "no flush: each step streams the weights (%.2f GB)" % (step_bytes / 1e9)
+                             + (", which fit in L2" if latency else " (> 126 MB L2)"),
                        "step_bytes": step_bytes, "step_gbs": step_gbs,
                        "step_roofline_frac": step_gbs / (peak * world), "prefill_s": prefill_s,
-                       "kernel_ms_per_step": prof},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": (achieved / peak) if achieved else None,
-                         # dram__bytes_read.sum + dram__bytes_write.sum of one full-width launch
-                         # (ncu capture of the same kernel and shape), scaled to this rank's shard
-                         "traffic": GATEUP_NCU_TRAFFIC * Fl / F, "traffic_unit": "bytes per launch",
-                         "kernel": f"k_gemv gate/up+SwiGLU (per launch: 2*{Fl}*4096 bf16 weights)",
-                         "peak_kind": peak_kind},
+                       "kernel_ms_per_step": prof, "rank_ms": rank_ms, "ranks_agree": ranks_agree,
+                       "ids_checksum": checksum, "e2e_ids_equal_timed_ids": e2e_same,
+                       "tokens_per_s": steps / (ms * 1e-3)},
+            "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 12,
-                    "d2h_bytes_per_step": 20},
+            "e2e": {"value": (e2e_s * 1e3 / steps) if latency else steps / e2e_s, "unit": "ms" if latency else "tokens/s",
+                    "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 20},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
@@ -554,19 +605,22 @@ def run_tokenize(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=DECODE_STEPS)
+    ap.add_argument("--steps", type=int, default=0, help="timed steps (0: the workload's own count)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
-    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs use a short one)")
+    ap.add_argument("--prompt", type=int, default=None, help="prompt length (profiling runs use a short one)")
+    ap.add_argument("--preset", type=int, default=3, choices=[1, 2, 3],
+                    help="decode workload: 3 Llama-3-8B shape (the headline), 2 TinyLlama-1.1B shape, 1 tiny fp32 d288")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch", "serve", "tokenize"],
                     help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence "
                          "decode; serve: continuous batching of 192 requests; tokenize: host tokenizer encode (no GPU)")
     ap.add_argument("--sample", default="", help="decode workload with sampling: temperature,top_p,top_k")
     args = ap.parse_args()
-    globals()["PROMPT"] = args.prompt
+    if args.prompt is not None:
+        globals()["PROMPT"] = args.prompt
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 
