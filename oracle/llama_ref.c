@@ -334,20 +334,28 @@ uint32_t orc_sample_select(const uint32_t* q, uint64_t n, float top_p, uint32_t 
 
 enum {
 	K_EMBED = 0, K_LM_HEAD = 1, K_FINAL_NORM = 2,
+	K_EMBED_PLE = 3, K_PLE_MODEL_PROJ = 4, K_PLE_PROJ_NORM = 5, /* Gemma, global */
 	K_WQ = 8, K_WK = 9, K_WV = 10, K_WO = 11, K_WGATE = 12, K_WUP = 13, K_WDOWN = 14,
 	K_ATTN_NORM = 15, K_FFN_NORM = 16,
+	K_Q_NORM = 17, K_K_NORM = 18, K_POST_ATTN_NORM = 19, K_POST_FFN_NORM = 20, /* Gemma, per layer */
+	K_PLE_GATE = 21, K_PLE_PROJ = 22, K_PLE_POST_NORM = 23,
 };
 
 typedef struct OrcLayer {
 	void *wq, *wk, *wv, *wo, *wg, *wu, *wd, *attn_norm, *ffn_norm;
+	/* Gemma */
+	void *q_norm, *k_norm, *post_attn_norm, *post_ffn_norm, *ple_gate, *ple_proj, *ple_post_norm;
 } OrcLayer;
 
 struct OrcModel {
 	OrcConfig cfg;
 	int       n_threads;
 	void*     embed;
-	void*     lm_head;
+	void*     lm_head;   /* the embedding itself for Gemma (tied) */
 	void*     final_norm;
+	void*     embed_ple;      /* Gemma: [vocab][n_layers * ple_dim] */
+	void*     ple_model_proj; /* Gemma: [n_layers * ple_dim][dim] */
+	void*     ple_proj_norm;  /* Gemma: [ple_dim] */
 	OrcLayer* layers;
 	float*    rope_cos;
 	float*    rope_sin;
@@ -388,6 +396,9 @@ const void* orc_model_weight(const OrcModel* m, int32_t layer, uint32_t kind)
 		case K_EMBED: return m->embed;
 		case K_LM_HEAD: return m->lm_head;
 		case K_FINAL_NORM: return m->final_norm;
+		case K_EMBED_PLE: return m->embed_ple;
+		case K_PLE_MODEL_PROJ: return m->ple_model_proj;
+		case K_PLE_PROJ_NORM: return m->ple_proj_norm;
 		default: return NULL;
 		}
 	}
@@ -403,6 +414,13 @@ const void* orc_model_weight(const OrcModel* m, int32_t layer, uint32_t kind)
 	case K_WDOWN: return L->wd;
 	case K_ATTN_NORM: return L->attn_norm;
 	case K_FFN_NORM: return L->ffn_norm;
+	case K_Q_NORM: return L->q_norm;
+	case K_K_NORM: return L->k_norm;
+	case K_POST_ATTN_NORM: return L->post_attn_norm;
+	case K_POST_FFN_NORM: return L->post_ffn_norm;
+	case K_PLE_GATE: return L->ple_gate;
+	case K_PLE_PROJ: return L->ple_proj;
+	case K_PLE_POST_NORM: return L->ple_post_norm;
 	default: return NULL;
 	}
 }
@@ -410,7 +428,7 @@ const void* orc_model_weight(const OrcModel* m, int32_t layer, uint32_t kind)
 OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 {
 	if (!cfg || cfg->n_heads == 0 || cfg->n_kv_heads == 0 || cfg->n_heads % cfg->n_kv_heads || cfg->head_dim % 2 ||
-	    cfg->head_dim > 512 ||
+	    cfg->head_dim > 512 || cfg->arch > 1 || (cfg->arch == 0 && (cfg->ple_dim || cfg->final_softcap != 0.0f)) ||
 	    cfg->n_slots == 0 || cfg->max_seq == 0)
 		return NULL;
 #ifdef _OPENMP
@@ -422,9 +440,18 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 	m->n_threads = n_threads;
 	const uint64_t V = cfg->vocab, d = cfg->dim, H = cfg->n_heads, KV = cfg->n_kv_heads, hd = cfg->head_dim,
 	               F = cfg->ffn, L = cfg->n_layers;
+	const int gemma = cfg->arch == 1;
+	const uint64_t P = cfg->ple_dim;
+	/* norm gains: 1.0 for Llama; Gemma scales by (1 + w), so its w are drawn like the weights */
+#define NORM(layer, kind, n) (gemma ? gen_tensor(m, seed, (layer), (kind), (n)) : ones_tensor(m, (n)))
 	m->embed = gen_tensor(m, seed, -1, K_EMBED, V * d);
-	m->lm_head = gen_tensor(m, seed, -1, K_LM_HEAD, V * d);
-	m->final_norm = ones_tensor(m, d);
+	m->lm_head = gemma ? m->embed : gen_tensor(m, seed, -1, K_LM_HEAD, V * d);
+	m->final_norm = NORM(-1, K_FINAL_NORM, d);
+	if (gemma && P) {
+		m->embed_ple = gen_tensor(m, seed, -1, K_EMBED_PLE, V * L * P);
+		m->ple_model_proj = gen_tensor(m, seed, -1, K_PLE_MODEL_PROJ, L * P * d);
+		m->ple_proj_norm = gen_tensor(m, seed, -1, K_PLE_PROJ_NORM, P);
+	}
 	m->layers = (OrcLayer*)calloc(L, sizeof(OrcLayer));
 	for (uint32_t l = 0; l < L; ++l) {
 		OrcLayer* Ly = &m->layers[l];
@@ -435,9 +462,21 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 		Ly->wg = gen_tensor(m, seed, (int32_t)l, K_WGATE, F * d);
 		Ly->wu = gen_tensor(m, seed, (int32_t)l, K_WUP, F * d);
 		Ly->wd = gen_tensor(m, seed, (int32_t)l, K_WDOWN, d * F);
-		Ly->attn_norm = ones_tensor(m, d);
-		Ly->ffn_norm = ones_tensor(m, d);
+		Ly->attn_norm = NORM((int32_t)l, K_ATTN_NORM, d);
+		Ly->ffn_norm = NORM((int32_t)l, K_FFN_NORM, d);
+		if (gemma) {
+			Ly->q_norm = gen_tensor(m, seed, (int32_t)l, K_Q_NORM, hd);
+			Ly->k_norm = gen_tensor(m, seed, (int32_t)l, K_K_NORM, hd);
+			Ly->post_attn_norm = gen_tensor(m, seed, (int32_t)l, K_POST_ATTN_NORM, d);
+			Ly->post_ffn_norm = gen_tensor(m, seed, (int32_t)l, K_POST_FFN_NORM, d);
+			if (P) {
+				Ly->ple_gate = gen_tensor(m, seed, (int32_t)l, K_PLE_GATE, P * d);
+				Ly->ple_proj = gen_tensor(m, seed, (int32_t)l, K_PLE_PROJ, d * P);
+				Ly->ple_post_norm = gen_tensor(m, seed, (int32_t)l, K_PLE_POST_NORM, d);
+			}
+		}
 	}
+#undef NORM
 	m->rope_cos = (float*)malloc(sizeof(float) * cfg->max_seq * (hd / 2));
 	m->rope_sin = (float*)malloc(sizeof(float) * cfg->max_seq * (hd / 2));
 	orc_rope_table(cfg->max_seq, (uint32_t)hd, cfg->rope_theta, m->rope_cos, m->rope_sin);
@@ -451,7 +490,8 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 	m->dbg_att = (float*)calloc(H * hd, 4);
 	m->dbg_h = (float*)calloc(F, 4);
 	m->dbg_r = (float*)calloc(d, 4);
-	if (!m->embed || !m->lm_head || !m->kcache || !m->vcache || !m->logits) {
+	if (!m->embed || !m->lm_head || !m->kcache || !m->vcache || !m->logits ||
+	    (cfg->arch == 1 && cfg->ple_dim && (!m->embed_ple || !m->ple_model_proj || !m->ple_proj_norm))) {
 		orc_model_destroy(m);
 		return NULL;
 	}
@@ -466,12 +506,16 @@ OrcModel* orc_model_create(const OrcConfig* cfg, uint64_t seed, int n_threads)
 void orc_model_destroy(OrcModel* m)
 {
 	if (!m) return;
-	free(m->embed); free(m->lm_head); free(m->final_norm);
+	if (m->lm_head != m->embed) free(m->lm_head);
+	free(m->embed); free(m->final_norm);
+	free(m->embed_ple); free(m->ple_model_proj); free(m->ple_proj_norm);
 	if (m->layers) {
 		for (uint32_t l = 0; l < m->cfg.n_layers; ++l) {
 			OrcLayer* Ly = &m->layers[l];
 			free(Ly->wq); free(Ly->wk); free(Ly->wv); free(Ly->wo);
 			free(Ly->wg); free(Ly->wu); free(Ly->wd); free(Ly->attn_norm); free(Ly->ffn_norm);
+			free(Ly->q_norm); free(Ly->k_norm); free(Ly->post_attn_norm); free(Ly->post_ffn_norm);
+			free(Ly->ple_gate); free(Ly->ple_proj); free(Ly->ple_post_norm);
 		}
 		free(m->layers);
 	}
@@ -708,6 +752,199 @@ static int forward_block(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32
 	return 0;
 }
 
+/* ---- Gemma-style decoder (arch 1; see OrcConfig) ------------------------------------ */
+
+/* the model's constants (embedding and per-layer-input scales) are rounded to bf16 (RNE) from
+ * double, for fp32 models too */
+static inline float bf16_const(double v) { return bf16f(f2bf((float)v)); }
+
+static inline double gelu_tanh(double x)
+{
+	return 0.5 * x * (1.0 + tanh(0.7978845608028654 * (x + 0.044715 * x * x * x)));
+}
+
+/* y = (x * (1/sqrt(mean(x^2) + eps))) * (1 + w), fp32 products in that order, not rounded */
+static void rms1p(const float* x, uint32_t dim, const void* g, int gbf, float eps, float* y)
+{
+	const float inv = rms_inv(x, dim, eps);
+	for (uint32_t i = 0; i < dim; ++i) y[i] = (x[i] * inv) * (1.0f + wval(g, gbf, i));
+}
+
+/* r += rms1p(x) */
+static void add_rms1p(float* r, const float* x, uint32_t dim, const void* g, int gbf, float eps)
+{
+	const float inv = rms_inv(x, dim, eps);
+	for (uint32_t i = 0; i < dim; ++i) r[i] = r[i] + (x[i] * inv) * (1.0f + wval(g, gbf, i));
+}
+
+static int forward_block_gemma(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t T, uint32_t pos0,
+                               float* logits_all, float* logits_last)
+{
+	const OrcConfig* c = &m->cfg;
+	const int bf = (int)c->bf16;
+	const uint32_t d = c->dim, H = c->n_heads, KV = c->n_kv_heads, hd = c->head_dim, F = c->ffn, L = c->n_layers;
+	const uint32_t P = c->ple_dim, group = H / KV, half = hd / 2;
+	const float attn_scale = (float)(1.0 / sqrt((double)hd));
+	const float eps = c->eps;
+	const float es = bf16_const(sqrt((double)d));
+	OrcBlockBufs B;
+	int rc = block_alloc(c, T, &B);
+	if (rc) return rc;
+	float* ple = NULL;  /* [T][L][P] bf16 values */
+	float* ptmp = NULL; /* [T][max(L*P, d)] */
+	if (P) {
+		ple = (float*)malloc(4 * (uint64_t)T * L * P);
+		ptmp = (float*)malloc(4 * (uint64_t)T * ((uint64_t)L * P > d ? (uint64_t)L * P : d));
+		if (!ple || !ptmp) {
+			free(ple);
+			free(ptmp);
+			block_free(&B);
+			return -5;
+		}
+	}
+	for (uint32_t t = 0; t < T; ++t)
+		for (uint32_t i = 0; i < d; ++i) B.r[(uint64_t)t * d + i] = wval(m->embed, bf, (uint64_t)ids[t] * d + i) * es;
+	if (P) {
+		/* per-layer inputs: (E_ple[id] * sqrt(P) + rms1p(W_pmp . bf16(r) * dim^-1/2)) * 2^-1/2 */
+		const float s_ple = bf16_const(sqrt((double)P)), s_proj = bf16_const(1.0 / sqrt((double)d)),
+		            s_sum = bf16_const(1.0 / sqrt(2.0));
+		for (uint64_t i = 0; i < (uint64_t)T * d; ++i) B.xh[i] = round_store(B.r[i], bf);
+		matmat(m->ple_model_proj, bf, (uint64_t)L * P, d, B.xh, T, ptmp);
+		float* nb = (float*)malloc(4 * (uint64_t)P);
+		if (!nb) {
+			free(ple);
+			free(ptmp);
+			block_free(&B);
+			return -5;
+		}
+		for (uint32_t t = 0; t < T; ++t)
+			for (uint32_t l = 0; l < L; ++l) {
+				float* v = ptmp + ((uint64_t)t * L + l) * P;
+				for (uint32_t j = 0; j < P; ++j) v[j] = v[j] * s_proj;
+				rms1p(v, P, m->ple_proj_norm, bf, eps, nb);
+				for (uint32_t j = 0; j < P; ++j) {
+					const float a = wval(m->embed_ple, bf, (uint64_t)ids[t] * L * P + (uint64_t)l * P + j) * s_ple;
+					ple[((uint64_t)t * L + l) * P + j] = round_store((a + nb[j]) * s_sum, bf);
+				}
+			}
+		free(nb);
+	}
+	for (uint32_t l = 0; l < L; ++l) {
+		const OrcLayer* Ly = &m->layers[l];
+		for (uint32_t t = 0; t < T; ++t) {
+			rms1p(B.r + (uint64_t)t * d, d, Ly->attn_norm, bf, eps, B.xh + (uint64_t)t * d);
+			for (uint32_t i = 0; i < d; ++i) B.xh[(uint64_t)t * d + i] = round_store(B.xh[(uint64_t)t * d + i], bf);
+		}
+		matmat(Ly->wq, bf, (uint64_t)H * hd, d, B.xh, T, B.q);
+		matmat(Ly->wk, bf, (uint64_t)KV * hd, d, B.xh, T, B.k);
+		matmat(Ly->wv, bf, (uint64_t)KV * hd, d, B.xh, T, B.v);
+		for (uint32_t t = 0; t < T; ++t) {
+			const uint32_t pos = pos0 + t;
+			const float* cs = m->rope_cos + (uint64_t)pos * half;
+			const float* sn = m->rope_sin + (uint64_t)pos * half;
+			float* q = B.q + (uint64_t)t * H * hd;
+			float* k = B.k + (uint64_t)t * KV * hd;
+			float* v = B.v + (uint64_t)t * KV * hd;
+			float tmp[512];
+			for (uint32_t h = 0; h < H; ++h) {
+				rms1p(q + (uint64_t)h * hd, hd, Ly->q_norm, bf, eps, tmp);
+				memcpy(q + (uint64_t)h * hd, tmp, 4 * hd);
+			}
+			for (uint32_t h = 0; h < KV; ++h) {
+				rms1p(k + (uint64_t)h * hd, hd, Ly->k_norm, bf, eps, tmp);
+				memcpy(k + (uint64_t)h * hd, tmp, 4 * hd);
+			}
+			rope_inplace(q, H, hd, cs, sn);
+			rope_inplace(k, KV, hd, cs, sn);
+			for (uint32_t i = 0; i < H * hd; ++i) q[i] = round_store(q[i], bf);
+			for (uint32_t i = 0; i < KV * hd; ++i) {
+				k[i] = round_store(k[i], bf);
+				v[i] = round_store(v[i], bf);
+			}
+			memcpy(kv_at(m, m->kcache, slot, l, pos), k, sizeof(float) * KV * hd);
+			memcpy(kv_at(m, m->vcache, slot, l, pos), v, sizeof(float) * KV * hd);
+		}
+#pragma omp parallel for schedule(dynamic, 1)
+		for (int64_t th = 0; th < (int64_t)T * H; ++th) {
+			const uint32_t t = (uint32_t)(th / H), h = (uint32_t)(th % H);
+			const uint32_t g = h / group, ctx = pos0 + t + 1;
+			const float* qh = B.q + (uint64_t)t * H * hd + (uint64_t)h * hd;
+			float* sc = B.scores + (uint64_t)omp_get_thread_num() * c->max_seq;
+			double mx = -INFINITY;
+			for (uint32_t p = 0; p < ctx; ++p) {
+				const float s = (float)dot_f32_d(kv_at(m, m->kcache, slot, l, p) + (uint64_t)g * hd, qh, hd) * attn_scale;
+				sc[p] = s;
+				if (s > mx) mx = s;
+			}
+			double den = 0.0;
+			for (uint32_t p = 0; p < ctx; ++p) {
+				sc[p] = (float)exp((double)sc[p] - mx);
+				den += sc[p];
+			}
+			double acc[512];
+			for (uint32_t i = 0; i < hd; ++i) acc[i] = 0.0;
+			for (uint32_t p = 0; p < ctx; ++p) {
+				const float* vt = kv_at(m, m->vcache, slot, l, p) + (uint64_t)g * hd;
+				for (uint32_t i = 0; i < hd; ++i) acc[i] += (double)sc[p] * (double)vt[i];
+			}
+			float* oh = B.att + (uint64_t)t * H * hd + (uint64_t)h * hd;
+			for (uint32_t i = 0; i < hd; ++i) oh[i] = round_store((float)(acc[i] / den), bf);
+		}
+		if (l == 0) {
+			const uint32_t t = T - 1;
+			memcpy(m->dbg_q, B.q + (uint64_t)t * H * hd, sizeof(float) * H * hd);
+			memcpy(m->dbg_k, B.k + (uint64_t)t * KV * hd, sizeof(float) * KV * hd);
+			memcpy(m->dbg_v, B.v + (uint64_t)t * KV * hd, sizeof(float) * KV * hd);
+			memcpy(m->dbg_att, B.att + (uint64_t)t * H * hd, sizeof(float) * H * hd);
+		}
+		matmat(Ly->wo, bf, d, (uint64_t)H * hd, B.att, T, B.o);
+		for (uint32_t t = 0; t < T; ++t) add_rms1p(B.r + (uint64_t)t * d, B.o + (uint64_t)t * d, d, Ly->post_attn_norm, bf, eps);
+		for (uint32_t t = 0; t < T; ++t) {
+			rms1p(B.r + (uint64_t)t * d, d, Ly->ffn_norm, bf, eps, B.xh + (uint64_t)t * d);
+			for (uint32_t i = 0; i < d; ++i) B.xh[(uint64_t)t * d + i] = round_store(B.xh[(uint64_t)t * d + i], bf);
+		}
+		matmat(Ly->wg, bf, F, d, B.xh, T, B.gate);
+		matmat(Ly->wu, bf, F, d, B.xh, T, B.up);
+		for (uint64_t j = 0; j < (uint64_t)T * F; ++j)
+			B.h[j] = round_store((float)(gelu_tanh((double)B.gate[j]) * (double)B.up[j]), bf);
+		if (l == 0) memcpy(m->dbg_h, B.h + (uint64_t)(T - 1) * F, sizeof(float) * F);
+		matmat(Ly->wd, bf, d, F, B.h, T, B.o);
+		for (uint32_t t = 0; t < T; ++t) add_rms1p(B.r + (uint64_t)t * d, B.o + (uint64_t)t * d, d, Ly->post_ffn_norm, bf, eps);
+		if (P) {
+			/* per-layer-embedding block: r += rms1p(W_proj . bf16(gelu_tanh(W_gate . bf16(r)) * ple_l)) */
+			for (uint64_t i = 0; i < (uint64_t)T * d; ++i) B.xh[i] = round_store(B.r[i], bf);
+			matmat(Ly->ple_gate, bf, P, d, B.xh, T, ptmp);
+			for (uint32_t t = 0; t < T; ++t)
+				for (uint32_t j = 0; j < P; ++j) {
+					const uint64_t i = (uint64_t)t * P + j;
+					B.h[i] = round_store((float)(gelu_tanh((double)ptmp[i]) * (double)ple[((uint64_t)t * L + l) * P + j]), bf);
+				}
+			matmat(Ly->ple_proj, bf, d, P, B.h, T, B.o);
+			for (uint32_t t = 0; t < T; ++t) add_rms1p(B.r + (uint64_t)t * d, B.o + (uint64_t)t * d, d, Ly->ple_post_norm, bf, eps);
+		}
+		if (l == 0) memcpy(m->dbg_r, B.r + (uint64_t)(T - 1) * d, sizeof(float) * d);
+	}
+	const uint32_t t0 = logits_all ? 0 : T - 1;
+	for (uint32_t t = t0; t < T; ++t) {
+		rms1p(B.r + (uint64_t)t * d, d, m->final_norm, bf, eps, B.xh + (uint64_t)(t - t0) * d);
+		for (uint32_t i = 0; i < d; ++i) B.xh[(uint64_t)(t - t0) * d + i] = round_store(B.xh[(uint64_t)(t - t0) * d + i], bf);
+	}
+	float* lo = logits_all ? logits_all : logits_last;
+	if (lo) {
+		matmat(m->lm_head, bf, c->vocab, d, B.xh, T - t0, lo);
+		if (c->final_softcap > 0.0f) {
+			const double cap = c->final_softcap;
+			for (uint64_t i = 0; i < (uint64_t)(T - t0) * c->vocab; ++i) lo[i] = (float)(cap * tanh((double)lo[i] / cap));
+		}
+		if (logits_all && logits_last)
+			memcpy(logits_last, logits_all + (uint64_t)(T - 1) * c->vocab, sizeof(float) * c->vocab);
+	}
+	free(ple);
+	free(ptmp);
+	block_free(&B);
+	return 0;
+}
+
 int orc_forward(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t n, uint32_t start_pos,
                 float* logits_all, float* logits_last, uint32_t* argmax_last)
 {
@@ -720,7 +957,8 @@ int orc_forward(OrcModel* m, uint32_t slot, const uint32_t* ids, uint32_t n, uin
 		const uint32_t T = (n - t0 < (uint32_t)kOrcBlock) ? n - t0 : (uint32_t)kOrcBlock;
 		const int last = (t0 + T == n);
 		float* la = logits_all ? logits_all + (uint64_t)t0 * c->vocab : NULL;
-		const int rc = forward_block(m, slot, ids + t0, T, start_pos + t0, la, last ? m->logits : NULL);
+		const int rc = c->arch == 1 ? forward_block_gemma(m, slot, ids + t0, T, start_pos + t0, la, last ? m->logits : NULL)
+		                            : forward_block(m, slot, ids + t0, T, start_pos + t0, la, last ? m->logits : NULL);
 		if (rc) return rc;
 	}
 	if (n > 0) {

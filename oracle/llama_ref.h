@@ -38,6 +38,18 @@ typedef struct OrcConfig {
 	float    eps;
 	float    rope_theta;
 	float    init_std;
+	/* Gemma-style decoder (arch 1), the features the reference lists as TODO for Gemma-4
+	 * (src/model.cuh:11 global_head_dim, :32-41 per-layer embeddings and the q/k, post-attention,
+	 * pre- and post-FFN norms, :51-55 the MLP and the PLE block); none has reference code, so
+	 * they are defined here from the published Gemma architecture:
+	 *   r = E[id] * bf16(sqrt(dim)); every RMSNorm scales by (1 + w); per head, q and k are
+	 *   RMS-normalised (gains [head_dim]) before RoPE; the attention and MLP outputs are
+	 *   RMS-normalised before their residual adds; the MLP is gelu_tanh(gate) * up; with
+	 *   ple_dim > 0 each layer ends with the per-layer-embedding block; the LM head is the
+	 *   embedding; final logits c * tanh(l / c) when final_softcap c > 0. */
+	uint32_t arch;          /* 0: Llama, 1: Gemma-style */
+	uint32_t ple_dim;       /* per-layer embedding width (Gemma; 0: none) */
+	float    final_softcap; /* Gemma; 0: none */
 } OrcConfig;
 
 typedef struct OrcModel OrcModel;
@@ -82,7 +94,8 @@ int orc_generate(OrcModel* m, uint32_t slot, const uint32_t* prompt, uint32_t n_
 int orc_fill_kv_synthetic(OrcModel* m, uint32_t slot, uint32_t ctx, uint64_t seed);
 /* per-stage debug output of the last forward (layer 0 only): q,k,v after RoPE, attention out */
 int orc_last_layer0(const OrcModel* m, float* q, float* k, float* v, float* attn);
-/* layer 0 SwiGLU product h and the residual after layer 0, of the last token */
+/* layer 0 MLP product h (SwiGLU, or GELU-tanh for Gemma) and the residual after layer 0, of the
+ * last token */
 int orc_last_layer0_mlp(const OrcModel* m, float* h, float* resid);
 /* K and V the cache holds for (slot, layer, pos): [n_kv_heads * head_dim] each */
 int orc_kv_read(const OrcModel* m, uint32_t slot, uint32_t layer, uint32_t pos, float* k, float* v);

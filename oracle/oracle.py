@@ -19,7 +19,9 @@ REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_kernels.so")
 
 # tensor kinds (orc_tensor_stream)
 K_EMBED, K_LM_HEAD, K_FINAL_NORM = 0, 1, 2
+K_EMBED_PLE, K_PLE_MODEL_PROJ, K_PLE_PROJ_NORM = 3, 4, 5  # Gemma-style models
 K_WQ, K_WK, K_WV, K_WO, K_WGATE, K_WUP, K_WDOWN, K_ATTN_NORM, K_FFN_NORM = range(8, 17)
+K_Q_NORM, K_K_NORM, K_POST_ATTN_NORM, K_POST_FFN_NORM, K_PLE_GATE, K_PLE_PROJ, K_PLE_POST_NORM = range(17, 24)
 
 STREAM_PROMPT = 0x1000000
 STREAM_CTX_LEN = 0x2000000
@@ -30,7 +32,7 @@ class OrcConfig(C.Structure):
         ("vocab", C.c_uint32), ("dim", C.c_uint32), ("n_layers", C.c_uint32), ("n_heads", C.c_uint32),
         ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("ffn", C.c_uint32), ("max_seq", C.c_uint32),
         ("n_slots", C.c_uint32), ("bf16", C.c_uint32), ("eps", C.c_float), ("rope_theta", C.c_float),
-        ("init_std", C.c_float),
+        ("init_std", C.c_float), ("arch", C.c_uint32), ("ple_dim", C.c_uint32), ("final_softcap", C.c_float),
     ]
 
 
@@ -182,7 +184,8 @@ class OracleModel:
             vocab=cfg["vocab"], dim=cfg["dim"], n_layers=cfg["n_layers"], n_heads=cfg["n_heads"],
             n_kv_heads=cfg["n_kv_heads"], head_dim=cfg["head_dim"], ffn=cfg["ffn"], max_seq=cfg["max_seq"],
             n_slots=n_slots, bf16=int(cfg["dtype"] == "bf16"), eps=cfg["eps"], rope_theta=cfg["rope_theta"],
-            init_std=cfg.get("init_std", 0.02),
+            init_std=cfg.get("init_std", 0.02), arch=int(cfg.get("arch", 0)), ple_dim=int(cfg.get("ple_dim", 0)),
+            final_softcap=float(cfg.get("final_softcap", 0.0)),
         )
         self.c = c
         self.h = lib().orc_model_create(C.byref(c), seed, n_threads)

@@ -170,8 +170,130 @@ class NpLlama:
         return np.array(ids, np.uint32), np.stack(logits)
 
 
+def gelu_tanh64(x):
+    x = np.asarray(x, np.float64)
+    return 0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
+
+
+class NpGemma:
+    """The Gemma-style decoder (arch 1 of the oracle) restated in numpy: embedding times
+    bf16(sqrt(dim)), every RMSNorm scaled by (1 + w), per-head RMSNorm of q and k before RoPE,
+    RMSNorm of the attention and MLP outputs before their residual adds, gelu_tanh(gate) * up,
+    the per-layer-embedding block after the MLP, the embedding as LM head, final soft-cap.
+    Projections accumulate in float64 and round to float32."""
+
+    def __init__(self, cfg: dict, seed: int):
+        self.cfg = cfg
+        bf = cfg["dtype"] == "bf16"
+        self.R = bf16_round if bf else (lambda a: np.asarray(a, dtype=np.float32))
+        V, d, L = cfg["vocab"], cfg["dim"], cfg["n_layers"]
+        H, KV, hd, F, P = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ffn"], cfg["ple_dim"]
+        std = cfg.get("init_std", 0.02)
+
+        def gen(layer, kind, shape):
+            t = normal_tensor(seed, tensor_stream(layer, kind), int(np.prod(shape)), std)
+            return self.R(t).reshape(shape)
+
+        self.embed = gen(-1, 0, (V, d))
+        self.final_norm = gen(-1, 2, (d,))
+        if P:
+            self.embed_ple = gen(-1, 3, (V, L * P))
+            self.ple_model_proj = gen(-1, 4, (L * P, d))
+            self.ple_proj_norm = gen(-1, 5, (P,))
+        self.layers = []
+        for l in range(L):
+            W = dict(wq=gen(l, 8, (H * hd, d)), wk=gen(l, 9, (KV * hd, d)), wv=gen(l, 10, (KV * hd, d)),
+                     wo=gen(l, 11, (d, H * hd)), wg=gen(l, 12, (F, d)), wu=gen(l, 13, (F, d)), wd=gen(l, 14, (d, F)),
+                     attn_norm=gen(l, 15, (d,)), ffn_norm=gen(l, 16, (d,)), q_norm=gen(l, 17, (hd,)),
+                     k_norm=gen(l, 18, (hd,)), post_attn=gen(l, 19, (d,)), post_ffn=gen(l, 20, (d,)))
+            if P:
+                W.update(ple_gate=gen(l, 21, (P, d)), ple_proj=gen(l, 22, (d, P)), ple_post=gen(l, 23, (d,)))
+            self.layers.append(W)
+        half = hd // 2
+        p = np.arange(cfg["max_seq"], dtype=np.float64)[:, None]
+        inv = np.power(float(np.float32(cfg["rope_theta"])), -2.0 * np.arange(half, dtype=np.float64) / hd)
+        self.cos = np.cos(p * inv).astype(np.float32)
+        self.sin = np.sin(p * inv).astype(np.float32)
+        self.K = np.zeros((L, cfg["max_seq"], KV, hd), np.float32)
+        self.V = np.zeros_like(self.K)
+        self.dbg = None
+
+    @staticmethod
+    def mv(W, x):
+        return (W.astype(np.float64) @ np.asarray(x, np.float64)).astype(np.float32)
+
+    def rms1p(self, x, w):
+        x = np.asarray(x, np.float32)
+        ss = np.float32(np.dot(x.astype(np.float64), x.astype(np.float64)))
+        inv = np.float32(1.0) / np.sqrt(ss / np.float32(x.size) + np.float32(self.cfg["eps"]), dtype=np.float32)
+        return (x * inv) * (np.float32(1.0) + w.astype(np.float32))
+
+    def rope(self, x, pos):
+        hd = self.cfg["head_dim"]
+        half = hd // 2
+        x = x.reshape(-1, hd).copy()
+        a, b = x[:, :half].copy(), x[:, half:].copy()
+        c, s = self.cos[pos], self.sin[pos]
+        x[:, :half] = a * c - b * s
+        x[:, half:] = b * c + a * s
+        return x.reshape(-1)
+
+    def token(self, tid, pos, want_logits):
+        cfg = self.cfg
+        d, L = cfg["dim"], cfg["n_layers"]
+        H, KV, hd, P = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ple_dim"]
+        R = self.R
+        c32 = lambda v: bf16_round(np.float32(v))  # a constant in the model dtype
+        grp = H // KV
+        r = self.embed[tid].astype(np.float32) * c32(np.sqrt(d))
+        if P:
+            pm = (self.mv(self.ple_model_proj, R(r)) * c32(1.0 / np.sqrt(d))).reshape(L, P)
+            a = self.embed_ple[tid].reshape(L, P) * c32(np.sqrt(P))
+            ple = np.stack([R((a[l] + self.rms1p(pm[l], self.ple_proj_norm)) * c32(1.0 / np.sqrt(2.0)))
+                            for l in range(L)])
+        for l, W in enumerate(self.layers):
+            xh = R(self.rms1p(r, W["attn_norm"]))
+            q = self.mv(W["wq"], xh).reshape(H, hd)
+            k = self.mv(W["wk"], xh).reshape(KV, hd)
+            v = R(self.mv(W["wv"], xh))
+            q = R(self.rope(np.concatenate([self.rms1p(q[h], W["q_norm"]) for h in range(H)]), pos))
+            k = R(self.rope(np.concatenate([self.rms1p(k[h], W["k_norm"]) for h in range(KV)]), pos))
+            self.K[l, pos] = k.reshape(KV, hd)
+            self.V[l, pos] = v.reshape(KV, hd)
+            att = np.zeros(H * hd, np.float32)
+            scale = np.float32(1.0 / np.sqrt(hd))
+            for h in range(H):
+                g = h // grp
+                s = (self.K[l, : pos + 1, g].astype(np.float64) @ q[h * hd:(h + 1) * hd].astype(np.float64)).astype(
+                    np.float32) * scale
+                e = np.exp(s.astype(np.float64) - float(s.max()))
+                att[h * hd:(h + 1) * hd] = (e @ self.V[l, : pos + 1, g].astype(np.float64)) / e.sum()
+            att = R(att)
+            r = r + self.rms1p(self.mv(W["wo"], att), W["post_attn"])
+            xh = R(self.rms1p(r, W["ffn_norm"]))
+            h_ = R((gelu_tanh64(self.mv(W["wg"], xh)) * self.mv(W["wu"], xh).astype(np.float64)).astype(np.float32))
+            if l == 0:
+                self.dbg = (q.copy(), k.copy(), v.copy(), att.copy(), h_.copy())
+            r = r + self.rms1p(self.mv(W["wd"], h_), W["post_ffn"])
+            if P:
+                z = self.mv(W["ple_gate"], R(r))
+                y = R((gelu_tanh64(z) * ple[l].astype(np.float64)).astype(np.float32))
+                r = r + self.rms1p(self.mv(W["ple_proj"], y), W["ple_post"])
+        if not want_logits:
+            return None
+        lg = self.mv(self.embed, R(self.rms1p(r, self.final_norm)))
+        cap = cfg.get("final_softcap", 0.0)
+        if cap > 0:
+            lg = (cap * np.tanh(lg.astype(np.float64) / cap)).astype(np.float32)
+        return lg
+
+    generate = NpLlama.generate
+
+
 TINY = dict(vocab=512, dim=64, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=16, ffn=160, max_seq=64,
             eps=1e-5, rope_theta=10000.0)
+TINY_GEMMA = dict(vocab=512, dim=64, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=32, ffn=128, max_seq=64,
+                  eps=1e-6, rope_theta=10000.0, arch=1, ple_dim=16, final_softcap=30.0)
 
 
 def main():
@@ -188,6 +310,15 @@ def main():
             wd1_tail=m.layers[1]["wd"][-2:].copy(), lm_head_sum=np.float64(m.lm_head.astype(np.float64).sum()),
             rope_cos=m.cos, rope_sin=m.sin)
         print(dtype, "ids", ids)
+    for dtype in ("fp32", "bf16"):
+        cfg = dict(TINY_GEMMA, dtype=dtype)
+        m = NpGemma(cfg, seed=0)
+        prompt = uniform_ids(1, 0x1000000, 8, 0, cfg["vocab"] - 1)
+        ids, logits = m.generate(prompt, 12)
+        q, k, v, att, h = m.dbg
+        np.savez_compressed(os.path.join(HERE, f"tiny_gemma_{dtype}.npz"), prompt=prompt, ids=ids, logits=logits,
+                            layer0_q=q, layer0_k=k, layer0_v=v, layer0_att=att, layer0_h=h)
+        print("gemma", dtype, "ids", ids)
     # synthetic-stream vectors: raw Philox words, ids and context lengths of the workloads
     words = philox_vec(np.arange(4, dtype=np.uint64), stream_key(0, tensor_stream(0, 8)))
     np.savez_compressed(

@@ -92,6 +92,40 @@ def test_oracle_layer0_stages_match_golden(dtype):
     np.testing.assert_allclose(a, g["layer0_att"], atol=tol)
 
 
+TINY_GEMMA = dict(vocab=512, dim=64, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=32, ffn=128, max_seq=64,
+                  eps=1e-6, rope_theta=10000.0, arch=1, ple_dim=16, final_softcap=30.0)
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_gemma_oracle_matches_numpy_restatement(dtype):
+    """The Gemma-style decoder of the C oracle against the independent numpy restatement
+    (tests/golden/gen_golden.py, NpGemma): ids identical, logits and layer-0 stages close."""
+    g = np.load(os.path.join(GOLD, f"tiny_gemma_{dtype}.npz"))
+    m = O.OracleModel(dict(TINY_GEMMA, dtype=dtype), seed=0)
+    ids, logits = m.generate(g["prompt"], 12, want_logits=True)
+    np.testing.assert_array_equal(ids, g["ids"])
+    np.testing.assert_allclose(logits, g["logits"], atol=2e-5, rtol=0)
+    q, k, v, a = m.layer0()
+    h, _ = m.layer0_mlp()
+    tol = 1e-2 if dtype == "bf16" else 1e-5
+    for got, name in ((q, "q"), (k, "k"), (v, "v"), (a, "att"), (h, "h")):
+        np.testing.assert_allclose(got, g[f"layer0_{name}"], atol=tol, err_msg=name)
+    # the LM head is the embedding (tied), and norm gains are drawn, not ones
+    assert m.weight(-1, O.K_LM_HEAD, (4,)).tolist() == m.weight(-1, O.K_EMBED, (4,)).tolist()
+    assert len(set(m.weight(0, O.K_ATTN_NORM, (64,)).tolist())) > 10
+
+
+def test_gemma_prefill_equals_tokenwise():
+    cfg = dict(TINY_GEMMA, dtype="bf16")
+    m = O.OracleModel(cfg, seed=0)
+    ids = O.gen_ids(5, 40, 512)
+    la, _ = m.forward(ids, 0, all_logits=True)
+    m2 = O.OracleModel(cfg, seed=0)
+    for t in range(40):
+        lt, _ = m2.forward(ids[t:t + 1], t)
+        np.testing.assert_array_equal(lt, la[t])
+
+
 def test_rope_table_matches_golden():
     g = np.load(os.path.join(GOLD, "tiny_fp32.npz"))
     cs, sn = O.rope_table(64, 16, 10000.0)
