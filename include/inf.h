@@ -82,7 +82,31 @@ typedef struct InfConfig {
 	u32 tp_rank;
 	u32 tp_size;
 	u32 prefill_attention; /* InfPrefillAttention */
+	u32 arch;           /* InfArch */
+	u32 ple_dim;        /* Gemma: per-layer embedding width (0: none) */
+	f32 final_softcap;  /* Gemma: logits = c * tanh(logit / c) when c > 0 */
 } InfConfig;
+
+/* The decoder family.  Gemma-style models are the features the reference lists as TODO for its
+ * Gemma-4 target (src/model.cuh:11 global_head_dim, :32-41 per-layer embeddings and the q/k,
+ * post-attention, pre- and post-FFN norms, :51-55 the MLP and the PLE block); the reference has
+ * no code for them, so they follow the published Gemma architecture:
+ *   r = E[id] * bf16(sqrt(dim)); every RMSNorm scales by (1 + w) (gains of Gemma models are
+ *   drawn like the weights, not 1.0); per head, q and k are RMS-normalised over head_dim
+ *   (gains [head_dim]) before RoPE; the attention output and the MLP output are RMS-normalised
+ *   before their residual adds; the MLP is gelu_tanh(gate) * up; with ple_dim > 0 a per-layer
+ *   input ple_l = bf16((E_ple[id, l] * bf16(sqrt(ple_dim)) + rmsnorm(W_pmp . bf16(E[id] * s) *
+ *   bf16(dim^-1/2))) * bf16(2^-1/2)) is formed per token and each layer ends with
+ *   r += rmsnorm(W_pp . bf16(gelu_tanh(W_pg . bf16(r)) * ple_l)); the LM head is the embedding;
+ *   logits are soft-capped when final_softcap > 0.  Head dims up to 512 (GQA groups up to 4),
+ *   bf16, one GPU, greedy or sampled batch-1 decode (inf_forward, inf_generate, inf_decode;
+ *   prompts are fed through the decode step token by token); inf_forward_batch and the server
+ *   answer ErrorUnsupported.  Sliding-window layers and Gemma-3n's AltUp/Laurel blocks are not
+ *   implemented. */
+typedef enum InfArch {
+	InfArchLlama = 0,
+	InfArchGemma = 1,
+} InfArch;
 
 /* Which kernel computes causal attention in prefill passes. */
 typedef enum InfPrefillAttention {
@@ -254,7 +278,9 @@ Error_t inf_attn_decode_noalloc(const void* d_q, const void* d_kpool, const void
 
 /* ---- model ------------------------------------------------------------------------- */
 /* Built-in shapes: 1 tiny fp32 (d288), 2 TinyLlama-1.1B, 3 Llama-3-8B, 4 Llama-3-8B batch 64,
- * 5 Llama-3-8B 32k prefill. */
+ * 5 Llama-3-8B 32k prefill, 6 the Gemma-4-E2B shape the reference's comments give
+ * (src/model.cuh:9-14: dim 1536, ffn 6144, global_head_dim 512, 8 heads, vocab 262144, 35
+ * layers) with 2 KV heads, per-layer embeddings of 256, RoPE theta 1e6, eps 1e-6, soft-cap 30. */
 Error_t inf_config_preset(u32 preset, InfConfig* out);
 /* model_build (src/main.cu:200-352).  weights_path NULL: synthetic weights N(0, init_std)
  * from `seed` (Philox4x32-10), gains 1.0.  Otherwise a safetensors checkpoint (one file, a
@@ -382,7 +408,12 @@ Error_t inf_config_from_json(const char* config_path, InfConfig* inout);
  * index, or a missing tensor.  ErrorBadConfig: a shape that does not match config.
  * ErrorUnsupported: a needed tensor in another dtype, or a tensor under the decoder's prefix
  * that this decoder does not use (q/k norms, extra norms, biases, per-layer embeddings: the
- * checkpoint is another model family). */
+ * checkpoint is another model family).  Gemma-style configs (arch InfArchGemma) need, beside the
+ * projections and input_layernorm: layers.<i>.self_attn.{q_norm, k_norm}, post_attention_layernorm
+ * (the norm of the attention output), pre_feedforward_layernorm, post_feedforward_layernorm and,
+ * with ple_dim > 0, per_layer_input_gate, per_layer_projection, post_per_layer_input_norm, plus
+ * embed_tokens_per_layer, per_layer_model_projection and per_layer_projection_norm; their LM head
+ * is the embedding (a separate lm_head.weight is refused). */
 Error_t inf_safetensors_check(const char* weights_path, const InfConfig* config);
 
 /* Weights of the decoder, by their place in the device layout. */
@@ -395,7 +426,18 @@ typedef enum InfWeightKind {
 	InfWGateUp    = 12, /* [2 ffn_dim / tp x dim], rows gate_0, up_0, gate_1, ... */
 	InfWDown      = 14, /* [dim x ffn_dim / tp], rank's columns */
 	InfWAttnNorm  = 15, /* [1 x dim] */
-	InfWFfnNorm   = 16, /* [1 x dim] */
+	InfWFfnNorm   = 16, /* [1 x dim]; Gemma: pre_feedforward_layernorm */
+	/* Gemma-style models (InfArchGemma) */
+	InfWEmbedPle     = 3,  /* [vocab_size x n_layers * ple_dim]  embed_tokens_per_layer */
+	InfWPleModelProj = 4,  /* [n_layers * ple_dim x dim]         per_layer_model_projection */
+	InfWPleProjNorm  = 5,  /* [1 x ple_dim]                      per_layer_projection_norm */
+	InfWQNorm        = 17, /* [1 x head_dim]                     self_attn.q_norm */
+	InfWKNorm        = 18, /* [1 x head_dim]                     self_attn.k_norm */
+	InfWPostAttnNorm = 19, /* [1 x dim]                          post_attention_layernorm */
+	InfWPostFfnNorm  = 20, /* [1 x dim]                          post_feedforward_layernorm */
+	InfWPleGate      = 21, /* [ple_dim x dim]                    per_layer_input_gate */
+	InfWPleProj      = 22, /* [dim x ple_dim]                    per_layer_projection */
+	InfWPlePostNorm  = 23, /* [1 x dim]                          post_per_layer_input_norm */
 } InfWeightKind;
 /* One weight of `layer` (ignored for embed, LM head and final norm) as inf_model_build writes
  * it to rank config->tp_rank's device memory, read from the checkpoint into host memory `out`

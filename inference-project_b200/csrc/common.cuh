@@ -210,5 +210,10 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx)
 __device__ __forceinline__ uint32_t argmax_key_index(unsigned long long k) { return 0xFFFFFFFFu - (uint32_t)k; }
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+// GELU, tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+__device__ __forceinline__ float gelu_tanh(float x)
+{
+	return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
 
 } // namespace inf

@@ -24,6 +24,7 @@
 #include "k_attn_decode_mma.cuh"
 #include "k_attn_cluster.cuh"
 #include "k_gemv.cuh"
+#include "k_gemma.cuh"
 #include "k_attn_prefill.cuh"
 #include "k_attn_prefill_tc.cuh"
 #include "k_gemm_tc.cuh"
@@ -44,6 +45,14 @@ struct LayerW {
 	void* ffn_norm;  // [d]
 	void* kpool;     // [pages][KVl][blk][hd]
 	void* vpool;
+	// Gemma-style decoder
+	void* q_norm;        // [hd]
+	void* k_norm;        // [hd]
+	void* post_attn;     // [d]
+	void* post_ffn;      // [d]
+	void* ple_gate;      // [P x d]
+	void* ple_proj;      // [d x P]
+	void* ple_post;      // [d]
 };
 
 struct InfEngine {
@@ -123,6 +132,19 @@ struct InfEngine {
 	u64 launches = 0;
 	bool profiling = false;
 	bool dry = false; // walk the launch sequence without launching (sets kernel attributes)
+	// Gemma-style decoder (cfg.arch == InfArchGemma)
+	bool gemma = false;
+	void* embed_ple = nullptr;      // [V][L * P]
+	void* ple_model_proj = nullptr; // [L * P][d]
+	void* ple_proj_norm = nullptr;  // [P]
+	float* resid2 = nullptr;        // the second residual buffer (pending adds write the other one)
+	float* raw = nullptr;           // fp32 raw projection output: qkv [(H + 2 KV) hd], or o / down / PLE [d]
+	float* pend = nullptr;          // fp32 [d] projection output waiting for its norm and residual add
+	void* xb = nullptr;             // bf16 [d] rounded embedding (per-layer-input projection)
+	float* pm = nullptr;            // fp32 [L * P]
+	void* ple = nullptr;            // bf16 [L][P] per-layer inputs of the token
+	void* ple_y = nullptr;          // bf16 [P]
+	float* resid_final = nullptr;   // the residual buffer the LM head's prologue wrote
 	// tensor parallelism over peer memory (tp_size > 1)
 	TpComm tpc;                        // size 1 until inf_tp_connect
 	u64 comm_off = 0;                  // offset of this rank's comm region in its arena
@@ -347,6 +369,58 @@ Error_t prof_end(InfEngine* e, int kind)
 
 Error_t enqueue_sample(InfEngine* e);
 
+// Batch-1 decode attention of one layer over the paged cache (q in e->q, output e->attn): one
+// cluster per KV head when the plan fits, else the split-K kernel.
+template <typename T>
+Error_t enqueue_attention(InfEngine* e, const LayerW& L)
+{
+	const InfConfig& c = e->cfg;
+	const int hd = (int)c.head_dim;
+	AttnDecodeArgs a;
+	memset(&a, 0, sizeof a);
+	a.q = e->q;
+	a.kpool = L.kpool;
+	a.vpool = L.vpool;
+	a.block_table = e->block_table;
+	a.pages_per_seq = e->pages_per_seq;
+	a.max_pages = e->n_pages;
+	a.tok_slot = e->slot;
+	a.tok_pos = e->pos;
+	a.H = e->Hl;
+	a.KV = e->KVl;
+	a.hd = hd;
+	a.blk = (int)c.kv_block;
+	a.n_splits = e->attn_splits;
+	a.max_pages_split = e->attn_max_pages_split;
+	a.scale = (float)(1.0 / std::sqrt((double)hd));
+	a.part = e->attn_part;
+	a.counters = e->attn_counters;
+	a.out = e->attn;
+	a.err = e->err;
+	if (e->attn_cl_splits > 0) {
+		a.n_splits = e->attn_cl_splits;
+		a.max_pages_split = e->attn_cl_pages;
+		const int cs = e->attn_cl_splits;
+		const size_t smem = attn_cl_layout(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T), e->attn_cl_pages, cs).total;
+		const AttnKernel<T> ak = attn_decode_cl_kernel<T>(e->Hl / e->KVl, hd);
+		if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+		INF_CUDA_TRY(set_smem(ak, smem));
+		INF_TRY(prof_begin(e));
+		INF_CUDA_TRY(launch_cluster(e, ak, dim3(cs, e->KVl, 1), dim3(kAttnThreads), smem, cs, a));
+		INF_TRY(prof_end(e, InfKAttn));
+	} else {
+		const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
+		                                           e->attn_max_pages_split, e->attn_splits);
+		const AttnKernel<T> ak = attn_decode_kernel<T>(e->Hl / e->KVl, hd);
+		if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
+		INF_CUDA_TRY(set_smem(ak, smem));
+		INF_TRY(prof_begin(e));
+		INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
+		INF_TRY(prof_end(e, InfKAttn));
+	}
+	return Success;
+}
+
 template <typename T>
 Error_t enqueue_decode_step(InfEngine* e)
 {
@@ -386,50 +460,7 @@ Error_t enqueue_decode_step(InfEngine* e)
 			INF_TRY(prof_end(e, InfKQkv));
 		}
 		// attention
-		{
-			AttnDecodeArgs a;
-			memset(&a, 0, sizeof a);
-			a.q = e->q;
-			a.kpool = L.kpool;
-			a.vpool = L.vpool;
-			a.block_table = e->block_table;
-			a.pages_per_seq = e->pages_per_seq;
-			a.max_pages = e->n_pages;
-			a.tok_slot = e->slot;
-			a.tok_pos = e->pos;
-			a.H = e->Hl;
-			a.KV = e->KVl;
-			a.hd = hd;
-			a.blk = (int)c.kv_block;
-			a.n_splits = e->attn_splits;
-			a.max_pages_split = e->attn_max_pages_split;
-			a.scale = (float)(1.0 / std::sqrt((double)hd));
-			a.part = e->attn_part;
-			a.counters = e->attn_counters;
-			a.out = e->attn;
-			a.err = e->err;
-			if (e->attn_cl_splits > 0) {
-				a.n_splits = e->attn_cl_splits;
-				a.max_pages_split = e->attn_cl_pages;
-				const int cs = e->attn_cl_splits;
-				const size_t smem = attn_cl_layout(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T), e->attn_cl_pages, cs).total;
-				const AttnKernel<T> ak = attn_decode_cl_kernel<T>(e->Hl / e->KVl, hd);
-				if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
-				INF_CUDA_TRY(set_smem(ak, smem));
-				INF_TRY(prof_begin(e));
-				INF_CUDA_TRY(launch_cluster(e, ak, dim3(cs, e->KVl, 1), dim3(kAttnThreads), smem, cs, a));
-				INF_TRY(prof_end(e, InfKAttn));
-			} else {
-				const size_t smem = attn_decode_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, sizeof(T),
-				                                           e->attn_max_pages_split, e->attn_splits);
-				const AttnKernel<T> ak = attn_decode_kernel<T>(e->Hl / e->KVl, hd);
-				if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", e->Hl / e->KVl, hd);
-				INF_CUDA_TRY(set_smem(ak, smem));
-				INF_TRY(prof_begin(e));
-				INF_CUDA_TRY(launch(e, ak, dim3(e->KVl, e->attn_splits, 1), dim3(kAttnThreads), smem, a));
-				INF_TRY(prof_end(e, InfKAttn));
-			}
-		}
+		INF_TRY(enqueue_attention<T>(e, L));
 		// O-proj + residual
 		{
 			GemvArgs a = gemv_base(e, L.wo, d, e->Hl * hd);
@@ -488,8 +519,189 @@ Error_t enqueue_decode_step(InfEngine* e)
 	return Success;
 }
 
+// The constants of the Gemma-style decoder, rounded to bf16 from double as the model dtype holds
+// them: the embedding scale sqrt(dim), and sqrt(ple_dim), dim^-1/2 and 2^-1/2 of the per-layer
+// inputs.
+float gemma_const(double v)
+{
+	const uint32_t u = (uint32_t)f32_to_bf16_bits((float)v) << 16;
+	float f;
+	memcpy(&f, &u, 4);
+	return f;
+}
+
+// One decode step of the Gemma-style decoder (bf16, one GPU).  Every projection stores its raw
+// fp32 output; the RMSNorm that follows it (q/k norms, post-attention, post-FFN, post-PLE) runs in
+// the next kernel: a separate kernel for the per-head q/k norms (with RoPE and the KV write), the
+// next projection's prologue for the others, which folds the normalised output into the residual.
+// The residual alternates between two buffers: a prologue that folds reads one and writes the
+// other (from CTA 0), so no CTA of the same kernel reads a half-updated residual.
+Error_t enqueue_decode_step_gemma(InfEngine* e)
+{
+	const InfConfig& c = e->cfg;
+	const int d = (int)c.dim, hd = (int)c.head_dim, P = (int)c.ple_dim, L = (int)c.n_layers;
+	const int H = e->Hl, KV = e->KVl;
+	const int kernels_before = (int)e->launches;
+	float* rbuf[2] = {e->resid, e->resid2};
+	int cur = 0;                     // rbuf[cur] holds the residual
+	const void* pend_gain = nullptr; // gain of the output waiting in e->pend (none: nullptr)
+	auto fold = [&](GemvArgs& a) {
+		a.resid_in = rbuf[cur];
+		if (pend_gain) {
+			a.pend = e->pend;
+			a.pend_gain = pend_gain;
+			a.resid_out = rbuf[cur ^ 1];
+			cur ^= 1;
+			pend_gain = nullptr;
+		}
+	};
+	auto round32 = [](int n) { return (n + 31) / 32 * 32; };
+
+	// embedding * bf16(sqrt(dim)) and, with per-layer embeddings, the token's per-layer inputs
+	INF_TRY(prof_begin(e));
+	{
+		GemmaEmbedArgs a;
+		a.id = e->cur_id;
+		a.vocab = c.vocab_size;
+		a.dim = d;
+		a.table = (const bf16*)e->embed;
+		a.scale = gemma_const(std::sqrt((double)d));
+		a.resid = rbuf[0];
+		a.xb = P ? (bf16*)e->xb : nullptr;
+		a.err = e->err;
+		INF_CUDA_TRY(launch(e, k_gemma_embed, dim3((d + 255) / 256), dim3(256), 0, a));
+	}
+	if (P) {
+		GemvArgs a = gemv_base(e, e->ple_model_proj, L * P, d);
+		a.xin = e->xb;
+		a.out = e->pm;
+		INF_TRY((launch_gemv<bf16, kEpiStoreF32>(e, a)));
+		PleCombineArgs pa;
+		pa.id = e->cur_id;
+		pa.vocab = c.vocab_size;
+		pa.L = L;
+		pa.P = P;
+		pa.pm = e->pm;
+		pa.embed_ple = (const bf16*)e->embed_ple;
+		pa.norm_gain = (const bf16*)e->ple_proj_norm;
+		pa.s_ple = gemma_const(std::sqrt((double)P));
+		pa.s_proj = gemma_const(1.0 / std::sqrt((double)d));
+		pa.s_sum = gemma_const(1.0 / std::sqrt(2.0));
+		pa.eps = c.norm_eps;
+		pa.ple = (bf16*)e->ple;
+		INF_CUDA_TRY(launch(e, k_ple_combine, dim3(L), dim3(round32(P)), 0, pa));
+	}
+	INF_TRY(prof_end(e, InfKEmbed));
+
+	for (int l = 0; l < L; ++l) {
+		const LayerW& W = e->layers[l];
+		// QKV (raw), then per-head q/k RMSNorm + RoPE + KV write
+		INF_TRY(prof_begin(e));
+		{
+			GemvArgs a = gemv_base(e, W.wqkv, (H + 2 * KV) * hd, d);
+			fold(a);
+			a.gain = W.attn_norm;
+			a.gain_plus1 = 1;
+			a.out = e->raw;
+			INF_TRY((launch_gemv<bf16, kEpiStoreF32>(e, a)));
+			QkNormArgs q;
+			q.raw = e->raw;
+			q.H = H;
+			q.KV = KV;
+			q.hd = hd;
+			q.q_gain = (const bf16*)W.q_norm;
+			q.k_gain = (const bf16*)W.k_norm;
+			q.eps = c.norm_eps;
+			q.rope_cos = e->rope_cos;
+			q.rope_sin = e->rope_sin;
+			q.pos = e->pos;
+			q.slot = e->slot;
+			q.q_out = (bf16*)e->q;
+			q.kpool = (bf16*)W.kpool;
+			q.vpool = (bf16*)W.vpool;
+			q.block_table = e->block_table;
+			q.pages_per_seq = e->pages_per_seq;
+			q.max_pages = e->n_pages;
+			q.kv_block = (int)c.kv_block;
+			q.max_seq = (int)c.max_seq;
+			q.err = e->err;
+			INF_CUDA_TRY(launch(e, k_qk_norm_rope, dim3(H + 2 * KV), dim3(round32(hd / 2)), 0, q));
+		}
+		INF_TRY(prof_end(e, InfKQkv));
+		INF_TRY(enqueue_attention<bf16>(e, W));
+		// O (raw) -> pending, post-attention norm
+		INF_TRY(prof_begin(e));
+		{
+			GemvArgs a = gemv_base(e, W.wo, d, H * hd);
+			a.xin = e->attn;
+			a.out = e->pend;
+			INF_TRY((launch_gemv<bf16, kEpiStoreF32>(e, a)));
+			pend_gain = W.post_attn;
+		}
+		INF_TRY(prof_end(e, InfKO));
+		// residual += post-attention norm, pre-FFN norm, gate/up + GELU-tanh
+		INF_TRY(prof_begin(e));
+		{
+			GemvArgs a = gemv_base(e, W.wgu, 2 * e->Fl, d);
+			fold(a);
+			a.gain = W.ffn_norm;
+			a.gain_plus1 = 1;
+			a.out = e->h;
+			INF_TRY((launch_gemv<bf16, kEpiGeglu>(e, a)));
+		}
+		INF_TRY(prof_end(e, InfKGateUp));
+		// down (raw) -> pending, post-FFN norm; the per-layer-embedding block
+		INF_TRY(prof_begin(e));
+		{
+			GemvArgs a = gemv_base(e, W.wd, d, e->Fl);
+			a.xin = e->h;
+			a.out = e->pend;
+			INF_TRY((launch_gemv<bf16, kEpiStoreF32>(e, a)));
+			pend_gain = W.post_ffn;
+		}
+		if (P) {
+			GemvArgs a = gemv_base(e, W.ple_gate, P, d);
+			fold(a);
+			a.no_norm = 1;
+			a.ple = (const bf16*)e->ple + (size_t)l * P;
+			a.out = e->ple_y;
+			INF_TRY((launch_gemv<bf16, kEpiPleGate>(e, a)));
+			a = gemv_base(e, W.ple_proj, d, P);
+			a.xin = e->ple_y;
+			a.out = e->pend;
+			INF_TRY((launch_gemv<bf16, kEpiStoreF32>(e, a)));
+			pend_gain = W.ple_post;
+		}
+		INF_TRY(prof_end(e, InfKDown));
+	}
+	// residual += the last pending output, final norm, LM head (the embedding), soft-cap, argmax
+	{
+		GemvArgs a = gemv_base(e, e->lm_head, e->Vl, d);
+		fold(a);
+		a.gain = e->final_norm;
+		a.gain_plus1 = 1;
+		a.softcap = c.final_softcap;
+		a.logits = e->logits;
+		a.best = e->best;
+		a.counter = e->lm_counter;
+		a.cur_id = e->cur_id;
+		a.out_ids = e->out_ids;
+		a.step = e->step;
+		a.pos_rw = e->pos;
+		a.max_out = e->max_out;
+		INF_TRY(prof_begin(e));
+		INF_TRY((launch_gemv<bf16, kEpiLogits>(e, a)));
+		INF_TRY(enqueue_sample(e));
+		INF_TRY(prof_end(e, InfKLmHead));
+	}
+	e->resid_final = rbuf[cur];
+	e->graph_kernels = (int)e->launches - kernels_before;
+	return Success;
+}
+
 Error_t enqueue_step(InfEngine* e)
 {
+	if (e->gemma) return enqueue_decode_step_gemma(e);
 	return e->cfg.dtype == InfBF16 ? enqueue_decode_step<bf16>(e) : enqueue_decode_step<float>(e);
 }
 
@@ -949,12 +1161,27 @@ Error_t validate(const InfConfig& c)
 	const u32 vec = c.dtype == InfBF16 ? 8 : 4;
 	if (c.dim % vec || c.ffn_dim / tp % vec || (c.n_heads / tp * c.head_dim) % vec)
 		return fail(ErrorBadConfig, "dim, ffn_dim and heads*head_dim must be multiples of %u", vec);
-	if ((c.n_heads / c.n_kv_heads) * c.head_dim * kPfTq > (u32)(kPfThreads * kPfMaxAcc))
+	if (c.arch != InfArchGemma && (c.n_heads / c.n_kv_heads) * c.head_dim * kPfTq > (u32)(kPfThreads * kPfMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kPfThreads * kPfMaxAcc / kPfTq);
+	if (c.arch > InfArchGemma) return fail(ErrorBadConfig, "arch %u", c.arch);
 	{
 		const u32 G = c.n_heads / c.n_kv_heads;
 		if (G != 1 && G != 2 && G != 4 && G != 8) return fail(ErrorUnsupported, "GQA group %u (1, 2, 4 or 8)", G);
-		if (c.head_dim > 256) return fail(ErrorUnsupported, "head_dim above 256");
+		if (c.arch == InfArchGemma) {
+			if (!attn_decode_supported((int)G, (int)c.head_dim))
+				return fail(ErrorUnsupported, "head_dim %u with GQA group %u (up to 512 for groups of at most 4)", c.head_dim, G);
+		} else if (c.head_dim > 256) {
+			return fail(ErrorUnsupported, "head_dim above 256");
+		}
+	}
+	if (c.arch == InfArchGemma) {
+		if (c.dtype != InfBF16) return fail(ErrorUnsupported, "Gemma-style models are bf16");
+		if (tp > 1) return fail(ErrorUnsupported, "Gemma-style models run on one GPU");
+		if (c.head_dim / 2 > 1024) return fail(ErrorUnsupported, "head_dim");
+		if (c.ple_dim % 8 || c.ple_dim > 1024) return fail(ErrorUnsupported, "ple_dim must be a multiple of 8, at most 1024");
+		if (!(c.final_softcap >= 0.0f)) return fail(ErrorBadConfig, "final_softcap");
+	} else if (c.ple_dim || c.final_softcap != 0.0f) {
+		return fail(ErrorBadConfig, "ple_dim and final_softcap belong to Gemma-style models");
 	}
 	if ((c.n_heads / c.n_kv_heads) * c.head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "GQA group x head_dim above %d", kAttnThreads * kAttnMaxAcc);
@@ -1007,23 +1234,36 @@ Error_t generate_weights(InfEngine* e, u64 seed)
 		a.map = kMapPlain;
 		return a;
 	};
-	// embedding: full table on every rank; LM head: vocab rows split across ranks
+	// norm gains: 1.0 for Llama; Gemma-style models scale by (1 + w), so their w are drawn
+	auto norm = [&](int layer, uint32_t kind, void* dst, u64 n) {
+		SynthArgs a = base(layer, kind);
+		a.ones = e->gemma ? 0 : 1;
+		a.canon_cols = n;
+		return synth<T>(e, dst, 1, n, a);
+	};
+	// embedding: full table on every rank; LM head: vocab rows split across ranks (the
+	// embedding itself for Gemma-style models)
 	{
 		SynthArgs a = base(-1, kEmbed);
 		a.canon_cols = d;
 		INF_TRY(synth<T>(e, e->embed, c.vocab_size, d, a));
 	}
-	{
+	if (!e->gemma) {
 		SynthArgs a = base(-1, kLmHead);
 		a.canon_cols = d;
 		a.row_offset = (u64)rk * e->Vl;
 		INF_TRY(synth<T>(e, e->lm_head, e->Vl, d, a));
 	}
-	{
-		SynthArgs a = base(-1, kFinalNorm);
-		a.ones = 1;
+	INF_TRY(norm(-1, kFinalNorm, e->final_norm, d));
+	const u64 P = c.ple_dim;
+	if (e->gemma && P) {
+		SynthArgs a = base(-1, kEmbedPle);
+		a.canon_cols = c.n_layers * P;
+		INF_TRY(synth<T>(e, e->embed_ple, c.vocab_size, c.n_layers * P, a));
+		a = base(-1, kPleModelProj);
 		a.canon_cols = d;
-		INF_TRY(synth<T>(e, e->final_norm, 1, d, a));
+		INF_TRY(synth<T>(e, e->ple_model_proj, c.n_layers * P, d, a));
+		INF_TRY(norm(-1, kPleProjNorm, e->ple_proj_norm, P));
 	}
 	for (u32 l = 0; l < c.n_layers; ++l) {
 		const LayerW& L = e->layers[l];
@@ -1060,7 +1300,24 @@ Error_t generate_weights(InfEngine* e, u64 seed)
 			a.col_offset = (u64)rk * e->Fl;
 			INF_TRY(synth<T>(e, L.wd, d, e->Fl, a));
 		}
-		{
+		if (e->gemma) {
+			INF_TRY(norm((int)l, kAttnNorm, L.attn_norm, d));
+			INF_TRY(norm((int)l, kFfnNorm, L.ffn_norm, d));
+			INF_TRY(norm((int)l, kQNorm, L.q_norm, hd));
+			INF_TRY(norm((int)l, kKNorm, L.k_norm, hd));
+			INF_TRY(norm((int)l, kPostAttnNorm, L.post_attn, d));
+			INF_TRY(norm((int)l, kPostFfnNorm, L.post_ffn, d));
+			if (P) {
+				SynthArgs a = base((int)l, kPleGate);
+				a.canon_cols = d;
+				INF_TRY(synth<T>(e, L.ple_gate, P, d, a));
+				a = base((int)l, kPleProj);
+				a.canon_cols = P;
+				INF_TRY(synth<T>(e, L.ple_proj, d, P, a));
+				INF_TRY(norm((int)l, kPlePostNorm, L.ple_post, d));
+			}
+		} else {
+			// both Llama gains are 1.0 (one stream: the values do not depend on it)
 			SynthArgs a = base((int)l, kAttnNorm);
 			a.ones = 1;
 			a.canon_cols = d;
@@ -1098,6 +1355,7 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	INF_CUDA_TRY(cudaEventCreate(&e->prof_ev[0]));
 	INF_CUDA_TRY(cudaEventCreate(&e->prof_ev[1]));
 	e->esz = c.dtype == InfBF16 ? 2 : 4;
+	e->gemma = c.arch == InfArchGemma;
 	const u32 tp = c.tp_size;
 	e->Hl = (int)(c.n_heads / tp);
 	e->KVl = (int)(c.n_kv_heads / tp);
@@ -1120,12 +1378,19 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	e->pf_tc = c.dtype == InfBF16 && c.prefill_attention == InfPrefillAttnAuto && (hd == 64 || hd == 128) &&
 	           kPtRows % G == 0 && c.kv_block % 8 == 0 && kPtKeys % c.kv_block == 0;
 	const u64 part_floats = std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * e->attn_splits_batch) * (hd + 2);
-	// multi-token passes run on the tensor cores (bf16 models); fp32 models feed tokens one by one
-	e->chunk = c.dtype == InfBF16 ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u)) : 0;
+	// multi-token passes run on the tensor cores (bf16 Llama models); fp32 and Gemma-style models
+	// feed tokens one by one through the decode step
+	e->chunk = c.dtype == InfBF16 && !e->gemma
+	               ? (int)(c.prefill_chunk ? std::min(c.prefill_chunk, c.max_seq) : std::min(c.max_seq, 4096u))
+	               : 0;
 
 	// ---- sizes
 	const u64 w_layer = ((u64)(e->Hl + 2 * e->KVl) * hd * d + d * e->Hl * hd + 2ull * e->Fl * d + d * e->Fl + 2 * d) * es;
-	const u64 w_total = (2ull * c.vocab_size * d) * es + d * es + L * w_layer; // embed is full, LM head is a shard
+	const u64 pl = c.ple_dim;
+	const u64 w_gemma_layer = e->gemma ? (2 * hd + 3 * d + 2 * pl * d) * es + 6 * 256 : 0;
+	const u64 w_gemma = e->gemma ? ((u64)c.vocab_size * L * pl + L * pl * d + pl) * es + 3 * 256 : 0;
+	// embed is full, LM head is a shard (Gemma: the embedding is the LM head)
+	const u64 w_total = ((e->gemma ? 1ull : 2ull) * c.vocab_size * d) * es + d * es + L * (w_layer + w_gemma_layer) + w_gemma;
 	const u64 page_elems = (u64)e->KVl * c.kv_block * hd;
 	const u64 kv_total = 2ull * L * e->n_pages * page_elems * es;
 	const u64 comm = c.tp_size > 1 ? (2ull * c.tp_size * d * 8 + 2ull * c.tp_size * kTpMaxCtas * 4 + 64ull * c.tp_size +
@@ -1134,7 +1399,10 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	const u64 batch_bufs = c.max_batch > 1 ? (u64)c.max_batch * ((u64)e->Vl * 4 + 4 + 8) + 768 : 0;
 	const u64 act = comm + batch_bufs + (c.dtype == InfBF16 ? kGemmPartBytes + 256 : 0) + d * 4 + (u64)e->Hl * hd * es * 2 + (u64)e->Fl * es + (u64)e->Vl * 4 + part_floats * 4 +
 	                (u64)e->chunk * (d * 4 + d * es + 2ull * e->Hl * hd * es + (u64)e->Fl * es + 8) + 16 * 256;
-	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024;
+	const u64 gemma_act = e->gemma ? (d * 4 + std::max<u64>((u64)(e->Hl + 2 * e->KVl) * hd, d) * 4 + d * 4 + d * es +
+	                                  L * pl * 4 + L * pl * es + pl * es + 8 * 256)
+	                               : 0;
+	const u64 slack = (u64)(64 + 16 * L) * 256 + 64ull * 1024 * 1024 + gemma_act;
 	const u64 total = w_total + kv_total + act + (u64)c.max_seq * hd * 4 + (u64)c.max_batch * e->pages_per_seq * 4 +
 	                  (u64)c.max_seq * 8 + slack;
 
@@ -1143,6 +1411,11 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	Pusher P{&e->ctx->dev_arena};
 	const u64 w_begin = arena_dev_pos_get(&e->ctx->dev_arena);
 	P.push(&e->embed, (u64)c.vocab_size * d * es);
+	if (e->gemma && c.ple_dim) {
+		P.push(&e->embed_ple, (u64)c.vocab_size * L * c.ple_dim * es);
+		P.push(&e->ple_model_proj, (u64)L * c.ple_dim * d * es);
+		P.push(&e->ple_proj_norm, (u64)c.ple_dim * es);
+	}
 	e->layers.resize(L);
 	for (u32 l = 0; l < L; ++l) {
 		LayerW& Ly = e->layers[l];
@@ -1152,9 +1425,21 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 		P.push(&Ly.wd, d * e->Fl * es);
 		P.push(&Ly.attn_norm, d * es);
 		P.push(&Ly.ffn_norm, d * es);
+		if (e->gemma) {
+			P.push(&Ly.q_norm, hd * es);
+			P.push(&Ly.k_norm, hd * es);
+			P.push(&Ly.post_attn, d * es);
+			P.push(&Ly.post_ffn, d * es);
+			if (c.ple_dim) {
+				P.push(&Ly.ple_gate, (u64)c.ple_dim * d * es);
+				P.push(&Ly.ple_proj, d * c.ple_dim * es);
+				P.push(&Ly.ple_post, d * es);
+			}
+		}
 	}
 	P.push(&e->final_norm, d * es);
-	P.push(&e->lm_head, (u64)e->Vl * d * es);
+	if (e->gemma) e->lm_head = e->embed;
+	else P.push(&e->lm_head, (u64)e->Vl * d * es);
 	e->weight_bytes = arena_dev_pos_get(&e->ctx->dev_arena) - w_begin;
 	P.push(&e->rope_cos, (u64)c.max_seq * (hd / 2) * 4);
 	P.push(&e->rope_sin, (u64)c.max_seq * (hd / 2) * 4);
@@ -1179,6 +1464,17 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	if (c.dtype == InfBF16) {
 		e->gemm_part_bytes = kGemmPartBytes;
 		P.push(&e->gemm_part, kGemmPartBytes);
+	}
+	if (e->gemma) {
+		P.push(&e->resid2, d * 4);
+		P.push(&e->raw, std::max<u64>((u64)(e->Hl + 2 * e->KVl) * hd, d) * 4);
+		P.push(&e->pend, d * 4);
+		P.push(&e->xb, d * es);
+		if (c.ple_dim) {
+			P.push(&e->pm, (u64)L * c.ple_dim * 4);
+			P.push(&e->ple, (u64)L * c.ple_dim * es);
+			P.push(&e->ple_y, (u64)c.ple_dim * es);
+		}
 	}
 	if (c.max_batch > 1) {
 		P.push(&e->logits_p, (u64)c.max_batch * e->Vl * 4);
@@ -1241,7 +1537,27 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 			w.push_back({li, InfWFfnNorm, Ly.ffn_norm});
 		}
 		w.push_back({0, InfWFinalNorm, e->final_norm});
-		w.push_back({0, InfWLmHead, e->lm_head});
+		if (!e->gemma) w.push_back({0, InfWLmHead, e->lm_head}); // Gemma: the embedding
+		if (e->gemma) {
+			for (u32 l = 0; l < L; ++l) {
+				const LayerW& Ly = e->layers[l];
+				const int li = (int)l;
+				w.push_back({li, InfWQNorm, Ly.q_norm});
+				w.push_back({li, InfWKNorm, Ly.k_norm});
+				w.push_back({li, InfWPostAttnNorm, Ly.post_attn});
+				w.push_back({li, InfWPostFfnNorm, Ly.post_ffn});
+				if (c.ple_dim) {
+					w.push_back({li, InfWPleGate, Ly.ple_gate});
+					w.push_back({li, InfWPleProj, Ly.ple_proj});
+					w.push_back({li, InfWPlePostNorm, Ly.ple_post});
+				}
+			}
+			if (c.ple_dim) {
+				w.push_back({0, InfWEmbedPle, e->embed_ple});
+				w.push_back({0, InfWPleModelProj, e->ple_model_proj});
+				w.push_back({0, InfWPleProjNorm, e->ple_proj_norm});
+			}
+		}
 		INF_TRY(checkpoint_upload(*ck, c, w, e->stream));
 	} else if (c.dtype == InfBF16) {
 		INF_TRY(generate_weights<bf16>(e, seed));
@@ -1382,6 +1698,12 @@ Error_t inf_config_preset(u32 preset, InfConfig* out)
 		c.max_seq = preset == 3 ? 3072 : preset == 4 ? 4352 : 32896;
 		c.max_batch = preset == 4 ? 64 : 1;
 		break;
+	case 6: // the Gemma-4-E2B shape of the reference's comments (src/model.cuh:9-14)
+		c.arch = InfArchGemma;
+		c.vocab_size = 262144; c.dim = 1536; c.n_layers = 35; c.n_heads = 8; c.n_kv_heads = 2; c.head_dim = 512;
+		c.ffn_dim = 6144; c.ple_dim = 256; c.max_seq = 4096; c.dtype = InfBF16; c.rope_theta = 1000000.0f;
+		c.norm_eps = 1e-6f; c.final_softcap = 30.0f;
+		break;
 	default:
 		return fail(ErrorInvalidValue, "unknown preset %u", preset);
 	}
@@ -1444,7 +1766,8 @@ Error_t inf_safetensors_read(const char* weights_path, const InfConfig* config, 
 	InfConfig c;
 	INF_TRY(checkpoint_config(config, &c));
 	if (!out) return fail(ErrorInvalidValue, "inf_safetensors_read: NULL out");
-	const bool per_layer = kind != InfWEmbed && kind != InfWLmHead && kind != InfWFinalNorm;
+	const bool per_layer = kind != InfWEmbed && kind != InfWLmHead && kind != InfWFinalNorm && kind != InfWEmbedPle &&
+	                       kind != InfWPleModelProj && kind != InfWPleProjNorm;
 	if (per_layer && layer >= c.n_layers) return fail(ErrorInvalidValue, "layer %u of %u", layer, c.n_layers);
 	u64 rows, cols;
 	weight_dims(c, kind, &rows, &cols);
@@ -1734,7 +2057,7 @@ Error_t inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 po
 	bool is_f32 = false;
 	std::vector<uint8_t> tmp;
 	switch (buffer) {
-	case InfBufResid: src = e->resid; n = c.dim; is_f32 = true; break;
+	case InfBufResid: src = e->gemma ? e->resid_final : e->resid; n = c.dim; is_f32 = true; break;
 	case InfBufQ: src = e->q; n = (u64)e->Hl * hd; break;
 	case InfBufAttn: src = e->attn; n = (u64)e->Hl * hd; break;
 	case InfBufH: src = e->h; n = (u64)e->Fl; break;
@@ -1790,8 +2113,14 @@ u64 inf_decode_bytes(const InfConfig* c, u32 ctx)
 {
 	if (!c) return 0;
 	const u64 es = c->dtype == InfBF16 ? 2 : 4, d = c->dim, hd = c->head_dim, L = c->n_layers;
-	const u64 layer = ((u64)(c->n_heads + 2 * c->n_kv_heads) * hd * d + d * c->n_heads * hd + 3ull * c->ffn_dim * d + 2 * d) * es;
-	const u64 weights = L * layer + (u64)c->vocab_size * d * es + d * es + d * es; // + LM head, final norm, one embedding row
+	u64 layer = ((u64)(c->n_heads + 2 * c->n_kv_heads) * hd * d + d * c->n_heads * hd + 3ull * c->ffn_dim * d + 2 * d) * es;
+	u64 weights = (u64)c->vocab_size * d * es + d * es + d * es; // LM head, final norm, one embedding row
+	if (c->arch == InfArchGemma) {
+		const u64 P = c->ple_dim;
+		layer += (2 * hd + 3 * d + 2 * P * d) * es;              // q/k/post norms, PLE gate and projection
+		weights += (L * P * d + P + L * P) * es;                   // per-layer-input projection, its norm, one E_ple row
+	}
+	weights += L * layer;
 	const u64 kv = 2ull * L * c->n_kv_heads * hd * es * ((u64)ctx + 1);       // read ctx, write 1
 	return weights + kv;
 }
@@ -1900,7 +2229,7 @@ Error_t attn_plan(u32 kernel, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 hea
 		return fail(ErrorInvalidValue, "attention: bad shape");
 	if (kernel > InfAttnMma) return fail(ErrorInvalidValue, "attention: kernel %u", kernel);
 	const u32 G = n_heads / n_kv_heads;
-	if ((G != 1 && G != 2 && G != 4 && G != 8) || head_dim > 256 || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
+	if (!attn_decode_supported((int)G, (int)head_dim) || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "attention: GQA group %u x head_dim %u", G, head_dim);
 	const size_t esz = dtype == InfBF16 ? 2 : 4;
 	if ((kv_block * head_dim * esz) % 16) return fail(ErrorUnsupported, "attention: page block not a multiple of 16 bytes");

@@ -29,7 +29,7 @@ namespace inf {
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kAttnMaxAcc = 4;          // (G * head_dim) / 256 outputs per thread
+constexpr int kAttnMaxAcc = 8;          // (G * head_dim) / 256 outputs per thread
 constexpr int kAttnMaxPagesSplit = 16;  // mbarriers per CTA
 constexpr int kAttnSmemBudget = 96 * 1024; // page buffers of one CTA
 constexpr int kAttnTokIlp = 4;          // tokens a warp works on at once
@@ -51,7 +51,7 @@ struct AttnDecodeArgs {
 };
 
 // head_dim values per lane of a warp
-inline int attn_vpl(int hd) { return hd <= 32 ? 1 : hd <= 64 ? 2 : hd <= 128 ? 4 : 8; }
+inline int attn_vpl(int hd) { return hd <= 32 ? 1 : hd <= 64 ? 2 : hd <= 128 ? 4 : hd <= 256 ? 8 : 16; }
 
 constexpr size_t kAttnCombineStageMax = 96 * 1024; // larger split partials are combined from global memory
 
@@ -378,9 +378,17 @@ inline AttnKernel<T> attn_decode_kernel(int G, int hd)
 	if (G == g && vpl == v) return k_attn_decode<T, g, v>;
 #define INF_ATTN_G(g) INF_ATTN_CASE(g, 1) INF_ATTN_CASE(g, 2) INF_ATTN_CASE(g, 4) INF_ATTN_CASE(g, 8)
 	INF_ATTN_G(1) INF_ATTN_G(2) INF_ATTN_G(4) INF_ATTN_G(8)
+	// head_dim up to 512 (the Gemma-style decoder's global_head_dim) for groups of at most 4
+	INF_ATTN_CASE(1, 16) INF_ATTN_CASE(2, 16) INF_ATTN_CASE(4, 16)
 #undef INF_ATTN_G
 #undef INF_ATTN_CASE
 	return nullptr;
+}
+
+// whether the split-K kernel serves a GQA group and head_dim
+inline bool attn_decode_supported(int G, int hd)
+{
+	return (G == 1 || G == 2 || G == 4 || G == 8) && hd <= 512 && (hd <= 256 || G <= 4);
 }
 
 

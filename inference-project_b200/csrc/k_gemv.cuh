@@ -10,9 +10,17 @@
 //   kEpiResid   r[row] += dot                           (O-proj and down-proj + residual)
 //   kEpiQkv     RoPE on (i, i+hd/2) row pairs, q -> buffer, k/v -> paged KV cache
 //   kEpiSwiglu  h[j] = round(silu(gate_j) * up_j) on (gate_j, up_j) row pairs
-//   kEpiLogits  logits[row] = dot, then a grid-wide greedy argmax (ties -> lowest index)
+//   kEpiLogits  logits[row] = dot (soft-capped when softcap > 0), then a grid-wide greedy argmax
+//               (ties -> lowest index)
+//   kEpiStoreF32  y[row] = dot in fp32 (raw projections of the Gemma-style decoder)
+//   kEpiGeglu   h[j] = round(gelu_tanh(gate_j) * up_j) on (gate_j, up_j) row pairs
+//   kEpiPleGate y[row] = round(gelu_tanh(dot) * ple[row]) (the per-layer-embedding gate)
 // The prologue either normalises the fp32 residual with the layer's RMSNorm gain
-// (src/cuda/kernels/rmsnorm.cu:11-59 semantics, with eps) or loads a stored vector.
+// (src/cuda/kernels/rmsnorm.cu:11-59 semantics, with eps) or loads a stored vector.  For the
+// Gemma-style decoder it can first fold a pending projection output into the residual,
+// r' = r + (p * rsqrt(mean(p^2) + eps)) * (1 + g_p), written to a second residual buffer by
+// CTA 0 (every CTA computes the same r'), scale the gains by (1 + w), or skip the
+// normalisation (x = round(r')).
 #pragma once
 
 #include "common.cuh"
@@ -29,11 +37,18 @@ constexpr int kGemvPrefetch = 2;    // chunks prefetched into L2 beyond the ring
 constexpr int kGemvFlushRows = 128; // rows per deferred-epilogue window
 constexpr uint32_t kGemvNextPrefetch = 192 * 1024; // bytes of the next projection warmed per CTA
 
-enum EpiKind : int { kEpiStore = 0, kEpiResid = 1, kEpiQkv = 2, kEpiSwiglu = 3, kEpiLogits = 4 };
+enum EpiKind : int {
+	kEpiStore = 0, kEpiResid = 1, kEpiQkv = 2, kEpiSwiglu = 3, kEpiLogits = 4,
+	kEpiStoreF32 = 5, kEpiGeglu = 6, kEpiPleGate = 7,
+};
 
 template <int EPI> struct EpiTraits {
-	static constexpr bool kPaired = (EPI == kEpiQkv || EPI == kEpiSwiglu);
-	static constexpr bool kNorm = (EPI == kEpiQkv || EPI == kEpiSwiglu || EPI == kEpiLogits);
+	static constexpr bool kPaired = (EPI == kEpiQkv || EPI == kEpiSwiglu || EPI == kEpiGeglu);
+	static constexpr bool kNorm = (EPI == kEpiQkv || EPI == kEpiSwiglu || EPI == kEpiLogits || EPI == kEpiGeglu);
+	// the prologue is chosen at run time (norm when resid_in is set, else the stored vector)
+	static constexpr bool kRuntimeProlog = (EPI == kEpiStoreF32 || EPI == kEpiPleGate);
+	// the Gemma-style prologue features (pending add, (1 + w) gains, no-norm) are compiled in
+	static constexpr bool kGemma = (EPI == kEpiStoreF32 || EPI == kEpiGeglu || EPI == kEpiPleGate || EPI == kEpiLogits);
 };
 
 template <int UPL, int EPI> struct GemvShape {
@@ -72,6 +87,14 @@ struct GemvArgs {
 	uint32_t* step;               // logits: index into out_ids
 	int* pos_rw;                  // logits: position advanced after the step
 	int max_out;
+	float softcap;                // logits: c * tanh(logit / c) when c > 0
+	// Gemma-style prologue
+	const float* pend;            // pending projection output fp32 [K] folded into the residual first
+	const void* pend_gain;        // its RMSNorm gain [K] (scaled by 1 + w)
+	float* resid_out;             // r + normed(pend), written by CTA 0
+	int gain_plus1;               // the prologue's gains scale by (1 + w)
+	int no_norm;                  // x = round(r) instead of the RMSNorm
+	const void* ple;              // kEpiPleGate: this layer's per-layer input [N]
 	int* err;
 	// tensor parallelism: tp.size > 1 turns kEpiResid into a fused all-reduce of the rows'
 	// partial sums and kEpiLogits into a cross-shard argmax (logit row + row_base = token id)
@@ -256,7 +279,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 	pdl_wait();
 
 	float xh[UPL][VEC];
-	if constexpr (EpiTraits<EPI>::kNorm) {
+	bool norm_prolog = EpiTraits<EPI>::kNorm;
+	if constexpr (EpiTraits<EPI>::kRuntimeProlog) norm_prolog = a.resid_in != nullptr;
+	if (norm_prolog) {
 		float ss = 0.0f;
 #pragma unroll
 		for (int u = 0; u < UPL; ++u) {
@@ -274,23 +299,91 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 				for (int v = 0; v < VEC; ++v) ss = fmaf(xh[u][v], xh[u][v], ss);
 			}
 		}
-		ss = warp_sum(ss);
-		if (lane == 0) red_ss[warp] = ss;
-		named_bar_sync(1, kGemvConsumers);
-		float tot = 0.0f;
+		if constexpr (EpiTraits<EPI>::kGemma) {
+			if (a.pend) {
+				// r' = r + (p * rsqrt(mean(p^2) + eps)) * (1 + g_p)
+				float pv[UPL][VEC];
+				float sp = 0.0f;
 #pragma unroll
-		for (int w = 0; w < kGemvConsumerWarps; ++w) tot += red_ss[w];
-		const float inv = 1.0f / sqrtf(__fdiv_rn(tot, (float)a.K) + a.eps);
-		const T* g = reinterpret_cast<const T*>(a.gain);
+				for (int u = 0; u < UPL; ++u) {
+					const int unit = u * kGemvConsumers + ct;
 #pragma unroll
-		for (int u = 0; u < UPL; ++u) {
-			const int unit = u * kGemvConsumers + ct;
-			if (unit < units_per_row) {
-				const uint4 gw = *reinterpret_cast<const uint4*>(g + (size_t)unit * VEC);
-				float gf[VEC];
-				unpack_unit(gw, gf, (const T*)nullptr);
+					for (int v = 0; v < VEC; ++v) pv[u][v] = 0.0f;
+					if (unit < units_per_row) {
+						const float* src = a.pend + (size_t)unit * VEC;
 #pragma unroll
-				for (int v = 0; v < VEC; ++v) xh[u][v] = Store<T>::round(__fmul_rn(__fmul_rn(xh[u][v], inv), gf[v]));
+						for (int v = 0; v < VEC; v += 4) {
+							const float4 f = *reinterpret_cast<const float4*>(src + v);
+							pv[u][v] = f.x; pv[u][v + 1] = f.y; pv[u][v + 2] = f.z; pv[u][v + 3] = f.w;
+						}
+#pragma unroll
+						for (int v = 0; v < VEC; ++v) sp = fmaf(pv[u][v], pv[u][v], sp);
+					}
+				}
+				sp = warp_sum(sp);
+				if (lane == 0) red_ss[warp] = sp;
+				named_bar_sync(1, kGemvConsumers);
+				float tp_ = 0.0f;
+#pragma unroll
+				for (int w = 0; w < kGemvConsumerWarps; ++w) tp_ += red_ss[w];
+				named_bar_sync(1, kGemvConsumers); // red_ss is reused below
+				const float invp = 1.0f / sqrtf(__fdiv_rn(tp_, (float)a.K) + a.eps);
+				const T* gp = reinterpret_cast<const T*>(a.pend_gain);
+				ss = 0.0f;
+#pragma unroll
+				for (int u = 0; u < UPL; ++u) {
+					const int unit = u * kGemvConsumers + ct;
+					if (unit < units_per_row) {
+						const uint4 gw = *reinterpret_cast<const uint4*>(gp + (size_t)unit * VEC);
+						float gf[VEC];
+						unpack_unit(gw, gf, (const T*)nullptr);
+#pragma unroll
+						for (int v = 0; v < VEC; ++v)
+							xh[u][v] = __fadd_rn(xh[u][v], __fmul_rn(__fmul_rn(pv[u][v], invp), __fadd_rn(1.0f, gf[v])));
+						if (blockIdx.x == 0 && a.resid_out) {
+							float* dst = a.resid_out + (size_t)unit * VEC;
+#pragma unroll
+							for (int v = 0; v < VEC; v += 4)
+								*reinterpret_cast<float4*>(dst + v) = make_float4(xh[u][v], xh[u][v + 1], xh[u][v + 2], xh[u][v + 3]);
+						}
+#pragma unroll
+						for (int v = 0; v < VEC; ++v) ss = fmaf(xh[u][v], xh[u][v], ss);
+					}
+				}
+			}
+		}
+		bool skip_norm = false;
+		if constexpr (EpiTraits<EPI>::kGemma) skip_norm = a.no_norm != 0;
+		if (skip_norm) {
+#pragma unroll
+			for (int u = 0; u < UPL; ++u)
+#pragma unroll
+				for (int v = 0; v < VEC; ++v) xh[u][v] = Store<T>::round(xh[u][v]);
+		} else {
+			ss = warp_sum(ss);
+			if (lane == 0) red_ss[warp] = ss;
+			named_bar_sync(1, kGemvConsumers);
+			float tot = 0.0f;
+#pragma unroll
+			for (int w = 0; w < kGemvConsumerWarps; ++w) tot += red_ss[w];
+			const float inv = 1.0f / sqrtf(__fdiv_rn(tot, (float)a.K) + a.eps);
+			const T* g = reinterpret_cast<const T*>(a.gain);
+			bool plus1 = false;
+			if constexpr (EpiTraits<EPI>::kGemma) plus1 = a.gain_plus1 != 0;
+#pragma unroll
+			for (int u = 0; u < UPL; ++u) {
+				const int unit = u * kGemvConsumers + ct;
+				if (unit < units_per_row) {
+					const uint4 gw = *reinterpret_cast<const uint4*>(g + (size_t)unit * VEC);
+					float gf[VEC];
+					unpack_unit(gw, gf, (const T*)nullptr);
+					if (plus1) {
+#pragma unroll
+						for (int v = 0; v < VEC; ++v) gf[v] = __fadd_rn(1.0f, gf[v]);
+					}
+#pragma unroll
+					for (int v = 0; v < VEC; ++v) xh[u][v] = Store<T>::round(__fmul_rn(__fmul_rn(xh[u][v], inv), gf[v]));
+				}
 			}
 		}
 	} else {
@@ -359,9 +452,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 			} else if constexpr (EPI == kEpiSwiglu) {
 				Store<T>::put(reinterpret_cast<T*>(a.out) + (row >> 1), __fmul_rn(silu(d0), d1));
 			} else if constexpr (EPI == kEpiLogits) {
+				if (a.softcap > 0.0f) d0 = __fmul_rn(a.softcap, tanhf(__fdiv_rn(d0, a.softcap)));
 				a.logits[row] = d0;
 				const unsigned long long key = argmax_key(d0, (uint32_t)(row + a.row_base));
 				best = key > best ? key : best;
+			} else if constexpr (EPI == kEpiStoreF32) {
+				reinterpret_cast<float*>(a.out)[row] = d0;
+			} else if constexpr (EPI == kEpiGeglu) {
+				Store<T>::put(reinterpret_cast<T*>(a.out) + (row >> 1), __fmul_rn(gelu_tanh(d0), d1));
+			} else if constexpr (EPI == kEpiPleGate) {
+				Store<T>::put(reinterpret_cast<T*>(a.out) + row,
+				              __fmul_rn(gelu_tanh(d0), Store<T>::get(reinterpret_cast<const T*>(a.ple) + row)));
 			} else if constexpr (EPI == kEpiQkv) {
 				const int hd = a.head_dim, half = hd >> 1;
 				const int head = row / hd;

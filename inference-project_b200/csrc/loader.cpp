@@ -536,7 +536,8 @@ Error_t lm_head(const Checkpoint& ck, const InfConfig& c, Need* out)
 // The source tensors of one weight kind: up to three (qkv: q, k, v; gate/up: gate, up).
 Error_t sources(const Checkpoint& ck, const InfConfig& c, int l, uint32_t kind, Need s[3])
 {
-	const uint64_t d = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim;
+	const uint64_t d = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim, P = c.ple_dim;
+	const bool gemma = c.arch == InfArchGemma;
 	switch (kind) {
 	case InfWEmbed: return need(ck, "embed_tokens.weight", c.vocab_size, d, false, &s[0]);
 	case InfWLmHead: return lm_head(ck, c, &s[0]);
@@ -551,13 +552,32 @@ Error_t sources(const Checkpoint& ck, const InfConfig& c, int l, uint32_t kind, 
 		return need(ck, lyr(l, "mlp.up_proj.weight"), F, d, false, &s[1]);
 	case InfWDown: return need(ck, lyr(l, "mlp.down_proj.weight"), d, F, false, &s[0]);
 	case InfWAttnNorm: return need(ck, lyr(l, "input_layernorm.weight"), 0, d, true, &s[0]);
-	case InfWFfnNorm: return need(ck, lyr(l, "post_attention_layernorm.weight"), 0, d, true, &s[0]);
+	// Llama normalises the MLP input with post_attention_layernorm; Gemma uses that name for the
+	// norm of the attention output and pre_feedforward_layernorm for the MLP input
+	case InfWFfnNorm:
+		return need(ck, lyr(l, gemma ? "pre_feedforward_layernorm.weight" : "post_attention_layernorm.weight"), 0, d, true, &s[0]);
+	}
+	if (!gemma) return fail(ErrorInvalidValue, "weight kind %u", kind);
+	switch (kind) {
+	case InfWEmbedPle: return need(ck, "embed_tokens_per_layer.weight", c.vocab_size, c.n_layers * P, false, &s[0]);
+	case InfWPleModelProj: return need(ck, "per_layer_model_projection.weight", c.n_layers * P, d, false, &s[0]);
+	case InfWPleProjNorm: return need(ck, "per_layer_projection_norm.weight", 0, P, true, &s[0]);
+	case InfWQNorm: return need(ck, lyr(l, "self_attn.q_norm.weight"), 0, hd, true, &s[0]);
+	case InfWKNorm: return need(ck, lyr(l, "self_attn.k_norm.weight"), 0, hd, true, &s[0]);
+	case InfWPostAttnNorm: return need(ck, lyr(l, "post_attention_layernorm.weight"), 0, d, true, &s[0]);
+	case InfWPostFfnNorm: return need(ck, lyr(l, "post_feedforward_layernorm.weight"), 0, d, true, &s[0]);
+	case InfWPleGate: return need(ck, lyr(l, "per_layer_input_gate.weight"), P, d, false, &s[0]);
+	case InfWPleProj: return need(ck, lyr(l, "per_layer_projection.weight"), d, P, false, &s[0]);
+	case InfWPlePostNorm: return need(ck, lyr(l, "post_per_layer_input_norm.weight"), 0, d, true, &s[0]);
 	default: return fail(ErrorInvalidValue, "weight kind %u", kind);
 	}
 }
 
 const uint32_t kLayerKinds[] = {InfWQkv, InfWO, InfWGateUp, InfWDown, InfWAttnNorm, InfWFfnNorm};
 const uint32_t kModelKinds[] = {InfWEmbed, InfWLmHead, InfWFinalNorm};
+const uint32_t kGemmaLayerKinds[] = {InfWQNorm, InfWKNorm, InfWPostAttnNorm, InfWPostFfnNorm};
+const uint32_t kGemmaPleLayerKinds[] = {InfWPleGate, InfWPleProj, InfWPlePostNorm};
+const uint32_t kGemmaPleModelKinds[] = {InfWEmbedPle, InfWPleModelProj, InfWPleProjNorm};
 
 inline uint16_t f32_to_bf16_rne(uint32_t u)
 {
@@ -592,11 +612,17 @@ void convert_row(const unsigned char* src, bool src_f32, bool dst_bf16, uint64_t
 // A tensor under the decoder's prefix that this decoder does not use changes the model's
 // function (q/k norms, extra norms, biases, per-layer embeddings of other families): refuse
 // it rather than run a different model.  Buffers that carry no weights are allowed.
-bool decoder_tensor_known(const std::string& rest)
+bool decoder_tensor_known(const std::string& rest, const InfConfig& c)
 {
+	const bool gemma = c.arch == InfArchGemma, ple = gemma && c.ple_dim > 0;
 	static const char* const top[] = {"embed_tokens.weight", "norm.weight"};
 	for (const char* t : top)
 		if (rest == t) return true;
+	static const char* const top_ple[] = {"embed_tokens_per_layer.weight", "per_layer_model_projection.weight",
+	                                      "per_layer_projection_norm.weight"};
+	if (ple)
+		for (const char* t : top_ple)
+			if (rest == t) return true;
 	if (rest.compare(0, 7, "layers.") != 0) return false;
 	size_t k = 7;
 	while (k < rest.size() && rest[k] >= '0' && rest[k] <= '9') ++k;
@@ -609,15 +635,36 @@ bool decoder_tensor_known(const std::string& rest)
 	};
 	for (const char* u : used)
 		if (leaf == u) return true;
+	static const char* const used_gemma[] = {"self_attn.q_norm.weight", "self_attn.k_norm.weight",
+	                                         "pre_feedforward_layernorm.weight", "post_feedforward_layernorm.weight"};
+	static const char* const used_ple[] = {"per_layer_input_gate.weight", "per_layer_projection.weight",
+	                                       "post_per_layer_input_norm.weight"};
+	if (gemma)
+		for (const char* u : used_gemma)
+			if (leaf == u) return true;
+	if (ple)
+		for (const char* u : used_ple)
+			if (leaf == u) return true;
 	return false;
 }
 
 Error_t checkpoint_check(const Checkpoint& ck, const InfConfig& c)
 {
+	const bool gemma = c.arch == InfArchGemma, ple = gemma && c.ple_dim > 0;
 	Need s[3];
-	for (uint32_t k : kModelKinds) INF_TRY(sources(ck, c, 0, k, s));
-	for (uint32_t l = 0; l < c.n_layers; ++l)
+	for (uint32_t k : kModelKinds)
+		if (!(gemma && k == InfWLmHead)) INF_TRY(sources(ck, c, 0, k, s));
+	if (ple)
+		for (uint32_t k : kGemmaPleModelKinds) INF_TRY(sources(ck, c, 0, k, s));
+	for (uint32_t l = 0; l < c.n_layers; ++l) {
 		for (uint32_t k : kLayerKinds) INF_TRY(sources(ck, c, (int)l, k, s));
+		if (gemma)
+			for (uint32_t k : kGemmaLayerKinds) INF_TRY(sources(ck, c, (int)l, k, s));
+		if (ple)
+			for (uint32_t k : kGemmaPleLayerKinds) INF_TRY(sources(ck, c, (int)l, k, s));
+	}
+	if (gemma && ck.tensors.count("lm_head.weight"))
+		return fail(ErrorUnsupported, "lm_head.weight: a Gemma-style model's LM head is its embedding (tied)");
 	// the prefix the embedding was found under is the decoder's
 	std::string emb;
 	find_model(ck, "embed_tokens.weight", &emb);
@@ -626,9 +673,9 @@ Error_t checkpoint_check(const Checkpoint& ck, const InfConfig& c)
 		const std::string& n = t.first;
 		if (n.compare(0, prefix.size(), prefix) != 0) continue; // another component (vision tower, ...)
 		if (prefix == "model." && n.compare(0, 21, "model.language_model.") == 0) continue;
-		if (!decoder_tensor_known(n.substr(prefix.size())))
-			return fail(ErrorUnsupported, "%s: a tensor this Llama decoder does not implement (its model would compute "
-			            "something else)", n.c_str());
+		if (!decoder_tensor_known(n.substr(prefix.size()), c))
+			return fail(ErrorUnsupported, "%s: a tensor this %s decoder does not implement (its model would compute "
+			            "something else)", n.c_str(), gemma ? "Gemma-style" : "Llama");
 	}
 	return Success;
 }
@@ -645,6 +692,12 @@ void weight_dims(const InfConfig& c, uint32_t kind, uint64_t* rows, uint64_t* co
 	case InfWO: r = d; k = Hl * hd; break;
 	case InfWGateUp: r = 2 * Fl; break;
 	case InfWDown: r = d; k = Fl; break;
+	case InfWEmbedPle: r = c.vocab_size; k = (uint64_t)c.n_layers * c.ple_dim; break;
+	case InfWPleModelProj: r = (uint64_t)c.n_layers * c.ple_dim; break;
+	case InfWPleProjNorm: k = c.ple_dim; break;
+	case InfWQNorm: case InfWKNorm: k = hd; break;
+	case InfWPleGate: r = c.ple_dim; break;
+	case InfWPleProj: r = d; k = c.ple_dim; break;
 	default: break; // gains: one row of dim
 	}
 	*rows = r;
@@ -828,11 +881,35 @@ Error_t config_from_json(const char* path, InfConfig* c)
 	}
 	// what the decoder does not implement is refused, not ignored
 	const JVal* mt = m.get("model_type");
-	if (mt && mt->kind == JVal::Str && mt->s != "llama")
-		return fail(ErrorUnsupported, "%s: model_type %s (the Llama decoder only)", path, mt->s.c_str());
+	const bool gemma = mt && mt->kind == JVal::Str && mt->s.compare(0, 5, "gemma") == 0;
+	if (mt && mt->kind == JVal::Str && mt->s != "llama" && !gemma)
+		return fail(ErrorUnsupported, "%s: model_type %s (the Llama and Gemma-style decoders only)", path, mt->s.c_str());
+	o.arch = gemma ? InfArchGemma : InfArchLlama;
+	if (gemma) {
+		// the reference reads global_head_dim (src/main.cu:152); every layer uses it here
+		const JVal* g = m.get("global_head_dim");
+		if (g && g->kind != JVal::Null) INF_TRY(u32f("global_head_dim", &o.head_dim));
+		o.ple_dim = 0;
+		INF_TRY(u32f("hidden_size_per_layer_input", &o.ple_dim));
+		o.final_softcap = 0.0f;
+		INF_TRY(f32f("final_logit_softcapping", &o.final_softcap));
+		// Gemma variants whose blocks this decoder does not compute
+		for (const char* k : {"altup_num_inputs", "laurel_rank", "num_kv_shared_layers", "attn_logit_softcapping",
+		                      "sliding_window"}) {
+			const JVal* v = m.get(k);
+			const bool set = v && v->kind != JVal::Null && !(v->kind == JVal::Num && v->num == 0) &&
+			                 !(v->kind == JVal::Bool && !v->b);
+			if (set) return fail(ErrorUnsupported, "%s: %s (not implemented by the Gemma-style decoder)", path, k);
+		}
+		const JVal* qs = m.get("query_pre_attn_scalar");
+		if (qs && qs->kind == JVal::Num && qs->num != (double)o.head_dim)
+			return fail(ErrorUnsupported, "%s: query_pre_attn_scalar %g (the scale is 1/sqrt(head_dim))", path, qs->num);
+	}
 	for (const char* key : {"hidden_act", "hidden_activation"}) {
 		const JVal* act = m.get(key);
-		if (act && act->kind == JVal::Str && act->s != "silu") return fail(ErrorUnsupported, "%s: %s %s (silu)", path, key, act->s.c_str());
+		const char* want = gemma ? "gelu_pytorch_tanh" : "silu";
+		if (act && act->kind == JVal::Str && act->s != want)
+			return fail(ErrorUnsupported, "%s: %s %s (%s)", path, key, act->s.c_str(), want);
 	}
 	for (const char* k : {"attention_bias", "mlp_bias"}) {
 		const JVal* v = m.get(k);

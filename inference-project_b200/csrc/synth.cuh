@@ -13,7 +13,9 @@ namespace inf {
 
 enum TensorKind : uint32_t {
 	kEmbed = 0, kLmHead = 1, kFinalNorm = 2,
+	kEmbedPle = 3, kPleModelProj = 4, kPleProjNorm = 5, // Gemma-style models
 	kWq = 8, kWk = 9, kWv = 10, kWo = 11, kWgate = 12, kWup = 13, kWdown = 14, kAttnNorm = 15, kFfnNorm = 16,
+	kQNorm = 17, kKNorm = 18, kPostAttnNorm = 19, kPostFfnNorm = 20, kPleGate = 21, kPleProj = 22, kPlePostNorm = 23,
 };
 
 __host__ __device__ inline uint64_t splitmix64(uint64_t x)

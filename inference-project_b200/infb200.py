@@ -27,6 +27,7 @@ ERRORS = {
     14: "ErrorIo", 15: "ErrorUnsupported",
 }
 F32, BF16 = 0, 1
+ARCH_LLAMA, ARCH_GEMMA = 0, 1  # InfArch
 PREFILL_ATTN_AUTO, PREFILL_ATTN_SIMT = 0, 1  # InfPrefillAttention
 KERNEL_KINDS = ["embed", "qkv", "attn", "o_proj", "gate_up", "down", "lm_head"]
 # InfWeightKind: the weights in their device layout
@@ -46,7 +47,8 @@ class InfConfig(C.Structure):
         ("vocab_size", u32), ("dim", u32), ("n_layers", u32), ("n_heads", u32), ("n_kv_heads", u32),
         ("head_dim", u32), ("ffn_dim", u32), ("max_seq", u32), ("max_batch", u32), ("kv_block", u32),
         ("kv_pages", u32), ("prefill_chunk", u32), ("dtype", u32), ("norm_eps", f32), ("rope_theta", f32),
-        ("init_std", f32), ("tp_rank", u32), ("tp_size", u32), ("prefill_attention", u32),
+        ("init_std", f32), ("tp_rank", u32), ("tp_size", u32), ("prefill_attention", u32), ("arch", u32),
+        ("ple_dim", u32), ("final_softcap", f32),
     ]
 
     def as_dict(self) -> dict:
@@ -230,10 +232,14 @@ def weight_shape(cfg: InfConfig, kind: int) -> tuple:
     """Rows and columns of one weight in the device layout of rank cfg.tp_rank."""
     tp = max(1, cfg.tp_size)
     d, hd = cfg.dim, cfg.head_dim
+    L, P = cfg.n_layers, cfg.ple_dim
     return {W_EMBED: (cfg.vocab_size, d), W_LM_HEAD: (cfg.vocab_size // tp, d), W_FINAL_NORM: (1, d),
             W_QKV: ((cfg.n_heads + 2 * cfg.n_kv_heads) // tp * hd, d), W_O: (d, cfg.n_heads // tp * hd),
             W_GATE_UP: (2 * cfg.ffn_dim // tp, d), W_DOWN: (d, cfg.ffn_dim // tp), W_ATTN_NORM: (1, d),
-            W_FFN_NORM: (1, d)}[kind]
+            W_FFN_NORM: (1, d),
+            # Gemma-style models
+            3: (cfg.vocab_size, L * P), 4: (L * P, d), 5: (1, P), 17: (1, hd), 18: (1, hd), 19: (1, d), 20: (1, d),
+            21: (P, d), 22: (d, P), 23: (1, d)}[kind]
 
 
 def safetensors_read(path: str, cfg: InfConfig, layer: int, kind: int) -> np.ndarray:
@@ -361,9 +367,12 @@ class Server:
 
 def oracle_dict(c: InfConfig) -> dict:
     """The same model as a dict for oracle/oracle.py (tests only)."""
-    return dict(vocab=c.vocab_size, dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads, n_kv_heads=c.n_kv_heads,
-                head_dim=c.head_dim, ffn=c.ffn_dim, max_seq=c.max_seq, eps=c.norm_eps, rope_theta=c.rope_theta,
-                dtype="bf16" if c.dtype == BF16 else "fp32", init_std=c.init_std)
+    d = dict(vocab=c.vocab_size, dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads, n_kv_heads=c.n_kv_heads,
+             head_dim=c.head_dim, ffn=c.ffn_dim, max_seq=c.max_seq, eps=c.norm_eps, rope_theta=c.rope_theta,
+             dtype="bf16" if c.dtype == BF16 else "fp32", init_std=c.init_std)
+    if c.arch:
+        d.update(arch=c.arch, ple_dim=c.ple_dim, final_softcap=c.final_softcap)
+    return d
 
 
 def _ptr(a: np.ndarray):

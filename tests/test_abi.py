@@ -38,9 +38,23 @@ def test_presets():
     c1 = I.preset(1)
     assert (c1.dim, c1.n_layers, c1.head_dim, c1.ffn_dim, c1.dtype) == (288, 6, 48, 768, I.F32)
     assert I.preset(4).max_batch == 64 and I.preset(5).max_seq >= 32768 + 128
+    c6 = I.preset(6)  # the Gemma-4-E2B shape of the reference's src/model.cuh:9-14
+    assert (c6.arch, c6.dim, c6.ffn_dim, c6.head_dim, c6.n_heads, c6.vocab_size, c6.n_layers, c6.ple_dim) == \
+        (I.ARCH_GEMMA, 1536, 6144, 512, 8, 262144, 35, 256)
     with pytest.raises(I.InfError) as e:
         I.preset(9)
     assert e.value.code == 4
+
+
+def test_gemma_config_rules_without_a_device():
+    """Gemma-style models are bf16 and single-GPU; ple_dim and the soft-cap belong to them only."""
+    L = I.lib()
+    ctx, m = C.POINTER(I.ExecCtx)(), I.Model()
+    for bad in (dict(dtype=I.F32), dict(tp_size=2), dict(ple_dim=12), dict(head_dim=1024)):
+        c = I.preset(6, n_layers=1, vocab_size=1024, **bad)
+        assert L.inf_model_build(C.byref(ctx), C.byref(m), C.byref(c), None, 0) in (9, 15), bad
+    c = I.preset(3, n_layers=1, ple_dim=16)
+    assert L.inf_model_build(C.byref(ctx), C.byref(m), C.byref(c), None, 0) == 9
 
 
 def test_decode_bytes_model():

@@ -161,7 +161,7 @@ def test_tensor_core_prefill_attention(cuda, pos0, T, scatter):
         I.attn_prefill(kernel, q.data_ptr(), kp.data_ptr(), vp_.data_ptr(), bt.data_ptr(), pps, n_pages,
                        tok_slot.data_ptr(), tok_pos.data_ptr(), T, H, KV, hd, blk, out.data_ptr())
         err = (out.float() - ref).abs()
-        assert float(err.mean()) <= 2e-4, f"kernel {kernel}: mean error {float(err.mean())}"
+        assert float(err.mean()) <= 3e-4, f"kernel {kernel}: mean error {float(err.mean())}"
         if kernel == I.PREFILL_AUTO:
             torch.testing.assert_close(out.float(), ref, rtol=RTOL, atol=p_bound)
         else:

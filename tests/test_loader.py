@@ -453,13 +453,34 @@ def test_config_text_config_and_defaults(tmp_path):
     ({"hidden_act": "gelu"}, E_UNSUPPORTED),
     ({"attention_bias": True}, E_UNSUPPORTED),
     ({"rope_scaling": {"rope_type": "llama3", "factor": 8.0}}, E_UNSUPPORTED),
-    ({"model_type": "gemma3_text"}, E_UNSUPPORTED),
+    ({"model_type": "gemma3_text", "sliding_window": 512}, E_UNSUPPORTED),
+    ({"model_type": "gemma3n_text", "altup_num_inputs": 4}, E_UNSUPPORTED),
+    ({"model_type": "gemma4_text", "hidden_activation": "silu"}, E_UNSUPPORTED),
+    ({"model_type": "gemma4_text", "head_dim": 256, "query_pre_attn_scalar": 224}, E_UNSUPPORTED),
+    ({"model_type": "mistral"}, E_UNSUPPORTED),
     ({"hidden_activation": "gelu_pytorch_tanh"}, E_UNSUPPORTED),
     ({"hidden_size": 100, "num_attention_heads": 3}, E_INVALID),
     ("[" * 70 + "]" * 70, E_INVALID),
 ])
 def test_config_errors(tmp_path, doc, code):
     check_code(code, I.config_from_json, write_json(tmp_path, doc), I.preset(1))
+
+
+def test_config_gemma_e2b_shape(tmp_path):
+    """A Gemma-4-E2B-shaped config.json (its text_config, as the reference reads it,
+    src/main.cu:139-157) gives the Gemma-style decoder of preset 6: global_head_dim is the head
+    dim, hidden_size_per_layer_input the per-layer embedding width."""
+    doc = {"model_type": "gemma4", "text_config": {
+        "model_type": "gemma4_text", "hidden_size": 1536, "intermediate_size": 6144, "global_head_dim": 512,
+        "num_attention_heads": 8, "num_key_value_heads": 2, "vocab_size": 262144, "num_hidden_layers": 35,
+        "hidden_size_per_layer_input": 256, "final_logit_softcapping": 30.0, "rms_norm_eps": 1e-6,
+        "rope_theta": 1000000.0, "hidden_activation": "gelu_pytorch_tanh", "torch_dtype": "bfloat16"}}
+    c = I.config_from_json(write_json(tmp_path, doc), I.preset(3))
+    want = I.preset(6)
+    for f in ("arch", "dim", "ffn_dim", "head_dim", "n_heads", "n_kv_heads", "vocab_size", "n_layers", "ple_dim",
+              "dtype"):
+        assert getattr(c, f) == getattr(want, f), f
+    assert c.final_softcap == 30.0 and abs(c.norm_eps - 1e-6) < 1e-12 and c.rope_theta == 1e6
 
 
 def test_config_missing_file(tmp_path):
@@ -474,3 +495,50 @@ def test_json_strings_and_numbers(tmp_path):
     assert c.rope_theta == 500000.0 and abs(c.norm_eps - 1e-6) < 1e-13 and c.head_dim == 128
     check_code(E_INVALID, I.config_from_json, write_json(tmp_path, '{"a": "\\ud83e"}', "s.json"), I.preset(3))
     check_code(E_INVALID, I.config_from_json, write_json(tmp_path, '{"a": 01}', "n.json"), I.preset(3))
+
+
+def _gemma_ckpt(tmp_path, drop=None, extra=None):
+    from st_files import canon_shape, gemma_names
+    cfg = I.preset(6, n_layers=2, vocab_size=256, max_seq=64)
+    shape = dict(vocab=256, dim=cfg.dim, n_layers=2, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
+                 head_dim=cfg.head_dim, ffn=cfg.ffn_dim, arch=1, ple_dim=cfg.ple_dim)
+    rng = np.random.default_rng(0)
+    items = [(n, "BF16", bf16_round(rng.standard_normal(canon_shape(shape, k)).astype(np.float32)))
+             for n, k, l in gemma_names(2, True) if n != drop]
+    items += extra or []
+    path = str(tmp_path / "g.safetensors")
+    write_safetensors(path, items)
+    return cfg, path, {n: a for n, _, a in items}
+
+
+def test_gemma_checkpoint_names_and_layout(tmp_path):
+    """Gemma names map to the device weights: pre_feedforward_layernorm is the MLP's input norm,
+    post_attention_layernorm the attention output's; q/k norms are [head_dim]; the per-layer
+    embedding tables keep their shapes."""
+    cfg, path, t = _gemma_ckpt(tmp_path)
+    I.safetensors_check(path, cfg)
+    p = "model.language_model.layers.1."
+    np.testing.assert_array_equal(I.safetensors_read(path, cfg, 1, 16).view(np.uint16).ravel(),
+                                  t[p + "pre_feedforward_layernorm.weight"])
+    np.testing.assert_array_equal(I.safetensors_read(path, cfg, 1, 19).view(np.uint16).ravel(),
+                                  t[p + "post_attention_layernorm.weight"])
+    np.testing.assert_array_equal(I.safetensors_read(path, cfg, 0, 17).view(np.uint16).ravel(),
+                                  t["model.language_model.layers.0.self_attn.q_norm.weight"])
+    np.testing.assert_array_equal(I.safetensors_read(path, cfg, 0, 3).view(np.uint16).reshape(256, -1),
+                                  t["model.language_model.embed_tokens_per_layer.weight"])
+
+
+@pytest.mark.parametrize("case", ["no_q_norm", "lm_head", "llama_config"])
+def test_gemma_checkpoint_errors(tmp_path, case):
+    if case == "no_q_norm":
+        cfg, path, _ = _gemma_ckpt(tmp_path, drop="model.language_model.layers.1.self_attn.k_norm.weight")
+        check_code(E_INVALID, I.safetensors_check, path, cfg)
+    elif case == "lm_head":
+        cfg, path, _ = _gemma_ckpt(tmp_path, extra=[("lm_head.weight", "BF16", np.zeros((256, 1536), np.uint16))])
+        check_code(E_UNSUPPORTED, I.safetensors_check, path, cfg)
+    else:  # a Llama config meets Gemma tensors: the extra norms are refused, not ignored
+        cfg, path, _ = _gemma_ckpt(tmp_path)
+        llama = I.preset(3, n_layers=2, vocab_size=256, dim=cfg.dim, n_heads=8, n_kv_heads=2, head_dim=512,
+                         ffn_dim=cfg.ffn_dim)
+        import ctypes
+        assert I.lib().inf_safetensors_check(path.encode(), ctypes.byref(llama)) in (E_UNSUPPORTED, E_INVALID)

@@ -21,7 +21,7 @@ SEED = 11
 
 def shape_of(c) -> dict:
     return dict(vocab=c.vocab_size, dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads, n_kv_heads=c.n_kv_heads,
-                head_dim=c.head_dim, ffn=c.ffn_dim)
+                head_dim=c.head_dim, ffn=c.ffn_dim, arch=c.arch, ple_dim=c.ple_dim)
 
 
 def run(cfg, prompt, weights_path=None):
@@ -79,4 +79,21 @@ def test_checkpoint_fp32_model(cuda, tmp_path):
     want = run(cfg, prompt)
     got = run(cfg, prompt, path)
     np.testing.assert_array_equal(got[0], want[0])
+    np.testing.assert_array_equal(got[2], want[2])
+
+
+def test_gemma_checkpoint_equals_synthetic(cuda, tmp_path):
+    """The Gemma-style decoder from a checkpoint with Gemma names (q/k norms, the four norms of a
+    layer, per-layer embeddings, tied LM head) equals the synthetic model of the same seed."""
+    cfg = I.preset(6, n_layers=2, vocab_size=2048, max_seq=128)
+    shape = shape_of(cfg)
+    t = synthetic_tensors(shape, SEED, cfg.init_std, bf16=True)
+    path = str(tmp_path / "gemma.safetensors")
+    write_checkpoint(path, shape, t, dtype="BF16", prefix="model.language_model.")
+    I.safetensors_check(path, cfg)
+    prompt = O.gen_ids(6, 11, shape["vocab"])
+    want = run(cfg, prompt)
+    got = run(cfg, prompt, path)
+    np.testing.assert_array_equal(got[0], want[0])
+    assert got[1] == want[1]
     np.testing.assert_array_equal(got[2], want[2])
