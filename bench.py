@@ -50,6 +50,12 @@ DECODE = {
             prompt=512, steps=512, name="tinyllama-1.1b-shape",
             metric="batch-1 decode tokens/s and % of HBM roofline (TinyLlama-1.1B shape, bf16), 1 GPU"),
     3: dict(model=_LLAMA3, prompt=2048, steps=1024, name="llama-3-8b-shape", metric=METRIC),
+    # the Gemma-4-E2B shape of the reference's comments (src/model.cuh:9-14); not a BASELINE config
+    6: dict(model=dict(vocab=262144, dim=1536, n_layers=35, n_heads=8, n_kv_heads=2, head_dim=512, ffn=6144,
+                       max_seq=4096, eps=1e-6, rope_theta=1000000.0, dtype="bf16", init_std=0.02, arch=1, ple_dim=256,
+                       final_softcap=30.0),
+            prompt=1024, steps=512, name="gemma-4-e2b-shape",
+            metric="batch-1 decode tokens/s and % of HBM roofline (Gemma-4-E2B shape, bf16), 1 GPU"),
 }
 
 
@@ -611,8 +617,9 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--prompt", type=int, default=None, help="prompt length (profiling runs use a short one)")
-    ap.add_argument("--preset", type=int, default=3, choices=[1, 2, 3],
-                    help="decode workload: 3 Llama-3-8B shape (the headline), 2 TinyLlama-1.1B shape, 1 tiny fp32 d288")
+    ap.add_argument("--preset", type=int, default=3, choices=[1, 2, 3, 6],
+                    help="decode workload: 3 Llama-3-8B shape (the headline), 2 TinyLlama-1.1B shape, 1 tiny fp32 d288, "
+                         "6 Gemma-4-E2B shape (Gemma-style decoder)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch", "serve", "tokenize"],
                     help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence "

@@ -159,23 +159,20 @@ __device__ __forceinline__ float reduce_rows(const float (&p)[RPC], int lane)
 	}
 }
 
+// One row's dot product over this lane's units, already in registers (zero units contribute nothing).
 template <typename T, int UPL>
-__device__ __forceinline__ float gemv_row_dot(const uint8_t* row, int units_per_row, int ct, const float (&xh)[UPL][Store<T>::kVec])
+__device__ __forceinline__ float gemv_unit_dot(const uint4 (&w)[UPL], const float (&xh)[UPL][Store<T>::kVec])
 {
 	constexpr int VEC = Store<T>::kVec;
 	float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
 	for (int u = 0; u < UPL; ++u) {
-		const int unit = u * kGemvConsumers + ct;
-		if (unit < units_per_row) {
-			const uint4 w = *reinterpret_cast<const uint4*>(row + (size_t)unit * 16);
-			float wf[VEC];
-			unpack_unit(w, wf, (const T*)nullptr);
+		float wf[VEC];
+		unpack_unit(w[u], wf, (const T*)nullptr);
 #pragma unroll
-			for (int v = 0; v < VEC; v += 2) {
-				a0 = fmaf(wf[v], xh[u][v], a0);
-				a1 = fmaf(wf[v + 1], xh[u][v + 1], a1);
-			}
+		for (int v = 0; v < VEC; v += 2) {
+			a0 = fmaf(wf[v], xh[u][v], a0);
+			a1 = fmaf(wf[v + 1], xh[u][v + 1], a1);
 		}
 	}
 	return a0 + a1;
@@ -420,14 +417,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 		const bool ok = mbar_wait(&full[s], (i / S) & 1, abort_flag, a.err);
 		const int rows = min(RPC, n_rows - i * RPC);
 		const uint8_t* stage = ring + (size_t)s * a.stage_bytes;
-		float part[RPC];
+		// this lane's units of the chunk into registers, then the slot goes back to the producer
+		// at once: the unpacking, FMAs and reductions below run while the next copy is in flight
+		uint4 wreg[RPC][UPL];
 #pragma unroll
-		for (int r = 0; r < RPC; ++r) {
-			part[r] = 0.0f;
-			if (ok && r < rows) part[r] = gemv_row_dot<T, UPL>(stage + (size_t)r * row_bytes, units_per_row, ct, xh);
-		}
+		for (int r = 0; r < RPC; ++r)
+#pragma unroll
+			for (int u = 0; u < UPL; ++u) {
+				const int unit = u * kGemvConsumers + ct;
+				wreg[r][u] = (ok && r < rows && unit < units_per_row)
+				                 ? *reinterpret_cast<const uint4*>(stage + (size_t)r * row_bytes + (size_t)unit * 16)
+				                 : make_uint4(0, 0, 0, 0);
+			}
 		__syncwarp();
 		if (lane == 0) mbar_arrive(&empty[s]);
+		float part[RPC];
+#pragma unroll
+		for (int r = 0; r < RPC; ++r) part[r] = gemv_unit_dot<T, UPL>(wreg[r], xh);
 		const float v = reduce_rows<RPC>(part, lane);
 		if (row_writer && my_row < rows) wpart[warp * kGemvFlushRows + (i * RPC - w0) + my_row] = v;
 		if ((i + 1) % kChunksPerFlush != 0 && i + 1 != n_chunks) continue;

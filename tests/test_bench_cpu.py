@@ -17,7 +17,7 @@ def _bench():
     return m
 
 
-@pytest.mark.parametrize("preset", [1, 2, 3])
+@pytest.mark.parametrize("preset", [1, 2, 3, 6])
 def test_bench_models_are_the_library_presets(preset):
     b = _bench()
     want = I.oracle_dict(I.preset(preset))
