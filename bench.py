@@ -190,7 +190,8 @@ def run_ours(args, rank: int, world: int, dist):
     w = DECODE[args.preset]
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    cfg = I.preset(args.preset, n_layers=args.layers, tp_rank=rank if world > 1 else 0, tp_size=world)
+    layers = args.layers or w["model"]["n_layers"]
+    cfg = I.preset(args.preset, n_layers=layers, tp_rank=rank if world > 1 else 0, tp_size=world)
     prompt_len = w["prompt"] if args.prompt is None else args.prompt
     steps, warmup = args.steps or w["steps"], args.warmup
     if prompt_len + max(steps, warmup) > cfg.max_seq:
@@ -285,7 +286,7 @@ def run_ours(args, rank: int, world: int, dist):
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
-        rate, n, el, threads, setup_s = oracle_decode_rate(dict(w["model"], n_layers=args.layers), prompt_len,
+        rate, n, el, threads, setup_s = oracle_decode_rate(dict(w["model"], n_layers=layers), prompt_len,
                                                            args.cpu_budget)
         cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": f"{n} decode tokens ({el:.1f}s) at ctx {prompt_len}+ with a synthetic KV cache, CPU "
@@ -294,7 +295,7 @@ def run_ours(args, rank: int, world: int, dist):
     latency = args.preset == 1  # weights in L2: latency per step is the figure of merit
     value = ms_per_step if latency else steps / (ms * 1e-3)  # tensor parallel: every rank works on the same tokens
     if rank == 0:
-        model = w["name"] if args.layers == DECODE[args.preset]["model"]["n_layers"] else f"{w['name']}-{args.layers}-layers"
+        model = w["name"] if layers == DECODE[args.preset]["model"]["n_layers"] else f"{w['name']}-{layers}-layers"
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": (achieved / peak) if achieved else None,
                     "kernel": f"k_gemv gate/up+SwiGLU (per launch: 2*{Fl}*{d} weights)", "peak_kind": peak_kind}
@@ -351,7 +352,7 @@ def run_workload(args, rank: int, world: int, dist):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     preset = 5 if args.workload == "prefill" else 4
-    cfg = I.preset(preset, n_layers=args.layers, tp_rank=rank if world > 1 else 0, tp_size=world)
+    cfg = I.preset(preset, n_layers=args.layers or 32, tp_rank=rank if world > 1 else 0, tp_size=world)
     eng = I.Engine(cfg, seed=0)
     if world > 1:
         gloo = dist.new_group(backend="gloo")
@@ -620,7 +621,8 @@ def main():
     ap.add_argument("--preset", type=int, default=3, choices=[1, 2, 3, 6],
                     help="decode workload: 3 Llama-3-8B shape (the headline), 2 TinyLlama-1.1B shape, 1 tiny fp32 d288, "
                          "6 Gemma-4-E2B shape (Gemma-style decoder)")
-    ap.add_argument("--layers", type=int, default=32, help="decoder layers; fewer only for ncu captures of the same shapes")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers (0: the workload's own); fewer only for ncu captures of the same shapes")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch", "serve", "tokenize"],
                     help="decode: batch-1 decode (the headline); prefill: 32768-token prefill; batch: 64-sequence "
                          "decode; serve: continuous batching of 192 requests; tokenize: host tokenizer encode (no GPU)")

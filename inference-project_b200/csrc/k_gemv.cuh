@@ -273,6 +273,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 	// ---------------- consumers ----------------
 	const int ct = tid; // 0..255
 	const int units_per_row = (int)(row_bytes >> 4);
+	// the norm gain is a weight: with at most two units a lane it is read before the dependency
+	// wait, taking a cold HBM read off the prologue (more units would spill registers)
+	constexpr bool kEarlyGain = UPL <= 2;
+	uint4 graw[UPL];
+	if constexpr (kEarlyGain) {
+		bool norm_early = EpiTraits<EPI>::kNorm;
+		if constexpr (EpiTraits<EPI>::kRuntimeProlog) norm_early = a.resid_in != nullptr;
+		const T* g = reinterpret_cast<const T*>(a.gain);
+#pragma unroll
+		for (int u = 0; u < UPL; ++u) {
+			const int unit = u * kGemvConsumers + ct;
+			graw[u] = (norm_early && g && unit < units_per_row) ? *reinterpret_cast<const uint4*>(g + (size_t)unit * VEC)
+			                                                  : make_uint4(0, 0, 0, 0);
+		}
+	}
 	pdl_wait();
 
 	float xh[UPL][VEC];
@@ -371,7 +386,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 			for (int u = 0; u < UPL; ++u) {
 				const int unit = u * kGemvConsumers + ct;
 				if (unit < units_per_row) {
-					const uint4 gw = *reinterpret_cast<const uint4*>(g + (size_t)unit * VEC);
+					uint4 gw;
+					if constexpr (kEarlyGain) gw = graw[u];
+					else gw = *reinterpret_cast<const uint4*>(g + (size_t)unit * VEC);
 					float gf[VEC];
 					unpack_unit(gw, gf, (const T*)nullptr);
 					if (plus1) {
