@@ -201,7 +201,10 @@ cudaError_t launch(InfEngine* e, void (*kern)(KArgs...), dim3 grid, dim3 block, 
 }
 
 // Raises a kernel's dynamic shared-memory ceiling to `bytes` if it is below it (models of
-// different shapes in one process need different sizes for the same kernel).
+// different shapes in one process need different sizes for the same kernel), and asks for
+// the largest shared-memory carveout: the driver otherwise sizes an SM's carveout for the
+// kernel that occupies it (a projection CTA alone gets too little room for an attention CTA
+// beside it, so the next kernel's CTAs could not start before the dependency resolves).
 template <typename K>
 cudaError_t set_smem(K kern, size_t bytes)
 {
@@ -209,7 +212,9 @@ cudaError_t set_smem(K kern, size_t bytes)
 	std::lock_guard<std::mutex> lk(g_attr_mutex);
 	size_t& cur = set_to[reinterpret_cast<const void*>(kern)];
 	if (bytes <= cur) return cudaSuccess;
-	const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+	cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+	if (e == cudaSuccess)
+		e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
 	if (e == cudaSuccess) cur = bytes;
 	return e;
 }

@@ -27,6 +27,8 @@ namespace inf {
 constexpr int kAttnClMaxSplits = 16;       // cluster size (16 needs the non-portable opt-in)
 constexpr int kAttnClMaxPages = 16;        // mbarriers per CTA
 constexpr size_t kAttnClSmemMax = 112 * 1024; // leaves room for a projection CTA on the same SM
+static_assert(kAttnClSmemMax + 2 * kSmemReservedPerCta + kGemvSmemFloor <= kSmemPerSm,
+              "a cluster-attention CTA and a projection CTA share an SM");
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank)

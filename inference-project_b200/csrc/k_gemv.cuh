@@ -600,11 +600,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 	}
 }
 
-inline size_t gemv_smem_bytes()
+// Shared memory of one SM on sm_100 and the part the hardware reserves per CTA.
+constexpr size_t kSmemPerSm = 228 * 1024;
+constexpr size_t kSmemReservedPerCta = 1024;
+// A projection CTA takes just over half of an SM's shared memory, whatever its own needs, so
+// two of them never share an SM: with programmatic dependent launch the block scheduler
+// otherwise doubles up the CTAs of a low-register projection (the O-proj) on some SMs and
+// lets the next projection's early CTAs stream their ring on the SMs left free, and the
+// doubled-up CTAs finish ~3 us after the others.  A decode-attention CTA still fits beside one.
+constexpr size_t kGemvSmemFloor = kSmemPerSm / 2 - kSmemReservedPerCta + 512;
+
+constexpr size_t gemv_smem_need()
 {
 	return (size_t)kGemvRingBytes + 2 * kGemvMaxStages * sizeof(uint64_t) +
 	       (kGemvConsumerWarps * kGemvFlushRows + kGemvConsumerWarps + 8) * sizeof(float) +
 	       kGemvConsumerWarps * sizeof(unsigned long long) + 16 + kTpMaxRowsCta * sizeof(float);
 }
+static_assert(gemv_smem_need() <= kGemvSmemFloor, "projection shared memory above the floor");
+static_assert(2 * (kGemvSmemFloor + kSmemReservedPerCta) > kSmemPerSm, "two projection CTAs fit on one SM");
+
+inline size_t gemv_smem_bytes() { return kGemvSmemFloor; }
 
 } // namespace inf
