@@ -234,14 +234,18 @@ Error_t inf_attn_decode(const void* d_q, const void* d_kpool, const void* d_vpoo
  * context a sequence may reach) exactly as in the model, whose pages_per_seq is
  * ceil(max_seq / kv_block). */
 typedef enum InfAttnKernel {
-	InfAttnAuto    = 0, /* what the decode step picks: InfAttnCluster for one token when it fits, else
-	                       InfAttnMma for several tokens where it applies, else InfAttnSplitK */
+	InfAttnAuto    = 0, /* what the decode step picks for one token: InfAttnClusterTc when it applies
+	                       and fits, else InfAttnCluster when it fits; for several tokens InfAttnMma
+	                       where it applies; else InfAttnSplitK */
 	InfAttnSplitK  = 1, /* CTAs per (token, KV head, split), partials combined through the scratch by
 	                       the last CTA of each (token, KV head) */
 	InfAttnCluster = 2, /* one thread-block cluster of 8 or 16 CTAs per (token, KV head), the split
 	                       combine in distributed shared memory; pages_per_seq up to 16 per CTA */
 	InfAttnMma     = 3, /* the batched step's tensor-core kernel (mma.m16n8k16, TMA page loads): bf16,
 	                       kv_block 16, head_dim 64 or 128 */
+	InfAttnClusterTc = 4, /* the cluster split of InfAttnCluster on the tensor cores (mma.m16n8k16, TMA
+	                       page loads, the combine pushed into each output's owner CTA): bf16,
+	                       kv_block 16, head_dim 64 or 128, GQA group <= 8, up to 16 pages per CTA */
 } InfAttnKernel;
 /* inf_attn_decode with the kernel chosen by the caller (InfAttnKernel); ErrorUnsupported when
  * that kernel cannot serve the shape.  For tests and measurements of one kernel. */

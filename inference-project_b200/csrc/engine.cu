@@ -23,6 +23,7 @@
 #include "k_attn_decode_stream.cuh"
 #include "k_attn_decode_mma.cuh"
 #include "k_attn_cluster.cuh"
+#include "k_attn_cluster_tc.cuh"
 #include "k_gemv.cuh"
 #include "k_gemma.cuh"
 #include "k_attn_prefill.cuh"
@@ -110,6 +111,7 @@ struct InfEngine {
 	bool gemm_split = false;      // split-K allowed (batched decode; prefill keeps one K pass per tile)
 	int attn_cl_splits = 0;       // batch-1 decode attention as one cluster per KV head (0: split-K)
 	int attn_cl_pages = 0;
+	int attn_cl_tc = 0;           // ... on the tensor cores (k_attn_decode_clt)
 	// multi-token (prefill) buffers, prefill_chunk rows each
 	int chunk = 0;
 	float* resid_p = nullptr;  // [chunk][d] f32
@@ -325,11 +327,55 @@ Error_t attn_cl_plan(int G, int hd, int blk, size_t esz, int pages_per_seq, int 
 	return Success;
 }
 
+// The same plan for the tensor-core cluster kernel (bf16, 16-position pages, head_dim 64 or
+// 128, G <= 8): *splits = 0 when it does not apply or fit.
+Error_t attn_cltc_plan(int G, int hd, int blk, size_t esz, int pages_per_seq, int kv_heads, int* splits, int* pages)
+{
+	*splits = 0;
+	*pages = 0;
+	const AttnClTcKernel k = attn_decode_cltc_kernel(G, hd);
+	if (esz != 2 || blk != 16 || !k) return Success;
+	for (int cs = kAttnClMaxSplits; cs >= 8; cs >>= 1) {
+		const int mp = attn_cltc_pages_per_split(cs, pages_per_seq, hd, G);
+		if (mp == 0) continue;
+		const size_t smem = attn_cltc_layout(G, hd, mp, cs).total;
+		INF_CUDA_TRY(set_smem(k, smem));
+		if (cs > 8) INF_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+		cudaLaunchConfig_t lc = {};
+		lc.gridDim = dim3(cs, kv_heads, 1);
+		lc.blockDim = dim3(kClTcThreads);
+		lc.dynamicSmemBytes = smem;
+		cudaLaunchAttribute attr[1];
+		attr[0].id = cudaLaunchAttributeClusterDimension;
+		attr[0].val.clusterDim.x = cs;
+		attr[0].val.clusterDim.y = 1;
+		attr[0].val.clusterDim.z = 1;
+		lc.attrs = attr;
+		lc.numAttrs = 1;
+		int n = 0;
+		if (cudaOccupancyMaxActiveClusters(&n, k, &lc) != cudaSuccess) {
+			(void)cudaGetLastError();
+			continue;
+		}
+		if (n < 1) continue;
+		*splits = cs;
+		*pages = mp;
+		return Success;
+	}
+	return Success;
+}
+
 Error_t attn_cl_choose(InfEngine* e, int G, int hd)
 {
+	INF_TRY(attn_cltc_plan(G, hd, (int)e->cfg.kv_block, e->esz, e->pages_per_seq, e->KVl, &e->attn_cl_splits,
+	                       &e->attn_cl_pages));
+	e->attn_cl_tc = e->attn_cl_splits > 0;
+	if (e->attn_cl_tc) return Success;
 	return attn_cl_plan(G, hd, (int)e->cfg.kv_block, e->esz, e->pages_per_seq, e->KVl, &e->attn_cl_splits,
 	                    &e->attn_cl_pages);
 }
+
+Error_t tensor_map_kv(CUtensorMap* m, const void* base, u32 hd, u32 blk, u32 kv, u32 pages, u32 box_pages);
 
 // launch with a cluster of cluster_x CTAs along x and the programmatic-dependency edge
 template <typename... KArgs, typename... Args>
@@ -402,7 +448,21 @@ Error_t enqueue_attention(InfEngine* e, const LayerW& L)
 	a.counters = e->attn_counters;
 	a.out = e->attn;
 	a.err = e->err;
-	if (e->attn_cl_splits > 0) {
+	if (e->attn_cl_splits > 0 && e->attn_cl_tc) {
+		a.n_splits = e->attn_cl_splits;
+		a.max_pages_split = e->attn_cl_pages;
+		const int cs = e->attn_cl_splits, G = e->Hl / e->KVl;
+		const size_t smem = attn_cltc_layout(G, hd, e->attn_cl_pages, cs).total;
+		const AttnClTcKernel ak = attn_decode_cltc_kernel(G, hd);
+		if (!ak) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, hd);
+		CUtensorMap tk, tv; // one page (16 positions x 64 head dims) per box
+		INF_TRY(tensor_map_kv(&tk, L.kpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
+		INF_TRY(tensor_map_kv(&tv, L.vpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
+		INF_CUDA_TRY(set_smem(ak, smem));
+		INF_TRY(prof_begin(e));
+		INF_CUDA_TRY(launch_cluster(e, ak, dim3(cs, e->KVl, 1), dim3(kClTcThreads), smem, cs, tk, tv, a));
+		INF_TRY(prof_end(e, InfKAttn));
+	} else if (e->attn_cl_splits > 0) {
 		a.n_splits = e->attn_cl_splits;
 		a.max_pages_split = e->attn_cl_pages;
 		const int cs = e->attn_cl_splits;
@@ -2232,7 +2292,7 @@ Error_t attn_plan(u32 kernel, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 hea
 	if (n_tokens == 0 || n_heads == 0 || n_kv_heads == 0 || head_dim == 0 || head_dim % 2 || kv_block == 0 ||
 	    pages_per_seq == 0 || n_heads % n_kv_heads || (dtype != InfBF16 && dtype != InfF32) || n_tokens > 65535)
 		return fail(ErrorInvalidValue, "attention: bad shape");
-	if (kernel > InfAttnMma) return fail(ErrorInvalidValue, "attention: kernel %u", kernel);
+	if (kernel > InfAttnClusterTc) return fail(ErrorInvalidValue, "attention: kernel %u", kernel);
 	const u32 G = n_heads / n_kv_heads;
 	if (!attn_decode_supported((int)G, (int)head_dim) || G * head_dim > (u32)(kAttnThreads * kAttnMaxAcc))
 		return fail(ErrorUnsupported, "attention: GQA group %u x head_dim %u", G, head_dim);
@@ -2251,7 +2311,15 @@ Error_t attn_plan(u32 kernel, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 hea
 	p->part_bytes = (size_t)n_tokens * n_heads * (size_t)std::max(sk_splits, mma_ok ? mma_splits : 1) * hd2 * sizeof(float);
 	p->counter_bytes = (size_t)n_tokens * n_kv_heads * sizeof(unsigned) + 16; // + error word
 	int k = (int)kernel;
-	int cl_splits = 0, cl_pages = 0;
+	int cl_splits = 0, cl_pages = 0, ct_splits = 0, ct_pages = 0;
+	if ((k == InfAttnAuto && n_tokens == 1) || k == InfAttnClusterTc) {
+		INF_TRY(attn_cltc_plan((int)G, (int)head_dim, (int)kv_block, esz, (int)pages_per_seq, (int)n_kv_heads, &ct_splits,
+		                       &ct_pages));
+		if (k == InfAttnClusterTc && ct_splits == 0)
+			return fail(ErrorUnsupported, "attention: the tensor-core cluster kernel needs bf16, 16-token pages, head_dim 64 "
+			                              "or 128, GQA group <= 8 and at most 16 pages per CTA");
+		if (ct_splits > 0) k = InfAttnClusterTc;
+	}
 	if (k == InfAttnAuto || k == InfAttnCluster) {
 		if (n_tokens == 1 || k == InfAttnCluster)
 			INF_TRY(attn_cl_plan((int)G, (int)head_dim, (int)kv_block, esz, (int)pages_per_seq, (int)n_kv_heads, &cl_splits,
@@ -2263,7 +2331,11 @@ Error_t attn_plan(u32 kernel, u32 n_tokens, u32 n_heads, u32 n_kv_heads, u32 hea
 		return fail(ErrorUnsupported, "attention: the tensor-core kernel needs bf16, 16-token pages and head_dim 64 or 128");
 	if (k == InfAttnAuto) k = cl_splits > 0 ? InfAttnCluster : (n_tokens > 1 && mma_ok) ? InfAttnMma : InfAttnSplitK;
 	p->kernel = k;
-	if (k == InfAttnCluster) {
+	if (k == InfAttnClusterTc) {
+		p->splits = ct_splits;
+		p->max_pages_split = ct_pages;
+		p->smem = attn_cltc_layout((int)G, (int)head_dim, ct_pages, ct_splits).total;
+	} else if (k == InfAttnCluster) {
 		p->splits = cl_splits;
 		p->max_pages_split = cl_pages;
 		p->smem = attn_cl_layout((int)G, (int)head_dim, (int)kv_block, esz, cl_pages, cl_splits).total;
@@ -2304,6 +2376,30 @@ Error_t attn_launch_t(const AttnPlan& P, const AttnDecodeArgs& a, u32 n_tokens, 
 		return Success;
 	}
 	if constexpr (sizeof(T) == 2) {
+		if (P.kernel == InfAttnClusterTc) {
+			const AttnClTcKernel k = attn_decode_cltc_kernel(G, a.hd);
+			if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);
+			if ((uintptr_t)a.q & 15) return fail(ErrorInvalidValue, "inf_attn_decode: q not 16-byte aligned");
+			CUtensorMap tk, tv; // one page (16 positions x 64 head dims) per box
+			INF_TRY(tensor_map_kv(&tk, a.kpool, (u32)a.hd, (u32)a.blk, (u32)a.KV, n_pages, 1));
+			INF_TRY(tensor_map_kv(&tv, a.vpool, (u32)a.hd, (u32)a.blk, (u32)a.KV, n_pages, 1));
+			INF_CUDA_TRY(set_smem(k, P.smem));
+			if (P.splits > 8) INF_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+			cudaLaunchConfig_t lc = {};
+			lc.gridDim = dim3((unsigned)P.splits, (unsigned)a.KV, n_tokens);
+			lc.blockDim = dim3(kClTcThreads);
+			lc.dynamicSmemBytes = P.smem;
+			lc.stream = st;
+			cudaLaunchAttribute attr[1];
+			attr[0].id = cudaLaunchAttributeClusterDimension;
+			attr[0].val.clusterDim.x = (unsigned)P.splits;
+			attr[0].val.clusterDim.y = 1;
+			attr[0].val.clusterDim.z = 1;
+			lc.attrs = attr;
+			lc.numAttrs = 1;
+			INF_CUDA_TRY(cudaLaunchKernelEx(&lc, k, tk, tv, a));
+			return Success;
+		}
 		if (P.kernel == InfAttnMma) {
 			const AttnMmaKernel k = attn_decode_mma_kernel(G, a.hd);
 			if (!k) return fail(ErrorUnsupported, "attention: GQA group %d, head_dim %d", G, a.hd);

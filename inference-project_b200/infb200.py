@@ -546,7 +546,7 @@ def attn_decode(d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_to
                                 scratch_bytes, vp(stream) if stream else None), "inf_attn_decode")
 
 
-ATTN_AUTO, ATTN_SPLITK, ATTN_CLUSTER, ATTN_MMA = 0, 1, 2, 3  # InfAttnKernel
+ATTN_AUTO, ATTN_SPLITK, ATTN_CLUSTER, ATTN_MMA, ATTN_CLUSTER_TC = 0, 1, 2, 3, 4  # InfAttnKernel
 
 
 def attn_decode_with(kernel, d_q, d_k, d_v, d_bt, pages_per_seq, n_pages, d_slot, d_pos, n_tokens, n_heads,

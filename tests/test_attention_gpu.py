@@ -2,7 +2,8 @@
 attention over the same paged cache (random page permutations unless stated):
 
 * batch-1 decode of the Llama-3-8B shape with the model's default max_seq 3072: 192 pages per
-  sequence, so the decode step runs the cluster kernel as 16 CTAs x 12 pages per KV head;
+  sequence, so the decode step runs the tensor-core cluster kernel as 16 CTAs x 12 pages per KV
+  head (the SIMT cluster kernel, which serves fp32 models and other head sizes, alongside);
 * the 64-sequence batched step (contexts 512-4096 from the seed-2 lengths, max_seq 4352): the
   tensor-core streaming kernel;
 * batch-1 decode after the 32k-token prefill (max_seq 32896): beyond one cluster, the split-K
@@ -19,6 +20,18 @@ from attn_ref import decode_attention, prefill_attention
 pytestmark = pytest.mark.gpu
 
 RTOL, ATOL = 2 ** -7, 2e-3  # bf16 output (8-bit mantissa); P rounded to bf16 in the tensor-core kernels
+
+
+def _within_one_ulp(torch, a, b):
+    """Two bf16 results of fp32-accurate computations: equal, or one bf16 rounding step apart
+    (a value in [2^e, 2^(e+1)) has a step of 2^(e-7) <= 2^-7 |value|), with an absolute floor of
+    1e-5 for outputs near zero, where the weighted sum cancels and the two fp32 summation orders
+    (~1e-6 of the terms' magnitude) exceed a step of the tiny result.  Returns (ok, fraction
+    identical, worst element as (a, b))."""
+    a, b = a.float().flatten(), b.float().flatten()
+    excess = (a - b).abs() - (torch.maximum(a.abs(), b.abs()) * 2 ** -7 + 1e-5)
+    i = int(excess.argmax())
+    return bool(excess[i] <= 0), float((a == b).float().mean()), (float(a[i]), float(b[i]))
 
 
 def _pools(torch, n_pages, KV, blk, hd, seed, q_rows, H, q_scale=1.5):
@@ -43,7 +56,9 @@ def _decode(torch, kernel, q, kp, vp_, bt, slots, pos, pps, n_pages, H, KV, hd, 
 def test_cluster_kernel_at_the_headline_plan(cuda):
     """Llama-3-8B heads (32 q / 8 kv, head_dim 128), max_seq 3072 -> 192 pages per sequence, the
     positions the headline decodes (2048 and on) plus both ends of the plan's range; one token per
-    call, as the batch-1 decode step runs it."""
+    call, as the batch-1 decode step runs it.  The tensor-core cluster kernel keeps each softmax
+    weight as three bf16 parts (~24 bits), so its output is the SIMT cluster kernel's (fp32
+    weights) or one bf16 rounding step away, and mostly identical."""
     torch = cuda
     H, KV, hd, blk, pps = 32, 8, 128, 16, 3072 // 16
     positions = [0, 15, 191, 2047, 2048, 2049, 2560, 3071]
@@ -57,8 +72,12 @@ def test_cluster_kernel_at_the_headline_plan(cuda):
         ref = decode_attention(torch, qi, kp, vp_, bt, slot, pos, H, KV, hd, blk)
         cl = _decode(torch, I.ATTN_CLUSTER, qi, kp, vp_, bt, slot, pos, pps, n_pages, H, KV, hd, blk)
         torch.testing.assert_close(cl.float(), ref, rtol=RTOL, atol=ATOL, msg=f"position {p}")
+        ct = _decode(torch, I.ATTN_CLUSTER_TC, qi, kp, vp_, bt, slot, pos, pps, n_pages, H, KV, hd, blk)
+        torch.testing.assert_close(ct.float(), ref, rtol=RTOL, atol=ATOL, msg=f"tensor-core cluster at position {p}")
+        ok, same, worst = _within_one_ulp(torch, ct, cl)
+        assert ok and same >= 0.9, f"position {p}: {same:.3f} identical to the SIMT cluster kernel, worst {worst}"
         auto = _decode(torch, I.ATTN_AUTO, qi, kp, vp_, bt, slot, pos, pps, n_pages, H, KV, hd, blk)
-        assert torch.equal(auto, cl), f"position {p}: the automatic choice is not the cluster kernel"
+        assert torch.equal(auto, ct), f"position {p}: the automatic choice is not the tensor-core cluster kernel"
         sk = _decode(torch, I.ATTN_SPLITK, qi, kp, vp_, bt, slot, pos, pps, n_pages, H, KV, hd, blk)
         torch.testing.assert_close(sk.float(), ref, rtol=RTOL, atol=ATOL, msg=f"split-K at position {p}")
 
@@ -81,11 +100,16 @@ def test_cluster_kernel_every_plan_size(cuda, H, KV, hd, max_seq):
     ref = decode_attention(torch, q, kp, vp_, bt, slots, pos, H, KV, hd, blk)
     out = _decode(torch, I.ATTN_CLUSTER, q, kp, vp_, bt, slots, pos, pps, n_pages, H, KV, hd, blk)
     torch.testing.assert_close(out.float(), ref, rtol=RTOL, atol=ATOL)
+    ct = _decode(torch, I.ATTN_CLUSTER_TC, q, kp, vp_, bt, slots, pos, pps, n_pages, H, KV, hd, blk)
+    torch.testing.assert_close(ct.float(), ref, rtol=RTOL, atol=ATOL)
+    ok, same, worst = _within_one_ulp(torch, ct, out)
+    assert ok and same >= 0.9, f"{same:.3f} identical to the SIMT cluster kernel, worst {worst}"
     if max_seq == 3328:  # one more page per sequence no longer fits one cluster (refused on the host)
         bt2 = torch.zeros(n, pps + 1, dtype=torch.int32, device="cuda")
-        with pytest.raises(I.InfError) as e:
-            _decode(torch, I.ATTN_CLUSTER, q, kp, vp_, bt2, slots, pos, pps + 1, n_pages, H, KV, hd, blk)
-        assert e.value.code == 15
+        for kernel in (I.ATTN_CLUSTER, I.ATTN_CLUSTER_TC):
+            with pytest.raises(I.InfError) as e:
+                _decode(torch, kernel, q, kp, vp_, bt2, slots, pos, pps + 1, n_pages, H, KV, hd, blk)
+            assert e.value.code == 15
 
 
 def test_mma_kernel_at_the_batched_workload(cuda):

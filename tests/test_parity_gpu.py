@@ -163,9 +163,15 @@ def test_slots_are_independent(cuda):
     with I.Engine(cfg) as eng:
         ra, _ = eng.forward(np.concatenate([pa, pa[:1]]), 0, slot=0)
     np.testing.assert_array_equal(lb, lb_again)  # same path, same slot-independent result
-    # one prefill pass vs prefill + one decode step: different kernels, bf16 tolerance
-    assert float(np.abs(la2 - ra).max()) <= LOGIT_ATOL_BF16
-    assert cosine(la2, ra) >= COSINE_MIN
+    # one prefill pass and prefill + one decode step run different kernels: each is held to the
+    # oracle's logits for the 13-token sequence within twice the measured fp32 drift of this shape
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0)
+    _, o_lg = orc.generate(np.concatenate([pa, pa[:1]]), 1, want_logits=True)
+    orc.close()
+    for name, lg in (("prefill + decode", la2), ("one prefill pass", ra)):
+        err = float(np.abs(lg - o_lg[0]).max())
+        assert err <= 2 * DRIFT_TINYLLAMA_2, f"{name}: max-abs {err}"
+        assert cosine(lg, o_lg[0]) >= COSINE_MIN, name
 
 
 def test_forward_batch_matches_single(cuda):

@@ -2,7 +2,8 @@
 with the oracle (q, K/V cache, attention output, SwiGLU product, logits) on identical
 weights and ids.  One layer keeps fp32 accumulation-order noise from cascading, so each
 stored bf16 value must equal the oracle's or sit one bf16 ulp away (a rounding-boundary
-flip), and the fraction of exact matches is high."""
+flip), and the fraction of exact matches is high.  The SwiGLU product is checked on the
+device's own attention output (a single upstream flip moves every residual element)."""
 import numpy as np
 import pytest
 
@@ -29,6 +30,47 @@ def assert_bf16_close(got, want, name, min_exact=0.97, max_ulps=1.0, abs_frac=1e
     worst = int(np.argmax(excess))
     assert float(excess.max()) <= 1e-12, f"{name}[{worst}]: {got[worst]} vs {want[worst]} (exact {exact:.4f})"
     assert exact >= min_exact, f"{name}: only {exact:.4f} exactly equal"
+
+
+def _bf16_round(x):
+    """fp32 -> nearest-even bf16, returned as fp32."""
+    a = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((a + 0x7FFF + ((a >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+def mlp_stage(orc, cfg, token, attn):
+    """The first layer's SwiGLU product for `token`, computed from a given attention output with
+    the oracle's weights and the oracle's rounding points (oracle/llama_ref.c: fp32 O-projection
+    output from a double dot product, fp32 residual add, RMSNorm with the double sum of squares
+    and fp32 scale, bf16 x-hat, fp32 gate/up from double dot products, silu(gate)*up in double
+    stored as bf16).  Lets the MLP stage be checked on the device's own attention output: one
+    rounding-boundary flip in the attention moves the whole residual through a W_o column."""
+    d, F, H, hd = cfg.dim, cfg.ffn_dim, cfg.n_heads, cfg.head_dim
+
+    def mv(kind, rows, cols, x):
+        W = orc.weight(0, kind, (rows, cols))
+        x64 = np.asarray(x, np.float64)
+        y = np.empty(rows, np.float32)
+        for r0 in range(0, rows, 2048):
+            y[r0:r0 + 2048] = (O.bf16_to_f32(W[r0:r0 + 2048]).astype(np.float64) @ x64).astype(np.float32)
+        return y
+
+    emb = O.bf16_to_f32(orc.weight(-1, 0, (cfg.vocab_size, d))[token]).astype(np.float32)
+    r1 = (emb + mv(11, d, H * hd, np.asarray(attn, np.float32))).astype(np.float32)
+    ss = float(np.sum(r1.astype(np.float64) ** 2))
+    inv = np.float32(1.0) / np.sqrt(np.float32(np.float32(ss) / np.float32(d) + np.float32(cfg.norm_eps)))
+    g = O.bf16_to_f32(orc.weight(0, 16, (d,))).astype(np.float32)
+    xh = _bf16_round((r1 * inv).astype(np.float32) * g)
+    gate = mv(12, F, d, xh).astype(np.float64)
+    up = mv(13, F, d, xh).astype(np.float64)
+    return _bf16_round((gate / (1.0 + np.exp(-gate)) * up).astype(np.float32)).astype(np.float64)
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30))
 
 
 def assert_f32_close(got, want, name, rtol=1e-4):
@@ -58,7 +100,9 @@ def test_decode_path_stages(cuda, preset):
             assert_bf16_close(kv[t][0], k, f"k[{t}]")
             assert_bf16_close(kv[t][1], v, f"v[{t}]")
         assert_bf16_close(got["attn"], att, "attention", min_exact=0.95)
-        assert_bf16_close(got["h"], h, "swiglu", min_exact=0.95)
+        # the MLP on its own input (the device's attention output), and end to end by cosine
+        assert_bf16_close(got["h"], mlp_stage(orc, cfg, int(prompt[-1]), got["attn"]), "swiglu", min_exact=0.97)
+        assert cosine(got["h"], h) >= 0.99999
         assert_f32_close(got["resid"], resid, "residual", rtol=2e-2)
         assert float(np.abs(got["logits"] - o_lg).max()) <= 2e-2
     else:
