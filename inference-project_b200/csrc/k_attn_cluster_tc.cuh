@@ -16,7 +16,8 @@
 //   * combine: CTA c owns outputs [c*per, (c+1)*per) of the G x head_dim block.  Every CTA
 //     stores each of its partial values straight into the owner's inbox (st.shared::cluster),
 //     with the (max, sum) of the heads the owner needs; one release/acquire cluster barrier,
-//     then each owner combines from its own shared memory.  A relaxed arrive at entry, waited
+//     then each owner combines from its own shared memory (per-source weights by one warp per
+//     head, then eight threads per output).  A relaxed arrive at entry, waited
 //     before the first remote store, guarantees every peer is running.
 // Positions past the context and pages with invalid ids are masked (the id error is recorded);
 // every CTA reaches both barrier phases on every path; the page waits are bounded, and a CTA
@@ -309,21 +310,38 @@ __global__ void __launch_bounds__(kClTcThreads)
 	cluster_arrive_release(); // phase 2: every partial is in its owner's inbox
 	cluster_wait_acquire();
 
-	// this CTA's outputs, combined from its own shared memory
+	// this CTA's outputs, combined from its own shared memory: first every source's weight for
+	// the heads the CTA owns (one warp per head, lane r = source r), then 8 threads per output
+	// sum every 8th source
 	bf16* ob = reinterpret_cast<bf16*>(a.out) + (size_t)b * a.H * HD + (size_t)kvh * G * HD;
-	const int e1 = min(G * HD, (split + 1) * per);
-	for (int e = split * per + tid; e < e1; e += kClTcThreads) {
-		const int g = e / HD, k = e - split * per;
-		float M = -INFINITY;
-		for (int r = 0; r < CS; ++r) M = fmaxf(M, inbox_ml[(r * G + g) * 2]);
-		float v = 0.0f, L = 0.0f;
-		for (int r = 0; r < CS; ++r) {
-			const float mr_ = inbox_ml[(r * G + g) * 2];
-			const float wt = (mr_ == -INFINITY) ? 0.0f : exp2f(mr_ - M);
-			v = fmaf(wt, inbox[r * per + k], v);
-			L = fmaf(wt, inbox_ml[(r * G + g) * 2 + 1], L);
+	const int e0 = split * per, e1 = min(G * HD, e0 + per);
+	const int g0 = e0 / HD;
+	const int nh = e1 > e0 ? (e1 - 1) / HD - g0 + 1 : 0;
+	float* wts = mo; // [nh][CS]; the merge region is free after the barrier
+	for (int gl = warp; gl < nh; gl += kClTcWarps) {
+		const int g = g0 + gl;
+		const float m = lane < CS ? inbox_ml[(lane * G + g) * 2] : -INFINITY;
+		const float ls = lane < CS ? inbox_ml[(lane * G + g) * 2 + 1] : 0.0f;
+		const float M = warp_max(m);
+		const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
+		const float L = warp_sum(w * ls);
+		if (lane < CS) wts[gl * CS + lane] = L > 0.0f ? w / L : 0.0f;
+	}
+	__syncthreads();
+	constexpr int kTpo = 8; // threads per output
+	const int sub = tid & (kTpo - 1);
+	for (int base = 0; base < per; base += kClTcThreads / kTpo) {
+		const int e = e0 + base + tid / kTpo;
+		const bool in = e < e1;
+		float v = 0.0f;
+		if (in) {
+			const int gl = e / HD - g0, k = e - e0;
+			for (int r = sub; r < CS; r += kTpo) v = fmaf(wts[gl * CS + r], inbox[r * per + k], v);
 		}
-		Store<bf16>::put(ob + e, L > 0.0f ? v / L : 0.0f);
+		v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+		v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+		v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+		if (in && sub == 0) Store<bf16>::put(ob + e, v);
 	}
 }
 
