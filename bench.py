@@ -384,7 +384,7 @@ def run_workload(args, rank: int, world: int, dist):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     if args.workload == "prefill":
-        T = 32768 if args.prompt == PROMPT else args.prompt
+        T = 32768 if args.prompt is None else args.prompt
         prompt = I.synth_ids(3, T, cfg.vocab_size)  # seed-3 uniform ids
         for _ in range(args.warmup):
             eng.reset(0)
@@ -630,6 +630,8 @@ def main():
     args = ap.parse_args()
     if args.prompt is not None:
         globals()["PROMPT"] = args.prompt
+    if args.steps == 0 and args.workload != "decode":  # the workload's own count
+        args.steps = {"prefill": 3, "batch": 64, "serve": 1, "tokenize": 20}[args.workload]
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 
