@@ -70,12 +70,6 @@ __host__ __device__ inline AttnClTcLayout attn_cltc_layout(int G, int hd, int ma
 	return L;
 }
 
-// byte offset of 16-byte chunk c16 of row r in half h of a page (SWIZZLE_128B atoms of 8 rows)
-__device__ __forceinline__ uint32_t cltc_off(int r, int c16, int h)
-{
-	return (uint32_t)h * 2048u + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c16 ^ (r & 7)) << 4));
-}
-
 template <int G, int HD>
 __global__ void __launch_bounds__(kClTcThreads)
     k_attn_decode_clt(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const AttnDecodeArgs a)
@@ -83,9 +77,9 @@ __global__ void __launch_bounds__(kClTcThreads)
 	static_assert(G >= 1 && G <= 8 && (HD == 64 || HD == 128), "rows / head_dim");
 	constexpr int kHalves = HD / 64;
 	constexpr uint32_t kPageBytes = kHalves * 2048u;
-	extern __shared__ __align__(16) uint8_t sm_base[];
+	extern __shared__ __align__(16) uint8_t clt_sm_base[];
 	// 1024-byte aligned (the SWIZZLE_128B atoms); the layout's total includes the slack
-	uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_base) + 1023) & ~(uintptr_t)1023);
+	uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(clt_sm_base) + 1023) & ~(uintptr_t)1023);
 	const int kvh = blockIdx.y, b = blockIdx.z;
 	const int split = (int)cluster_rank(); // gridDim.x == cluster size == n_splits
 	const int CS = a.n_splits;
@@ -173,7 +167,7 @@ __global__ void __launch_bounds__(kClTcThreads)
 				const size_t off = ((((size_t)cur_page * a.KV + kvh) * 16) + r) * HD * 2 + b8;
 				const uint2 kr = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(a.kpool) + off);
 				const uint2 vr = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(a.vpool) + off);
-				const uint32_t o = cltc_off(r, (b8 & 127) >> 4, b8 >> 7) + (b8 & 15);
+				const uint32_t o = page_sw_off(r, (b8 & 127) >> 4, b8 >> 7) + (b8 & 15);
 				*reinterpret_cast<uint2*>(kp + o) = kr;
 				*reinterpret_cast<uint2*>(vbuf + (size_t)j * kPageBytes + o) = vr;
 			}
@@ -187,7 +181,7 @@ __global__ void __launch_bounds__(kClTcThreads)
 #pragma unroll
 		for (int ks = 0; ks < HD / 16; ++ks) {
 			uint32_t b00, b01, b10, b11;
-			ldsm_x4(kc + cltc_off(krow, (ks & 3) * 2 + (mi & 1), ks >> 2), b00, b01, b10, b11);
+			ldsm_x4(kc + page_sw_off(krow, (ks & 3) * 2 + (mi & 1), ks >> 2), b00, b01, b10, b11);
 			const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
 			mma_bf16_16816(acc[0], af, b00, b01);
 			mma_bf16_16816(acc[1], af, b10, b11);
@@ -246,7 +240,7 @@ __global__ void __launch_bounds__(kClTcThreads)
 		for (int dt = 0; dt < HD / 8; dt += 2) {
 			const int d16 = dt + (mi >> 1); // 8-dim chunk over head_dim
 			uint32_t b0, b1, c0, c1;
-			ldsm_x4_trans(vc + cltc_off(vrow, d16 & 7, d16 >> 3), b0, b1, c0, c1);
+			ldsm_x4_trans(vc + page_sw_off(vrow, d16 & 7, d16 >> 3), b0, b1, c0, c1);
 			mma_bf16_16816(o[dt], pl, b0, b1); // smallest part first
 			mma_bf16_16816(o[dt + 1], pl, c0, c1);
 			mma_bf16_16816(o[dt], pm, b0, b1);

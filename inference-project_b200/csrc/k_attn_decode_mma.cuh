@@ -1,19 +1,20 @@
 // Decode attention for batches of tokens on the tensor cores (bf16, head_dim 64 or 128).
 //
-// The same decomposition as the streaming kernel (k_attn_decode_stream.cuh): grid
-// (kv_heads, splits, tokens), a CTA streams its pages through a ring of shared-memory chunks
-// of 64 positions.  Thread 0 reads the split's page ids into shared memory once and loads each
-// page of K and V with 4-D TMA boxes (64 head dims x 16 positions x 1 head x 1 page,
-// SWIZZLE_128B), one box per 64-dim half, so the K and V fragments come from ldmatrix (.x4 for
-// K, .x4.trans for V) without bank conflicts; pages of 16 positions only.
-// The arithmetic moves to warp-level mma.m16n8k16 (bf16 in, fp32 out): the
-// G query heads of the KV head are the rows of a 16-row A tile (rows >= G are zero), each of
-// the four warps takes 16 positions of a chunk, computes S = Q.K^T (2 x head_dim/16 MMAs),
-// keeps a per-row running max / sum (online softmax on the accumulator fragments), turns
-// its S fragments into the bf16 A fragments of P (the C layout of two 8-column tiles is the
-// A layout of one 16-deep step) and accumulates O += P.V (head_dim/8 MMAs).  At the end the
-// four warps' (max, sum, O) are merged through shared memory into the split's partial, and the
-// last CTA of each (token, KV head) combines the splits (atomic ticket, no spinning).
+// Grid (kv_heads, splits, tokens); a CTA covers a contiguous range of one token's pages.  Thread
+// 0-127 read the split's page ids into shared memory once; then each of the four warps streams
+// its own pages (q = warp, warp + 4, ...) through its own ring of kStBufs stages (one page of K
+// and of V per stage, one mbarrier per stage, 4-D TMA boxes of 64 head dims x 16 positions x 1
+// head x 1 page into SWIZZLE_128B atoms, so the K and V fragments come from ldmatrix (.x4 for
+// K, .x4.trans for V) without bank conflicts); lane 0 refills a stage as soon as its warp is
+// done with it, so no CTA-wide barrier paces the stream.  Pages of 16 positions only.
+// The arithmetic is warp-level mma.m16n8k16 (bf16 in, fp32 out): the G query heads of the KV
+// head are the rows of a 16-row A tile (rows >= G are zero); per page a warp computes S = Q.K^T
+// (2 x head_dim/16 MMAs), keeps a per-row running max / sum (online softmax on the accumulator
+// fragments; O is rescaled only when some row's max grew), turns its S fragments into the bf16
+// A fragments of P (the C layout of two 8-column tiles is the A layout of one 16-deep step) and
+// accumulates O += P.V (head_dim/8 MMAs).  At the end the four warps' (max, sum, O) are merged
+// through shared memory into the split's partial, and the last CTA of each (token, KV head)
+// combines the splits (atomic ticket, no spinning).
 // P is rounded to bf16 for the P.V product (the SIMT kernels keep it in fp32).
 #pragma once
 
@@ -24,7 +25,8 @@
 
 namespace inf {
 
-constexpr int kAmThreads = 128; // 4 warps x 16 positions = one 64-position chunk
+constexpr int kAmThreads = 128; // 4 warps, each streaming every 4th page of the split
+static_assert(kAmThreads / 32 == kStChunkPages, "the region holds kStBufs pages of K and V per warp");
 
 __host__ __device__ inline size_t attn_mma_region_bytes(int hd, int blk)
 {
@@ -32,10 +34,11 @@ __host__ __device__ inline size_t attn_mma_region_bytes(int hd, int blk)
 	const size_t merge = (size_t)4 * 16 * hd * 4 + 4 * 16 * 2 * 4; // O, then (m, l) of every warp
 	return ((ring > merge ? ring : merge) + 127) & ~(size_t)127;
 }
-// region, the split's page ids (at most pages_per_seq), the chunk mbarriers
+// region, the split's page ids (at most pages_per_seq), one mbarrier per stage of each warp
 inline size_t attn_mma_smem_bytes(int hd, int blk, int pages_per_seq)
 {
-	return 1024 + attn_mma_region_bytes(hd, blk) + (((size_t)pages_per_seq * 4 + 15) & ~(size_t)15) + kStBufs * sizeof(uint64_t);
+	return 1024 + attn_mma_region_bytes(hd, blk) + (((size_t)pages_per_seq * 4 + 15) & ~(size_t)15) +
+	       (kAmThreads / 32) * kStBufs * sizeof(uint64_t);
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
@@ -64,11 +67,12 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
 	             : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
 	             : "r"(addr));
 }
-// A chunk of K or V in shared memory: [head_dim / 64 halves][64 positions][128 bytes], each
-// half in SWIZZLE_128B atoms (8 positions x 128 bytes) as the TMA boxes write it.
-__device__ __forceinline__ uint32_t kv_sw_addr(uint32_t base, int r, int c16, int half)
+// Byte offset of 16-byte chunk c16 of row r (position) in half h of one page of K or V in
+// shared memory: [head_dim / 64 halves][16 positions][128 bytes], each half two SWIZZLE_128B
+// atoms (8 positions x 128 bytes) as the TMA box writes it.
+__device__ __forceinline__ uint32_t page_sw_off(int r, int c16, int h)
 {
-	return base + (uint32_t)half * 8192u + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c16 ^ (r & 7)) << 4));
+	return (uint32_t)h * 2048u + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c16 ^ (r & 7)) << 4));
 }
 
 template <int G, int HD>
@@ -80,11 +84,7 @@ __global__ void __launch_bounds__(kAmThreads)
 	// 1024-byte aligned: the TMA boxes are SWIZZLE_128B atoms
 	uint8_t* sm_raw = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_base) + 1023) & ~(uintptr_t)1023);
 	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
-	const int blk = a.blk;
-	const size_t blk_bytes = (size_t)blk * HD * 2;
-	const size_t chunk_bytes = (size_t)kStChunkPages * blk_bytes;
-	uint8_t* kbuf = sm_raw;
-	uint8_t* vbuf = kbuf + (size_t)kStBufs * chunk_bytes;
+	const int blk = a.blk; // 16 (the host checks)
 	int* pg_s = reinterpret_cast<int*>(sm_raw + attn_mma_region_bytes(HD, blk)); // this split's page ids
 	uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(pg_s) + (((size_t)a.pages_per_seq * 4 + 15) & ~(size_t)15));
 	__shared__ int abort_flag;
@@ -101,44 +101,44 @@ __global__ void __launch_bounds__(kAmThreads)
 	const int pps = (n_pages + a.n_splits - 1) / a.n_splits;
 	const int p_begin = split * pps;
 	const int np = max(0, min(n_pages, p_begin + pps) - p_begin);
-	const int n_chunks = (np + kStChunkPages - 1) / kStChunkPages;
 
 	if (tid == 0) {
 		abort_flag = 0;
-		for (int i = 0; i < kStBufs; ++i) mbar_init(&bars[i], 1);
+		for (int i = 0; i < (kAmThreads / 32) * kStBufs; ++i) mbar_init(&bars[i], 1);
 		mbar_fence_init();
 	}
 	// page ids once into shared memory (invalid ids as -1): the chunk issue and the mask read them
 	for (int q = tid; q < np; q += kAmThreads) {
 		const int page = a.block_table[(size_t)slot * a.pages_per_seq + p_begin + q];
-		pg_s[q] = (page >= 0 && page < a.max_pages) ? page : -1;
+		const bool ok = page >= 0 && page < a.max_pages;
+		if (!ok) report_err(a.err, kDevKvRange); // masked below
+		pg_s[q] = ok ? page : -1;
 	}
 	__syncthreads();
-	auto issue = [&](int c) {
-		const int buf = c % kStBufs;
-		const int q0 = c * kStChunkPages, q1 = min(np, q0 + kStChunkPages);
-		uint32_t bytes = 0;
-		for (int q = q0; q < q1; ++q)
-			if (pg_s[q] >= 0) bytes += (uint32_t)(2 * blk_bytes);
-		mbar_arrive_expect_tx(&bars[buf], bytes);
+	// this warp's pages q = warp + 4 i, i < n_mine, through its own ring
+	constexpr uint32_t kPage = (HD / 64) * 2048u; // one page of K (or V)
+	const int n_mine = np > warp ? (np - warp + 3) / 4 : 0;
+	uint8_t* ring = sm_raw + (size_t)warp * kStBufs * 2 * kPage;
+	uint64_t* wbar = bars + warp * kStBufs;
+	auto issue = [&](int i) { // lane 0
+		const int st = i % kStBufs;
+		const int page = pg_s[warp + 4 * i];
+		if (page < 0) {
+			mbar_arrive(&wbar[st]);
+			return;
+		}
+		mbar_arrive_expect_tx(&wbar[st], 2 * kPage);
 		const uint64_t pol = policy_evict_first();
-		for (int q = q0; q < q1; ++q) {
-			const int page = pg_s[q];
-			if (page < 0 || page >= a.max_pages) {
-				report_err(a.err, kDevKvRange);
-				continue; // masked below
-			}
-			// one box of blk positions x 64 head dims per half, swizzled for ldmatrix
-			for (int h = 0; h < HD / 64; ++h) {
-				tma_load_4d(kbuf + (size_t)buf * chunk_bytes + (size_t)h * 8192 + (size_t)(q - q0) * blk * 128, &tm_k, h * 64, 0,
-				            kvh, page, &bars[buf], pol);
-				tma_load_4d(vbuf + (size_t)buf * chunk_bytes + (size_t)h * 8192 + (size_t)(q - q0) * blk * 128, &tm_v, h * 64, 0,
-				            kvh, page, &bars[buf], pol);
-			}
+		uint8_t* dst = ring + (size_t)st * 2 * kPage;
+#pragma unroll
+		for (int h = 0; h < HD / 64; ++h) {
+			tma_load_4d(dst + h * 2048, &tm_k, h * 64, 0, kvh, page, &wbar[st], pol);
+			tma_load_4d(dst + kPage + h * 2048, &tm_v, h * 64, 0, kvh, page, &wbar[st], pol);
 		}
 	};
-	if (tid == 0)
-		for (int c = 0; c < min(n_chunks, kStBufs); ++c) issue(c);
+	int issued = 0;
+	if (lane == 0)
+		for (; issued < min(n_mine, kStBufs); ++issued) issue(issued);
 
 	// Q as A fragments (rows gr and gr + 8; rows >= G are zero)
 	uint32_t qa[HD / 16][4];
@@ -161,101 +161,106 @@ __global__ void __launch_bounds__(kAmThreads)
 	for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
 	float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f; // rows gr, gr + 8 (l: this thread's share)
 	const float sl2 = a.scale * 1.4426950408889634f;
+	const int mi = lane >> 3, mr = lane & 7; // the ldmatrix matrix and row this lane addresses
 
-	for (int c = 0; c < n_chunks; ++c) {
-		const int buf = c % kStBufs;
-		if (!abort_flag && !mbar_wait(&bars[buf], (uint32_t)(c / kStBufs) & 1u, (volatile int*)&abort_flag, a.err))
+	for (int i = 0; i < n_mine; ++i) {
+		const int st = i % kStBufs;
+		if (!abort_flag && !mbar_wait(&wbar[st], (uint32_t)(i / kStBufs) & 1u, (volatile int*)&abort_flag, a.err))
 			abort_flag = 1;
-		const int q0 = c * kStChunkPages;
-		const int n_tok = (min(np, q0 + kStChunkPages) - q0) * blk;
-		const int kb = warp * 16; // this warp's 16 positions of the chunk
-		if (kb < n_tok && !abort_flag) {
-			const uint32_t kc = smem_u32(kbuf + (size_t)buf * chunk_bytes);
-			const uint32_t vc = smem_u32(vbuf + (size_t)buf * chunk_bytes);
-			// S = Q.K^T for 16 positions (two 8-position tiles); ldmatrix x4: matrices
-			// (tile 0, dims +0..7), (tile 0, +8..15), (tile 1, +0..7), (tile 1, +8..15)
-			float s[2][4];
+		const int q = warp + 4 * i;
+		const uint32_t kc = smem_u32(ring + (size_t)st * 2 * kPage), vc = kc + kPage;
+		// S = Q.K^T for the page's 16 positions (two 8-position tiles); ldmatrix x4: matrices
+		// (tile 0, dims +0..7), (tile 0, +8..15), (tile 1, +0..7), (tile 1, +8..15)
+		float s[2][4];
 #pragma unroll
-			for (int nt = 0; nt < 2; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-			const int mi = lane >> 3, mr = lane & 7; // the matrix and row this lane addresses
-			const int krow = kb + (mi >> 1) * 8 + mr;
+		for (int nt = 0; nt < 2; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+		const int krow = (mi >> 1) * 8 + mr;
 #pragma unroll
-			for (int ks = 0; ks < HD / 16; ++ks) {
-				const int c16 = (ks & 3) * 2 + (mi & 1);
-				uint32_t b00, b01, b10, b11;
-				ldsm_x4(kv_sw_addr(kc, krow, c16, ks >> 2), b00, b01, b10, b11);
-				mma_bf16_16816(s[0], qa[ks], b00, b01);
-				mma_bf16_16816(s[1], qa[ks], b10, b11);
+		for (int ks = 0; ks < HD / 16; ++ks) {
+			uint32_t b00, b01, b10, b11;
+			ldsm_x4(kc + page_sw_off(krow, (ks & 3) * 2 + (mi & 1), ks >> 2), b00, b01, b10, b11);
+			mma_bf16_16816(s[0], qa[ks], b00, b01);
+			mma_bf16_16816(s[1], qa[ks], b10, b11);
+		}
+		// scale (log2 units) and mask positions past the context or on invalid pages
+		const int tok0 = (p_begin + q) * blk;
+		const bool pg_ok = pg_s[q] >= 0 && !abort_flag;
+		float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+		for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+			for (int j = 0; j < 2; ++j) {
+				const bool ok = pg_ok && tok0 + nt * 8 + gc + j < ctx;
+				s[nt][j] = ok ? s[nt][j] * sl2 : -INFINITY;
+				s[nt][2 + j] = ok ? s[nt][2 + j] * sl2 : -INFINITY;
+				mx0 = fmaxf(mx0, s[nt][j]);
+				mx1 = fmaxf(mx1, s[nt][2 + j]);
 			}
-			// scale (log2 units) and mask positions past the context or on invalid pages
-			const int tok0 = (p_begin + q0) * blk;
-			float mx0 = -INFINITY, mx1 = -INFINITY;
+		// the row's max over the quad (the four lanes that hold one row)
+		mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 1));
+		mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 2));
+		mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 1));
+		mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 2));
+		const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+		const float al0 = (m0 == -INFINITY) ? 0.0f : exp2f(m0 - n0);
+		const float al1 = (m1 == -INFINITY) ? 0.0f : exp2f(m1 - n1);
+		m0 = n0;
+		m1 = n1;
+		float ps[2][4];
 #pragma unroll
-			for (int nt = 0; nt < 2; ++nt)
+		for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-				for (int j = 0; j < 2; ++j) {
-					const int t = kb + nt * 8 + gc + j;
-					const bool ok = tok0 + t < ctx && pg_s[q0 + t / blk] >= 0;
-					s[nt][j] = ok ? s[nt][j] * sl2 : -INFINITY;
-					s[nt][2 + j] = ok ? s[nt][2 + j] * sl2 : -INFINITY;
-					mx0 = fmaxf(mx0, s[nt][j]);
-					mx1 = fmaxf(mx1, s[nt][2 + j]);
-				}
-			// the row's max over the quad (the four lanes that hold one row)
-			mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 1));
-			mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 2));
-			mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 1));
-			mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 2));
-			const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-			const float al0 = (m0 == -INFINITY) ? 0.0f : exp2f(m0 - n0);
-			const float al1 = (m1 == -INFINITY) ? 0.0f : exp2f(m1 - n1);
-			m0 = n0;
-			m1 = n1;
-			float ps[2][4];
-			float sum0 = 0.0f, sum1 = 0.0f;
-#pragma unroll
-			for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-				for (int j = 0; j < 2; ++j) {
-					ps[nt][j] = (n0 == -INFINITY) ? 0.0f : exp2f(s[nt][j] - n0);
-					ps[nt][2 + j] = (n1 == -INFINITY) ? 0.0f : exp2f(s[nt][2 + j] - n1);
-				}
-			uint32_t pa[4];
-			pa[0] = pack_bf16(ps[0][0], ps[0][1]);
-			pa[1] = pack_bf16(ps[0][2], ps[0][3]);
-			pa[2] = pack_bf16(ps[1][0], ps[1][1]);
-			pa[3] = pack_bf16(ps[1][2], ps[1][3]);
-			// the sums add the rounded values, the weights the MMA applies
-#pragma unroll
-			for (int i = 0; i < 4; i += 2) {
-				sum0 += __uint_as_float(pa[i] << 16) + __uint_as_float(pa[i] & 0xFFFF0000u);
-				sum1 += __uint_as_float(pa[i + 1] << 16) + __uint_as_float(pa[i + 1] & 0xFFFF0000u);
+			for (int j = 0; j < 2; ++j) {
+				ps[nt][j] = (n0 == -INFINITY) ? 0.0f : exp2f(s[nt][j] - n0);
+				ps[nt][2 + j] = (n1 == -INFINITY) ? 0.0f : exp2f(s[nt][2 + j] - n1);
 			}
-			l0 = l0 * al0 + sum0;
-			l1 = l1 * al1 + sum1;
-			// O = O * alpha + P.V
-			// ldmatrix x4 trans: matrices (positions +0..7, dims dt), (+8..15, dt), (+0..7, dt+1),
-			// (+8..15, dt+1) are the B fragments of two 8-dim output tiles
-			const int vrow = kb + (mi & 1) * 8 + mr;
+		uint32_t pa[4];
+		pa[0] = pack_bf16(ps[0][0], ps[0][1]);
+		pa[1] = pack_bf16(ps[0][2], ps[0][3]);
+		pa[2] = pack_bf16(ps[1][0], ps[1][1]);
+		pa[3] = pack_bf16(ps[1][2], ps[1][3]);
+		// the sums add the rounded values, the weights the MMA applies
+		float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
-			for (int dt = 0; dt < HD / 8; dt += 2) {
+		for (int k = 0; k < 4; k += 2) {
+			sum0 += __uint_as_float(pa[k] << 16) + __uint_as_float(pa[k] & 0xFFFF0000u);
+			sum1 += __uint_as_float(pa[k + 1] << 16) + __uint_as_float(pa[k + 1] & 0xFFFF0000u);
+		}
+		l0 = l0 * al0 + sum0;
+		l1 = l1 * al1 + sum1;
+		// O = O * alpha (only when some row's max grew) + P.V; ldmatrix x4 trans: matrices
+		// (positions +0..7, dims dt), (+8..15, dt), (+0..7, dt+1), (+8..15, dt+1) are the B
+		// fragments of two 8-dim output tiles
+		if (__any_sync(0xFFFFFFFFu, al0 != 1.0f || al1 != 1.0f)) {
 #pragma unroll
-				for (int u = 0; u < 2; ++u) {
-					o[dt + u][0] *= al0;
-					o[dt + u][1] *= al0;
-					o[dt + u][2] *= al1;
-					o[dt + u][3] *= al1;
-				}
-				const int d16 = dt + (mi >> 1); // 8-dim chunk index over head_dim
-				uint32_t b0, b1, c0, c1;
-				ldsm_x4_trans(kv_sw_addr(vc, vrow, d16 & 7, d16 >> 3), b0, b1, c0, c1);
-				mma_bf16_16816(o[dt], pa, b0, b1);
-				mma_bf16_16816(o[dt + 1], pa, c0, c1);
+			for (int dt = 0; dt < HD / 8; ++dt) {
+				o[dt][0] *= al0;
+				o[dt][1] *= al0;
+				o[dt][2] *= al1;
+				o[dt][3] *= al1;
 			}
 		}
-		__syncthreads(); // every warp is done with the chunk's buffer
-		if (tid == 0 && c + kStBufs < n_chunks) issue(c + kStBufs);
+		const int vrow = (mi & 1) * 8 + mr;
+#pragma unroll
+		for (int dt = 0; dt < HD / 8; dt += 2) {
+			const int d16 = dt + (mi >> 1); // 8-dim chunk index over head_dim
+			uint32_t b0, b1, c0, c1;
+			ldsm_x4_trans(vc + page_sw_off(vrow, d16 & 7, d16 >> 3), b0, b1, c0, c1);
+			mma_bf16_16816(o[dt], pa, b0, b1);
+			mma_bf16_16816(o[dt + 1], pa, c0, c1);
+		}
+		__syncwarp(); // every lane is done with the stage
+		if (lane == 0 && issued < n_mine && !abort_flag) issue(issued++);
 	}
+	// a warp that gave up lets its copies in flight land before the ring is reused
+	if (abort_flag && lane == 0) {
+		for (int k = max(0, issued - kStBufs); k < issued; ++k) {
+			const uint64_t t0 = global_timer_ns();
+			while (!mbar_try_wait(&wbar[k % kStBufs], (uint32_t)(k / kStBufs) & 1u) && global_timer_ns() - t0 < kWaitLimitNs) {
+			}
+		}
+	}
+	__syncthreads(); // every warp is done with its ring
 
 	// merge the four warps: (m, l, O) per row through shared memory (the ring is idle now)
 	float* mo = reinterpret_cast<float*>(sm_raw);       // [warps][16][HD]
