@@ -289,6 +289,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 		}
 	}
 	pdl_wait();
+	// kEpiResid on one GPU with the CTA's rows in one window: this thread's residual row, read now
+	// so that the epilogue adds to a register instead of waiting on L2 after the last chunk
+	const bool res_pre = EPI == kEpiResid && !tp_on && n_rows <= kGemvFlushRows;
+	float res_row = 0.0f;
+	if (res_pre && ct < n_rows) res_row = a.resid[r0 + ct];
 
 	float xh[UPL][VEC];
 	bool norm_prolog = EpiTraits<EPI>::kNorm;
@@ -471,6 +476,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a)
 				Store<T>::put(reinterpret_cast<T*>(a.out) + row, d0);
 			} else if constexpr (EPI == kEpiResid) {
 				if (tp_on) tp_stage[row - r0] = d0;
+				else if (res_pre) a.resid[row] = res_row + d0; // row == r0 + ct (one window)
 				else a.resid[row] += d0;
 			} else if constexpr (EPI == kEpiSwiglu) {
 				Store<T>::put(reinterpret_cast<T*>(a.out) + (row >> 1), __fmul_rn(silu(d0), d1));
