@@ -225,6 +225,82 @@ def test_batched_decode_ragged_contexts_steps(cuda, preset):
             pos += 1
 
 
+# One-layer model with the Llama-3-8B attention geometry (8 q / 2 kv heads, head_dim 128,
+# 16-token pages) at a narrow width (d 1024, F 2048, vocab 8192) so that the double-accumulating
+# oracle handles thousands of positions in seconds.  Drift of the oracle between fp32 and double
+# accumulation (orc_set_accum_f32), max-abs logits: the last token of one 4096-token pass, and two
+# decode steps of 16 sequences with contexts 256-1024 fed the same ids.
+NARROW = dict(n_layers=1, vocab_size=8192, dim=1024, ffn_dim=2048, n_heads=8, n_kv_heads=2, head_dim=128)
+DRIFT_NARROW_PREFILL_4096 = 0.0060
+DRIFT_NARROW_BATCH16 = 0.0081
+
+
+def test_prefill_4096_chunk_against_oracle(cuda):
+    """One 4096-token pass, the prefill chunk config 5 runs (tcgen05 GEMMs, the tensor-core
+    causal attention over 256 pages): K and V of positions across the chunk in the paged cache
+    within one bf16 step of the oracle's, and the last token's logits within twice the measured
+    fp32 drift."""
+    cfg = I.preset(3, max_seq=4352, max_batch=1, **NARROW)
+    prompt = I.synth_ids(31, 4096, cfg.vocab_size)
+    positions = (0, 1, 15, 16, 2047, 2048, 4094, 4095)
+    with I.Engine(cfg) as eng:
+        lg, am = eng.forward(prompt, 0)
+        kv = {t: (eng.debug_read("k", 0, 0, t), eng.debug_read("v", 0, 0, t)) for t in positions}
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0)
+    o_lg, o_am = orc.forward(prompt, 0)
+    for t in positions:
+        for got, want in zip(kv[t], orc.kv(0, t)):
+            got = np.asarray(got, np.float64)
+            want = np.asarray(want, np.float64)
+            step = np.exp2(np.floor(np.log2(np.maximum(np.abs(want), 1e-30))) - 7)
+            assert bool(np.all(np.abs(got - want) <= step + 1e-6)), f"position {t}"
+            assert float(np.mean(got == want)) >= 0.95, f"position {t}"
+    orc.close()
+    bound = 2 * DRIFT_NARROW_PREFILL_4096
+    assert float(np.abs(lg - o_lg).max()) <= bound
+    assert cosine(lg, o_lg) >= COSINE_MIN
+    top = np.sort(o_lg)
+    assert am == o_am or top[-1] - top[-2] < bound
+
+
+def test_batched_decode_against_oracle(cuda):
+    """The batched decode step (tcgen05 projections, one mma attention launch over 16 sequences
+    with contexts 256-1024, LM-head GEMM with the row argmax) against the oracle, two steps, both
+    sides fed the oracle's greedy ids: every sequence's logits within twice the measured fp32
+    drift, and its id equal wherever the oracle's top-2 margin exceeds that bound."""
+    B = 16
+    cfg = I.preset(3, max_seq=1088, max_batch=B, **NARROW)
+    lens = I.synth_uniform(2, I.STREAM_CTX_LEN, B, 256, 1024)
+    prompts = [I.synth_ids(100 + i, int(lens[i]), cfg.vocab_size) for i in range(B)]
+    orc = O.OracleModel(I.oracle_dict(cfg), seed=0, n_slots=B)
+    fed = [[orc.forward(p, 0, slot=i)[1] for i, p in enumerate(prompts)]]
+    o_lg = []
+    for s in range(2):
+        lg, nxt = [], []
+        for i in range(B):
+            l, a = orc.forward([fed[s][i]], int(lens[i]) + s, slot=i)
+            lg.append(l)
+            nxt.append(a)
+        o_lg.append(np.stack(lg))
+        fed.append(nxt)
+    orc.close()
+    bound = 2 * DRIFT_NARROW_BATCH16
+    with I.Engine(cfg) as eng:
+        for i, p in enumerate(prompts):
+            eng.forward(p, 0, slot=i)
+        pos = lens.astype(np.uint32).copy()
+        for s in range(2):
+            lg, am = eng.forward_batch(np.arange(B), np.array(fed[s], np.uint32), pos, want_logits=True)
+            for i in range(B):
+                err = float(np.abs(lg[i] - o_lg[s][i]).max())
+                assert err <= bound, f"step {s} sequence {i}: max-abs {err}"
+                assert cosine(lg[i], o_lg[s][i]) >= COSINE_MIN, f"step {s} sequence {i}"
+                top = np.sort(o_lg[s][i])
+                if top[-1] - top[-2] > bound:
+                    assert am[i] == fed[s + 1][i], f"step {s} sequence {i}"
+            pos += 1
+
+
 def test_errors_are_returned_not_aborted(cuda):
     cfg = I.preset(1, max_seq=32)
     with I.Engine(cfg) as eng:
