@@ -335,15 +335,24 @@ typedef struct InfSampling {
 	u64 seed;
 } InfSampling;
 /* Temperature / top-k / top-p sampling for every token the model chooses from then on
- * (inf_generate, inf_decode, and the id inf_forward reports).  With m the largest logit, each
+ * (inf_generate, inf_decode, and the id inf_forward reports; per-slot settings for the batched
+ * step are inf_set_slot_sampling's).  With m the largest logit, each
  * token weighs q = min(floor(expf((logit - m) / temperature) * 2^32), 2^32 - 1); top-k keeps the
  * tokens at or above the k-th largest q, top-p then the fewest of those (ties kept) whose q sum to
  * at least ceil(top_p * their total); the token is the first, in id order, whose running sum of
  * kept q exceeds floor(r * total / 2^64), r the 64-bit Philox4x32-10 draw keyed by
  * SplitMix64(SplitMix64(seed) ^ 0x3000000) at counter (position, slot << 32).  Deterministic
- * for a seed.  Batch-1 decode on one GPU only (ErrorUnsupported under tensor parallelism);
- * inf_forward_batch stays greedy. */
+ * for a seed.  Batch-1 decode on one GPU only (ErrorUnsupported under tensor parallelism). */
 Error_t inf_set_sampling(Model* model, const InfSampling* sampling);
+/* Sampling settings of one sequence slot for the tokens inf_forward_batch (and the server)
+ * chooses for it: the rule above with the counter (position of the new token, 0), so a sequence
+ * draws exactly what the batch-1 decode of slot 0 with the same seed would from the same logits,
+ * whichever slot it runs in.  One sampler CTA per
+ * sampled row follows the batched LM head; rows of greedy slots keep their argmax.  Temperature
+ * 0 (the default of every slot) is greedy.  The settings stay with the slot until changed.
+ * One GPU only; vocab_size a multiple of 4.  No counterpart in the reference (it has no
+ * decoder); a serving loop sets it per request. */
+Error_t inf_set_slot_sampling(Model* model, u32 seq_slot, const InfSampling* sampling);
 
 /* ---- continuous batching ------------------------------------------------------------ */
 typedef struct InfServer InfServer;
@@ -355,8 +364,11 @@ typedef struct InfServer InfServer;
  * do not depend on the load), and retires sequences that produced eos_id, reached max_new tokens or
  * ran out of positions, releasing their pages.  A request is admitted only when the KV pool can
  * hold every position it may write (prompt + max_new - 1, at most max_seq) on top of what the
- * running requests reserved; until then it waits at the head of the queue.  Greedy only
- * (ErrorUnsupported at admission while sampling is on).  A request whose prefill fails is retired
+ * running requests reserved; until then it waits at the head of the queue.  Greedy unless a
+ * request asks for sampling (inf_server_submit_sampled): its slot then carries its settings
+ * (inf_set_slot_sampling) for its first token and every batched step, so its ids are what it would
+ * draw alone; the model-wide inf_set_sampling must be off (ErrorUnsupported at admission).  A
+ * request whose prefill fails is retired
  * with that error and the others go on; a failing batched step retires the requests of its batch
  * with its error and returns it.  Not thread-safe. */
 Error_t inf_server_create(Model* model, u32 max_active, InfServer** out);
@@ -373,6 +385,9 @@ Error_t inf_server_destroy(InfServer** server);
  * positions need more KV pages than the whole pool holds. */
 Error_t inf_server_submit(InfServer* server, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id,
                           u64* request_id);
+/* inf_server_submit with the request's own sampling settings (NULL or temperature 0: greedy). */
+Error_t inf_server_submit_sampled(InfServer* server, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id,
+                                  const InfSampling* sampling, u64* request_id);
 /* One scheduling step; *n_finished (may be NULL) = requests retired in it. */
 Error_t inf_server_step(InfServer* server, u32* n_finished);
 /* The ids a request has produced so far (out_ids NULL: count only), *done = 1 once retired,
@@ -500,6 +515,8 @@ typedef enum InfBuffer {
 	InfBufK      = 5, /* K the cache holds for (layer, slot, pos) [n_kv_heads * head_dim] */
 	InfBufV      = 6, /* V the cache holds for (layer, slot, pos) */
 	InfBufSampleQ = 7, /* the sampler's fixed-point weights of the last step [vocab_size], raw u32 bits */
+	InfBufSampleQRow = 8, /* the per-slot sampler's weights of row `pos` of the last sampled rows
+	                        (the batched step's row order; 0 after a single forward) [vocab_size], raw u32 bits */
 } InfBuffer;
 /* Copy one engine buffer to host floats (bf16 widened).  For test and debugging; the
  * reference's equivalent is print_dev_buf_bf16 (src/main.cu:44-61). */

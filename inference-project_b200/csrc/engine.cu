@@ -130,6 +130,11 @@ struct InfEngine {
 	InfSampling samp = {};      // temperature 0: greedy
 	bool sampling = false;
 	uint32_t* sample_q = nullptr; // [Vl] fixed-point weights of the sampler
+	// per-slot sampling of the batched step and the server (inf_set_slot_sampling)
+	std::vector<InfSampling> slot_samp; // [max_batch], temperature 0: greedy
+	SampleRow* rows_d = nullptr;        // [max_batch] the rows' settings on the device
+	SampleRow* rows_h = nullptr;        // [max_batch] pinned staging
+	uint32_t* sample_q_rows = nullptr;  // [max_batch][Vl] fixed-point weights of the rows
 	int graph_kernels = 0;
 	u64 launches = 0;
 	bool profiling = false;
@@ -987,6 +992,38 @@ Error_t enqueue_sample(InfEngine* e)
 	return Success;
 }
 
+// Rows of logits [n][Vl] whose slot samples (inf_set_slot_sampling) replace their greedy id in
+// ids_dev by a draw, one sampler CTA per row, the counter (pos_new[i], 0).  The caller
+// has synchronised the stream since the last use of the pinned row staging.
+Error_t enqueue_sample_rows(InfEngine* e, int n, const float* logits, const u32* slots, const u32* pos_new,
+                            uint32_t* ids_dev)
+{
+	bool any = false;
+	for (int i = 0; i < n; ++i) {
+		const InfSampling& s = e->slot_samp[slots[i]];
+		SampleRow& r = e->rows_h[i];
+		r.on = s.temperature > 0.0f;
+		r.inv_temp = r.on ? (float)(1.0 / (double)s.temperature) : 0.0f;
+		r.top_p = s.top_p;
+		r.top_k = s.top_k;
+		r.pos_new = (int)pos_new[i];
+		r.slot = 0; // the counter's high word: draws do not depend on which slot a sequence runs in
+		r.key = stream_key(s.seed, kSampleStream);
+		any = any || r.on;
+	}
+	if (!any) return Success;
+	INF_CUDA_TRY(cudaMemcpyAsync(e->rows_d, e->rows_h, sizeof(SampleRow) * n, cudaMemcpyHostToDevice, e->stream));
+	SampleRowsArgs a;
+	a.logits = logits;
+	a.q = e->sample_q_rows;
+	a.V = e->Vl;
+	a.rows = e->rows_d;
+	a.ids = ids_dev;
+	INF_CUDA_TRY(set_smem(k_sample_rows, kSampleSmem));
+	INF_CUDA_TRY(launch(e, k_sample_rows, dim3(n), dim3(kSampleThreads), kSampleSmem, a));
+	return Success;
+}
+
 // Final norm + LM head + argmax of one residual row (the decode GEMV); advances the ctl
 // block exactly like a decode step (pos += 1, id = argmax, or the sampled id).
 Error_t enqueue_lm_head_row(InfEngine* e, const float* resid_row)
@@ -1522,6 +1559,8 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	P.push(&e->best, 16);
 	P.push(&e->lm_counter, 16);
 	P.push(&e->sample_q, (u64)e->Vl * 4);
+	P.push(&e->rows_d, (u64)c.max_batch * sizeof(SampleRow));
+	P.push(&e->sample_q_rows, (u64)c.max_batch * e->Vl * 4);
 	P.push(&e->out_ids, (u64)e->max_out * 4);
 	P.push(&e->d_ids, (u64)c.max_seq * 4);
 	P.push(&e->attn_part, part_floats * 4);
@@ -1643,6 +1682,8 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	INF_CUDA_TRY(cudaMallocHost(&e->h_pin, sizeof(uint32_t) * (c.max_seq + 16)));
 	INF_CUDA_TRY(cudaMallocHost(&e->h_ctl, sizeof(int) * 2 * kCtlWords));
 	if (e->chunk > 0) INF_CUDA_TRY(cudaMallocHost(&e->h_tok, sizeof(int) * 2 * e->chunk));
+	INF_CUDA_TRY(cudaMallocHost(&e->rows_h, sizeof(SampleRow) * c.max_batch));
+	e->slot_samp.assign(c.max_batch, InfSampling{});
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
 	INF_TRY(build_decode_graph(e));
 	return Success;
@@ -1658,6 +1699,7 @@ void engine_free(InfEngine* e)
 	if (e->h_pin) cudaFreeHost(e->h_pin);
 	if (e->h_ctl) cudaFreeHost(e->h_ctl);
 	if (e->h_tok) cudaFreeHost(e->h_tok);
+	if (e->rows_h) cudaFreeHost(e->rows_h);
 	for (auto& ev : e->prof_ev)
 		if (ev) cudaEventDestroy(ev);
 	if (e->stream) cudaStreamDestroy(e->stream);
@@ -1896,7 +1938,18 @@ Error_t inf::forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const
 		for (u32 i = 0; i < n_seqs; ++i) {
 			f32* lo = logits_out ? logits_out + (size_t)i * e->Vl : nullptr;
 			u32* am = argmax_out ? argmax_out + i : nullptr;
-			INF_TRY(inf_forward(model, ids + i, 1, positions[i], seq_slots[i], lo, am));
+			const bool samp = host_args && seq_slots[i] < c.max_batch && e->slot_samp[seq_slots[i]].temperature > 0.0f;
+			if (!samp) {
+				INF_TRY(inf_forward(model, ids + i, 1, positions[i], seq_slots[i], lo, am));
+				continue;
+			}
+			u32 id = 0;
+			INF_TRY(inf_forward(model, ids + i, 1, positions[i], seq_slots[i], lo, &id));
+			INF_TRY(sample_slot_token(model, seq_slots[i], positions[i] + 1, &id));
+			if (am) {
+				if (is_device_ptr(am)) INF_CUDA_TRY(cudaMemcpy(am, &id, 4, cudaMemcpyHostToDevice));
+				else *am = id;
+			}
 		}
 		return Success;
 	}
@@ -1921,13 +1974,50 @@ Error_t inf::forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const
 	const Error_t eb = enqueue_decode_batch(e, (int)n_seqs);
 	e->gemm_split = false;
 	INF_TRY(eb);
+	{
+		std::vector<u32> pos_new(positions, positions + n_seqs);
+		for (u32& p : pos_new) ++p;
+		INF_TRY(enqueue_sample_rows(e, (int)n_seqs, e->logits_p, seq_slots, pos_new.data(), e->argmax_p));
+	}
 	if (logits_out) INF_TRY(copy_out(e, logits_out, e->logits_p, sizeof(float) * e->Vl * n_seqs));
 	if (argmax_out) INF_TRY(copy_out(e, argmax_out, e->argmax_p, sizeof(u32) * n_seqs));
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
 	return check_dev_err(e);
 }
 
+Error_t inf::sample_slot_token(Model* model, u32 slot, u32 pos_new, u32* id)
+{
+	if (!model || !model->engine || !id) return fail(ErrorInvalidValue, "sample_slot_token: NULL argument");
+	InfEngine* e = model->engine;
+	if (slot >= e->cfg.max_batch || !(e->slot_samp[slot].temperature > 0.0f)) return Success;
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream)); // the pinned row staging may feed an earlier copy
+	// the forward left its logits in e->logits; the drawn id replaces the chosen one in the ctl
+	// block as well, so a decode that continues from here feeds it
+	*reinterpret_cast<uint32_t*>(e->h_pin) = *id;
+	INF_CUDA_TRY(cudaMemcpyAsync(e->cur_id, e->h_pin, 4, cudaMemcpyHostToDevice, e->stream));
+	INF_TRY(enqueue_sample_rows(e, 1, e->logits, &slot, &pos_new, e->cur_id));
+	INF_CUDA_TRY(cudaMemcpyAsync(e->h_pin, e->cur_id, 4, cudaMemcpyDeviceToHost, e->stream));
+	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
+	*id = *reinterpret_cast<uint32_t*>(e->h_pin);
+	return check_dev_err(e);
+}
+
 extern "C" {
+
+Error_t inf_set_slot_sampling(Model* model, u32 seq_slot, const InfSampling* s)
+{
+	if (!model || !model->engine || !s) return fail(ErrorInvalidValue, "inf_set_slot_sampling: NULL argument");
+	InfEngine* e = model->engine;
+	if (seq_slot >= e->cfg.max_batch) return fail(ErrorInvalidValue, "slot %u >= max_batch", seq_slot);
+	if (!(s->temperature >= 0.0f) || !std::isfinite(s->temperature)) return fail(ErrorInvalidValue, "temperature %g", (double)s->temperature);
+	const bool on = s->temperature > 0.0f; // greedy settings need no top_p
+	if (on && !(s->top_p > 0.0f && s->top_p <= 1.0f)) return fail(ErrorInvalidValue, "top_p %g outside (0, 1]", (double)s->top_p);
+	if (on && e->cfg.tp_size > 1) return fail(ErrorUnsupported, "sampling with the vocabulary split across ranks");
+	if (on && 1.0 / (double)s->temperature > 3.0e38) return fail(ErrorInvalidValue, "temperature %g too small", (double)s->temperature);
+	if (on && e->Vl % 4 != 0) return fail(ErrorUnsupported, "per-slot sampling needs vocab_size %% 4 == 0");
+	e->slot_samp[seq_slot] = *s;
+	return Success;
+}
 
 Error_t inf_generate(Model* model, const u32* prompt, u32 n_prompt, u32 n_new, u32* out_ids, InfStats* stats)
 {
@@ -2128,6 +2218,12 @@ Error_t inf_debug_read(Model* model, u32 buffer, u32 layer, u32 seq_slot, u32 po
 	case InfBufH: src = e->h; n = (u64)e->Fl; break;
 	case InfBufLogits: src = e->logits; n = (u64)e->Vl; is_f32 = true; break;
 	case InfBufSampleQ: src = e->sample_q; n = (u64)e->Vl; is_f32 = true; break; // raw u32 bits
+	case InfBufSampleQRow:
+		if (pos >= c.max_batch) return fail(ErrorInvalidValue, "inf_debug_read: row %u >= max_batch", pos);
+		src = e->sample_q_rows + (size_t)pos * e->Vl;
+		n = (u64)e->Vl;
+		is_f32 = true;
+		break;
 	case InfBufK:
 	case InfBufV: {
 		if (layer >= c.n_layers || seq_slot >= c.max_batch || pos >= c.max_seq)

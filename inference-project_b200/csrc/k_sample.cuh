@@ -47,6 +47,26 @@ struct SampleArgs {
 	const int* pos;      // position of the new token (already advanced by the LM head)
 	const int* slot;
 	int max_out;
+	uint32_t* row_id;    // non-null: the id goes here only (a row of the batched step)
+};
+
+// One row of the batched decode step: its sequence's settings and the draw's counter.
+struct SampleRow {
+	float inv_temp;
+	float top_p;
+	uint32_t top_k;
+	uint32_t on;         // 0: keep the row's greedy id
+	int pos_new;         // position of the token being chosen
+	int slot;            // the draw counter's high word
+	PhiloxKey key;
+};
+
+struct SampleRowsArgs {
+	const float* logits; // [rows][V]
+	uint32_t* q;         // [rows][V] scratch
+	int V;               // multiple of 4 (16-byte aligned rows)
+	const SampleRow* rows;
+	uint32_t* ids;       // [rows]: greedy ids in, sampled ids out where on
 };
 
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v)
@@ -158,11 +178,10 @@ __device__ uint32_t sample_radix_select(const SampleArgs& a, uint32_t floor_t, b
 	return prefix;
 }
 
-__global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
+// The whole draw of one token by one CTA of kSampleThreads threads (sub: the dynamic shared
+// memory of kSampleSmem bytes).
+__device__ __forceinline__ void sample_token(const SampleArgs& a, unsigned long long* sub)
 {
-	pdl_wait();
-	pdl_trigger();
-	extern __shared__ unsigned long long sub[]; // [kSampleWarps][kSampleSubStride]
 	__shared__ unsigned long long hist[256];
 	__shared__ unsigned long long red[kSampleThreads / 32];
 	__shared__ float redf[kSampleThreads / 32];
@@ -289,15 +308,56 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
 				cc += v[k];
 				if (cc > s) {
 					const uint32_t id = (uint32_t)(wbase + r * 128 + lane * 4 + k);
-					*a.cur_id = id;
-					const uint32_t st = *a.step;
-					if (st >= 1 && (int)(st - 1) < a.max_out) a.out_ids[st - 1] = id;
+					if (a.row_id) {
+						*a.row_id = id;
+					} else {
+						*a.cur_id = id;
+						const uint32_t st = *a.step;
+						if (st >= 1 && (int)(st - 1) < a.max_out) a.out_ids[st - 1] = id;
+					}
 					break;
 				}
 			}
 		}
 		break;
 	}
+}
+
+__global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a)
+{
+	pdl_wait();
+	pdl_trigger();
+	extern __shared__ unsigned long long sample_sub[]; // [kSampleWarps][kSampleSubStride]
+	sample_token(a, sample_sub);
+}
+
+// One CTA per row of the batched decode step: rows with sampling on replace their greedy id
+// by a draw under their sequence's settings, the counter being (position of the new token,
+// SampleRow::slot) -- the engine passes 0, so a sequence draws what the batch-1 decode of slot 0
+// would, whichever slot it runs in.
+__global__ void __launch_bounds__(kSampleThreads) k_sample_rows(const SampleRowsArgs ra)
+{
+	pdl_wait();
+	pdl_trigger();
+	extern __shared__ unsigned long long sample_sub[];
+	const SampleRow& r = ra.rows[blockIdx.x];
+	if (!r.on) return;
+	SampleArgs a;
+	a.logits = ra.logits + (size_t)blockIdx.x * ra.V;
+	a.q = ra.q + (size_t)blockIdx.x * ra.V;
+	a.V = ra.V;
+	a.inv_temp = r.inv_temp;
+	a.top_p = r.top_p;
+	a.top_k = r.top_k;
+	a.key = r.key;
+	a.cur_id = nullptr;
+	a.out_ids = nullptr;
+	a.step = nullptr;
+	a.pos = &r.pos_new;
+	a.slot = &r.slot;
+	a.max_out = 0;
+	a.row_id = ra.ids + blockIdx.x;
+	sample_token(a, sample_sub);
 }
 
 } // namespace inf

@@ -37,4 +37,8 @@ bool model_sampling_on(const Model* m);
 Error_t forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const u32* ids, const u32* positions,
                       f32* logits_out, u32* argmax_out, bool single_batched);
 
+// After an inf_forward of `slot` whose new token sits at pos_new: replaces *id (the token the
+// forward chose) by a draw under the slot's inf_set_slot_sampling settings, when they sample.
+Error_t sample_slot_token(Model* model, u32 slot, u32 pos_new, u32* id);
+
 } // namespace inf

@@ -20,6 +20,8 @@
 // src/main.cu:396-412); this is the scheduler a caller would otherwise write around
 // inf_forward_batch.
 #include <algorithm>
+#include <cmath>
+#include <cstring>
 #include <deque>
 #include <memory>
 #include <unordered_map>
@@ -39,6 +41,7 @@ struct Backend {
 	virtual u32 kv_block() const = 0; // positions per KV page
 	virtual u32 kv_pages() const = 0; // pages in the pool, shared by all slots
 	virtual Error_t release(u32 slot) = 0;
+	virtual Error_t set_sampling(u32 slot, const InfSampling& s) = 0; // the slot's request's settings
 	virtual Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) = 0;
 	virtual Error_t decode(u32 n, const u32* slots, const u32* ids, const u32* pos, u32* next) = 0;
 };
@@ -55,11 +58,14 @@ struct ModelBackend final : Backend {
 		return c.kv_pages ? c.kv_pages : c.max_batch * ((c.max_seq + kv_block() - 1) / kv_block());
 	}
 	Error_t release(u32 slot) override { return inf_seq_reset(m, slot); }
+	Error_t set_sampling(u32 slot, const InfSampling& s) override { return inf_set_slot_sampling(m, slot, &s); }
 	Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) override
 	{
-		// the batched decode is greedy; a sampled first token would mix two rules in one sequence
-		if (model_sampling_on(m)) return fail(ErrorUnsupported, "the server decodes greedily; turn sampling off");
-		return inf_forward(m, ids, n, 0, slot, nullptr, next);
+		// requests carry their own settings (per slot); the model-wide batch-1 setting would mix a
+		// second rule into the first token
+		if (model_sampling_on(m)) return fail(ErrorUnsupported, "the server samples per request; turn inf_set_sampling off");
+		INF_TRY(inf_forward(m, ids, n, 0, slot, nullptr, next));
+		return sample_slot_token(m, slot, n, next); // the new token sits at position n
 	}
 	Error_t decode(u32 n, const u32* s, const u32* ids, const u32* pos, u32* next) override
 	{
@@ -77,8 +83,9 @@ struct SyntheticBackend final : Backend {
 	u32 n_slots, seq, vocab, pages;
 	std::vector<u32> filled;   // positions written per slot
 	std::vector<char> poison;  // slot's prompt started with vocab - 1
+	std::vector<u64> salt;     // per slot: 0 greedy, else derived from the request's seed and settings
 	SyntheticBackend(u32 s, u32 ms, u32 v, u32 p)
-	    : n_slots(s), seq(ms), vocab(v), pages(p ? p : s * ((ms + 15) / 16)), filled(s, 0), poison(s, 0)
+	    : n_slots(s), seq(ms), vocab(v), pages(p ? p : s * ((ms + 15) / 16)), filled(s, 0), poison(s, 0), salt(s, 0)
 	{
 	}
 	u32 slots() const override { return n_slots; }
@@ -107,6 +114,17 @@ struct SyntheticBackend final : Backend {
 		poison[slot] = 0;
 		return Success;
 	}
+	// a sampling request's ids are a different hash, keyed by its seed and settings, so that a
+	// test can see each request's settings reach the slot it runs in
+	Error_t set_sampling(u32 slot, const InfSampling& s) override
+	{
+		if (slot >= n_slots) return fail(ErrorInvalidValue, "slot %u", slot);
+		u32 tb = 0, pb = 0;
+		memcpy(&tb, &s.temperature, 4);
+		memcpy(&pb, &s.top_p, 4);
+		salt[slot] = s.temperature > 0.0f ? (mix(s.seed) | 1ull) ^ ((u64)tb << 17) ^ ((u64)pb << 3) ^ s.top_k : 0;
+		return Success;
+	}
 	Error_t prefill(const u32* ids, u32 n, u32 slot, u32* next) override
 	{
 		if (slot >= n_slots || n == 0 || n > seq) return fail(ErrorInvalidValue, "prefill slot %u n %u", slot, n);
@@ -116,7 +134,7 @@ struct SyntheticBackend final : Backend {
 		for (u32 i = 0; i < n; ++i) h = mix(h * 31 + ids[i]);
 		filled[slot] = n;
 		poison[slot] = ids[0] == vocab - 1;
-		*next = mix(h ^ ((u64)n << 40)) % vocab;
+		*next = mix(h ^ ((u64)n << 40) ^ salt[slot]) % vocab;
 		return Success;
 	}
 	Error_t decode(u32 n, const u32* s, const u32* ids, const u32* pos, u32* next) override
@@ -134,7 +152,7 @@ struct SyntheticBackend final : Backend {
 			for (u32 i = 0; i < n; ++i) filled[s[i]] = pos[i];
 			return fail(ErrorArenaOutOfMemory, "KV cache out of pages");
 		}
-		for (u32 i = 0; i < n; ++i) next[i] = mix(((u64)ids[i] << 32) ^ pos[i]) % vocab;
+		for (u32 i = 0; i < n; ++i) next[i] = mix(((u64)ids[i] << 32) ^ pos[i] ^ salt[s[i]]) % vocab;
 		return Success;
 	}
 };
@@ -148,6 +166,7 @@ struct Request {
 	u32 pos = 0;      // position of the last output token (the next one fed)
 	u64 admitted = 0; // the step that prefilled it
 	u32 pages = 0;    // KV pages reserved while it holds a slot
+	InfSampling samp{}; // temperature 0: greedy
 	bool done = false;
 	Error_t err = Success;
 };
@@ -245,9 +264,20 @@ Error_t inf_server_destroy(InfServer** s)
 
 Error_t inf_server_submit(InfServer* s, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id, u64* request_id)
 {
+	return inf_server_submit_sampled(s, prompt, n_prompt, max_new, eos_id, nullptr, request_id);
+}
+
+Error_t inf_server_submit_sampled(InfServer* s, const u32* prompt, u32 n_prompt, u32 max_new, u32 eos_id,
+                                  const InfSampling* sampling, u64* request_id)
+{
 	if (!s || !prompt || !request_id || n_prompt == 0 || max_new == 0) return fail(ErrorInvalidValue, "inf_server_submit: arguments");
 	if (n_prompt >= s->be->max_seq()) return fail(ErrorKvOutOfRange, "prompt of %u tokens, %u positions per slot", n_prompt, s->be->max_seq());
+	if (sampling && (!(sampling->temperature >= 0.0f) || !std::isfinite(sampling->temperature) ||
+	                 (sampling->temperature > 0.0f && !(sampling->top_p > 0.0f && sampling->top_p <= 1.0f))))
+		return fail(ErrorInvalidValue, "inf_server_submit: temperature %g, top_p %g", (double)sampling->temperature,
+		            (double)sampling->top_p);
 	Request r;
+	if (sampling) r.samp = *sampling;
 	r.prompt.assign(prompt, prompt + n_prompt);
 	r.max_new = max_new;
 	r.eos = eos_id;
@@ -278,7 +308,8 @@ Error_t inf_server_step(InfServer* s, u32* n_finished)
 		s->free_slots.pop_back();
 		r.admitted = step;
 		u32 first = 0;
-		const Error_t e = s->be->prefill(r.prompt.data(), (u32)r.prompt.size(), (u32)r.slot, &first);
+		Error_t e = s->be->set_sampling((u32)r.slot, r.samp);
+		if (e == Success) e = s->be->prefill(r.prompt.data(), (u32)r.prompt.size(), (u32)r.slot, &first);
 		if (e != Success) { // this request fails alone; the others go on
 			r.err = e;
 			INF_TRY(retire(s, r));

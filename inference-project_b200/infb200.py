@@ -93,7 +93,7 @@ EXPORTS = [
     "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
     "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
     "inf_safetensors_read", "inf_tokenizer_build", "inf_tokenizer_destroy", "inf_tokenizer_vocab_size",
-    "inf_tokenizer_encode", "inf_tokenizer_encode_special", "inf_tokenizer_decode", "inf_set_sampling", "inf_server_create",
+    "inf_tokenizer_encode", "inf_tokenizer_encode_special", "inf_tokenizer_decode", "inf_set_sampling", "inf_set_slot_sampling", "inf_server_submit_sampled", "inf_server_create",
     "inf_server_create_synthetic", "inf_server_destroy", "inf_server_submit", "inf_server_step", "inf_server_result",
     "inf_server_release", "inf_server_stats",
 ]
@@ -172,6 +172,8 @@ def lib():
         "inf_tokenizer_encode_special": (E, [vp, C.c_char_p, vp, u64, C.POINTER(u64)]),
         "inf_tokenizer_decode": (E, [vp, vp, u64, C.c_char_p, u64, C.POINTER(u64)]),
         "inf_set_sampling": (E, [C.POINTER(Model), C.POINTER(InfSampling)]),
+        "inf_set_slot_sampling": (E, [C.POINTER(Model), u32, C.POINTER(InfSampling)]),
+        "inf_server_submit_sampled": (E, [vp, vp, u32, u32, u32, C.POINTER(InfSampling), C.POINTER(u64)]),
         "inf_server_create": (E, [C.POINTER(Model), u32, C.POINTER(vp)]),
         "inf_server_create_synthetic": (E, [u32, u32, u32, u32, u32, C.POINTER(vp)]),
         "inf_server_destroy": (E, [C.POINTER(vp)]),
@@ -320,10 +322,17 @@ class Server:
             check(lib().inf_server_create_synthetic(n_slots, max_seq, vocab, kv_pages, max_active, C.byref(self.h)),
                   "inf_server_create_synthetic")
 
-    def submit(self, prompt, max_new: int, eos: int = NO_EOS) -> int:
+    def submit(self, prompt, max_new: int, eos: int = NO_EOS, sampling: tuple | None = None) -> int:
+        """sampling: (temperature, top_p, top_k, seed) for this request (inf_server_submit_sampled)."""
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
         rid = u64()
-        check(lib().inf_server_submit(self.h, _ptr(p), p.size, max_new, eos, C.byref(rid)), "inf_server_submit")
+        if sampling is None:
+            check(lib().inf_server_submit(self.h, _ptr(p), p.size, max_new, eos, C.byref(rid)), "inf_server_submit")
+        else:
+            t, tp, tk, seed = sampling
+            smp = InfSampling(temperature=t, top_p=tp, top_k=tk, reserved=0, seed=seed)
+            check(lib().inf_server_submit_sampled(self.h, _ptr(p), p.size, max_new, eos, C.byref(smp), C.byref(rid)),
+                  "inf_server_submit_sampled")
         return rid.value
 
     def step(self) -> int:
@@ -471,7 +480,7 @@ class Engine:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         check(lib().inf_tp_connect(C.byref(self.model), buf, len(handles)), "inf_tp_connect")
 
-    BUFFERS = {"resid": 0, "q": 1, "attn": 2, "h": 3, "logits": 4, "k": 5, "v": 6, "sample_q": 7}
+    BUFFERS = {"resid": 0, "q": 1, "attn": 2, "h": 3, "logits": 4, "k": 5, "v": 6, "sample_q": 7, "sample_q_row": 8}
 
     def debug_read(self, name: str, layer: int = 0, slot: int = 0, pos: int = 0) -> np.ndarray:
         n = max(self.cfg.dim, self.cfg.ffn_dim, self.V, self.cfg.n_heads * self.cfg.head_dim)
@@ -482,14 +491,19 @@ class Engine:
         sizes = {"resid": self.cfg.dim, "q": self.cfg.n_heads // tp * self.cfg.head_dim,
                  "attn": self.cfg.n_heads // tp * self.cfg.head_dim, "h": self.cfg.ffn_dim // tp, "logits": self.V,
                  "k": self.cfg.n_kv_heads // tp * self.cfg.head_dim, "v": self.cfg.n_kv_heads // tp * self.cfg.head_dim,
-                 "sample_q": self.V}
+                 "sample_q": self.V, "sample_q_row": self.V}
         r = out[:sizes[name]].copy()
-        return r.view(np.uint32) if name == "sample_q" else r
+        return r.view(np.uint32) if name in ("sample_q", "sample_q_row") else r
 
     def set_sampling(self, temperature: float, top_p: float = 1.0, top_k: int = 0, seed: int = 0):
         """inf_set_sampling; temperature 0 restores greedy decoding."""
         s = InfSampling(temperature=temperature, top_p=top_p, top_k=top_k, reserved=0, seed=seed)
         check(lib().inf_set_sampling(C.byref(self.model), C.byref(s)), "inf_set_sampling")
+
+    def set_slot_sampling(self, slot: int, temperature: float, top_p: float = 1.0, top_k: int = 0, seed: int = 0):
+        """inf_set_slot_sampling: the slot's settings for the batched step; temperature 0 is greedy."""
+        s = InfSampling(temperature=temperature, top_p=top_p, top_k=top_k, reserved=0, seed=seed)
+        check(lib().inf_set_slot_sampling(C.byref(self.model), slot, C.byref(s)), "inf_set_slot_sampling")
 
     def reset(self, slot: int = 0):
         check(lib().inf_seq_reset(C.byref(self.model), slot), "inf_seq_reset")

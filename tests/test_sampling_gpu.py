@@ -96,3 +96,44 @@ def test_ragged_vocabulary(cuda):
         e.set_sampling(0.7, 1.0, 50257 - 3, seed=9)  # top-k just below the vocabulary
         ids, _ = e.decode(tok, pos, 1)
         assert int(ids[0]) == O.sample_select(e.debug_read("sample_q"), 1.0, 50257 - 3, 9, pos + 1)
+
+
+def test_batched_step_samples_each_slot_like_the_oracle(cuda):
+    """inf_set_slot_sampling: in the batched step each row draws under its own slot's settings.
+    The oracle's integer rule on the row's fixed-point weights (read back) gives the device's id
+    with the counter (position of the new token, 0); the weights agree with the oracle's from the
+    row's logits to within the fp32 exponential's rounding; greedy slots keep their argmax."""
+    cfg = I.preset(2, n_layers=2, max_seq=256, max_batch=8)
+    B = 8
+    settings = {0: (0.9, 0.9, 0, 5), 1: (1.3, 1.0, 40, 6), 2: (0.6, 0.5, 200, 7), 4: (1.0, 0.95, 0, 8),
+                5: (0.7, 1.0, 0, 9)}
+    with I.Engine(cfg, seed=0) as e:
+        cur, lens = [], []
+        for i in range(B):
+            p = O.gen_ids(40 + i, 10 + 7 * i, cfg.vocab_size)
+            _, am = e.forward(p, 0, slot=i)
+            cur.append(am)
+            lens.append(p.size)
+        for sl, (t, tp, tk, seed) in settings.items():
+            e.set_slot_sampling(sl, t, tp, tk, seed)
+        pos = np.array(lens, np.uint32)
+        differs = 0
+        for _ in range(6):
+            lg, am = e.forward_batch(np.arange(B), np.array(cur, np.uint32), pos, want_logits=True)
+            for i in range(B):
+                if i in settings:
+                    t, tp, tk, seed = settings[i]
+                    q = e.debug_read("sample_q_row", pos=i)
+                    assert int(am[i]) == O.sample_select(q, tp, tk, seed, int(pos[i]) + 1), f"row {i}"
+                    q_orc = O.sample_weights(lg[i], float(np.float32(1.0 / t))).astype(np.int64)
+                    assert np.all(np.abs(q_orc - q.astype(np.int64)) <= np.maximum(4, q_orc >> 20))
+                    differs += int(am[i]) != int(np.argmax(lg[i]))
+                else:
+                    assert int(am[i]) == int(np.argmax(lg[i])), f"greedy row {i}"
+            cur = [int(x) for x in am]
+            pos += 1
+        assert differs > 0  # the draws are not all the greedy choice
+        for sl in settings:
+            e.set_slot_sampling(sl, 0.0)
+        lg, am = e.forward_batch(np.arange(B), np.array(cur, np.uint32), pos, want_logits=True)
+        np.testing.assert_array_equal(am, np.argmax(lg, axis=1))  # greedy restored

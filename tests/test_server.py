@@ -182,3 +182,53 @@ def test_failing_batched_step_retires_its_requests():
         for rid in later:
             out, done, rc = s.result(rid)
             assert done and rc == 0 and out.size == 10
+
+
+def run_sampled(server, reqs):
+    """Submit (prompt, max_new, sampling or None) at step 0 and step until all retire."""
+    rids = [server.submit(p, m, I.NO_EOS, sampling=smp) for p, m, smp in reqs]
+    for _ in range(10_000):
+        server.step()
+        if all(server.result(r)[1] for r in rids):
+            return [server.result(r) for r in rids]
+    raise AssertionError("requests did not retire")
+
+
+def test_each_request_keeps_its_own_sampling_settings():
+    """Per-request settings (inf_server_submit_sampled) reach the slot the request runs in: the
+    stand-in's ids for a sampling request are a hash keyed by its settings.  A request's ids do not
+    depend on what shares its batch, two seeds differ, a greedy request between sampling ones
+    stays greedy, and a slot that a sampling request used serves a later greedy request greedily."""
+    rng = np.random.default_rng(7)
+    base = requests(rng, 12, 1000, 128)
+    settings = [None, (0.8, 0.9, 0, 1), (1.2, 1.0, 40, 2), None, (0.8, 0.9, 0, 3)]
+    reqs = [(p, m, settings[i % len(settings)]) for i, (p, m, _) in enumerate(base)]
+    with I.Server(synthetic=(3, 128, 1000)) as s:
+        together = run_sampled(s, reqs)
+    for (p, m, smp), (out, done, rc) in zip(reqs, together):
+        assert done and rc == 0 and out.size == m
+        with I.Server(synthetic=(1, 128, 1000)) as alone:
+            (solo, _, _), = run_sampled(alone, [(p, m, smp)])
+        np.testing.assert_array_equal(out, solo)
+        follows_greedy = all(out[k] == synthetic_next(int(out[k - 1]), len(p) + k - 1, 1000) for k in range(1, out.size))
+        if smp is None:
+            assert follows_greedy
+        elif out.size > 3:
+            assert not follows_greedy
+    # the same request under two seeds
+    p, m, _ = reqs[1]
+    outs = []
+    for seed in (11, 12):
+        with I.Server(synthetic=(1, 128, 1000)) as alone:
+            (o, _, _), = run_sampled(alone, [(p, 20, (0.8, 0.9, 0, seed))])
+            outs.append(o)
+    assert not np.array_equal(outs[0], outs[1])
+
+
+def test_sampling_settings_are_checked_at_submit():
+    with I.Server(synthetic=(1, 64, 100)) as s:
+        for bad in [(-1.0, 1.0, 0, 0), (1.0, 0.0, 0, 0), (1.0, 1.5, 0, 0), (float("nan"), 1.0, 0, 0)]:
+            with pytest.raises(I.InfError) as e:
+                s.submit(np.arange(4, dtype=np.uint32), 4, I.NO_EOS, sampling=bad)
+            assert e.value.code == 4
+        s.submit(np.arange(4, dtype=np.uint32), 4, I.NO_EOS, sampling=(0.0, 0.0, 0, 0))  # temperature 0: greedy, top_p unused

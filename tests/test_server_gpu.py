@@ -50,7 +50,53 @@ def test_batched_requests_equal_solo_runs(cuda):
         assert int(first[0]) == int(together[0][0][0])
 
 
+def test_sampled_requests_equal_solo_runs(cuda):
+    """Requests with their own sampling settings (inf_server_submit_sampled) among greedy ones:
+    every request's ids equal its run alone (the draws do not depend on the slot or the batch),
+    a sampled request's first id is the batch-1 prefill followed by the same rule (the decode of
+    slot 0 with its settings), and the sampled requests do not all decode greedily."""
+    cfg = I.preset(2, n_layers=2, max_seq=256, max_batch=8)
+    rng = np.random.default_rng(9)
+    reqs = []
+    for i in range(10):
+        smp = (0.8 + 0.05 * i, 0.9, 0 if i % 3 else 50, 100 + i) if i % 2 == 0 else None
+        reqs.append((O.gen_ids(60 + i, int(rng.integers(5, 50)), cfg.vocab_size), int(rng.integers(6, 20)), smp))
+
+    def run(server, batch):
+        rids = [server.submit(p, m, I.NO_EOS, sampling=smp) for p, m, smp in batch]
+        for _ in range(2000):
+            server.step()
+            if all(server.result(r)[1] for r in rids):
+                return [server.result(r) for r in rids]
+        raise AssertionError("requests did not retire")
+
+    with I.Engine(cfg, seed=0) as eng:
+        with I.Server(eng) as s:
+            together = run(s, reqs)
+        sampled_differs = 0
+        for (p, m, smp), (out, done, status) in zip(reqs, together):
+            assert done and status == 0 and out.size == m
+            with I.Server(eng, max_active=1) as alone:
+                (solo, _, _), = run(alone, [(p, m, smp)])
+            np.testing.assert_array_equal(out, solo)
+            if smp is not None:
+                with I.Server(eng, max_active=1) as alone:
+                    (greedy, _, _), = run(alone, [(p, m, None)])
+                sampled_differs += int(not np.array_equal(out, greedy))
+        assert sampled_differs > 0
+        # the first id: the batch-1 prefill, then the batch-1 sampler of slot 0 with the same settings
+        p, m, (t, tp, tk, seed) = reqs[0]
+        eng.reset(0)
+        eng.set_sampling(t, tp, tk, seed)
+        try:
+            first, _ = eng.generate(p, 1)
+        finally:
+            eng.set_sampling(0.0)
+        assert int(first[0]) == int(together[0][0][0])
+
+
 def test_server_refuses_sampling(cuda):
+    """Model-wide sampling (inf_set_sampling) is refused at admission: requests carry their own."""
     cfg = I.preset(2, n_layers=1, max_seq=64, max_batch=2)
     with I.Engine(cfg, seed=0) as eng:
         eng.set_sampling(1.0, 0.9, 0, seed=1)
