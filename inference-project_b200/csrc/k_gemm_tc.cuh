@@ -234,11 +234,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 	if (warp == 0) {
 		if (lane == 0) {
-			pdl_wait(); // X is written by the previous kernel
 			const uint64_t pol_w = policy_evict_first();
 			const uint64_t pol_x = policy_evict_last();
-			int issued = 0;
-			for (int kb = 0; kb < n_kb; ++kb) {
+			// the first stages' weight tiles before the dependency wait (W is never written by a
+			// kernel of the step); their X tiles, which the previous kernel writes, after it
+			const int pre = min(n_kb, kTcStages);
+			for (int kb = 0; kb < pre; ++kb) {
+				mbar_arrive_expect_tx(&full[kb], kTcStageBytes);
+				tma_load_2d(tiles + (size_t)kb * kTcStageBytes + kTcStageA, &tm_w, (kb0 + kb) * kTcBK, n_tile * kTcBN,
+				            &full[kb], pol_w);
+			}
+			pdl_wait();
+			for (int kb = 0; kb < pre; ++kb)
+				tma_load_2d(tiles + (size_t)kb * kTcStageBytes, &tm_x, (kb0 + kb) * kTcBK, m_tile * kTcBM, &full[kb], pol_x);
+			int issued = pre;
+			for (int kb = pre; kb < n_kb; ++kb) {
 				const int s = kb % kTcStages;
 				if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort_flag, a.err)) break;
 				uint8_t* sa = tiles + (size_t)s * kTcStageBytes;
