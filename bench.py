@@ -514,7 +514,7 @@ def run_workload(args, rank: int, world: int, dist):
             pos += 1
         torch.cuda.synchronize()
         barrier()
-        l0 = eng.launches
+        l0, h0 = eng.launches, eng.batch_h2d_bytes
         with ClockSampler(local) as clk:
             torch.cuda.nvtx.range_push("timed")
             w0 = time.perf_counter()
@@ -526,7 +526,7 @@ def run_workload(args, rank: int, world: int, dist):
             torch.cuda.synchronize()
             wall = time.perf_counter() - w0
             torch.cuda.nvtx.range_pop()
-        launches = eng.launches - l0
+        launches, h2d = eng.launches - l0, (eng.batch_h2d_bytes - h0) / args.steps
         barrier()
         ms, wall = max_over_ranks(ev0.elapsed_time(ev1)), max_over_ranks(wall)
         avg_ctx = float(lens.mean()) + args.warmup + (args.steps - 1) / 2
@@ -549,7 +549,7 @@ def run_workload(args, rank: int, world: int, dist):
                              "frac": achieved / hbm_peak, "traffic": None,
                              "kernel": "whole batched step (tcgen05 projections, split-K attention)",
                              "peak_kind": hbm_kind},
-                "e2e": {"value": B * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 12 * B,
+                "e2e": {"value": B * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": 4 * B},
                 "gpu_launches": launches, "clocks": clk.summary(),
             }), flush=True)

@@ -525,6 +525,9 @@ const char* inf_error_string(Error_t err);
 const char* inf_last_error_detail(void);
 void*       inf_model_stream(Model* model);
 u64         inf_kernel_launches(Model* model);
+/* Bytes inf_forward_batch has copied host -> device so far (ids, positions, slots and the
+ * attention work list of each step); the ids it returns are the device -> host side. */
+u64         inf_batch_h2d_bytes(Model* model);
 /* Bytes the decode step of one token streams from HBM: weights + KV read for ctx. */
 u64         inf_decode_bytes(const InfConfig* config, u32 ctx);
 /* Time each kernel kind of one eager (non-graph) decode step of token `id` at `pos` of

@@ -96,6 +96,12 @@ struct InfEngine {
 	float* attn_part = nullptr;  // split partials, sized for the larger of batch 1 and max_batch
 	int attn_splits_batch = 1;    // splits when max_batch tokens share one launch
 	int attn_max_pages_split_batch = 1;
+	// batched mma attention work list: (token, split | splits << 16) per unit, longest first
+	int* attn_units = nullptr;    // [max_batch * attn_unit_splits] int2
+	int* h_units = nullptr;       // pinned staging
+	int attn_unit_splits = 1;     // the most splits of one token (stride of the split partials)
+	int n_attn_units = 0;         // units of the batched step being enqueued (0: no list)
+	u64 h2d_bytes = 0;            // bytes staged host -> device by the batched step
 	float* logits_p = nullptr;    // [max_batch][Vl] batched-decode logits
 	uint32_t* argmax_p = nullptr; // [max_batch]
 	unsigned long long* batch_keys = nullptr; // [max_batch] argmax keys, zero between steps
@@ -816,9 +822,20 @@ Error_t tensor_map_kv(CUtensorMap* m, const void* base, u32 hd, u32 blk, u32 kv,
 	return Success;
 }
 
+// The RMSNorm that follows a residual projection (its gain, bf16 output and epsilon); when the
+// projection is split across K the norm runs inside the split-K sum (k_gemm_splitk_resid_norm)
+// and *done is set, otherwise the caller launches k_rmsnorm_rows.
+struct NormNext {
+	const void* gain;
+	void* out;
+	float eps;
+	bool* done;
+};
+
 // D[T x N] = X[T x K] . W[N x K]^T on the tensor cores, fused epilogue a.epi
-Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
+Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a, const NormNext* nn = nullptr)
 {
+	if (nn) *nn->done = false;
 	if (a.K % 8 != 0) return fail(ErrorUnsupported, "gemm: K %% 8 != 0");
 	CUtensorMap tx, tw;
 	INF_TRY(tensor_map_2d(&tx, X, (u64)a.T, (u64)a.K, kTcBM));
@@ -826,9 +843,8 @@ Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
 	const size_t smem = gemm_tc_smem_bytes();
 	INF_CUDA_TRY(set_smem(k_gemm_tc, smem));
 	a.err = e->err;
-	dim3 grid((a.N + kTcBN - 1) / kTcBN, (a.T + kTcBM - 1) / kTcBM);
 	// too few output tiles to stream the weights on every SM: split K across CTAs
-	const int tiles = (int)(grid.x * grid.y), n_kb = (a.K + kTcBK - 1) / kTcBK;
+	const int tiles = ((a.N + kTcBN - 1) / kTcBN) * ((a.T + kTcBM - 1) / kTcBM), n_kb = (a.K + kTcBK - 1) / kTcBK;
 	int splits = 1;
 	if (e->gemm_split && e->gemm_part && tiles * 2 <= e->sm_count) {
 		splits = std::min(e->sm_count / tiles, n_kb / 2);
@@ -838,20 +854,27 @@ Error_t launch_gemm_tc(InfEngine* e, const void* X, const void* W, TcArgs a)
 	if (splits >= 2) {
 		a.k_splits = splits;
 		a.partial = e->gemm_part;
-		grid.z = splits;
-		INF_CUDA_TRY(launch(e, k_gemm_tc, grid, dim3(kTcThreads), smem, tx, tw, a));
+		// persistent CTAs over the (tile, split) units, at most one per SM
+		INF_CUDA_TRY(launch(e, k_gemm_tc, dim3(std::min(tiles * splits, std::max(e->sm_count, 1))), dim3(kTcThreads), smem,
+		                    tx, tw, a));
+		if (nn && a.epi == kTcResid && a.N <= kResNormThreads * kResNormMaxCols) {
+			const auto kn = a.N <= kResNormThreads * 16 ? k_gemm_splitk_resid_norm<16> : k_gemm_splitk_resid_norm<kResNormMaxCols>;
+			INF_CUDA_TRY(launch(e, kn, dim3(a.T), dim3(kResNormThreads), 0, a, (bf16*)nn->out, (const bf16*)nn->gain, nn->eps));
+			*nn->done = true;
+			return Success;
+		}
 		const int groups = a.T * ((a.N + 31) / 32);
 		INF_CUDA_TRY(launch(e, k_gemm_splitk_reduce, dim3((groups + 7) / 8), dim3(256), 0, a));
 		return Success;
 	}
 	a.k_splits = 1;
-	INF_CUDA_TRY(launch(e, k_gemm_tc, grid, dim3(kTcThreads), smem, tx, tw, a));
+	INF_CUDA_TRY(launch(e, k_gemm_tc, dim3(std::min(tiles, std::max(e->sm_count, 1))), dim3(kTcThreads), smem, tx, tw, a));
 	return Success;
 }
 
 // Row-parallel projection + residual: local GEMM into the fp32 partial buffer, then the
 // two-shot peer-memory all-reduce adds the sum over ranks into the residual.
-Error_t launch_gemm_resid_tp(InfEngine* e, const void* X, const void* W, TcArgs a);
+Error_t launch_gemm_resid_tp(InfEngine* e, const void* X, const void* W, TcArgs a, const NormNext* nn = nullptr);
 
 TcArgs tc_base(InfEngine* e, int T, int N, int K, int epi)
 {
@@ -865,9 +888,10 @@ TcArgs tc_base(InfEngine* e, int T, int N, int K, int epi)
 	return a;
 }
 
-Error_t launch_gemm_resid_tp(InfEngine* e, const void* X, const void* W, TcArgs a)
+Error_t launch_gemm_resid_tp(InfEngine* e, const void* X, const void* W, TcArgs a, const NormNext* nn)
 {
-	if (e->tpc.size <= 1) return launch_gemm_tc(e, X, W, a);
+	if (e->tpc.size <= 1) return launch_gemm_tc(e, X, W, a, nn);
+	if (nn) *nn->done = false;
 	float* resid = a.resid;
 	a.epi = kTcStoreF32;
 	a.out = e->tpc.part[e->tpc.rank];
@@ -890,10 +914,12 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 	const size_t pf_smem = e->pf_tc ? attn_prefill_tc_smem_bytes(hd) : attn_prefill_smem_bytes(G, hd, (int)c.kv_block);
 	if (e->pf_tc) INF_CUDA_TRY(set_smem(k_attn_prefill_tc, pf_smem));
 	else INF_CUDA_TRY(set_smem(k_attn_prefill<bf16>, pf_smem));
+	bool normed = false; // xhat_p already holds the norm that the next projection reads
 	for (u32 l = 0; l < c.n_layers; ++l) {
 		const LayerW& L = e->layers[l];
-		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
-		                    (bf16*)e->xhat_p, T, d, (const bf16*)L.attn_norm, c.norm_eps));
+		if (!normed)
+			INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
+			                    (bf16*)e->xhat_p, T, d, (const bf16*)L.attn_norm, c.norm_eps));
 		{
 			TcArgs a = tc_base(e, T, (e->Hl + 2 * e->KVl) * hd, d, kTcQkv);
 			a.out = e->q_p;
@@ -950,10 +976,12 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 		{
 			TcArgs a = tc_base(e, T, d, e->Hl * hd, kTcResid);
 			a.resid = e->resid_p;
-			INF_TRY(launch_gemm_resid_tp(e, e->attn_p, L.wo, a));
+			const NormNext nn{L.ffn_norm, e->xhat_p, c.norm_eps, &normed};
+			INF_TRY(launch_gemm_resid_tp(e, e->attn_p, L.wo, a, &nn));
 		}
-		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
-		                    (bf16*)e->xhat_p, T, d, (const bf16*)L.ffn_norm, c.norm_eps));
+		if (!normed)
+			INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(T), dim3(256), 0, (const float*)e->resid_p,
+			                    (bf16*)e->xhat_p, T, d, (const bf16*)L.ffn_norm, c.norm_eps));
 		{
 			TcArgs a = tc_base(e, T, 2 * e->Fl, d, kTcSwiglu);
 			a.out = e->h_p;
@@ -962,7 +990,10 @@ Error_t enqueue_prefill_layers(InfEngine* e, int T)
 		{
 			TcArgs a = tc_base(e, T, d, e->Fl, kTcResid);
 			a.resid = e->resid_p;
-			INF_TRY(launch_gemm_resid_tp(e, e->h_p, L.wd, a));
+			// the next layer's attention norm (the last layer's residual goes to the LM head row)
+			const NormNext nn{l + 1 < c.n_layers ? e->layers[l + 1].attn_norm : nullptr, e->xhat_p, c.norm_eps, &normed};
+			INF_TRY(launch_gemm_resid_tp(e, e->h_p, L.wd, a, l + 1 < c.n_layers ? &nn : nullptr));
+			if (l + 1 == c.n_layers) normed = false;
 		}
 	}
 	return Success;
@@ -1073,6 +1104,42 @@ Error_t run_prefill(InfEngine* e, u32 n, u32 start, u32 slot)
 
 bool use_tc_prefill(const InfEngine* e, u32 n) { return e->cfg.dtype == InfBF16 && e->chunk > 0 && n > 1; }
 
+// Work list of the batched mma attention into h_units: each token's pages in units of about P
+// pages, P chosen for about kAttnUnitCtasPerSm CTAs per SM over the KV heads (at least
+// kAmUnitPagesMin pages), the units in decreasing page count, so the CTAs that start last are
+// the short ones.  Returns the number of units.  Measured on 64 sequences of 512-4096 positions
+// (Llama-3-8B shape): 2 CTAs per SM (every sequence one unit) 7.88 ms per step, 4 -> 8.20,
+// 8 -> 8.41, the grid of two splits per sequence in batch order 8.54.
+constexpr int kAttnUnitCtasPerSm = 2;
+int build_attn_units(InfEngine* e, const u32* positions, u32 n)
+{
+	const u32 blk = e->cfg.kv_block;
+	std::vector<int> np(n);
+	u64 total = 0;
+	for (u32 i = 0; i < n; ++i) {
+		np[i] = (int)((positions[i] + blk) / blk); // pages of positions 0 .. positions[i]
+		total += (u64)np[i];
+	}
+	const u64 target = std::max<u64>(1, (u64)kAttnUnitCtasPerSm * e->sm_count / (u64)std::max(1, e->KVl));
+	const int P = (int)std::max<u64>((u64)kAmUnitPagesMin, (total + target - 1) / target);
+	struct Unit {
+		int pages, b, code;
+	};
+	std::vector<Unit> list;
+	for (u32 i = 0; i < n; ++i) {
+		const int ns = std::min(e->attn_unit_splits, std::max(1, (np[i] + P - 1) / P));
+		const int pps = (np[i] + ns - 1) / ns;
+		for (int sp = 0; sp < ns; ++sp)
+			list.push_back({std::max(0, std::min(np[i], (sp + 1) * pps) - sp * pps), (int)i, sp | (ns << 16)});
+	}
+	std::stable_sort(list.begin(), list.end(), [](const Unit& x, const Unit& y) { return x.pages > y.pages; });
+	for (size_t k = 0; k < list.size(); ++k) {
+		e->h_units[2 * k] = list[k].b;
+		e->h_units[2 * k + 1] = list[k].code;
+	}
+	return (int)list.size();
+}
+
 // One decode token for each of B sequences (ids in d_ids, slots/positions in tok_slot/tok_pos):
 // the projections run once for all B tokens on the tensor cores (split-K when there are few
 // output tiles), attention is the streaming mma kernel with one grid slice per token, the LM
@@ -1083,10 +1150,12 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 	const int d = (int)c.dim, hd = (int)c.head_dim;
 	INF_CUDA_TRY(launch(e, k_embed<bf16, float>, dim3((d + 255) / 256, B), dim3(256), 0, (const uint32_t*)e->d_ids, B, d,
 	                    c.vocab_size, (const bf16*)e->embed, e->resid_p, e->err));
+	bool normed = false; // xhat_p already holds the norm that the next projection reads
 	for (u32 l = 0; l < c.n_layers; ++l) {
 		const LayerW& L = e->layers[l];
-		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
-		                    (bf16*)e->xhat_p, B, d, (const bf16*)L.attn_norm, c.norm_eps));
+		if (!normed)
+			INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
+			                    (bf16*)e->xhat_p, B, d, (const bf16*)L.attn_norm, c.norm_eps));
 		{
 			TcArgs a = tc_base(e, B, (e->Hl + 2 * e->KVl) * hd, d, kTcQkv);
 			a.out = e->q_p;
@@ -1136,7 +1205,13 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 				INF_TRY(tensor_map_kv(&tk, L.kpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
 				INF_TRY(tensor_map_kv(&tv, L.vpool, (u32)hd, c.kv_block, (u32)e->KVl, (u32)e->n_pages, 1));
 				INF_CUDA_TRY(set_smem(am, smem));
-				INF_CUDA_TRY(launch(e, am, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAmThreads), smem, tk, tv, a));
+				if (e->n_attn_units > 0) {
+					a.units = e->attn_units;
+					a.n_splits = e->attn_unit_splits;
+					INF_CUDA_TRY(launch(e, am, dim3(e->KVl, 1, e->n_attn_units), dim3(kAmThreads), smem, tk, tv, a));
+				} else {
+					INF_CUDA_TRY(launch(e, am, dim3(e->KVl, e->attn_splits_batch, B), dim3(kAmThreads), smem, tk, tv, a));
+				}
 			} else {
 				const size_t smem = attn_stream_smem_bytes(e->Hl / e->KVl, hd, (int)c.kv_block, 2);
 				const AttnKernel<bf16> ak = attn_decode_stream_kernel<bf16>(e->Hl / e->KVl, hd);
@@ -1148,10 +1223,12 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 		{
 			TcArgs a = tc_base(e, B, d, e->Hl * hd, kTcResid);
 			a.resid = e->resid_p;
-			INF_TRY(launch_gemm_resid_tp(e, e->attn_p, L.wo, a));
+			const NormNext nn{L.ffn_norm, e->xhat_p, c.norm_eps, &normed};
+			INF_TRY(launch_gemm_resid_tp(e, e->attn_p, L.wo, a, &nn));
 		}
-		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
-		                    (bf16*)e->xhat_p, B, d, (const bf16*)L.ffn_norm, c.norm_eps));
+		if (!normed)
+			INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
+			                    (bf16*)e->xhat_p, B, d, (const bf16*)L.ffn_norm, c.norm_eps));
 		{
 			TcArgs a = tc_base(e, B, 2 * e->Fl, d, kTcSwiglu);
 			a.out = e->h_p;
@@ -1160,11 +1237,15 @@ Error_t enqueue_decode_batch(InfEngine* e, int B)
 		{
 			TcArgs a = tc_base(e, B, d, e->Fl, kTcResid);
 			a.resid = e->resid_p;
-			INF_TRY(launch_gemm_resid_tp(e, e->h_p, L.wd, a));
+			// the next layer's attention norm, or the final norm before the LM head
+			const NormNext nn{l + 1 < c.n_layers ? e->layers[l + 1].attn_norm : e->final_norm, e->xhat_p, c.norm_eps,
+			                  &normed};
+			INF_TRY(launch_gemm_resid_tp(e, e->h_p, L.wd, a, &nn));
 		}
 	}
-	INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
-	                    (bf16*)e->xhat_p, B, d, (const bf16*)e->final_norm, c.norm_eps));
+	if (!normed)
+		INF_CUDA_TRY(launch(e, k_rmsnorm_rows<float, bf16, bf16>, dim3(B), dim3(256), 0, (const float*)e->resid_p,
+		                    (bf16*)e->xhat_p, B, d, (const bf16*)e->final_norm, c.norm_eps));
 	{
 		// logits and the greedy argmax of every row in the GEMM's epilogue
 		TcArgs a = tc_base(e, B, e->Vl, d, kTcLogitsArgmax);
@@ -1474,12 +1555,15 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	                 &e->attn_max_pages_split);
 	e->attn_splits_batch = attn_stream_splits(e->sm_count, e->KVl, (int)c.max_batch, e->pages_per_seq);
 	e->attn_max_pages_split_batch = 0;
+	e->attn_unit_splits = std::min(kAmUnitSplitsMax, (e->pages_per_seq + kAmUnitPagesMin - 1) / kAmUnitPagesMin);
 	// batch-1 decode: one cluster per KV head when the longest context fits its shared memory
 	// and the GPU can place a cluster of that size
 	INF_TRY(attn_cl_choose(e, G, (int)hd));
 	e->pf_tc = c.dtype == InfBF16 && c.prefill_attention == InfPrefillAttnAuto && (hd == 64 || hd == 128) &&
 	           kPtRows % G == 0 && c.kv_block % 8 == 0 && kPtKeys % c.kv_block == 0;
-	const u64 part_floats = std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * e->attn_splits_batch) * (hd + 2);
+	const u64 part_floats =
+	    std::max((u64)e->Hl * e->attn_splits, (u64)c.max_batch * e->Hl * std::max(e->attn_splits_batch, e->attn_unit_splits)) *
+	    (hd + 2);
 	// multi-token passes run on the tensor cores (bf16 Llama models); fp32 and Gemma-style models
 	// feed tokens one by one through the decode step
 	e->chunk = c.dtype == InfBF16 && !e->gemma
@@ -1565,6 +1649,7 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	P.push(&e->d_ids, (u64)c.max_seq * 4);
 	P.push(&e->attn_part, part_floats * 4);
 	P.push(&e->attn_counters, (u64)c.max_batch * e->KVl * 4);
+	P.push(&e->attn_units, (u64)c.max_batch * e->attn_unit_splits * 8);
 	if (c.dtype == InfBF16) {
 		e->gemm_part_bytes = kGemmPartBytes;
 		P.push(&e->gemm_part, kGemmPartBytes);
@@ -1682,6 +1767,7 @@ Error_t engine_build(InfEngine* e, u64 seed, const Checkpoint* ck)
 	INF_CUDA_TRY(cudaMallocHost(&e->h_pin, sizeof(uint32_t) * (c.max_seq + 16)));
 	INF_CUDA_TRY(cudaMallocHost(&e->h_ctl, sizeof(int) * 2 * kCtlWords));
 	if (e->chunk > 0) INF_CUDA_TRY(cudaMallocHost(&e->h_tok, sizeof(int) * 2 * e->chunk));
+	INF_CUDA_TRY(cudaMallocHost(&e->h_units, (size_t)c.max_batch * e->attn_unit_splits * 8));
 	INF_CUDA_TRY(cudaMallocHost(&e->rows_h, sizeof(SampleRow) * c.max_batch));
 	e->slot_samp.assign(c.max_batch, InfSampling{});
 	INF_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -1700,6 +1786,7 @@ void engine_free(InfEngine* e)
 	if (e->h_ctl) cudaFreeHost(e->h_ctl);
 	if (e->h_tok) cudaFreeHost(e->h_tok);
 	if (e->rows_h) cudaFreeHost(e->rows_h);
+	if (e->h_units) cudaFreeHost(e->h_units);
 	for (auto& ev : e->prof_ev)
 		if (ev) cudaEventDestroy(ev);
 	if (e->stream) cudaStreamDestroy(e->stream);
@@ -1970,9 +2057,20 @@ Error_t inf::forward_batch(Model* model, u32 n_seqs, const u32* seq_slots, const
 	INF_CUDA_TRY(cudaMemcpyAsync(e->d_ids, e->h_pin, sizeof(u32) * n_seqs, cudaMemcpyHostToDevice, e->stream));
 	INF_CUDA_TRY(cudaMemcpyAsync(e->tok_pos, e->h_tok, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, e->stream));
 	INF_CUDA_TRY(cudaMemcpyAsync(e->tok_slot, e->h_tok + e->chunk, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, e->stream));
+	e->h2d_bytes += 12ull * n_seqs;
+	e->n_attn_units = 0;
+	if (c.kv_block == 16 && attn_decode_mma_kernel(e->Hl / e->KVl, (int)c.head_dim)) {
+		e->n_attn_units = build_attn_units(e, positions, n_seqs);
+		if (e->n_attn_units > 0) {
+			INF_CUDA_TRY(cudaMemcpyAsync(e->attn_units, e->h_units, (size_t)e->n_attn_units * 8, cudaMemcpyHostToDevice,
+			                             e->stream));
+			e->h2d_bytes += (u64)e->n_attn_units * 8;
+		}
+	}
 	e->gemm_split = true;
 	const Error_t eb = enqueue_decode_batch(e, (int)n_seqs);
 	e->gemm_split = false;
+	e->n_attn_units = 0;
 	INF_TRY(eb);
 	{
 		std::vector<u32> pos_new(positions, positions + n_seqs);
@@ -2269,6 +2367,7 @@ Error_t inf_seq_reset(Model* model, u32 seq_slot)
 void* inf_model_stream(Model* model) { return model && model->engine ? (void*)model->engine->stream : nullptr; }
 
 u64 inf_kernel_launches(Model* model) { return model && model->engine ? model->engine->launches : 0; }
+u64 inf_batch_h2d_bytes(Model* model) { return model && model->engine ? model->engine->h2d_bytes : 0; }
 
 u64 inf_decode_bytes(const InfConfig* c, u32 ctx)
 {

@@ -48,6 +48,9 @@ struct AttnDecodeArgs {
 	unsigned* counters;      // [B][KV]
 	void* out;               // [B][H*hd]
 	int* err;
+	// batched mma kernel: per work unit (token, split | splits << 16); n_splits is then the
+	// stride of part (the most splits a token can have)
+	const int* units;
 };
 
 // head_dim values per lane of a warp

@@ -1,6 +1,8 @@
 // Decode attention for batches of tokens on the tensor cores (bf16, head_dim 64 or 128).
 //
-// Grid (kv_heads, splits, tokens); a CTA covers a contiguous range of one token's pages.  Thread
+// Grid (kv_heads, splits, tokens), or (kv_heads, 1, work units) where the host lists each unit's
+// (token, split, splits of the token) (a page budget per unit, longest contexts first, so the
+// CTAs that start last are short); a CTA covers a contiguous range of one token's pages.  Thread
 // 0-127 read the split's page ids into shared memory once; then each of the four warps streams
 // its own pages (q = warp, warp + 4, ...) through its own ring of kStBufs stages (one page of K
 // and of V per stage, one mbarrier per stage, 4-D TMA boxes of 64 head dims x 16 positions x 1
@@ -26,6 +28,8 @@
 namespace inf {
 
 constexpr int kAmThreads = 128; // 4 warps, each streaming every 4th page of the split
+constexpr int kAmUnitPagesMin = 16;  // pages of a work unit at least (host work list)
+constexpr int kAmUnitSplitsMax = 32; // splits of one token at most (host work list)
 static_assert(kAmThreads / 32 == kStChunkPages, "the region holds kStBufs pages of K and V per warp");
 
 __host__ __device__ inline size_t attn_mma_region_bytes(int hd, int blk)
@@ -83,7 +87,15 @@ __global__ void __launch_bounds__(kAmThreads)
 	extern __shared__ __align__(1024) uint8_t sm_base[];
 	// 1024-byte aligned: the TMA boxes are SWIZZLE_128B atoms
 	uint8_t* sm_raw = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_base) + 1023) & ~(uintptr_t)1023);
-	const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+	const int kvh = blockIdx.x;
+	// (token, split, splits of that token): from the grid, or from the host's work list
+	int b = blockIdx.z, split = blockIdx.y, ns = a.n_splits;
+	if (a.units) {
+		const int2 u = reinterpret_cast<const int2*>(a.units)[blockIdx.z];
+		b = u.x;
+		split = u.y & 0xFFFF;
+		ns = u.y >> 16;
+	}
 	const int blk = a.blk; // 16 (the host checks)
 	int* pg_s = reinterpret_cast<int*>(sm_raw + attn_mma_region_bytes(HD, blk)); // this split's page ids
 	uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(pg_s) + (((size_t)a.pages_per_seq * 4 + 15) & ~(size_t)15));
@@ -98,7 +110,7 @@ __global__ void __launch_bounds__(kAmThreads)
 	const int pos = a.tok_pos[b];
 	const int ctx = pos + 1;
 	const int n_pages = (ctx + blk - 1) / blk;
-	const int pps = (n_pages + a.n_splits - 1) / a.n_splits;
+	const int pps = (n_pages + ns - 1) / ns;
 	const int p_begin = split * pps;
 	const int np = max(0, min(n_pages, p_begin + pps) - p_begin);
 
@@ -312,7 +324,7 @@ __global__ void __launch_bounds__(kAmThreads)
 	__syncthreads();
 	if (tid == 0) {
 		const unsigned t = atomicAdd(&a.counters[b * a.KV + kvh], 1u);
-		last_flag = (t == (unsigned)a.n_splits - 1);
+		last_flag = (t == (unsigned)ns - 1);
 	}
 	__syncthreads();
 	if (!last_flag) return;
@@ -322,9 +334,9 @@ __global__ void __launch_bounds__(kAmThreads)
 		const int g = e / HD, i = e % HD;
 		const float* ph = a.part + ((size_t)b * a.H + kvh * G + g) * a.n_splits * hd2;
 		float M = -INFINITY;
-		for (int s = 0; s < a.n_splits; ++s) M = fmaxf(M, __ldcg(ph + (size_t)s * hd2 + HD));
+		for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(ph + (size_t)s * hd2 + HD));
 		float L = 0.0f, v = 0.0f;
-		for (int s = 0; s < a.n_splits; ++s) {
+		for (int s = 0; s < ns; ++s) {
 			const float ms = __ldcg(ph + (size_t)s * hd2 + HD);
 			const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
 			L = fmaf(w, __ldcg(ph + (size_t)s * hd2 + HD + 1), L);

@@ -90,7 +90,7 @@ EXPORTS = [
     "inf_attn_decode_with", "inf_attn_prefill",
     "inf_config_preset", "inf_model_build", "inf_model_destroy", "inf_forward", "inf_forward_batch",
     "inf_generate", "inf_decode", "inf_seq_reset", "inf_error_string", "inf_last_error_detail", "inf_model_stream",
-    "inf_kernel_launches", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
+    "inf_kernel_launches", "inf_batch_h2d_bytes", "inf_decode_bytes", "inf_profile_decode_step", "inf_synth_ids", "inf_debug_read",
     "inf_tp_export", "inf_tp_connect", "inf_attn_decode_noalloc", "inf_config_from_json", "inf_safetensors_check",
     "inf_safetensors_read", "inf_tokenizer_build", "inf_tokenizer_destroy", "inf_tokenizer_vocab_size",
     "inf_tokenizer_encode", "inf_tokenizer_encode_special", "inf_tokenizer_decode", "inf_set_sampling", "inf_set_slot_sampling", "inf_server_submit_sampled", "inf_server_create",
@@ -155,6 +155,7 @@ def lib():
         "inf_last_error_detail": (C.c_char_p, []),
         "inf_model_stream": (vp, [C.POINTER(Model)]),
         "inf_kernel_launches": (u64, [C.POINTER(Model)]),
+        "inf_batch_h2d_bytes": (u64, [C.POINTER(Model)]),
         "inf_decode_bytes": (u64, [C.POINTER(InfConfig), u32]),
         "inf_profile_decode_step": (u32, [C.POINTER(Model), u32, u32, u32, C.POINTER(f32), u32]),
         "inf_synth_ids": (E, [u64, u64, u64, u32, u32, vp]),
@@ -424,6 +425,11 @@ class Engine:
     @property
     def launches(self) -> int:
         return int(lib().inf_kernel_launches(C.byref(self.model)))
+
+    @property
+    def batch_h2d_bytes(self) -> int:
+        """Bytes the batched steps have copied host -> device so far."""
+        return int(lib().inf_batch_h2d_bytes(C.byref(self.model)))
 
     @property
     def weight_bytes(self) -> int:
