@@ -330,17 +330,25 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll
 				for (int c = 0; c < kHalfKeys; c += 32) tmem_ld_32cols_nowait(ts + (uint32_t)c, v + c);
 				asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+				// raw scores: the scale is applied to the max here and inside the exponent's FMA
+				// below (rounding is monotonic, so the max equals the max of the scaled scores)
+				if (masked) {
 #pragma unroll
-				for (int i = 0; i < kHalfKeys; ++i) {
-					v[i] *= sl2;
-					if (masked && kbase + i > pos) v[i] = -INFINITY;
-					mt = fmaxf(mt, v[i]);
+					for (int i = 0; i < kHalfKeys; ++i)
+						if (kbase + i > pos) v[i] = -INFINITY;
 				}
+				// four independent max chains (the max is exact, so the order does not matter)
+				float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+				for (int i = 0; i < kHalfKeys; ++i) m4[i & 3] = fmaxf(m4[i & 3], v[i]);
+				mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
 			}
+			// the exchange is between the two warps of this TMEM lane quarter only (rows r):
+			// one 64-thread named barrier per quarter
 			xmax[half * kPtRows + r] = mt;
-			named_bar_sync(1, 256);
+			named_bar_sync(1 + quarter, 64);
 			mt = fmaxf(mt, xmax[(half ^ 1) * kPtRows + r]);
-			named_bar_sync(1, 256); // both halves have read before the next tile's writes
+			named_bar_sync(1 + quarter, 64); // both halves have read before the next tile's writes
 			// rescale only when the max grows by more than 2^8 (or on the first finite max);
 			// both halves of a row take the same decision
 			const bool grow = mt > m + kPtRescaleLog2 || (m == -INFINITY && mt != -INFINITY);
@@ -367,22 +375,22 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 			if (ok && j >= 2) ok = wait_all(&p_free[j & 1], (uint32_t)((j >> 1) - 1) & 1u);
 			if (ok) {
 				uint8_t* pb = p_s + (size_t)(j & 1) * 2 * kPtAtom + (size_t)half * kPtAtom; // this half's 64 keys
-				float sum = 0.0f;
+				float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f}; // four independent add chains
 #pragma unroll
 				for (int c = 0; c < kHalfKeys; c += 8) {
 					uint32_t pk[4];
 #pragma unroll
 					for (int i = 0; i < 8; i += 2) {
-						const float p0 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i] - m);
-						const float p1 = m == -INFINITY ? 0.0f : ex2_approx(v[c + i + 1] - m);
+						const float p0 = m == -INFINITY ? 0.0f : ex2_approx(fmaf(v[c + i], sl2, -m));
+						const float p1 = m == -INFINITY ? 0.0f : ex2_approx(fmaf(v[c + i + 1], sl2, -m));
 						const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
 						// the row sum adds the rounded values, the weights the MMA applies
-						sum += __low2float(b) + __high2float(b);
+						sums[i >> 1] += __low2float(b) + __high2float(b);
 						pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&b);
 					}
 					*reinterpret_cast<uint4*>(pb + sw128_off(r, c >> 3)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 				}
-				l += sum;
+				l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
 				asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 				tc_fence_before();
 				mbar_arrive(bar_p);
@@ -390,7 +398,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 		}
 		// the row's sum: both halves
 		xmax[half * kPtRows + r] = l;
-		named_bar_sync(1, 256);
+		named_bar_sync(1 + quarter, 64);
 		const float lt = l + xmax[(half ^ 1) * kPtRows + r];
 		if (ok && wait_all(bar_o, (uint32_t)(n_tiles - 1) & 1u)) {
 			tc_fence_after();

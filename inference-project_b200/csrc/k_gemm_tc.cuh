@@ -67,6 +67,9 @@ struct TcArgs {
 	// folded into best_keys[row] with a 64-bit atomicMax (ties -> lowest column)
 	unsigned long long* best_keys;
 	uint32_t col_base;
+	// N tile width (a multiple of 16, 16 .. 256; 0: 256): narrower tiles when 256-wide ones
+	// would leave SMs idle
+	int bn;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy)
@@ -137,13 +140,13 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, float (&v)[32])
 // and columns n = n0 + lane (n0 a multiple of 32).  The column pairs of the
 // RoPE and SwiGLU epilogues are (even lane, odd lane); the argmax key of the 32 columns is
 // the warp's maximum, folded into the row's key by lane 0.
-__device__ __forceinline__ void tc_epilogue_lane(const TcArgs& a, int t, int n, float v)
+__device__ __forceinline__ void tc_epilogue_lane(const TcArgs& a, int t, int n, float v, int n_lim)
 {
 	const int lane = threadIdx.x & 31;
 	const float v1 = __shfl_down_sync(0xffffffffu, v, 1); // the odd partner of an even lane
 	if (a.epi == kTcStoreF32 || a.epi == kTcLogitsArgmax) {
 		unsigned long long k = 0ull;
-		if (n < a.N) {
+		if (n < n_lim) {
 			reinterpret_cast<float*>(a.out)[(size_t)t * a.N + n] = v;
 			k = argmax_key(v, (uint32_t)n + a.col_base);
 		}
@@ -156,14 +159,14 @@ __device__ __forceinline__ void tc_epilogue_lane(const TcArgs& a, int t, int n, 
 			if (lane == 0) atomicMax(a.best_keys + t, k);
 		}
 	} else if (a.epi == kTcStore) {
-		if (n < a.N) Store<bf16>::put(reinterpret_cast<bf16*>(a.out) + (size_t)t * a.N + n, v);
+		if (n < n_lim) Store<bf16>::put(reinterpret_cast<bf16*>(a.out) + (size_t)t * a.N + n, v);
 	} else if (a.epi == kTcResid) {
-		if (n < a.N) a.resid[(size_t)t * a.N + n] += v;
+		if (n < n_lim) a.resid[(size_t)t * a.N + n] += v;
 	} else if (a.epi == kTcSwiglu) {
-		if (!(lane & 1) && n + 1 < a.N)
+		if (!(lane & 1) && n + 1 < n_lim)
 			Store<bf16>::put(reinterpret_cast<bf16*>(a.out) + (size_t)t * (a.N >> 1) + (n >> 1), __fmul_rn(silu(v), v1));
 	} else if (a.epi == kTcQkv) {
-		if ((lane & 1) || n >= a.N) return;
+		if ((lane & 1) || n >= n_lim) return;
 		const int hd = a.head_dim, half = hd >> 1;
 		const int pos = a.tok_pos[t], slot = a.tok_slot[t];
 		const int head = n / hd, dim = (n % hd) >> 1;
@@ -203,7 +206,7 @@ __device__ __forceinline__ void tc_epilogue_lane(const TcArgs& a, int t, int n, 
 // row_pos / row_page of lane r.  Same arithmetic per element as tc_epilogue_lane.
 constexpr int kTcEpiRowGroup = 8;
 __device__ __forceinline__ void tc_epilogue_rows(const TcArgs& a, int t0, int rows, int n0, const float* st, int row_pos,
-                                                 int row_page)
+                                                 int row_page, int n_lim)
 {
 	const int lane = threadIdx.x & 31;
 	if (a.epi == kTcResid) {
@@ -213,22 +216,22 @@ __device__ __forceinline__ void tc_epilogue_rows(const TcArgs& a, int t0, int ro
 			float old[kTcEpiRowGroup];
 #pragma unroll
 			for (int j = 0; j < kTcEpiRowGroup; ++j)
-				old[j] = (r0 + j < rows && n < a.N) ? rp[(size_t)(r0 + j) * a.N] : 0.0f;
+				old[j] = (r0 + j < rows && n < n_lim) ? rp[(size_t)(r0 + j) * a.N] : 0.0f;
 #pragma unroll
 			for (int j = 0; j < kTcEpiRowGroup; ++j)
-				if (r0 + j < rows && n < a.N) rp[(size_t)(r0 + j) * a.N] = old[j] + st[(r0 + j) * 33 + lane];
+				if (r0 + j < rows && n < n_lim) rp[(size_t)(r0 + j) * a.N] = old[j] + st[(r0 + j) * 33 + lane];
 		}
 	} else if (a.epi == kTcSwiglu) {
 		const int p = lane & 15, n = n0 + 2 * p;
 		bf16* o = reinterpret_cast<bf16*>(a.out) + (n >> 1);
-		if (n + 1 < a.N)
+		if (n + 1 < n_lim)
 			for (int r = lane >> 4; r < rows; r += 2)
 				Store<bf16>::put(o + (size_t)(t0 + r) * (a.N >> 1), __fmul_rn(silu(st[r * 33 + 2 * p]), st[r * 33 + 2 * p + 1]));
 	} else if (a.epi == kTcQkv) {
 		const int hd = a.head_dim, half = hd >> 1;
 		const int p = lane & 15, n = n0 + 2 * p;
 		const int head = n / hd, dim = (n % hd) >> 1;
-		const bool ok = n < a.N;
+		const bool ok = n < n_lim;
 		const bool rope = head < a.n_q_heads + a.n_kv_heads; // q and k heads
 		const bool is_k = head >= a.n_q_heads && rope;
 		const int kvh = head - a.n_q_heads - (is_k ? 0 : a.n_kv_heads);
@@ -273,7 +276,7 @@ __device__ __forceinline__ void tc_epilogue_rows(const TcArgs& a, int t0, int ro
 		}
 	} else {
 		// store / f32 store / logits with argmax: nothing to load per row
-		for (int r = 0; r < rows; ++r) tc_epilogue_lane(a, t0 + r, n0 + lane, st[r * 33 + lane]);
+		for (int r = 0; r < rows; ++r) tc_epilogue_lane(a, t0 + r, n0 + lane, st[r * 33 + lane], n_lim);
 	}
 }
 
@@ -298,7 +301,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 	volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const int m_tiles = (a.T + kTcBM - 1) / kTcBM, n_tiles = (a.N + kTcBN - 1) / kTcBN;
+	const int BN = a.bn > 0 ? a.bn : kTcBN;
+	const int m_tiles = (a.T + kTcBM - 1) / kTcBM, n_tiles = (a.N + BN - 1) / BN;
+	const uint32_t stage_tx = kTcStageA + (uint32_t)BN * kTcBK * 2; // full boxes, out-of-range rows zero-filled
 	const int n_kb_all = (a.K + kTcBK - 1) / kTcBK;
 	const int S = a.k_splits > 1 ? a.k_splits : 1;
 	const int units = m_tiles * n_tiles * S;
@@ -348,9 +353,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 					// writes, after it
 					const int pre = min(n_kb, kTcStages);
 					for (; kb < pre; ++kb) {
-						mbar_arrive_expect_tx(&full[kb], kTcStageBytes);
+						mbar_arrive_expect_tx(&full[kb], stage_tx);
 						tma_load_2d(tiles + (size_t)kb * kTcStageBytes + kTcStageA, &tm_w, (kb0 + kb) * kTcBK,
-						            n_tile * kTcBN, &full[kb], pol_w);
+						            n_tile * BN, &full[kb], pol_w);
 					}
 					pdl_wait();
 					waited = true;
@@ -363,9 +368,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 					const int s = it % kTcStages;
 					if (it >= kTcStages && !mbar_wait(&empty[s], ((it / kTcStages) - 1) & 1, abort_flag, a.err)) break;
 					uint8_t* sa = tiles + (size_t)s * kTcStageBytes;
-					mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+					mbar_arrive_expect_tx(&full[s], stage_tx);
 					tma_load_2d(sa, &tm_x, (kb0 + kb) * kTcBK, m_tile * kTcBM, &full[s], pol_x);
-					tma_load_2d(sa + kTcStageA, &tm_w, (kb0 + kb) * kTcBK, n_tile * kTcBN, &full[s], pol_w);
+					tma_load_2d(sa + kTcStageA, &tm_w, (kb0 + kb) * kTcBK, n_tile * BN, &full[s], pol_w);
 				}
 			}
 			if (!waited) pdl_wait();
@@ -382,7 +387,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 		}
 	} else if (warp == 1) {
 		if (lane == 0) {
-			constexpr uint32_t idesc = umma_idesc_bf16(kTcBM, kTcBN);
+			const uint32_t idesc = umma_idesc_bf16(kTcBM, BN);
 			int it = 0, ub = 0;
 			for (int u = blockIdx.x; u < units; u += gridDim.x, ++ub) {
 				const int z = u / (m_tiles * n_tiles);
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 	} else {
 		// epilogue warps 2..9: TMEM lane quarter = warp % 4 (token rows t0 .. t0 + 31 of the
 		// tile); warps 2..5 take columns 0..127 of the tile, warps 6..9 columns 128..255
-		const int quarter = warp & 3, c_begin = ((warp - 2) >> 2) * (kTcBN / 2);
+		const int quarter = warp & 3, c_begin = ((warp - 2) >> 2) * (kTcBN / 2), c_end = min(c_begin + kTcBN / 2, BN);
 		float* st = stage_out + (warp - 2) * (32 * 33);
 		int ub = 0;
 		for (int u = blockIdx.x; u < units; u += gridDim.x, ++ub) {
@@ -434,9 +439,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 					if (row_pos >= 0 && row_pos < a.max_seq)
 						row_page = a.block_table[(size_t)a.tok_slot[t0 + lane] * a.pages_per_seq + row_pos / a.kv_block];
 				}
-				for (int c = c_begin; c < c_begin + kTcBN / 2; c += 32) {
-					const int n0 = n_tile * kTcBN + c;
-					if (n0 >= a.N) break;
+				// columns of this tile and half: n0 .. n_lim - 1 (the last chunk may be 16 wide)
+				const int n_lim = min(a.N, n_tile * BN + c_end);
+				for (int c = c_begin; c < c_end; c += 32) {
+					const int n0 = n_tile * BN + c;
+					if (n0 >= n_lim) break;
 					float v[32];
 					tmem_ld_32cols(tmem_d + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kTcBN + c), v);
 					// transpose through shared memory: lane = column, one row per step
@@ -445,10 +452,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 					__syncwarp();
 					if (S > 1) {
 						float* pp = a.partial + ((size_t)z * a.T + t0) * a.N + n0 + lane;
-						if (n0 + lane < a.N)
+						if (n0 + lane < n_lim)
 							for (int r = 0; r < rows; ++r) pp[(size_t)r * a.N] = st[r * 33 + lane];
 					} else {
-						tc_epilogue_rows(a, t0, rows, n0, st, row_pos, row_page);
+						tc_epilogue_rows(a, t0, rows, n0, st, row_pos, row_page, n_lim);
 					}
 					__syncwarp();
 				}
@@ -492,7 +499,7 @@ __global__ void __launch_bounds__(256) k_gemm_splitk_reduce(const TcArgs a)
 #pragma unroll 4
 		for (int z = 0; z < a.k_splits; ++z) v += __ldcg(p + z * zs);
 	}
-	tc_epilogue_lane(a, t, n, v);
+	tc_epilogue_lane(a, t, n, v, a.N);
 }
 
 // A residual projection's split-K sum (O or down, kTcResid) added to the residual row, then
