@@ -401,9 +401,11 @@ def test_chunked_prefill_matches_single_pass(cuda):
 
 
 @pytest.mark.parametrize("T,N,K", [(1, 64, 64), (7, 200, 160), (128, 256, 4096), (300, 6144, 4096),
-                                   (130, 4096, 14336), (64, 28672, 4096)])
+                                   (130, 4096, 14336), (64, 28672, 4096), (200, 1000, 256), (16, 2560, 512)])
 def test_gemm_tc_vs_torch_fp32(cuda, T, N, K):
-    """tcgen05 GEMM against a plain PyTorch fp32 reference of the same op."""
+    """tcgen05 GEMM against a plain PyTorch fp32 reference of the same op.  With few output tiles
+    the GEMM narrows its N tiles (28672 columns at 64 rows: 208-wide tiles whose last 32-column
+    chunk is half full; 200 and 1000 columns: 128-wide tiles with a ragged last tile)."""
     torch = cuda
     g = torch.Generator(device="cuda").manual_seed(T * 7 + N + K)
     x = (torch.randn(T, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
